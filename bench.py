@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""Benchmark of the fused f64 HMC leapfrog chain (the hot path's headline).
+
+Workload (one "step" = one call of the fused chain over one batch):
+anisotropic Gaussian target, d = 1000, diagonal precision prec_i ~ U(0.5, 2)
+(seed 3), 4096 independent chains per GPU, q0, p0 ~ N(0, 1), inv_mass = 1,
+eps = 0.01, L = 32 leapfrog steps per trajectory, f64.  Outputs are the
+reference contract's q/p/grad trajectories [chain][k][i] and logp [chain][k].
+
+  value  chain-steps/s over all ranks, inputs resident in HBM, timed per step
+         with CUDA events on the launching stream, L2 flushed between steps.
+  e2e    the same metric through the C ABI with host buffers: every step
+         uploads q0/p0/inv_mass/prec from pinned host memory and downloads the
+         four outputs into pinned host memory (nxv_buf_upload/_download).
+  roofline  algorithmic bytes of one call / its measured duration, against
+         the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  cpu_baseline  the oracle (C restatement, OpenMP over all host cores) on a
+         bounded sample of the same workload.
+
+Multi-GPU (torchrun, one process per GPU): chains are independent, so each
+rank integrates its own 4096 chains (weak scaling) and one NCCL all-gather
+collects the per-chain diagnostics (final logp) each step.
+`--impl reference` times the CPU restatement of the reference path instead.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+D, CHAINS, L, EPS = 1000, 4096, 32, 0.01
+METRIC = "f64 leapfrog steps/s (chains×L)"
+UNIT = "chain-steps/s"
+# algorithmic bytes of one call: read q0, p0, inv_mass (3*d*8 per chain),
+# write q/p/grad trajectories (3*L*d*8 per chain) and logp (L*8 per chain);
+# prec (d*8) is read once.
+def algo_bytes(chains, d=D, steps=L):
+    return chains * (3 * d * 8 + 3 * steps * d * 8 + steps * 8) + d * 8
+
+
+def gauss_inputs(chains, d=D, seed=3):
+    r = np.random.default_rng(seed)
+    prec = r.uniform(0.5, 2.0, d)
+    q0 = r.normal(size=(chains, d))
+    p0 = r.normal(size=(chains, d))
+    return prec, q0, p0, np.ones((chains, d))
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"nxv_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample(seconds_min=10.0, seconds_max=30.0, chains=256):
+    """Oracle (C restatement, all host threads) on a bounded sample."""
+    from oracle import binding as orc
+    nthreads = orc.max_threads()
+    prec, q0, p0, m = gauss_inputs(chains)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        orc.chain_gauss_f64(q0, p0, m, prec, 0.0, D, chains, L, EPS, nthreads=nthreads)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds_min or (el * (done + 1) / done) > seconds_max:
+            break
+    rate = done * chains * L / el
+    return {"value": rate, "unit": UNIT, "cores": nthreads, "kind": "port",
+            "sample": f"{done} x {chains} chains x L={L} x d={D} (f64), {el:.1f} s, "
+                      f"oracle C restatement with OpenMP; nproc={os.cpu_count()}"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    per_step = []
+    from oracle import binding as orc
+    nthreads = orc.max_threads()
+    chains = 256
+    prec, q0, p0, m = gauss_inputs(chains)
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        orc.chain_gauss_f64(q0, p0, m, prec, 0.0, D, chains, L, EPS, nthreads=nthreads)
+        if i >= args.warmup:
+            per_step.append(time.perf_counter() - t0)
+    t = sum(per_step)
+    value = args.steps * chains * L / t
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded numpy: prec~U(0.5,2) seed 3, q0,p0~N(0,1))",
+        "config": {"workload": "anisotropic Gaussian HMC leapfrog (reference path restated on CPU)",
+                   "chains": chains, "d": D, "L": L, "eps": EPS},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
+                         "sample": f"{chains} chains x L={L} x d={D} per step; the reference's "
+                                   "Vulkan/Elixir stack cannot run here, so its CPU path is the "
+                                   "oracle's C restatement of Nx.BinaryBackend semantics"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--chains", type=int, default=CHAINS)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from nx_vulkan_b200 import _native, vulkan as nxv
+    lib = _native.load()
+    assert nxv.init_devices([local]) == "ok", _native.last_error()
+    stream = torch.cuda.current_stream()
+    lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
+
+    chains = args.chains
+    prec, q0, p0, m = gauss_inputs(chains, seed=3 + 1000 * rank)
+    tq0 = torch.from_numpy(q0).to(dev)
+    tp0 = torch.from_numpy(p0).to(dev)
+    tm = torch.from_numpy(m).to(dev)
+    tprec = torch.from_numpy(prec).to(dev)
+    outs = [torch.empty(chains * L * D, dtype=torch.float64, device=dev) for _ in range(3)]
+    outs.append(torch.empty(chains * L, dtype=torch.float64, device=dev))
+    wrap = lambda t: lib.nxv_buf_wrap(C.c_void_p(t.data_ptr()), t.numel() * t.element_size())
+    h_in = [wrap(t) for t in (tq0, tp0, tm, tprec)]
+    h_out = [wrap(t) for t in outs]
+    spv = nxv.shader_path("leapfrog_chain_gauss_f64_batched.spv")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 2x L2
+
+    def step():
+        rc = lib.nxv_leapfrog_chain_gauss_f64_batched(*h_out, *h_in, D, chains, L, EPS, 0.0, spv)
+        if rc != 0:
+            raise RuntimeError(f"leapfrog failed: {rc} {_native.last_error()}")
+
+    diag = torch.empty(world * chains, dtype=torch.float64, device=dev)
+
+    def diagnostics():
+        if world > 1:
+            last = outs[3].view(chains, L)[:, -1].contiguous()
+            dist.all_gather_into_tensor(diag, last)
+
+    for _ in range(args.warmup):
+        step()
+        diagnostics()
+    torch.cuda.synchronize()
+    n_launch0 = lib.nxv_launch_count()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            evs[i][0].record(stream)
+            step()
+            diagnostics()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = (lib.nxv_launch_count() - n_launch0) // args.steps * args.steps
+    per_ms = [a.elapsed_time(b) for a, b in evs]
+    t_ms = sum(per_ms)
+    t_all = torch.tensor([t_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
+    t_ms = float(t_all.item())
+    value = world * chains * L * args.steps / (t_ms / 1e3)
+    clocks = clk.summary()
+
+    # Roofline of the dominant kernel: one call (chain kernel + its tile fold),
+    # timed alone (no collective) per step with events.
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(max(3, args.steps // 2))]
+    for a, b in kev:
+        flush.zero_()
+        a.record(stream)
+        step()
+        b.record(stream)
+    torch.cuda.synchronize()
+    k_ms = statistics.median([a.elapsed_time(b) for a, b in kev])
+    peak, peak_kind = peaks()
+    abytes = algo_bytes(chains)
+    achieved = abytes / (k_ms / 1e3) / 1e9
+    traffic = None
+    tr_path = ROOT / "profiles" / "leapfrog_gauss_f64_traffic.json"
+    if tr_path.exists():
+        tr = json.loads(tr_path.read_text())
+        traffic = tr.get("bytes_per_launch_scaled", tr.get("bytes_per_launch"))
+
+    # e2e through the C ABI with host buffers (library-owned device buffers).
+    e2e = None
+    if not args.no_e2e:
+        lib.nxv_set_stream(None)
+        hb_in = [torch.from_numpy(a.reshape(-1)).pin_memory() for a in (q0, p0, m, prec)]
+        hb_out = [torch.empty(o.numel(), dtype=torch.float64).pin_memory() for o in outs]
+        d_in = [lib.nxv_buf_alloc(t.numel() * 8) for t in hb_in]
+        d_out = [lib.nxv_buf_alloc(t.numel() * 8) for t in hb_out]
+
+        def e2e_step():
+            for h, t in zip(d_in, hb_in):
+                assert lib.nxv_buf_upload(h, C.c_void_p(t.data_ptr()), t.numel() * 8) == 0
+            rc = lib.nxv_leapfrog_chain_gauss_f64_batched(*d_out, *d_in, D, chains, L, EPS, 0.0, spv)
+            assert rc == 0, _native.last_error()
+            for h, t in zip(d_out, hb_out):
+                assert lib.nxv_buf_download(h, C.c_void_p(t.data_ptr()), t.numel() * 8) == 0
+
+        for _ in range(2):
+            e2e_step()
+        n_e2e = max(3, min(args.steps, 5))
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            e2e_step()
+        el = time.perf_counter() - t0
+        el_t = torch.tensor([el], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(el_t, op=dist.ReduceOp.MAX)
+        el = float(el_t.item())
+        for h in d_in + d_out:
+            lib.nxv_buf_free(h)
+        e2e = {"value": world * chains * L * n_e2e / el, "unit": UNIT,
+               "h2d_bytes_per_step": sum(t.numel() * 8 for t in hb_in),
+               "d2h_bytes_per_step": sum(t.numel() * 8 for t in hb_out),
+               "steps": n_e2e, "timing": "host wall clock around synchronous C-ABI calls, max over ranks"}
+        lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
+
+    secondary = None
+    if not args.no_secondary and rank == 0:
+        secondary = fused_elementwise_gbs(lib, nxv, torch, dev, stream, peak)
+
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        cpu = cpu_sample()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded numpy: prec~U(0.5,2) seed 3, q0,p0~N(0,1); rank r uses seed 3+1000r)",
+            "config": {"workload": "anisotropic Gaussian HMC leapfrog, fused K-step chain",
+                       "chains_per_gpu": chains, "d": D, "L": L, "eps": EPS, "inv_mass": 1.0,
+                       "parallelism": f"chains sharded, {world} rank(s), NCCL all-gather of final logp per step"
+                       if world > 1 else "1 GPU",
+                       "l2": "256 MiB buffer written between timed steps (L2 flush); per-step traffic 3.25 GB"},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": abytes, "launch_ms": k_ms,
+                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        if secondary:
+            line["secondary"] = secondary
+        print(json.dumps(line), flush=True)
+    for h in h_in + h_out:
+        lib.nxv_buf_free(h)
+    lib.nxv_set_stream(None)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def fused_elementwise_gbs(lib, nxv, torch, dev, stream, peak):
+    """tanh(exp(x*y + z) - 1.0) on f32/f64[1,048,576] (x,y,z ~ U(-1,1), seed 0), one
+    fused kernel per call, rotating over buffer sets totalling > 2x L2."""
+    res = {}
+    n = 1 << 20
+    for dt, name, code in ((torch.float32, "f32", 0), (torch.float64, "f64", 1)):
+        es = 4 if code == 0 else 8
+        sets = max(4, (512 << 20) // (4 * n * es))
+        g = torch.Generator(device="cpu").manual_seed(0)
+        bufs = []
+        for s in range(sets):
+            xs = [(torch.rand(n, generator=g, dtype=torch.float64) * 2 - 1).to(dt).to(dev) for _ in range(3)]
+            out = torch.empty(n, dtype=dt, device=dev)
+            hs = [lib.nxv_buf_wrap(C.c_void_p(t.data_ptr()), n * es) for t in xs + [out]]
+            bufs.append((xs, out, hs))
+        ops = (C.c_uint * 8)(1, 0, 100, 2, 106, 255, 255, 255)
+        src = (C.c_uint * 8)(1, 2, 1, 0, 1, 1, 1, 1)
+        imm = (C.c_double * 8)(0, 0, 0, 1.0, 0, 0, 0, 0)
+        spv = nxv.shader_path("fused_elementwise_imm.spv")
+
+        def call(s):
+            _, _, hs = bufs[s % sets]
+            rc = lib.nxv_fused_chain_imm(hs[3], hs[0], hs[1], hs[2], None, n, 5, ops, src, imm, code, spv)
+            assert rc == 0
+
+        for s in range(sets):
+            call(s)
+        reps = 20 * sets
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for s in range(reps):
+            call(s)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        gbs = 4 * n * es / (ms / 1e3) / 1e9
+        res[f"fused_elementwise_{name}"] = {
+            "metric": "fused-elementwise HBM GB/s", "value": gbs, "unit": "GB/s",
+            "frac_of_hbm": gbs / peak, "us_per_call": ms * 1e3,
+            "bytes_per_call": 4 * n * es,
+            "config": f"tanh(exp(x*y+z)-1.0), {name}[1048576], {sets} rotating buffer sets "
+                      f"({sets * 4 * n * es >> 20} MiB > 2x L2), back-to-back launches"}
+        for _, _, hs in bufs:
+            for h in hs:
+                lib.nxv_buf_free(h)
+    return res
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,389 @@
+// k_leapfrog.cu -- fused K-step HMC leapfrog chains (sm_100a).
+//
+// One kernel template serves every chain family of the reference
+// (c_src/nx_vulkan_shim.h:191-280; lib/nx_vulkan.ex:582-726) and the batched
+// f64 Gaussian of the anisotropic-target workload.  Per step k and element i:
+//     p_h = p + (eps/2) * g            (g = grad log p at the current q)
+//     q   = q + (eps * m_i) * p_h
+//     g   = grad log p(q)
+//     p   = p_h + (eps/2) * g
+// (the corrected sign, PLAN_FUSED_LEAPFROG.md:18-24), then q, p, g are
+// written to the [chain][k][i] trajectories and the step's log density
+// logp = scale * sum_i term(q_i) + cst goes to logp[chain][k].
+//
+// B200 design: the work is HBM-write bound (3 * sizeof(T) bytes per element
+// and step; the inputs are read once).  A CTA owns one tile of NT*VPT
+// consecutive elements of one chain, keeps q, p, g, m (and the per-element
+// target parameter) in registers for all K steps, and streams the three
+// trajectory rows out with coalesced evict-first stores.  The per-step sum
+// is a warp-shuffle tree whose per-warp results wait in shared memory; one
+// barrier every 32 steps folds them (fixed order, so deterministic) instead
+// of a barrier per step as in the reference shader's 256-wide tree.  When a
+// chain spans several tiles, tiles write partial sums to scratch and a
+// small second kernel folds them in tile order.
+#include "kernels.h"
+#include "ops_common.cuh"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+namespace nxv {
+
+namespace {
+
+constexpr int KC = 32;  // steps per logp flush
+
+// ---- families (per-element math matches the CPU oracle op by op) -----------
+
+struct NoParam {};
+
+struct FamNormal32 {
+    float mu, sigma, inv_var;
+    using P = NoParam;
+    __device__ P load(const void*, size_t) const { return P{}; }
+    __device__ float grad(float q, P) const { return -mul_(sub_(q, mu), inv_var); }
+    __device__ double term(float q, P) const {
+        float z = div_(sub_(q, mu), sigma);
+        return (double)mul_(z, z);
+    }
+};
+struct FamExp32 {
+    float lambda;
+    using P = NoParam;
+    __device__ P load(const void*, size_t) const { return P{}; }
+    __device__ float grad(float q, P) const { return sub_(1.0f, mul_(lambda, expf(q))); }
+    __device__ double term(float q, P) const { return (double)sub_(q, mul_(lambda, expf(q))); }
+};
+struct FamStudentT32 {
+    float mu, sigma, nu, logp_const;
+    using P = NoParam;
+    __device__ P load(const void*, size_t) const { return P{}; }
+    __device__ float grad(float q, P) const {
+        float d = sub_(q, mu);
+        return -div_(mul_(add_(nu, 1.0f), d), add_(mul_(nu, mul_(sigma, sigma)), mul_(d, d)));
+    }
+    __device__ double term(float q, P) const {
+        float z = div_(sub_(q, mu), sigma);
+        float l = log1pf(div_(mul_(z, z), nu));
+        return (double)sub_(logp_const, mul_(mul_(add_(nu, 1.0f), 0.5f), l));
+    }
+};
+struct FamCauchy32 {
+    float loc, scale, log_pi_scale;
+    using P = NoParam;
+    __device__ P load(const void*, size_t) const { return P{}; }
+    __device__ float grad(float q, P) const {
+        float d = sub_(q, loc);
+        return -div_(mul_(2.0f, d), add_(mul_(scale, scale), mul_(d, d)));
+    }
+    __device__ double term(float q, P) const {
+        float z = div_(sub_(q, loc), scale);
+        return (double)sub_(log_pi_scale, log1pf(mul_(z, z)));
+    }
+};
+struct FamHalfNormal32 {
+    float sigma, log_const;
+    using P = NoParam;
+    __device__ P load(const void*, size_t) const { return P{}; }
+    __device__ float grad(float q, P) const {
+        return sub_(1.0f, div_(expf(mul_(2.0f, q)), mul_(sigma, sigma)));
+    }
+    __device__ double term(float q, P) const {
+        float e2 = expf(mul_(2.0f, q));
+        return (double)sub_(add_(log_const, q), div_(e2, mul_(2.0f, mul_(sigma, sigma))));
+    }
+};
+struct FamWeibull32 {
+    float k, lambda;
+    using P = NoParam;
+    __device__ P load(const void*, size_t) const { return P{}; }
+    __device__ float grad(float q, P) const {
+        float r = powf(div_(expf(q), lambda), k);
+        return mul_(k, sub_(1.0f, r));
+    }
+    __device__ double term(float q, P) const {
+        float r = powf(div_(expf(q), lambda), k);
+        return (double)sub_(mul_(k, q), r);
+    }
+};
+// f64 Gaussian with a per-element precision (prec == nullptr: scalar).
+struct FamGauss64 {
+    const double* prec;
+    double prec_s, mu;
+    using P = double;
+    __device__ P load(const void*, size_t i) const { return prec ? __ldg(prec + i) : prec_s; }
+    __device__ double grad(double q, P pr) const { return -mul_(pr, sub_(q, mu)); }
+    __device__ double term(double q, P pr) const {
+        double d = sub_(q, mu);
+        return mul_(mul_(pr, d), d);
+    }
+};
+
+template <typename T>
+struct ChainArgs {
+    T* qc;
+    T* pc;
+    T* gc;
+    T* logp;          // [chain][k] (mode 0, tiles == 1) or [k][tile] (mode 1)
+    double* partial;  // [chain][k][tile] when tiles > 1 in mode 0
+    const T* q0;
+    const T* p0;
+    const T* m;
+    size_t n;
+    unsigned chains, tiles, K;
+    T eps, he;
+    double scale, cst;
+    const double* cst_dev;  // added to cst when non-null
+    int mode;               // 0: per-chain logp; 1: per-256-group partials (_lg)
+};
+
+template <typename T>
+__device__ __forceinline__ void st_stream(T* p, T v) { __stcs(p, v); }
+
+template <typename T, class Fam, int NT, int VPT>
+__global__ void __launch_bounds__(NT) k_chain(ChainArgs<T> g, Fam fam) {
+    constexpr int NW = NT / 32;
+    __shared__ double red[KC][NW];
+    const unsigned tile = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const double cst = g.cst + (g.cst_dev ? *g.cst_dev : 0.0);
+    for (unsigned chain = blockIdx.y; chain < g.chains; chain += gridDim.y) {
+        const size_t cbase = (size_t)chain * g.n;
+        T q[VPT], p[VPT], gr[VPT], em[VPT];
+        typename Fam::P ep[VPT];
+        bool ok[VPT];
+#pragma unroll
+        for (int v = 0; v < VPT; v++) {
+            size_t i = (size_t)tile * (NT * VPT) + (size_t)v * NT + tid;
+            ok[v] = i < g.n;
+            size_t ii = ok[v] ? i : 0;
+            q[v] = ok[v] ? g.q0[cbase + ii] : T(0);
+            p[v] = ok[v] ? g.p0[cbase + ii] : T(0);
+            em[v] = ok[v] ? g.m[cbase + ii] : T(0);
+            ep[v] = fam.load(nullptr, ii);
+            gr[v] = fam.grad(q[v], ep[v]);
+        }
+        const T eps = g.eps, he = g.he;
+        for (unsigned k0 = 0; k0 < g.K; k0 += KC) {
+            const unsigned kn = (g.K - k0) < (unsigned)KC ? (g.K - k0) : (unsigned)KC;
+            for (unsigned kk = 0; kk < kn; kk++) {
+                const unsigned k = k0 + kk;
+                const size_t row = ((size_t)chain * g.K + k) * g.n;
+                double t = 0.0;
+#pragma unroll
+                for (int v = 0; v < VPT; v++) {
+                    T ph = add_(p[v], mul_(he, gr[v]));
+                    q[v] = add_(q[v], mul_(mul_(eps, em[v]), ph));
+                    gr[v] = fam.grad(q[v], ep[v]);
+                    p[v] = add_(ph, mul_(he, gr[v]));
+                    if (ok[v]) {
+                        size_t i = (size_t)tile * (NT * VPT) + (size_t)v * NT + tid;
+                        st_stream(g.qc + row + i, q[v]);
+                        st_stream(g.pc + row + i, p[v]);
+                        st_stream(g.gc + row + i, gr[v]);
+                        t = __dadd_rn(t, fam.term(q[v], ep[v]));
+                    }
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+                    t = __dadd_rn(t, __shfl_down_sync(0xffffffffu, t, off));
+                if (lane == 0) red[kk][warp] = t;
+            }
+            __syncthreads();
+            if (tid < (int)kn) {
+                double s = red[tid][0];
+#pragma unroll
+                for (int w = 1; w < NW; w++) s = __dadd_rn(s, red[tid][w]);
+                const unsigned k = k0 + tid;
+                if (g.mode == 1) {
+                    double val = g.scale * s + (tile == 0 ? cst : 0.0);
+                    g.logp[(size_t)k * g.tiles + tile] = (T)val;
+                } else if (g.tiles == 1) {
+                    g.logp[(size_t)chain * g.K + k] = (T)(g.scale * s + cst);
+                } else {
+                    g.partial[((size_t)chain * g.K + k) * g.tiles + tile] = s;
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+template <typename T>
+__global__ void k_chain_fold(ChainArgs<T> g) {
+    size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    size_t total = (size_t)g.chains * g.K;
+    if (t >= total) return;
+    const double cst = g.cst + (g.cst_dev ? *g.cst_dev : 0.0);
+    const double* pp = g.partial + t * g.tiles;
+    double s = pp[0];
+    for (unsigned i = 1; i < g.tiles; i++) s = __dadd_rn(s, pp[i]);
+    g.logp[t] = (T)(g.scale * s + cst);
+}
+
+// 0.5 * sum_i log prec_i - n * log sqrt(2 pi), fixed-order block tree.
+__global__ void __launch_bounds__(256) k_gauss_const(const double* __restrict__ prec, size_t n,
+                                                     double* out) {
+    __shared__ double sm[8];
+    double s = 0.0;
+    for (size_t i = threadIdx.x; i < n; i += 256) s = __dadd_rn(s, log(prec[i]));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s = __dadd_rn(s, __shfl_down_sync(0xffffffffu, s, off));
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = sm[0];
+        for (int w = 1; w < 8; w++) t = __dadd_rn(t, sm[w]);
+        *out = 0.5 * t - (double)n * 0.91893853320467274178;
+    }
+}
+
+// Launch configuration: NT threads x VPT elements per thread per tile.
+// NXV_LF_CFG="NTxVPT" overrides the heuristic (256x1, 256x2, 256x4, 256x8, 128x8).
+struct Cfg { int nt, vpt; };
+
+Cfg pick_cfg(Ctx& c, size_t n, size_t chains, int mode) {
+    if (mode == 1) return Cfg{256, 1};
+    const char* env = getenv("NXV_LF_CFG");
+    if (env && *env) {
+        int a = 0, b = 0;
+        if (sscanf(env, "%dx%d", &a, &b) == 2) {
+            if ((a == 256 && (b == 1 || b == 2 || b == 4 || b == 8)) || (a == 128 && b == 8))
+                return Cfg{a, b};
+        }
+    }
+    // Small-n chains: one tile covers the chain.  Large batches: 256-element
+    // tiles balance best across 148 SMs.
+    size_t slots = (size_t)c.dev->sm_count * 8;
+    size_t tiles1 = (n + 255) / 256;
+    if (tiles1 * chains >= 2 * slots) return Cfg{256, 1};
+    if (n <= 512) return Cfg{256, 2};
+    if (n <= 1024) return Cfg{256, 4};
+    return Cfg{256, 8};
+}
+
+template <typename T, class Fam, int NT, int VPT>
+int launch_cfg(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
+    g.tiles = (unsigned)((g.n + NT * VPT - 1) / (NT * VPT));
+    if (g.mode == 0 && g.tiles > 1 && !g.partial) {
+        g.partial = (double*)scratch(c, (size_t)g.chains * g.K * g.tiles * sizeof(double));
+        if (!g.partial) return E_CUDA;
+    }
+    unsigned gy = g.chains < 65535u ? g.chains : 65535u;
+    dim3 grid(g.tiles, gy);
+    k_chain<T, Fam, NT, VPT><<<grid, NT, 0, c.stream>>>(g, fam);
+    count_launch();
+    if (g.mode == 0 && g.tiles > 1) {
+        size_t total = (size_t)g.chains * g.K;
+        k_chain_fold<T><<<(unsigned)((total + 255) / 256), 256, 0, c.stream>>>(g);
+        count_launch();
+    }
+    return finish(c);
+}
+
+template <typename T, class Fam>
+int launch_family(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
+    if (g.n == 0 || g.K == 0 || g.chains == 0) return OK;
+    ScratchGuard guard(c);
+    if (g.tiles > 65535u) {
+        set_error("chain dimension too large");
+        return E_ARG;
+    }
+    Cfg cf = pick_cfg(c, g.n, g.chains, g.mode);
+    if (cf.nt == 128) return launch_cfg<T, Fam, 128, 8>(c, g, fam);
+    switch (cf.vpt) {
+        case 1: return launch_cfg<T, Fam, 256, 1>(c, g, fam);
+        case 2: return launch_cfg<T, Fam, 256, 2>(c, g, fam);
+        case 4: return launch_cfg<T, Fam, 256, 4>(c, g, fam);
+        default: return launch_cfg<T, Fam, 256, 8>(c, g, fam);
+    }
+}
+
+}  // namespace
+
+int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void* gc,
+                     void* logp, const void* q0, const void* p0, const void* m, size_t n,
+                     size_t chains, unsigned K, float eps, int logp_mode) {
+    ChainArgs<float> g{};
+    g.qc = (float*)qc;
+    g.pc = (float*)pc;
+    g.gc = (float*)gc;
+    g.logp = (float*)logp;
+    g.q0 = (const float*)q0;
+    g.p0 = (const float*)p0;
+    g.m = (const float*)m;
+    g.n = n;
+    g.chains = (unsigned)chains;
+    g.K = K;
+    g.eps = eps;
+    g.he = 0.5f * eps;
+    g.mode = logp_mode;
+    g.scale = 1.0;
+    g.cst = 0.0;
+    switch (fam) {
+        case FAM_NORMAL: {
+            g.scale = -0.5;
+            g.cst = -(double)n * (log((double)prm[1]) + 0.91893853320467274178);
+            FamNormal32 f{prm[0], prm[1], 1.0f / (prm[1] * prm[1])};
+            return launch_family(c, g, f);
+        }
+        case FAM_EXP: {
+            g.cst = (double)n * log((double)prm[0]);
+            return launch_family(c, g, FamExp32{prm[0]});
+        }
+        case FAM_STUDENTT: return launch_family(c, g, FamStudentT32{prm[0], prm[1], prm[2], prm[3]});
+        case FAM_CAUCHY: return launch_family(c, g, FamCauchy32{prm[0], prm[1], prm[2]});
+        case FAM_HALFNORMAL: return launch_family(c, g, FamHalfNormal32{prm[0], prm[1]});
+        case FAM_WEIBULL: {
+            g.cst = (double)prm[2];
+            return launch_family(c, g, FamWeibull32{prm[0], prm[1]});
+        }
+    }
+    set_error("unknown chain family %d", fam);
+    return E_ARG;
+}
+
+int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
+                           const void* p0, const void* m, const void* prec, double prec_scalar,
+                           double mu, size_t n, size_t chains, unsigned K, double eps) {
+    ChainArgs<double> g{};
+    g.qc = (double*)qc;
+    g.pc = (double*)pc;
+    g.gc = (double*)gc;
+    g.logp = (double*)logp;
+    g.q0 = (const double*)q0;
+    g.p0 = (const double*)p0;
+    g.m = (const double*)m;
+    g.n = n;
+    g.chains = (unsigned)chains;
+    g.K = K;
+    g.eps = eps;
+    g.he = 0.5 * eps;
+    g.mode = 0;
+    g.scale = -0.5;
+    if (n == 0 || K == 0 || chains == 0) return OK;
+    ScratchGuard guard(c);
+    if (prec) {
+        // The constant needs sum(log prec): one tiny launch ahead of the
+        // chain writes it to scratch[0]; tile partials (if any) follow at
+        // byte offset 256 of the same scratch region.
+        Cfg cf = pick_cfg(c, n, chains, 0);
+        size_t tiles = (n + (size_t)cf.nt * cf.vpt - 1) / ((size_t)cf.nt * cf.vpt);
+        size_t need = 256 + (tiles > 1 ? chains * (size_t)K * tiles * sizeof(double) : 0);
+        char* base = (char*)scratch(c, need);
+        if (!base) return E_CUDA;
+        k_gauss_const<<<1, 256, 0, c.stream>>>((const double*)prec, n, (double*)base);
+        count_launch();
+        g.cst = 0.0;
+        g.cst_dev = (const double*)base;
+        if (tiles > 1) g.partial = (double*)(base + 256);
+        return launch_family(c, g, FamGauss64{(const double*)prec, 0.0, mu});
+    }
+    // scalar precision: the reference's Normal(mu, sigma) f64 chain with
+    // prec = 1/sigma^2; the constant is -n (log sigma + log sqrt(2 pi)).
+    g.cst = 0.5 * (double)n * log(prec_scalar) - (double)n * 0.91893853320467274178;
+    return launch_family(c, g, FamGauss64{nullptr, prec_scalar, mu});
+}
+
+}  // namespace nxv

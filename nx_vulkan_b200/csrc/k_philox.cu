@@ -1,0 +1,109 @@
+// k_philox.cu -- counter-based Philox-2x32-10 (Salmon et al., SC'11).
+//
+// The reference runs Random123 Philox 2x32-10 (PLAN_FUSED_LEAPFROG.md:27-29)
+// but its counter layout exists only inside a compiled shader, so this
+// library defines and documents its own mapping (identical in the CPU
+// oracle, which pins it bit for bit):
+//   f32 uniform:  element i <- word (i & 1) of philox(ctr = (i >> 1, 0), key = seed),
+//                 u = (w >> 8) * 2^-24 in [0, 1)
+//   f32 normal:   pair c <- u1 = ((w0 >> 8) + 1) * 2^-24, u2 = (w1 >> 8) * 2^-24,
+//                 r = sqrt(-2 ln u1): (r cos 2 pi u2, r sin 2 pi u2) in f64, rounded
+//   f64 uniform:  element i <- philox((i, 1), seed): (((w0 << 32) | w1) >> 11) * 2^-53
+//   f64 normal:   pair c <- u1 = philox((2c, 1)) + 2^-53, u2 = philox((2c + 1, 1))
+// Write-bound: one thread per pair, vector stores when aligned.
+#include "kernels.h"
+
+#include <math.h>
+
+namespace nxv {
+
+namespace {
+
+__device__ __forceinline__ void philox2x32(uint32_t x0, uint32_t x1, uint32_t key, uint32_t& o0,
+                                           uint32_t& o1) {
+#pragma unroll
+    for (int r = 0; r < 10; r++) {
+        uint32_t lo = x0 * 0xD256D193u;
+        uint32_t hi = __umulhi(x0, 0xD256D193u);
+        x0 = hi ^ key ^ x1;
+        x1 = lo;
+        key += 0x9E3779B9u;
+    }
+    o0 = x0;
+    o1 = x1;
+}
+
+constexpr double kTwoPi = 6.283185307179586476925286766559;
+
+__global__ void k_random_f32(float* __restrict__ out, size_t n, uint32_t seed, unsigned dist) {
+    size_t pairs = (n + 1) / 2;
+    size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t c = (size_t)blockIdx.x * blockDim.x + threadIdx.x; c < pairs; c += stride) {
+        uint32_t w0, w1;
+        philox2x32((uint32_t)c, 0u, seed, w0, w1);
+        float v0, v1;
+        if (dist == 0) {
+            v0 = (float)(w0 >> 8) * 0x1.0p-24f;
+            v1 = (float)(w1 >> 8) * 0x1.0p-24f;
+        } else {
+            double u1 = ((double)(w0 >> 8) + 1.0) * 0x1.0p-24;
+            double u2 = (double)(w1 >> 8) * 0x1.0p-24;
+            double r = sqrt(-2.0 * log(u1));
+            double a = kTwoPi * u2;
+            v0 = (float)(r * cos(a));
+            v1 = (float)(r * sin(a));
+        }
+        if (2 * c + 1 < n) {
+            if ((((uintptr_t)(out + 2 * c)) & 7) == 0) {
+                *reinterpret_cast<float2*>(out + 2 * c) = make_float2(v0, v1);
+            } else {
+                out[2 * c] = v0;
+                out[2 * c + 1] = v1;
+            }
+        } else {
+            out[2 * c] = v0;
+        }
+    }
+}
+
+__device__ __forceinline__ double u53(uint32_t i, uint32_t seed) {
+    uint32_t w0, w1;
+    philox2x32(i, 1u, seed, w0, w1);
+    unsigned long long v = ((((unsigned long long)w0) << 32) | w1) >> 11;
+    return (double)v * 0x1.0p-53;
+}
+
+__global__ void k_random_f64(double* __restrict__ out, size_t n, uint32_t seed, unsigned dist) {
+    size_t stride = (size_t)gridDim.x * blockDim.x;
+    if (dist == 0) {
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+            out[i] = u53((uint32_t)i, seed);
+        return;
+    }
+    size_t pairs = (n + 1) / 2;
+    for (size_t c = (size_t)blockIdx.x * blockDim.x + threadIdx.x; c < pairs; c += stride) {
+        double u1 = u53((uint32_t)(2 * c), seed) + 0x1.0p-53;
+        double u2 = u53((uint32_t)(2 * c + 1), seed);
+        double r = sqrt(-2.0 * log(u1));
+        double a = kTwoPi * u2;
+        out[2 * c] = r * cos(a);
+        if (2 * c + 1 < n) out[2 * c + 1] = r * sin(a);
+    }
+}
+
+}  // namespace
+
+int launch_random(Ctx& c, int dt, void* out, size_t n, uint32_t seed, unsigned dist) {
+    if (n == 0) return OK;
+    if (n > 0x100000000ull) {
+        set_error("random: at most 2^32 elements per call (32-bit counter)");
+        return E_ARG;
+    }
+    unsigned g = grid_for(c, (n + 1) / 2, 256, 8);
+    if (dt == F32) k_random_f32<<<g, 256, 0, c.stream>>>((float*)out, n, seed, dist);
+    else k_random_f64<<<g, 256, 0, c.stream>>>((double*)out, n, seed, dist);
+    count_launch();
+    return finish(c);
+}
+
+}  // namespace nxv

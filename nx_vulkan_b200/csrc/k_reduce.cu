@@ -1,0 +1,388 @@
+// k_reduce.cu -- deterministic reductions, argmax, logsumexp, kinetic energy.
+//
+// Layout: every reduction is over the middle axis of a virtual
+// (outer, R, inner) row-major tensor (c_src/nx_vulkan_shim.h:129-134); a full
+// reduce is (1, n, 1).  Two kernel shapes:
+//   rows (inner == 1): a CTA reduces one segment of one row with 16-byte
+//     vector loads; S segments per row when rows are few (a full reduce uses
+//     up to 4 CTAs per SM), each segment's partial goes to scratch and a
+//     second launch folds the S partials of a row in index order;
+//   cols (inner > 1): a thread owns one (o, j) column and walks r in order,
+//     loads coalesced across j; R is split into S segments the same way when
+//     outer*inner is too small to fill the GPU.
+// The grid shape depends only on (outer, R, inner) and the SM count, and
+// every combine happens in a fixed tree, so results are bit-reproducible.
+// Accumulators: f32 sums in f64 (rounded once), f64 sums in double-double,
+// max/min in the input type with NaN propagation, argmax as (value, index)
+// under a total order (NaN first, then larger value, then lower index).
+#include "kernels.h"
+#include "ops_common.cuh"
+
+#include <math.h>
+
+namespace nxv {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+// ---- reducers -----------------------------------------------------------------
+
+template <typename T> struct SumR;
+template <> struct SumR<float> {
+    using Acc = double;
+    using Out = float;
+    __device__ static Acc init() { return 0.0; }
+    __device__ static Acc add(Acc a, float x, long long) { return __dadd_rn(a, (double)x); }
+    __device__ static Acc combine(Acc a, Acc b) { return __dadd_rn(a, b); }
+    __device__ static Acc shfl(Acc a, int off) { return __shfl_down_sync(0xffffffffu, a, off); }
+    __device__ static Out out(Acc a) { return (float)a; }
+};
+template <> struct SumR<double> {
+    using Acc = dd;
+    using Out = double;
+    __device__ static Acc init() { return dd{0.0, 0.0}; }
+    __device__ static Acc add(Acc a, double x, long long) { return dd_add_d(a, x); }
+    __device__ static Acc combine(Acc a, Acc b) { return dd_add(a, b); }
+    __device__ static Acc shfl(Acc a, int off) {
+        return dd{__shfl_down_sync(0xffffffffu, a.hi, off), __shfl_down_sync(0xffffffffu, a.lo, off)};
+    }
+    __device__ static Out out(Acc a) { return dd_value(a); }
+};
+
+template <typename T, bool MAX> struct MaxR {
+    using Acc = T;
+    using Out = T;
+    __device__ static Acc init() { return MAX ? -INFINITY : INFINITY; }
+    __device__ static Acc combine(Acc a, Acc b) {
+        if (a != a) return a;
+        if (b != b) return b;
+        return MAX ? ((b > a) ? b : a) : ((b < a) ? b : a);
+    }
+    __device__ static Acc add(Acc a, T x, long long) { return combine(a, x); }
+    __device__ static Acc shfl(Acc a, int off) { return __shfl_down_sync(0xffffffffu, a, off); }
+    __device__ static Out out(Acc a) { return a; }
+};
+
+template <typename T> struct ArgAcc {
+    T v;
+    long long i;
+};
+template <typename T, bool MIN> struct ArgR {
+    using Acc = ArgAcc<T>;
+    using Out = long long;
+    __device__ static Acc init() { return Acc{MIN ? (T)INFINITY : (T)-INFINITY, -1}; }
+    // true when b should replace a
+    __device__ static bool better(Acc a, Acc b) {
+        if (b.i < 0) return false;
+        if (a.i < 0) return true;
+        bool an = a.v != a.v, bn = b.v != b.v;
+        if (an || bn) {
+            if (an && bn) return b.i < a.i;
+            return bn;
+        }
+        if (b.v == a.v) return b.i < a.i;
+        return MIN ? (b.v < a.v) : (b.v > a.v);
+    }
+    __device__ static Acc combine(Acc a, Acc b) { return better(a, b) ? b : a; }
+    __device__ static Acc add(Acc a, T x, long long idx) { return combine(a, Acc{x, idx}); }
+    __device__ static Acc shfl(Acc a, int off) {
+        return Acc{__shfl_down_sync(0xffffffffu, a.v, off), __shfl_down_sync(0xffffffffu, a.i, off)};
+    }
+    __device__ static Out out(Acc a) { return a.i < 0 ? 0 : a.i; }
+};
+
+template <class R>
+__device__ typename R::Acc block_reduce(typename R::Acc a) {
+    __shared__ typename R::Acc sm[kThreads / 32];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) a = R::combine(a, R::shfl(a, off));
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) sm[w] = a;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        a = sm[0];
+        for (int k = 1; k < (int)(blockDim.x >> 5); k++) a = R::combine(a, sm[k]);
+    }
+    return a;  // valid in thread 0
+}
+
+template <class R, typename T>
+__device__ void write_out(void* out, size_t idx, typename R::Acc a, int index_bytes) {
+    if constexpr (sizeof(typename R::Out) == 8 && !std::is_floating_point<typename R::Out>::value) {
+        long long v = R::out(a);
+        if (index_bytes == 4) ((int*)out)[idx] = (int)v;
+        else ((long long*)out)[idx] = v;
+    } else {
+        ((typename R::Out*)out)[idx] = R::out(a);
+    }
+}
+
+// rows kernel: grid (S, rows).  Segment s of row r covers [s*L, min(R, (s+1)*L)).
+// final: S == 1, writes the output; else writes Acc partial [r][s].
+template <class R, typename T>
+__global__ void __launch_bounds__(kThreads)
+k_rows(const T* __restrict__ a, size_t R_, size_t L, void* out, typename R::Acc* partial,
+       int S, int index_bytes) {
+    size_t r = blockIdx.y;
+    size_t s = blockIdx.x;
+    size_t beg = s * L, end = beg + L < R_ ? beg + L : R_;
+    const T* row = a + r * R_;
+    typename R::Acc acc = R::init();
+    constexpr int W = (int)(16 / sizeof(T));
+    // vector body when the segment start is 16-byte aligned
+    size_t i = beg;
+    if ((((uintptr_t)(row + beg)) & 15) == 0) {
+        size_t nv = (end - beg) / W;
+        for (size_t v = threadIdx.x; v < nv; v += blockDim.x) {
+            T x[W];
+            vload(row + beg + v * W, x);
+#pragma unroll
+            for (int j = 0; j < W; j++) acc = R::add(acc, x[j], (long long)(beg + v * W + j));
+        }
+        i = beg + nv * W;
+    }
+    for (size_t e = i + threadIdx.x; e < end; e += blockDim.x) acc = R::add(acc, row[e], (long long)e);
+    acc = block_reduce<R>(acc);
+    if (threadIdx.x == 0) {
+        if (S == 1) write_out<R, T>(out, r, acc, index_bytes);
+        else partial[r * S + s] = acc;
+    }
+}
+
+// Fold S partials per output in index order.
+template <class R, typename T>
+__global__ void k_fold(const typename R::Acc* __restrict__ partial, size_t n_out, int S,
+                       size_t inner, void* out, int index_bytes) {
+    // partial layout: [o][s][j] with n_out = outer*inner; rows case has inner = 1.
+    size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n_out) return;
+    size_t o = t / inner, j = t - o * inner;
+    typename R::Acc acc = partial[(o * S) * inner + j];
+    for (int s = 1; s < S; s++) acc = R::combine(acc, partial[(o * S + s) * inner + j]);
+    write_out<R, T>(out, t, acc, index_bytes);
+}
+
+// cols kernel: grid (ceil(inner/256), S, outer); thread owns column j.
+template <class R, typename T>
+__global__ void __launch_bounds__(kThreads)
+k_cols(const T* __restrict__ a, size_t R_, size_t inner, size_t L, void* out,
+       typename R::Acc* partial, int S, int index_bytes) {
+    size_t j = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    size_t s = blockIdx.y, o = blockIdx.z;
+    if (j >= inner) return;
+    size_t beg = s * L, end = beg + L < R_ ? beg + L : R_;
+    const T* base = a + o * R_ * inner + j;
+    typename R::Acc acc = R::init();
+    for (size_t r = beg; r < end; r++) acc = R::add(acc, base[r * inner], (long long)r);
+    if (S == 1) write_out<R, T>(out, o * inner + j, acc, index_bytes);
+    else partial[(o * S + s) * inner + j] = acc;
+}
+
+template <class R, typename T>
+int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* out,
+               int index_bytes) {
+    if (outer == 0 || inner == 0) return OK;
+    using Acc = typename R::Acc;
+    ScratchGuard guard(c);
+    const size_t sms = (size_t)c.dev->sm_count;
+    if (inner == 1) {
+        // Segments per row: enough CTAs to fill the GPU, each >= 4096 elements.
+        size_t S = 1;
+        if (outer < 2 * sms) {
+            size_t want = (4 * sms + outer - 1) / outer;
+            size_t max_by_len = (R_ + 4095) / 4096;
+            S = want < max_by_len ? want : max_by_len;
+            if (S < 1) S = 1;
+        }
+        size_t L = (R_ + S - 1) / S;
+        // keep segment starts 16-byte aligned when rows are
+        L = (L + 3) & ~(size_t)3;
+        if (L == 0) L = 4;
+        S = (R_ + L - 1) / L;
+        if (S == 0) S = 1;
+        Acc* part = nullptr;
+        if (S > 1) {
+            part = (Acc*)scratch(c, outer * S * sizeof(Acc));
+            if (!part) return E_CUDA;
+        }
+        if (outer > 65535 && S > 1) {
+            set_error("too many rows for a segmented reduce");
+            return E_ARG;
+        }
+        if (outer > 65535) {
+            // one launch per 65535-row slab (grid.y limit)
+            for (size_t r0 = 0; r0 < outer; r0 += 65535) {
+                size_t rows = outer - r0 < 65535 ? outer - r0 : 65535;
+                dim3 grid(1, (unsigned)rows);
+                void* o2 = (char*)out + r0 * (index_bytes ? (size_t)index_bytes : sizeof(typename R::Out));
+                k_rows<R, T><<<grid, kThreads, 0, c.stream>>>(a + r0 * R_, R_, L, o2, nullptr, 1,
+                                                              index_bytes);
+                count_launch();
+            }
+            return finish(c);
+        }
+        dim3 grid((unsigned)S, (unsigned)outer);
+        k_rows<R, T><<<grid, kThreads, 0, c.stream>>>(a, R_, L, out, part, (int)S, index_bytes);
+        count_launch();
+        if (S > 1) {
+            k_fold<R, T><<<(unsigned)((outer + 127) / 128), 128, 0, c.stream>>>(part, outer, (int)S, 1,
+                                                                               out, index_bytes);
+            count_launch();
+        }
+        return finish(c);
+    }
+    size_t cols = outer * inner;
+    size_t S = 1;
+    size_t target = 4 * sms * kThreads;
+    if (cols < target && R_ > 256) {
+        S = (target + cols - 1) / cols;
+        size_t max_s = R_ / 64;
+        if (S > max_s) S = max_s;
+        if (S > 1024) S = 1024;
+        if (S < 1) S = 1;
+    }
+    size_t L = (R_ + S - 1) / S;
+    S = (R_ + L - 1) / L;
+    if (S == 0) S = 1;
+    if (outer > 65535) {
+        set_error("outer extent %zu exceeds the grid limit", outer);
+        return E_ARG;
+    }
+    Acc* part = nullptr;
+    if (S > 1) {
+        part = (Acc*)scratch(c, cols * S * sizeof(Acc));
+        if (!part) return E_CUDA;
+    }
+    dim3 grid((unsigned)((inner + kThreads - 1) / kThreads), (unsigned)S, (unsigned)outer);
+    k_cols<R, T><<<grid, kThreads, 0, c.stream>>>(a, R_, inner, L, out, part, (int)S, index_bytes);
+    count_launch();
+    if (S > 1) {
+        k_fold<R, T><<<(unsigned)((cols + 127) / 128), 128, 0, c.stream>>>(part, cols, (int)S, inner,
+                                                                          out, index_bytes);
+        count_launch();
+    }
+    return finish(c);
+}
+
+// ---- logsumexp (f32 in/out, f64 math) --------------------------------------------
+
+__global__ void __launch_bounds__(kThreads)
+k_lse_rows(const float* __restrict__ a, size_t R_, float* out) {
+    const float* row = a + (size_t)blockIdx.x * R_;
+    float mx = -INFINITY;
+    for (size_t e = threadIdx.x; e < R_; e += blockDim.x) mx = fmaxf(mx, row[e]);
+    mx = block_reduce<MaxR<float, true>>(mx);
+    __shared__ float s_mx;
+    if (threadIdx.x == 0) s_mx = mx;
+    __syncthreads();
+    double m = (double)s_mx;
+    double s = 0.0;
+    for (size_t e = threadIdx.x; e < R_; e += blockDim.x) s += exp((double)row[e] - m);
+    __syncthreads();
+    s = block_reduce<SumR<float>>(s);
+    if (threadIdx.x == 0) out[blockIdx.x] = (float)(log(s) + m);
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_lse_cols(const float* __restrict__ a, size_t R_, size_t inner, float* out) {
+    size_t j = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    size_t o = blockIdx.y;
+    if (j >= inner) return;
+    const float* base = a + o * R_ * inner + j;
+    double mx = -INFINITY;
+    for (size_t r = 0; r < R_; r++) {
+        double v = base[r * inner];
+        if (v > mx) mx = v;
+    }
+    double s = 0.0;
+    for (size_t r = 0; r < R_; r++) s += exp((double)base[r * inner] - mx);
+    out[o * inner + j] = (float)(log(s) + mx);
+}
+
+// ---- kinetic energy partials -------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads)
+k_kinetic(const float* __restrict__ p, const float* __restrict__ m, size_t n, float* out) {
+    size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x;
+    double t = 0.0;
+    if (i < n) t = (double)mul_(mul_(p[i], p[i]), m[i]);
+    t = block_reduce<SumR<float>>(t);
+    if (threadIdx.x == 0) out[blockIdx.x] = (float)(0.5 * t);
+}
+
+}  // namespace
+
+int launch_reduce_full(Ctx& c, int dt, void* out_dev, const void* a, size_t n, unsigned op) {
+    if (n == 0) {
+        set_error("reduce of an empty tensor");
+        return E_ARG;
+    }
+    if (dt == F32) {
+        const float* x = (const float*)a;
+        if (op == 0) return run_reduce<SumR<float>, float>(c, x, 1, n, 1, out_dev, 0);
+        if (op == 1) return run_reduce<MaxR<float, false>, float>(c, x, 1, n, 1, out_dev, 0);
+        return run_reduce<MaxR<float, true>, float>(c, x, 1, n, 1, out_dev, 0);
+    }
+    const double* x = (const double*)a;
+    if (op == 0) return run_reduce<SumR<double>, double>(c, x, 1, n, 1, out_dev, 0);
+    if (op == 1) return run_reduce<MaxR<double, false>, double>(c, x, 1, n, 1, out_dev, 0);
+    return run_reduce<MaxR<double, true>, double>(c, x, 1, n, 1, out_dev, 0);
+}
+
+int launch_reduce_axis(Ctx& c, int dt, void* out, const void* a, size_t outer, size_t R,
+                       size_t inner, unsigned op) {
+    if (R == 0) {
+        set_error("reduce over an empty axis");
+        return E_ARG;
+    }
+    if (dt == F32) {
+        const float* x = (const float*)a;
+        if (op == 0) return run_reduce<SumR<float>, float>(c, x, outer, R, inner, out, 0);
+        if (op == 1) return run_reduce<MaxR<float, true>, float>(c, x, outer, R, inner, out, 0);
+        return run_reduce<MaxR<float, false>, float>(c, x, outer, R, inner, out, 0);
+    }
+    const double* x = (const double*)a;
+    if (op == 0) return run_reduce<SumR<double>, double>(c, x, outer, R, inner, out, 0);
+    if (op == 1) return run_reduce<MaxR<double, true>, double>(c, x, outer, R, inner, out, 0);
+    return run_reduce<MaxR<double, false>, double>(c, x, outer, R, inner, out, 0);
+}
+
+int launch_argmax(Ctx& c, int dt, void* out, const void* a, size_t outer, size_t R,
+                  size_t inner, int is_min, int index_bytes) {
+    if (R == 0) {
+        set_error("argmax over an empty axis");
+        return E_ARG;
+    }
+    if (dt == F32) {
+        if (is_min) return run_reduce<ArgR<float, true>, float>(c, (const float*)a, outer, R, inner, out, index_bytes);
+        return run_reduce<ArgR<float, false>, float>(c, (const float*)a, outer, R, inner, out, index_bytes);
+    }
+    if (is_min) return run_reduce<ArgR<double, true>, double>(c, (const double*)a, outer, R, inner, out, index_bytes);
+    return run_reduce<ArgR<double, false>, double>(c, (const double*)a, outer, R, inner, out, index_bytes);
+}
+
+int launch_logsumexp(Ctx& c, void* out, const void* a, size_t outer, size_t R, size_t inner) {
+    if (R == 0 || outer == 0 || inner == 0) return OK;
+    if (inner == 1) {
+        if (outer > 0x7fffffff) return E_ARG;
+        k_lse_rows<<<(unsigned)outer, kThreads, 0, c.stream>>>((const float*)a, R, (float*)out);
+    } else {
+        if (outer > 65535) return E_ARG;
+        dim3 grid((unsigned)((inner + kThreads - 1) / kThreads), (unsigned)outer);
+        k_lse_cols<<<grid, kThreads, 0, c.stream>>>((const float*)a, R, inner, (float*)out);
+    }
+    count_launch();
+    return finish(c);
+}
+
+int launch_kinetic_energy(Ctx& c, void* out, const void* p, const void* m, size_t n) {
+    if (n == 0) return OK;
+    size_t groups = (n + kThreads - 1) / kThreads;
+    k_kinetic<<<(unsigned)groups, kThreads, 0, c.stream>>>((const float*)p, (const float*)m, n,
+                                                           (float*)out);
+    count_launch();
+    return finish(c);
+}
+
+}  // namespace nxv

@@ -1,0 +1,90 @@
+// kernels.h -- host launchers for the sm_100a kernels (internal API).
+#pragma once
+#include "runtime.h"
+
+namespace nxv {
+
+enum DType : int { F32 = 0, F64 = 1 };
+
+// Op tape for the fused elementwise kernel (lib/nx_vulkan.ex:457-538).
+struct Tape {
+    unsigned n_ops;
+    unsigned ops[8];   // 0..9 binary, 100..114 unary, 255 nop
+    unsigned src[8];   // binary operand: 0 imm, 1 b, 2 c, 3 d
+    double imm[8];
+};
+
+// elementwise (k_elementwise.cu)
+int launch_binary(Ctx& c, int dt, void* out, const void* a, const void* b, size_t n, unsigned op);
+int launch_unary(Ctx& c, int dt, void* out, const void* a, size_t n, unsigned op);
+int launch_cast(Ctx& c, int to_f64, void* out, const void* a, size_t n);
+int launch_broadcast(Ctx& c, int dt, void* out, const void* a, const void* b, unsigned op,
+                     unsigned ndim, const unsigned* shape, const unsigned* as, const unsigned* bs);
+int launch_fused(Ctx& c, int dt, void* out, const void* a, const void* b, const void* cc,
+                 const void* d, size_t n, const Tape& t);
+int launch_transpose(Ctx& c, int dt, void* out, const void* a, unsigned m, unsigned n);
+// transpose without the finish() check (for use inside multi-launch ops)
+int enqueue_transpose(Ctx& c, int dt, void* out, const void* a, unsigned m, unsigned n);
+int launch_normal_logpdf(Ctx& c, void* out, const void* x, const void* mu, const void* sigma,
+                         size_t n);
+int launch_leapfrog_step_f32(Ctx& c, void* qn, void* pn, const void* q, const void* p,
+                             const void* m, size_t n, float eps, float mu, float sigma);
+
+// reductions (k_reduce.cu)
+// Full reduce to a device scalar of the input type.  op: 0 sum 1 min 2 max.
+int launch_reduce_full(Ctx& c, int dt, void* out_dev, const void* a, size_t n, unsigned op);
+// (outer, R, inner) -> (outer, inner); op: 0 sum 1 max 2 min.
+int launch_reduce_axis(Ctx& c, int dt, void* out, const void* a, size_t outer, size_t R,
+                       size_t inner, unsigned op);
+int launch_argmax(Ctx& c, int dt, void* out, const void* a, size_t outer, size_t R,
+                  size_t inner, int is_min, int index_bytes);
+int launch_logsumexp(Ctx& c, void* out, const void* a, size_t outer, size_t R, size_t inner);
+int launch_kinetic_energy(Ctx& c, void* out, const void* p, const void* m, size_t n);
+
+// random (k_philox.cu)
+int launch_random(Ctx& c, int dt, void* out, size_t n, uint32_t seed, unsigned dist);
+
+// leapfrog chains (k_leapfrog.cu)
+enum Family : int { FAM_NORMAL = 0, FAM_EXP = 1, FAM_STUDENTT = 2, FAM_CAUCHY = 3,
+                    FAM_HALFNORMAL = 4, FAM_WEIBULL = 5 };
+// f32 families; logp_mode 0: logp[chain][k]; 1: partial logp [k][group of 256]
+int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void* gc,
+                     void* logp, const void* q0, const void* p0, const void* m, size_t n,
+                     size_t chains, unsigned K, float eps, int logp_mode);
+// f64 Gaussian: prec == nullptr means prec_i = prec_scalar for all i.
+int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
+                           const void* p0, const void* m, const void* prec, double prec_scalar,
+                           double mu, size_t n, size_t chains, unsigned K, double eps);
+int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
+                            const void* p0, const void* X, const void* y, size_t n_obs,
+                            size_t n_dim, size_t chains, unsigned K, double eps);
+
+// matmul (k_matmul.cu): strided, batched or split-K GEMM parameters.
+template <typename T>
+struct GemmP {
+    const T* A;
+    const T* B;
+    T* C;
+    int M, N, K;
+    int lda, ldb, ldc;
+    long long sA, sB, sC;  // batch strides (elements); sC is also the split-K partial stride
+    int ksplit;            // > 0: blockIdx.z indexes K slices of this length
+    int vecA, vecB;        // set by the launcher
+    int batch;             // grid.z: batch count or number of K slices
+};
+int gemm_f64(Ctx& c, const GemmP<double>& P);
+int launch_matmul_f64(Ctx& c, void* C, const void* A, const void* B, size_t batch, size_t m,
+                      size_t n, size_t k);
+int launch_matmul_f32(Ctx& c, void* C, const void* A, const void* B, size_t batch, size_t m,
+                      size_t n, size_t k);
+
+// Grid helper: blocks for a grid-stride kernel.
+inline unsigned grid_for(Ctx& c, size_t work_items, unsigned threads, unsigned per_sm) {
+    size_t want = (work_items + threads - 1) / threads;
+    size_t cap = (size_t)c.dev->sm_count * per_sm;
+    if (want > cap) want = cap;
+    if (want == 0) want = 1;
+    return (unsigned)want;
+}
+
+}  // namespace nxv

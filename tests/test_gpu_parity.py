@@ -1,0 +1,322 @@
+"""CUDA path vs the CPU oracle on identical seeded inputs.
+
+Tolerances (written per assertion): bit-exact for integer/index work and for
+IEEE-exact ops (+ - * / sqrt, compare, max/min, abs, neg, ceil, floor, sign,
+relu, square, reciprocal, casts, transposes, uniform Philox); f32
+transcendentals within 1e-5 relative + 1e-6 absolute; f64 within 1e-12
+relative (+1e-14 absolute for results near zero)."""
+import numpy as np
+import pytest
+
+from gpu_util import close, down, unwrap, up
+
+pytestmark = pytest.mark.gpu
+
+SIZES = [1, 3, 4, 255, 256, 257, 1000, 4097, 65536 + 3]
+EXACT_BIN = [0, 1, 2, 3, 5, 6, 7, 8, 9]
+EXACT_UN = [2, 3, 4, 7, 8, 9, 10, 11, 12]
+TRANS_UN = [0, 1, 5, 6, 13, 14]
+
+
+def data(seed, n, dtype, lo=-2.0, hi=2.0):
+    return np.random.default_rng(seed).uniform(lo, hi, n).astype(dtype)
+
+
+@pytest.mark.parametrize("n", SIZES)
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_binary_all_ops(nxv, orc, n, dt):
+    a, b = data(1, n, dt), data(2, n, dt)
+    b[::7] = a[::7]  # exercise equal / ties of max-min
+    spv = nxv.shader_path("elementwise_binary.spv" if dt == np.float32 else "elementwise_binary_f64.spv")
+    ta, tb = up(nxv, a), up(nxv, b)
+    for op in range(10):
+        got = down(nxv, unwrap(nxv.apply_binary(ta, tb, op, spv, a.itemsize, 9)), dt)
+        want = orc.binary(a, b, op)
+        if op in EXACT_BIN:
+            assert np.array_equal(got.view(np.uint8), want.view(np.uint8)) or np.array_equal(got, want), op
+        else:  # pow
+            pa = np.abs(a) + 0.1
+            got = down(nxv, unwrap(nxv.apply_binary(up(nxv, pa), tb, op, spv, a.itemsize, 9)), dt)
+            want = orc.binary(pa, b, op)
+            close(got, want, 1e-5 if dt == np.float32 else 1e-12, 1e-6 if dt == np.float32 else 1e-14)
+
+
+@pytest.mark.parametrize("n", SIZES)
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_unary_all_ops(nxv, orc, n, dt):
+    a = data(3, n, dt, -3, 3)
+    a[:1] = 0.0
+    spv = nxv.shader_path("elementwise_unary.spv" if dt == np.float32 else "elementwise_unary_f64.spv")
+    ta = up(nxv, a)
+    for op in range(15):
+        src = np.abs(a) + 0.01 if op in (1, 2) else a
+        t = ta if src is a else up(nxv, src)
+        got = down(nxv, unwrap(nxv.apply_unary(t, op, spv, a.itemsize)), dt)
+        want = orc.unary(src, op)
+        if op in EXACT_UN:
+            assert np.array_equal(got, want), op
+        else:
+            close(got, want, 1e-5 if dt == np.float32 else 1e-12, 1e-6 if dt == np.float32 else 1e-14)
+
+
+def test_unary_specials(nxv, orc):
+    a = np.array([np.inf, -np.inf, np.nan, 0.0, -0.0, 1e-40, -1e-40, 88.0, -104.0], np.float32)
+    spv = nxv.shader_path("elementwise_unary.spv")
+    ta = up(nxv, a)
+    for op in range(15):
+        got = down(nxv, unwrap(nxv.apply_unary(ta, op, spv, 4)), np.float32)
+        close(got, orc.unary(a, op), 1e-5, 1e-6)
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_broadcast_shapes(nxv, orc, dt):
+    r = np.random.default_rng(5)
+    cases = [((3, 5), (5,)), ((3, 5), (3, 1)), ((2, 3, 4), (3, 1)), ((2, 1, 4, 3), (5, 1)),
+             ((4, 8), (1, 8)), ((7,), ()), ((64, 256), (256,)), ((3, 1, 5), (1, 4, 1))]
+    spv = nxv.shader_path("elementwise_binary_broadcast.spv" if dt == np.float32
+                          else "elementwise_binary_broadcast_f64.spv")
+    for sa, sb in cases:
+        out = np.broadcast_shapes(sa, sb)
+        a, b = r.normal(size=sa).astype(dt), r.normal(size=sb).astype(dt)
+        ast, bst = nxv.broadcast_strides(sa, out), nxv.broadcast_strides(sb, out)
+        for op in (0, 1, 2, 3, 5, 8):
+            t = unwrap(nxv._broadcast(up(nxv, a.reshape(-1) if a.size else a), up(nxv, b.reshape(-1)),
+                                      op, len(out), nxv._pad4(out), ast, bst, spv, a.itemsize))
+            got = down(nxv, t, dt)
+            want = orc.broadcast(a.reshape(-1), b.reshape(-1), op, len(out), list(out), ast, bst)
+            assert np.array_equal(got, want), (sa, sb, op)
+
+
+def test_broadcast_config_rows(nxv, orc):
+    """x f32/f64[4096,4096] + b[4096] along rows (the reductions+broadcast workload)."""
+    for dt in (np.float32, np.float64):
+        r = np.random.default_rng(1)
+        x = r.normal(size=(4096, 4096)).astype(dt)
+        b = r.normal(size=4096).astype(dt)
+        spv = "elementwise_binary_broadcast.spv" if dt == np.float32 else "elementwise_binary_broadcast_f64.spv"
+        t = unwrap(nxv._broadcast(up(nxv, x), up(nxv, b), 0, 2, [4096, 4096, 0, 0], [4096, 1, 0, 0],
+                                  [0, 1, 0, 0], nxv.shader_path(spv), x.itemsize))
+        assert np.array_equal(down(nxv, t, dt).reshape(4096, 4096), x + b)
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_fused_chain_config1(nxv, orc, dt):
+    """tanh(exp(x*y + z) - 1.0) on [1,048,576] ~ U(-1,1), seed 0, one kernel.
+
+    f32: 1e-5 relative + 1e-6 absolute.  f64: exp(u) - 1 cancels near u = 0,
+    so the bound is 1e-12 relative to the largest intermediate, 2 + |e^u|."""
+    n = 1 << 20
+    r = np.random.default_rng(0)
+    x, y, z = (r.uniform(-1, 1, n).astype(dt) for _ in range(3))
+    ops, src, imm = [1, 0, 100, 2, 106], [1, 2, 1, 0, 1], [0, 0, 0, 1.0, 0]
+    t = unwrap(nxv.fused_chain_imm(up(nxv, x), [up(nxv, y), up(nxv, z)],
+                                   [("multiply", 1), ("add", 2), "exp", ("subtract", ("imm", 1.0)), "tanh"],
+                                   dtype="f32" if dt == np.float32 else "f64"))
+    got = down(nxv, t, dt)
+    want = orc.fused(x, [y, z], ops, src, imm)
+    if dt == np.float32:
+        close(got, want, 1e-5, 1e-6)
+    else:
+        scale = 2.0 + np.exp(x.astype(np.float64) * y + z)
+        assert np.all(np.abs(got - want) <= 1e-12 * np.maximum(np.abs(want), scale))
+
+
+@pytest.mark.parametrize("n", [1, 5, 1000, 100003])
+def test_fused_generic_tapes(nxv, orc, n):
+    r = np.random.default_rng(9)
+    a, b, c, d = (r.uniform(0.1, 2, n).astype(np.float32) for _ in range(4))
+    tapes = [
+        ([0, 1, 2, 3, 112, 100, 101, 102], [1, 1, 1, 1, 1, 1, 1, 1]),
+        ([103, 105, 1, 2, 106], [1, 1, 2, 3, 1]),
+        ([1, 0], [1, 2]),
+        ([1, 1, 0], [1, 2, 3]),
+        ([110, 107, 108, 109, 104, 111, 0], [1, 1, 1, 1, 1, 1, 3]),
+        ([5, 6, 4], [2, 3, 1]),
+    ]
+    ta, tb, tc, td = (up(nxv, v) for v in (a, b, c, d))
+    names = {0: "add", 1: "multiply", 2: "subtract", 3: "divide", 4: "pow", 5: "max", 6: "min"}
+    unames = {v: k for k, v in nxv.OP_CODES.items() if v >= 100}
+    for ops, src in tapes:
+        items = [(names[o], s) if o < 100 else unames[o] for o, s in zip(ops, src)]
+        got = down(nxv, unwrap(nxv.fused_chain_imm(ta, [tb, tc, td], items)), np.float32)
+        close(got, orc.fused(a, [b, c, d], ops, src), 1e-5, 1e-6)
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (1, 16777216, 1), (4096, 4096, 1), (1, 4096, 4096),
+                                   (3, 1000, 7), (2, 5, 100003), (100003, 3, 1), (1, 257, 1),
+                                   (70000, 2, 1), (7, 3, 1)])
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_reduce_axis_and_full(nxv, orc, shape, dt):
+    outer, R, inner = shape
+    if outer * R * inner > 16777216 and dt == np.float64 and shape != (4096, 4096, 1):
+        pytest.skip("size")
+    x = np.random.default_rng(1).normal(size=outer * R * inner).astype(dt)
+    t = up(nxv, x)
+    spv = "reduce_axis.spv" if dt == np.float32 else "reduce_axis_f64.spv"
+    for op in (0, 1, 2):
+        got = down(nxv, unwrap(nxv._reduce_axis(t, outer, R, inner, op, nxv.shader_path(spv), x.itemsize)), dt)
+        want = orc.reduce_axis(x, outer, R, inner, op)
+        if op == 0:
+            if dt == np.float32:
+                close(got, want, 1e-5, 1e-6)
+            else:  # |got - seq| <= 1e-12 |seq| + 4 eps sum|x| (tree vs sequential order)
+                xs = np.abs(x.reshape(outer, R, inner)).sum(axis=1).reshape(-1)
+                assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 4 * 2.2e-16 * xs)
+        else:
+            assert np.array_equal(got, want)
+    if inner == 1 and outer == 1:
+        if dt == np.float32:
+            for op in (0, 1, 2):
+                g = {0: nxv.sum, 1: nxv.reduce_min, 2: nxv.reduce_max}[op](t)[1]
+                w = orc.reduce_full(x, op)
+                assert abs(g - w) <= 1e-5 * abs(w) + 1e-6 if op == 0 else g == w
+        else:
+            for op in (0, 1, 2):
+                g = unwrap(nxv.reduce_f64(t, op))
+                w = orc.reduce_full(x, op)
+                if op == 0:
+                    exact = orc.sum_exact(x)
+                    assert abs(g - exact) <= 1e-12 * abs(exact) + 1e-15 * orc.sum_abs(x)
+                    assert abs(g - w) <= 1e-12 * abs(w) + 4 * 2.2e-16 * orc.sum_abs(x)
+                else:
+                    assert g == w
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096, 1), (1, 16777216, 1), (3, 1000, 7), (1, 1, 1),
+                                   (5, 4097, 3), (100003, 2, 1)])
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_argmax_bit_exact(nxv, orc, shape, dt):
+    outer, R, inner = shape
+    r = np.random.default_rng(1)
+    x = r.normal(size=outer * R * inner).astype(dt)
+    x[:: 97] = np.round(x[:: 97])  # plant ties
+    t = up(nxv, x)
+    for is_min in (False, True):
+        for ib in (8, 4):
+            got = down(nxv, unwrap(nxv.argmax_axis(t, outer, R, inner, dtype="f32" if dt == np.float32 else "f64",
+                                                   is_min=is_min, index_bytes=ib)),
+                       np.int64 if ib == 8 else np.int32)
+            want = orc.argmax_axis(x, outer, R, inner, is_min)
+            assert np.array_equal(got.astype(np.int64), want)
+
+
+def test_argmax_ties_and_nan(nxv, orc):
+    x = np.array([1, 3, 3, 2, 5, 5, np.nan, 5, np.nan, 0, 0, 0], np.float32)
+    t = up(nxv, x)
+    got = down(nxv, unwrap(nxv.argmax_axis(t, 3, 4, 1)), np.int64)
+    assert np.array_equal(got, orc.argmax_axis(x, 3, 4, 1))
+    assert list(got) == [1, 2, 0]
+
+
+def test_logsumexp(nxv, orc):
+    for shape in [(64, 1000, 1), (3, 50, 17)]:
+        x = np.random.default_rng(2).normal(size=int(np.prod(shape))).astype(np.float32) * 10
+        got = down(nxv, unwrap(nxv.logsumexp(up(nxv, x), *shape)), np.float32)
+        close(got, orc.logsumexp(x, *shape), 1e-5, 1e-6)
+
+
+@pytest.mark.parametrize("mnk", [(1, 1, 1), (2, 2, 2), (17, 33, 9), (128, 128, 128), (130, 70, 257),
+                                 (256, 512, 100), (1, 300, 1000)])
+def test_matmul_f64(nxv, orc, mnk):
+    m, n, k = mnk
+    r = np.random.default_rng(2)
+    a, b = r.normal(size=m * k), r.normal(size=k * n)
+    got = down(nxv, unwrap(nxv.matmul_batched(up(nxv, a), up(nxv, b), 1, m, n, k, "f64")), np.float64)
+    want = orc.matmul(a, b, m, n, k)
+    bound = np.abs(a.reshape(m, k)) @ np.abs(b.reshape(k, n))
+    assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 2 * k * 2.2e-16 * bound.reshape(-1))
+
+
+@pytest.mark.parametrize("mnk", [(1, 1, 3), (2, 2, 2), (17, 33, 9), (128, 128, 128), (130, 70, 257),
+                                 (333, 129, 65)])
+def test_matmul_f32_3xtf32(nxv, orc, mnk):
+    """3xTF32 stays within f32 accuracy: |err| <= 1e-5 |C| + 1e-6 + k * 2^-22 sum|a||b|."""
+    m, n, k = mnk
+    r = np.random.default_rng(3)
+    a, b = r.normal(size=m * k).astype(np.float32), r.normal(size=k * n).astype(np.float32)
+    got = down(nxv, unwrap(nxv.matmul(up(nxv, a), up(nxv, b), m, n, k)), np.float32)
+    want = orc.matmul(a, b, m, n, k)
+    bound = (np.abs(a.reshape(m, k)).astype(np.float64) @ np.abs(b.reshape(k, n))).reshape(-1)
+    assert np.all(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-6 + 4 * 2.0 ** -24 * bound)
+
+
+def test_matmul_config_sizes(nxv, orc):
+    """A.B with A,B [2048,2048] ~ N(0, 1/2048) (f32 and f64), batched f64 64x256^3.
+    Checked on 256 sampled rows against the oracle."""
+    r = np.random.default_rng(2)
+    n = 2048
+    rows = r.choice(n, 256, replace=False)
+    for dt in (np.float64, np.float32):
+        a = (r.normal(size=(n, n)) / np.sqrt(n)).astype(dt)
+        b = (r.normal(size=(n, n)) / np.sqrt(n)).astype(dt)
+        if dt == np.float64:
+            t = unwrap(nxv.matmul_batched(up(nxv, a), up(nxv, b), 1, n, n, n, "f64"))
+        else:
+            t = unwrap(nxv.matmul(up(nxv, a), up(nxv, b), n, n, n))
+        got = down(nxv, t, dt).reshape(n, n)[rows]
+        want = orc.matmul(np.ascontiguousarray(a[rows]), b, 256, n, n).reshape(256, n)
+        bound = np.abs(a[rows]).astype(np.float64) @ np.abs(b).astype(np.float64)
+        if dt == np.float64:
+            assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 2 * n * 2.2e-16 * bound)
+        else:
+            assert np.all(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-6 + 4 * 2.0 ** -24 * bound)
+    a = r.normal(size=(64, 256, 256)) / 16
+    b = r.normal(size=(64, 256, 256)) / 16
+    got = down(nxv, unwrap(nxv.matmul_batched(up(nxv, a), up(nxv, b), 64, 256, 256, 256, "f64")), np.float64)
+    want = orc.matmul(a, b, 256, 256, 256, batch=64)
+    bound = np.einsum("bik,bkj->bij", np.abs(a), np.abs(b)).reshape(-1)
+    assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 2 * 256 * 2.2e-16 * bound)
+
+
+@pytest.mark.parametrize("n", [1, 2, 7, 1024, 1000001])
+def test_philox_matches_oracle(nxv, orc, n):
+    for seed in (0, 42, 0xDEADBEEF):
+        u = down(nxv, unwrap(nxv.uniform(n, seed)), np.float32)
+        assert np.array_equal(u, orc.random_f32(n, seed, 0))  # bit-exact
+        g = down(nxv, unwrap(nxv.normal(n, seed)), np.float32)
+        close(g, orc.random_f32(n, seed, 1), 1e-6, 1e-6)
+        u64 = down(nxv, unwrap(nxv.random_f64(n, seed, 0)), np.float64)
+        assert np.array_equal(u64, orc.random_f64(n, seed, 0))
+        g64 = down(nxv, unwrap(nxv.random_f64(n, seed, 1)), np.float64)
+        close(g64, orc.random_f64(n, seed, 1), 1e-12, 1e-14)
+
+
+@pytest.mark.parametrize("mn", [(1, 1), (3, 5), (33, 65), (1000, 17), (4096, 4096)])
+def test_transpose_and_cast(nxv, orc, mn):
+    m, n = mn
+    a = np.random.default_rng(4).normal(size=m * n).astype(np.float32)
+    got = down(nxv, unwrap(nxv.transpose_2d(up(nxv, a), m, n)), np.float32)
+    assert np.array_equal(got, orc.transpose(a, m, n))
+    d = down(nxv, unwrap(nxv.cast_f32_to_f64(up(nxv, a), m * n)), np.float64)
+    assert np.array_equal(d, a.astype(np.float64))
+    b = np.random.default_rng(5).normal(size=m * n) * 1e3
+    f = down(nxv, unwrap(nxv.cast_f64_to_f32(up(nxv, b), m * n)), np.float32)
+    assert np.array_equal(f, b.astype(np.float32))
+
+
+def test_kinetic_energy_and_logpdf_large(nxv, orc):
+    r = np.random.default_rng(6)
+    n = 100003
+    p, m = r.normal(size=n).astype(np.float32), r.uniform(0.5, 2, n).astype(np.float32)
+    parts = down(nxv, unwrap(nxv.kinetic_energy(up(nxv, p), up(nxv, m))), np.float32)
+    assert parts.size == (n + 255) // 256
+    assert abs(parts.astype(np.float64).sum() - orc.kinetic_energy(p, m)) <= 1e-5 * orc.kinetic_energy(p, m)
+    x, mu, s = r.normal(size=n).astype(np.float32), r.normal(size=n).astype(np.float32), r.uniform(0.5, 2, n).astype(np.float32)
+    got = down(nxv, unwrap(nxv.normal_logpdf(up(nxv, x), up(nxv, mu), up(nxv, s))), np.float32)
+    close(got, orc.normal_logpdf(x, mu, s), 1e-5, 1e-6)
+
+
+def test_errors_are_reported(nxv):
+    from nx_vulkan_b200 import _native
+    lib = _native.load()
+    a = unwrap(nxv.upload_f32([1.0] * 8))
+    # unknown kernel basename
+    assert lib.nxv_apply_unary(a.handle, a.handle, 8, 0, b"nope.spv") == -2
+    # element count beyond the buffer
+    assert lib.nxv_apply_unary(a.handle, a.handle, 9, 0, nxv.shader_path("elementwise_unary.spv")) == -3
+    assert "buffer" in _native.last_error()
+    # bad op
+    assert lib.nxv_apply_binary(a.handle, a.handle, a.handle, 8, 10, nxv.shader_path("elementwise_binary.spv")) == -3
+    # empty tensor ops are no-ops, not errors
+    e = unwrap(nxv.upload_f32([]))
+    assert lib.nxv_apply_unary(e.handle, e.handle, 0, 0, nxv.shader_path("elementwise_unary.spv")) == 0
