@@ -365,7 +365,8 @@ int nxv_init_devices(const int* ids, int n);
 int nxv_set_device(int id);
 
 /* Run this thread's work for the current device on a caller-owned
- * cudaStream_t (passed as void*); NULL restores the library's own stream. */
+ * cudaStream_t (passed as void*); NULL restores the library's own stream.
+ * To use the legacy default stream pass cudaStreamLegacy ((void*)1). */
 int nxv_set_stream(void* cuda_stream);
 
 /* Wait for all work queued on the current device.  0, or -4 with the CUDA

@@ -105,13 +105,16 @@ int run_map(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* i3, 
     return finish(c);
 }
 
-template <typename T> struct BinF {
+// EX: f32 transcendentals evaluated in f64 and rounded (Nx.BinaryBackend
+// semantics) when true, f32 library functions when false (the default;
+// NXV_EXACT_F32=1 selects the first).
+template <typename T, bool EX> struct BinF {
     unsigned op;
-    __device__ T operator()(const T* x) const { return bin_op<T>(x[0], x[1], op); }
+    __device__ T operator()(const T* x) const { return bin_op<T, EX>(x[0], x[1], op); }
 };
-template <typename T> struct UnF {
+template <typename T, bool EX> struct UnF {
     unsigned op;
-    __device__ T operator()(const T* x) const { return un_op<T>(x[0], op); }
+    __device__ T operator()(const T* x) const { return un_op<T, EX>(x[0], op); }
 };
 
 // ---- fused op tape: generic interpreter --------------------------------------
@@ -123,7 +126,7 @@ template <typename T> struct TapeDev {
     T imm[8];
 };
 
-template <typename T> struct TapeF {
+template <typename T, bool EX> struct TapeF {
     TapeDev<T> t;
     // x[0] = a, x[1] = b, x[2] = c, x[3] = d (unused ones are never read)
     __device__ T operator()(const T* x) const {
@@ -134,9 +137,9 @@ template <typename T> struct TapeF {
             if (op < 100) {
                 unsigned s = t.src[k];
                 T rhs = (s == 0) ? t.imm[k] : x[s];
-                r = bin_op<T>(r, rhs, op);
+                r = bin_op<T, EX>(r, rhs, op);
             } else if (op != 255) {
-                r = un_op<T>(r, op - 100);
+                r = un_op<T, EX>(r, op - 100);
             }
         }
         return r;
@@ -146,10 +149,10 @@ template <typename T> struct TapeF {
 // ---- fused op tape: compile-time specialisations of hot chains -------------
 
 // tanh(exp(a*b + c) - imm0): the Nx.Defn chain tanh(exp(x*y + z) - 1.0).
-template <typename T> struct ChainMulAddExpSubTanh {
+template <typename T, bool EX> struct ChainMulAddExpSubTanh {
     T imm;
     __device__ T operator()(const T* x) const {
-        return tanh_(sub_(exp_(add_(mul_(x[0], x[1]), x[2])), imm));
+        return un_op<T, EX>(sub_(un_op<T, EX>(add_(mul_(x[0], x[1]), x[2]), 0), imm), 6);
     }
 };
 // a*b + c: Fast.leapfrog_position / fused_chain_4 [{mul,1},{add,2}].
@@ -180,14 +183,14 @@ bool tape_is(const Tape& t, std::initializer_list<unsigned> ops,
     return k == t.n_ops;
 }
 
-template <typename T>
+template <typename T, bool EX>
 int fused_typed(Ctx& c, T* out, const T* a, const T* b, const T* cc, const T* d, size_t n,
                 const Tape& t) {
     // Hot chains first.
     if (tape_is(t, {1, 0, 100, 2, 106}, {1, 2, 9, 0, 9}) && b && cc) {
         unsigned k = 0;
         while (t.ops[k] == 255 || t.ops[k] != 2) k++;
-        ChainMulAddExpSubTanh<T> f{(T)t.imm[k]};
+        ChainMulAddExpSubTanh<T, EX> f{(T)t.imm[k]};
         return run_map<T, 3>(c, out, a, b, cc, nullptr, n, f);
     }
     if (tape_is(t, {1, 0}, {1, 2}) && b && cc)
@@ -199,7 +202,7 @@ int fused_typed(Ctx& c, T* out, const T* a, const T* b, const T* cc, const T* d,
     bool used[4] = {true, false, false, false};
     for (unsigned k = 0; k < t.n_ops; k++)
         if (t.ops[k] < 100 && t.src[k] >= 1 && t.src[k] <= 3) used[t.src[k]] = true;
-    TapeF<T> f;
+    TapeF<T, EX> f;
     f.t.n_ops = t.n_ops;
     for (int k = 0; k < 8; k++) {
         f.t.ops[k] = t.ops[k];
@@ -306,7 +309,7 @@ struct NormalLogpdfF {
     __device__ float operator()(const float* x) const {
         float z = div_(sub_(x[0], x[1]), x[2]);
         float z2 = mul_(z, z);
-        return sub_(sub_(mul_(z2, -0.5f), logf(x[2])), 0.918938533204672742f);
+        return sub_(sub_(mul_(z2, -0.5f), (float)log((double)x[2])), 0.918938533204672742f);
     }
 };
 
@@ -330,19 +333,25 @@ k_leapfrog_step(float* __restrict__ qn, float* __restrict__ pn, const float* __r
 
 int launch_binary(Ctx& c, int dt, void* out, const void* a, const void* b, size_t n,
                   unsigned op) {
+    if (dt == F32 && fast_f32())
+        return run_map<float, 2>(c, (float*)out, (const float*)a, (const float*)b, nullptr,
+                                 nullptr, n, BinF<float, false>{op});
     if (dt == F32)
         return run_map<float, 2>(c, (float*)out, (const float*)a, (const float*)b, nullptr,
-                                 nullptr, n, BinF<float>{op});
+                                 nullptr, n, BinF<float, true>{op});
     return run_map<double, 2>(c, (double*)out, (const double*)a, (const double*)b, nullptr,
-                              nullptr, n, BinF<double>{op});
+                              nullptr, n, BinF<double, true>{op});
 }
 
 int launch_unary(Ctx& c, int dt, void* out, const void* a, size_t n, unsigned op) {
+    if (dt == F32 && fast_f32())
+        return run_map<float, 1>(c, (float*)out, (const float*)a, nullptr, nullptr, nullptr, n,
+                                 UnF<float, false>{op});
     if (dt == F32)
         return run_map<float, 1>(c, (float*)out, (const float*)a, nullptr, nullptr, nullptr, n,
-                                 UnF<float>{op});
+                                 UnF<float, true>{op});
     return run_map<double, 1>(c, (double*)out, (const double*)a, nullptr, nullptr, nullptr, n,
-                              UnF<double>{op});
+                              UnF<double, true>{op});
 }
 
 int launch_cast(Ctx& c, int to_f64, void* out, const void* a, size_t n) {
@@ -390,11 +399,14 @@ int launch_broadcast(Ctx& c, int dt, void* out, const void* a, const void* b, un
 
 int launch_fused(Ctx& c, int dt, void* out, const void* a, const void* b, const void* cc,
                  const void* d, size_t n, const Tape& t) {
+    if (dt == F32 && fast_f32())
+        return fused_typed<float, false>(c, (float*)out, (const float*)a, (const float*)b,
+                                         (const float*)cc, (const float*)d, n, t);
     if (dt == F32)
-        return fused_typed<float>(c, (float*)out, (const float*)a, (const float*)b,
-                                  (const float*)cc, (const float*)d, n, t);
-    return fused_typed<double>(c, (double*)out, (const double*)a, (const double*)b,
-                               (const double*)cc, (const double*)d, n, t);
+        return fused_typed<float, true>(c, (float*)out, (const float*)a, (const float*)b,
+                                        (const float*)cc, (const float*)d, n, t);
+    return fused_typed<double, true>(c, (double*)out, (const double*)a, (const double*)b,
+                                     (const double*)cc, (const double*)d, n, t);
 }
 
 int launch_transpose(Ctx& c, int dt, void* out, const void* a, unsigned m, unsigned n) {

@@ -38,6 +38,10 @@ constexpr int KC = 32;  // steps per logp flush
 
 struct NoParam {};
 
+// f32 family transcendentals are evaluated in f64 and rounded once, as
+// Nx.BinaryBackend does for every f32 op.
+__device__ __forceinline__ float ex(float x) { return (float)exp((double)x); }
+
 struct FamNormal32 {
     float mu, sigma, inv_var;
     using P = NoParam;
@@ -52,8 +56,8 @@ struct FamExp32 {
     float lambda;
     using P = NoParam;
     __device__ P load(const void*, size_t) const { return P{}; }
-    __device__ float grad(float q, P) const { return sub_(1.0f, mul_(lambda, expf(q))); }
-    __device__ double term(float q, P) const { return (double)sub_(q, mul_(lambda, expf(q))); }
+    __device__ float grad(float q, P) const { return sub_(1.0f, mul_(lambda, ex(q))); }
+    __device__ double term(float q, P) const { return (double)sub_(q, mul_(lambda, ex(q))); }
 };
 struct FamStudentT32 {
     float mu, sigma, nu, logp_const;
@@ -65,7 +69,7 @@ struct FamStudentT32 {
     }
     __device__ double term(float q, P) const {
         float z = div_(sub_(q, mu), sigma);
-        float l = log1pf(div_(mul_(z, z), nu));
+        float l = (float)log1p((double)div_(mul_(z, z), nu));
         return (double)sub_(logp_const, mul_(mul_(add_(nu, 1.0f), 0.5f), l));
     }
 };
@@ -79,7 +83,7 @@ struct FamCauchy32 {
     }
     __device__ double term(float q, P) const {
         float z = div_(sub_(q, loc), scale);
-        return (double)sub_(log_pi_scale, log1pf(mul_(z, z)));
+        return (double)sub_(log_pi_scale, (float)log1p((double)mul_(z, z)));
     }
 };
 struct FamHalfNormal32 {
@@ -87,10 +91,10 @@ struct FamHalfNormal32 {
     using P = NoParam;
     __device__ P load(const void*, size_t) const { return P{}; }
     __device__ float grad(float q, P) const {
-        return sub_(1.0f, div_(expf(mul_(2.0f, q)), mul_(sigma, sigma)));
+        return sub_(1.0f, div_(ex(mul_(2.0f, q)), mul_(sigma, sigma)));
     }
     __device__ double term(float q, P) const {
-        float e2 = expf(mul_(2.0f, q));
+        float e2 = ex(mul_(2.0f, q));
         return (double)sub_(add_(log_const, q), div_(e2, mul_(2.0f, mul_(sigma, sigma))));
     }
 };
@@ -98,14 +102,9 @@ struct FamWeibull32 {
     float k, lambda;
     using P = NoParam;
     __device__ P load(const void*, size_t) const { return P{}; }
-    __device__ float grad(float q, P) const {
-        float r = powf(div_(expf(q), lambda), k);
-        return mul_(k, sub_(1.0f, r));
-    }
-    __device__ double term(float q, P) const {
-        float r = powf(div_(expf(q), lambda), k);
-        return (double)sub_(mul_(k, q), r);
-    }
+    __device__ float r_(float q) const { return (float)pow((double)div_(ex(q), lambda), (double)k); }
+    __device__ float grad(float q, P) const { return mul_(k, sub_(1.0f, r_(q))); }
+    __device__ double term(float q, P) const { return (double)sub_(mul_(k, q), r_(q)); }
 };
 // f64 Gaussian with a per-element precision (prec == nullptr: scalar).
 struct FamGauss64 {
@@ -210,6 +209,113 @@ __global__ void __launch_bounds__(NT) k_chain(ChainArgs<T> g, Fam fam) {
     }
 }
 
+// ---- staged-store variant (TMA bulk stores) ----------------------------------
+//
+// One tile per chain (n <= NT*VPT).  S consecutive steps of the q/p/grad
+// rows are written to shared memory and leave as three bulk copies
+// (cp.async.bulk.global.shared::cta) of S*n*sizeof(T) contiguous bytes each:
+// rows k0..k0+S-1 of one chain are adjacent in the [chain][k][i] layout.  Two
+// staging buffers alternate; before a buffer is rewritten the issuing thread
+// waits until the bulk copies that read it two blocks earlier have finished
+// reading (cp.async.bulk.wait_group.read 1), which is a completion wait on
+// this CTA's own copies and always ends.  Requires n*sizeof(T) % 16 == 0.
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, unsigned bytes) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(ssrc);
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(gdst), "r"(s),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+
+template <typename T, class Fam, int NT, int VPT, int S>
+__global__ void __launch_bounds__(NT) k_chain_tma(ChainArgs<T> g, Fam fam) {
+    static_assert(KC % S == 0, "S must divide KC");
+    constexpr int NW = NT / 32;
+    __shared__ double red[KC][NW];
+    extern __shared__ __align__(128) unsigned char dsm[];
+    T* sbuf = reinterpret_cast<T*>(dsm);  // [2][3][S][n]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t n = g.n, arr = (size_t)S * n, bufsz = 3 * arr;
+    const double cst = g.cst + (g.cst_dev ? *g.cst_dev : 0.0);
+    T* outs[3] = {g.qc, g.pc, g.gc};
+    int bsel = 0;
+    for (unsigned chain = blockIdx.x; chain < g.chains; chain += gridDim.x) {
+        const size_t cbase = (size_t)chain * n;
+        T q[VPT], p[VPT], gr[VPT], em[VPT];
+        typename Fam::P ep[VPT];
+        bool ok[VPT];
+#pragma unroll
+        for (int v = 0; v < VPT; v++) {
+            size_t i = (size_t)v * NT + tid;
+            ok[v] = i < n;
+            size_t ii = ok[v] ? i : 0;
+            q[v] = ok[v] ? g.q0[cbase + ii] : T(0);
+            p[v] = ok[v] ? g.p0[cbase + ii] : T(0);
+            em[v] = ok[v] ? g.m[cbase + ii] : T(0);
+            ep[v] = fam.load(nullptr, ii);
+            gr[v] = fam.grad(q[v], ep[v]);
+        }
+        const T eps = g.eps, he = g.he;
+        for (unsigned k0 = 0; k0 < g.K; k0 += S) {
+            const unsigned kn = (g.K - k0) < (unsigned)S ? (g.K - k0) : (unsigned)S;
+            if (tid == 0) bulk_wait_read1();
+            __syncthreads();
+            T* b = sbuf + (size_t)bsel * bufsz;
+            for (unsigned kk = 0; kk < kn; kk++) {
+                double t = 0.0;
+#pragma unroll
+                for (int v = 0; v < VPT; v++) {
+                    T ph = add_(p[v], mul_(he, gr[v]));
+                    q[v] = add_(q[v], mul_(mul_(eps, em[v]), ph));
+                    gr[v] = fam.grad(q[v], ep[v]);
+                    p[v] = add_(ph, mul_(he, gr[v]));
+                    if (ok[v]) {
+                        size_t i = (size_t)v * NT + tid;
+                        b[kk * n + i] = q[v];
+                        b[arr + kk * n + i] = p[v];
+                        b[2 * arr + kk * n + i] = gr[v];
+                        t = __dadd_rn(t, fam.term(q[v], ep[v]));
+                    }
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+                    t = __dadd_rn(t, __shfl_down_sync(0xffffffffu, t, off));
+                if (lane == 0) red[(k0 + kk) % KC][warp] = t;
+            }
+            fence_proxy_async_smem();
+            __syncthreads();
+            if (tid == 0) {
+                const size_t goff = ((size_t)chain * g.K + k0) * n;
+                const unsigned bytes = (unsigned)(kn * n * sizeof(T));
+#pragma unroll
+                for (int a = 0; a < 3; a++) bulk_store(outs[a] + goff, b + a * arr, bytes);
+                bulk_commit();
+            }
+            bsel ^= 1;
+            const unsigned kend = k0 + kn;
+            if (kend % KC == 0 || kend == g.K) {
+                const unsigned kbase = ((kend - 1) / KC) * KC;
+                if (tid < (int)(kend - kbase)) {
+                    double s = red[tid][0];
+#pragma unroll
+                    for (int w = 1; w < NW; w++) s = __dadd_rn(s, red[tid][w]);
+                    g.logp[(size_t)chain * g.K + kbase + tid] = (T)(g.scale * s + cst);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (tid == 0) bulk_wait_all();
+}
+
 template <typename T>
 __global__ void k_chain_fold(ChainArgs<T> g) {
     size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -253,14 +359,26 @@ Cfg pick_cfg(Ctx& c, size_t n, size_t chains, int mode) {
                 return Cfg{a, b};
         }
     }
-    // Small-n chains: one tile covers the chain.  Large batches: 256-element
-    // tiles balance best across 148 SMs.
-    size_t slots = (size_t)c.dev->sm_count * 8;
-    size_t tiles1 = (n + 255) / 256;
-    if (tiles1 * chains >= 2 * slots) return Cfg{256, 1};
+    // One tile per chain up to n = 2048 (no partial-sum pass); measured on
+    // B200 for 4096 chains x d=1000 x L=32: 256x8 0.539 ms, 128x8 0.551,
+    // 256x4 0.571, 256x1 (4 tiles + fold) 0.578.
+    (void)c;
+    (void)chains;
     if (n <= 512) return Cfg{256, 2};
-    if (n <= 1024) return Cfg{256, 4};
     return Cfg{256, 8};
+}
+
+// NXV_LF_OCC=k caps the resident CTAs per SM at k (by reserving shared
+// memory); 0 or unset leaves occupancy to the register budget.
+size_t occupancy_smem(Ctx& c) {
+    const char* env = getenv("NXV_LF_OCC");
+    int occ = env ? atoi(env) : 0;
+    if (occ <= 0) return 0;
+    int dev = c.dev->id, per_sm = 0;
+    if (cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess)
+        return 0;
+    size_t want = (size_t)per_sm / (size_t)occ;
+    return want > 4096 ? want - 4096 : 0;
 }
 
 template <typename T, class Fam, int NT, int VPT>
@@ -270,9 +388,19 @@ int launch_cfg(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
         g.partial = (double*)scratch(c, (size_t)g.chains * g.K * g.tiles * sizeof(double));
         if (!g.partial) return E_CUDA;
     }
+    if (g.tiles > 65535u) {
+        set_error("chain dimension too large");
+        return E_ARG;
+    }
     unsigned gy = g.chains < 65535u ? g.chains : 65535u;
     dim3 grid(g.tiles, gy);
-    k_chain<T, Fam, NT, VPT><<<grid, NT, 0, c.stream>>>(g, fam);
+    size_t dyn = occupancy_smem(c);
+    if (dyn > 0) {
+        cudaError_t e = cudaFuncSetAttribute(k_chain<T, Fam, NT, VPT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_chain)");
+    }
+    k_chain<T, Fam, NT, VPT><<<grid, NT, dyn, c.stream>>>(g, fam);
     count_launch();
     if (g.mode == 0 && g.tiles > 1) {
         size_t total = (size_t)g.chains * g.K;
@@ -282,13 +410,50 @@ int launch_cfg(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
     return finish(c);
 }
 
+// The staged-store kernel is the default whenever a chain fits one tile
+// (n <= 2048) and its rows are 16-byte multiples.  Measured on B200 for
+// 4096 chains x d=1000 x L=32 (f64): register stores 0.538 ms (92% of the
+// measured HBM copy bandwidth); staged S=1 0.521, S=2 0.503 (98.5%),
+// S=4 0.509.  NXV_LF_TMA=S (1, 2, 4) picks S; NXV_LF_TMA=0 disables it.
+int tma_steps() {
+    const char* env = getenv("NXV_LF_TMA");
+    if (!env || !*env) return 2;
+    int s = atoi(env);
+    return (s == 1 || s == 2 || s == 4) ? s : 0;
+}
+
+template <typename T, class Fam, int VPT, int S>
+int launch_tma(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
+    size_t smem = 2 * 3 * (size_t)S * g.n * sizeof(T);
+    int per_block = 0;
+    cudaDeviceGetAttribute(&per_block, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.dev->id);
+    if (smem + KC * 8 * 8 > (size_t)per_block) return E_KERNEL;  // caller falls back
+    cudaError_t e = cudaFuncSetAttribute(k_chain_tma<T, Fam, 256, VPT, S>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_chain_tma)");
+    g.tiles = 1;
+    unsigned grid = g.chains < 0x7fffffffu ? g.chains : 0x7fffffffu;
+    k_chain_tma<T, Fam, 256, VPT, S><<<grid, 256, smem, c.stream>>>(g, fam);
+    count_launch();
+    return finish(c);
+}
+
+template <typename T, class Fam, int VPT>
+int launch_tma_s(Ctx& c, ChainArgs<T>& g, const Fam& fam, int s) {
+    if (s == 1) return launch_tma<T, Fam, VPT, 1>(c, g, fam);
+    if (s == 2) return launch_tma<T, Fam, VPT, 2>(c, g, fam);
+    return launch_tma<T, Fam, VPT, 4>(c, g, fam);
+}
+
 template <typename T, class Fam>
 int launch_family(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
     if (g.n == 0 || g.K == 0 || g.chains == 0) return OK;
     ScratchGuard guard(c);
-    if (g.tiles > 65535u) {
-        set_error("chain dimension too large");
-        return E_ARG;
+    int s = tma_steps();
+    if (s && g.mode == 0 && g.n <= 2048 && (g.n * sizeof(T)) % 16 == 0) {
+        int rc = g.n <= 1024 ? launch_tma_s<T, Fam, 4>(c, g, fam, s)
+                             : launch_tma_s<T, Fam, 8>(c, g, fam, s);
+        if (rc != E_KERNEL) return rc;
     }
     Cfg cf = pick_cfg(c, g.n, g.chains, g.mode);
     if (cf.nt == 128) return launch_cfg<T, Fam, 128, 8>(c, g, fam);

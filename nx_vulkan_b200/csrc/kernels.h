@@ -6,6 +6,13 @@ namespace nxv {
 
 enum DType : int { F32 = 0, F64 = 1 };
 
+// f32 elementwise transcendentals (exp log sigmoid tanh erf expm1 pow) use
+// the f32 library functions by default (2-4 ulp, the precision class of the
+// reference's f32 shaders).  NXV_EXACT_F32=1 evaluates them in f64 and
+// rounds once, which reproduces Nx.BinaryBackend bit for bit at about half
+// the throughput (B200 runs f64 at half the f32 rate).
+bool fast_f32();
+
 // Op tape for the fused elementwise kernel (lib/nx_vulkan.ex:457-538).
 struct Tape {
     unsigned n_ops;

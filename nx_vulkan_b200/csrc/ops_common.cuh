@@ -46,14 +46,19 @@ __device__ __forceinline__ double floor_(double x) { return floor(x); }
 __device__ __forceinline__ float abs_(float x) { return fabsf(x); }
 __device__ __forceinline__ double abs_(double x) { return fabs(x); }
 
-template <typename T>
+template <bool EXACT>
+__device__ __forceinline__ float pow_sel(float a, float b);
+template <bool EXACT>
+__device__ __forceinline__ double pow_sel(double a, double b) { return pow(a, b); }
+
+template <typename T, bool EXACT = true>
 __device__ __forceinline__ T bin_op(T a, T b, unsigned op) {
     switch (op) {
         case 0: return add_(a, b);
         case 1: return mul_(a, b);
         case 2: return sub_(a, b);
         case 3: return div_(a, b);
-        case 4: return pow_(a, b);
+        case 4: return pow_sel<EXACT>(a, b);
         case 5: return (a >= b) ? a : b;
         case 6: return (a <= b) ? a : b;
         case 7: return (a == b) ? T(1) : T(0);
@@ -63,26 +68,75 @@ __device__ __forceinline__ T bin_op(T a, T b, unsigned op) {
     }
 }
 
-template <typename T>
+// f32 transcendentals.  Nx.BinaryBackend evaluates every f32 op in double
+// and rounds the result to f32 once; EXACT = true does the same on the GPU
+// (f64 evaluation, one rounding), which makes f32 exp/log/tanh/sigmoid/erf/
+// expm1/pow agree with the CPU oracle bit for bit except where the two
+// libraries' f64 results straddle an f32 rounding boundary.  EXACT = false
+// uses the f32 library functions (2-4 ulp) for throughput.
+template <bool EXACT>
+__device__ __forceinline__ float tr_f32(float x, unsigned op) {
+    if constexpr (EXACT) {
+        double d = (double)x;
+        switch (op) {
+            case 0: return (float)exp(d);
+            case 1: return (float)log(d);
+            case 5: return (float)(1.0 / (1.0 + exp(-d)));
+            case 6: return (float)tanh(d);
+            case 13: return (float)erf(d);
+            default: return (float)expm1(d);
+        }
+    } else {
+        switch (op) {
+            case 0: return expf(x);
+            case 1: return logf(x);
+            case 5: return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+            case 6: return tanhf(x);
+            case 13: return erff(x);
+            default: return expm1f(x);
+        }
+    }
+}
+
+template <typename T, bool EXACT = true>
 __device__ __forceinline__ T un_op(T x, unsigned op) {
     switch (op) {
-        case 0: return exp_(x);
-        case 1: return log_(x);
+        case 0:
+        case 1:
+        case 5:
+        case 6:
+        case 13:
+        case 14:
+            if constexpr (sizeof(T) == 4) {
+                return tr_f32<EXACT>(x, op);
+            } else {
+                switch (op) {
+                    case 0: return exp(x);
+                    case 1: return log(x);
+                    case 5: return div_(T(1), add_(T(1), exp(-x)));
+                    case 6: return tanh(x);
+                    case 13: return erf(x);
+                    default: return expm1(x);
+                }
+            }
         case 2: return sqrt_(x);
         case 3: return abs_(x);
         case 4: return -x;
-        case 5: return div_(T(1), add_(T(1), exp_(-x)));
-        case 6: return tanh_(x);
         case 7: return (x > T(0)) ? x : T(0);
         case 8: return ceil_(x);
         case 9: return floor_(x);
         case 10: return (x > T(0)) ? T(1) : ((x < T(0)) ? T(-1) : x);
         case 11: return div_(T(1), x);
         case 12: return mul_(x, x);
-        case 13: return erf_(x);
-        case 14: return expm1_(x);
         default: return x;
     }
+}
+
+// f32 pow, exact (f64 evaluation) or fast.
+template <bool EXACT>
+__device__ __forceinline__ float pow_sel(float a, float b) {
+    if constexpr (EXACT) return (float)pow((double)a, (double)b);
+    else return powf(a, b);
 }
 
 // 16-byte vector of T for coalesced 128-bit loads/stores.

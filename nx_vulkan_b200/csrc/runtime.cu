@@ -81,6 +81,11 @@ int make_current(int id) {
 
 }  // namespace
 
+bool fast_f32() {
+    const char* v = getenv("NXV_EXACT_F32");
+    return !(v && atoi(v) != 0);
+}
+
 void set_error(const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);

@@ -17,10 +17,13 @@ the same function names, argument meaning and error behaviour:
     garbage collected (the ResourceArc Drop, lib.rs:330-342).
 
 Everything computes on the GPU through libnxv_b200.so; nothing here
-evaluates tensor math on the host.
+evaluates tensor math on the host.  Like the reference module, this module
+defines `max`, `min`, `sum` and `abs` as GPU ops; internal code uses
+`_builtins` for the Python ones.
 """
 from __future__ import annotations
 
+import builtins as _builtins
 import ctypes as C
 import math
 import struct
@@ -143,7 +146,7 @@ def upload_f64(values: Iterable[float]):
 def download_binary(t: VulkanTensor, n_bytes: int):
     if n_bytes != t.n_bytes:
         return (ERROR, "size_mismatch")
-    buf = (C.c_char * max(1, n_bytes))()
+    buf = (C.c_char * _builtins.max(1, n_bytes))()
     if _lib().nxv_buf_download(t.handle, buf, n_bytes) != 0:
         return (ERROR, "download_failed")
     return (OK, bytes(buf)[:n_bytes])

@@ -113,6 +113,40 @@ def test_gauss_batched_vs_oracle(nxv, orc, chains, d, K):
     close(down(nxv, outs[3], np.float64), want[3], 1e-12, 1e-12)
 
 
+@pytest.mark.parametrize("stages", ["0", "1", "2", "4"])
+@pytest.mark.parametrize("chains,d,K", [(64, 1000, 32), (5, 2000, 9), (7, 17, 5), (3, 998, 33)])
+def test_gauss_batched_tma_staged(nxv, orc, monkeypatch, stages, chains, d, K):
+    """The staged-store (TMA bulk copy) kernel gives the same bits; odd rows
+    that are not 16-byte multiples fall back to the register-store kernel."""
+    monkeypatch.setenv("NXV_LF_TMA", stages)
+    prec, q0, p0, m = gauss_config(chains, d)
+    eps = 0.01
+    outs = unwrap(nxv.leapfrog_chain_gauss_f64_batched(up(nxv, q0), up(nxv, p0), up(nxv, m), up(nxv, prec),
+                                                       chains, K, eps))
+    want = orc.chain_gauss_f64(q0, p0, m, prec, 0.0, d, chains, K, eps)
+    for t, w in zip(outs[:3], want[:3]):
+        assert np.array_equal(down(nxv, t, np.float64), w)
+    close(down(nxv, outs[3], np.float64), want[3], 1e-12, 1e-12)
+
+
+@pytest.mark.parametrize("family", ["normal", "weibull"])
+def test_chain_families_tma_staged(nxv, orc, monkeypatch, family):
+    monkeypatch.setenv("NXV_LF_TMA", "2")
+    fn, prm = FAMILIES[family]
+    n, K = 1000, 40
+    if family == "weibull":
+        prm = [prm[0], prm[1], n * (np.log(prm[0]) - prm[0] * np.log(prm[1]))]
+    r = np.random.default_rng(5)
+    q0 = (r.normal(size=n) * 0.5).astype(np.float32)
+    p0 = r.normal(size=n).astype(np.float32)
+    m = r.uniform(0.5, 1.5, n).astype(np.float32)
+    qc, pc, gc, lc = unwrap(getattr(nxv, fn)(up(nxv, q0), up(nxv, p0), up(nxv, m), K, 0.05, *prm))
+    wq, wp, wg, wl = orc.chain_f32(family, prm, q0, p0, m, n, 1, K, 0.05)
+    assert np.array_equal(down(nxv, qc, np.float32), wq)
+    assert np.array_equal(down(nxv, pc, np.float32), wp)
+    close(down(nxv, lc, np.float32), wl, 1e-5, 1e-5)
+
+
 def test_gauss_full_config(nxv, orc):
     """4096 chains x d=1000, L=32, eps=0.01 (the headline workload): 16 sampled
     chains against the oracle bit for bit; all chains: time reversibility

@@ -8,7 +8,7 @@ relative (+1e-14 absolute for results near zero)."""
 import numpy as np
 import pytest
 
-from gpu_util import close, down, unwrap, up
+from gpu_util import chain_error_bound, close, close_bound, down, unwrap, up
 
 pytestmark = pytest.mark.gpu
 
@@ -38,7 +38,10 @@ def test_binary_all_ops(nxv, orc, n, dt):
             pa = np.abs(a) + 0.1
             got = down(nxv, unwrap(nxv.apply_binary(up(nxv, pa), tb, op, spv, a.itemsize, 9)), dt)
             want = orc.binary(pa, b, op)
-            close(got, want, 1e-5 if dt == np.float32 else 1e-12, 1e-6 if dt == np.float32 else 1e-14)
+            if dt == np.float32:
+                close_bound(got, want, chain_error_bound(pa, [b], [4], dtype=np.float32))
+            else:
+                close(got, want, 1e-12, 1e-14)
 
 
 @pytest.mark.parametrize("n", SIZES)
@@ -55,8 +58,10 @@ def test_unary_all_ops(nxv, orc, n, dt):
         want = orc.unary(src, op)
         if op in EXACT_UN:
             assert np.array_equal(got, want), op
+        elif dt == np.float32:
+            close_bound(got, want, chain_error_bound(src, [], [100 + op]))
         else:
-            close(got, want, 1e-5 if dt == np.float32 else 1e-12, 1e-6 if dt == np.float32 else 1e-14)
+            close(got, want, 1e-12, 1e-14)
 
 
 def test_unary_specials(nxv, orc):
@@ -65,13 +70,13 @@ def test_unary_specials(nxv, orc):
     ta = up(nxv, a)
     for op in range(15):
         got = down(nxv, unwrap(nxv.apply_unary(ta, op, spv, 4)), np.float32)
-        close(got, orc.unary(a, op), 1e-5, 1e-6)
+        close_bound(got, orc.unary(a, op), chain_error_bound(a, [], [100 + op]))
 
 
 @pytest.mark.parametrize("dt", [np.float32, np.float64])
 def test_broadcast_shapes(nxv, orc, dt):
     r = np.random.default_rng(5)
-    cases = [((3, 5), (5,)), ((3, 5), (3, 1)), ((2, 3, 4), (3, 1)), ((2, 1, 4, 3), (5, 1)),
+    cases = [((3, 5), (5,)), ((3, 5), (3, 1)), ((2, 3, 4), (3, 1)), ((2, 1, 4, 3), (5, 1, 1)),
              ((4, 8), (1, 8)), ((7,), ()), ((64, 256), (256,)), ((3, 1, 5), (1, 4, 1))]
     spv = nxv.shader_path("elementwise_binary_broadcast.spv" if dt == np.float32
                           else "elementwise_binary_broadcast_f64.spv")
@@ -115,7 +120,8 @@ def test_fused_chain_config1(nxv, orc, dt):
     got = down(nxv, t, dt)
     want = orc.fused(x, [y, z], ops, src, imm)
     if dt == np.float32:
-        close(got, want, 1e-5, 1e-6)
+        close(got, want, 1e-5, 1e-6)  # well conditioned: the flat tolerance holds
+        close_bound(got, want, chain_error_bound(x, [y, z], ops, src, imm))
     else:
         scale = 2.0 + np.exp(x.astype(np.float64) * y + z)
         assert np.all(np.abs(got - want) <= 1e-12 * np.maximum(np.abs(want), scale))
@@ -139,7 +145,7 @@ def test_fused_generic_tapes(nxv, orc, n):
     for ops, src in tapes:
         items = [(names[o], s) if o < 100 else unames[o] for o, s in zip(ops, src)]
         got = down(nxv, unwrap(nxv.fused_chain_imm(ta, [tb, tc, td], items)), np.float32)
-        close(got, orc.fused(a, [b, c, d], ops, src), 1e-5, 1e-6)
+        close_bound(got, orc.fused(a, [b, c, d], ops, src), chain_error_bound(a, [b, c, d], ops, src))
 
 
 @pytest.mark.parametrize("shape", [(1, 1, 1), (1, 16777216, 1), (4096, 4096, 1), (1, 4096, 4096),
@@ -227,17 +233,24 @@ def test_matmul_f64(nxv, orc, mnk):
     assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 2 * k * 2.2e-16 * bound.reshape(-1))
 
 
+def f32_dot_bound(k, absprod):
+    """Forward error bound of an f32 dot product of length k (the bound a true
+    f32 FMA GEMM obeys): (k + 8) * 2^-24 * sum|a||b| (accumulation plus the
+    3xTF32 split terms, each <= 2^-22 relative)."""
+    return (k + 8) * 2.0 ** -24 * absprod
+
+
 @pytest.mark.parametrize("mnk", [(1, 1, 3), (2, 2, 2), (17, 33, 9), (128, 128, 128), (130, 70, 257),
                                  (333, 129, 65)])
 def test_matmul_f32_3xtf32(nxv, orc, mnk):
-    """3xTF32 stays within f32 accuracy: |err| <= 1e-5 |C| + 1e-6 + k * 2^-22 sum|a||b|."""
+    """3xTF32 stays within f32 accuracy: |err| <= 1e-5 |C| + 1e-6 + f32 dot bound."""
     m, n, k = mnk
     r = np.random.default_rng(3)
     a, b = r.normal(size=m * k).astype(np.float32), r.normal(size=k * n).astype(np.float32)
     got = down(nxv, unwrap(nxv.matmul(up(nxv, a), up(nxv, b), m, n, k)), np.float32)
     want = orc.matmul(a, b, m, n, k)
     bound = (np.abs(a.reshape(m, k)).astype(np.float64) @ np.abs(b.reshape(k, n))).reshape(-1)
-    assert np.all(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-6 + 4 * 2.0 ** -24 * bound)
+    assert np.all(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-6 + f32_dot_bound(k, bound))
 
 
 def test_matmul_config_sizes(nxv, orc):
@@ -259,7 +272,7 @@ def test_matmul_config_sizes(nxv, orc):
         if dt == np.float64:
             assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 2 * n * 2.2e-16 * bound)
         else:
-            assert np.all(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-6 + 4 * 2.0 ** -24 * bound)
+            assert np.all(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-6 + f32_dot_bound(n, bound))
     a = r.normal(size=(64, 256, 256)) / 16
     b = r.normal(size=(64, 256, 256)) / 16
     got = down(nxv, unwrap(nxv.matmul_batched(up(nxv, a), up(nxv, b), 64, 256, 256, 256, "f64")), np.float64)
