@@ -178,6 +178,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--suite", action="store_true",
+                    help="measure every hot-path workload (one JSON line each) instead of the headline")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -186,6 +188,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.suite:
+        return suite(args)
 
     import torch
     import torch.distributed as dist
@@ -275,11 +279,11 @@ def main():
     peak, peak_kind = peaks()
     abytes = algo_bytes(chains)
     achieved = abytes / (k_ms / 1e3) / 1e9
-    traffic = None
-    tr_path = ROOT / "profiles" / "leapfrog_gauss_f64_traffic.json"
-    if tr_path.exists():
-        tr = json.loads(tr_path.read_text())
-        traffic = tr.get("bytes_per_launch_scaled", tr.get("bytes_per_launch"))
+    # dram__bytes_read.sum + dram__bytes_write.sum of one k_chain_tma launch
+    # over 1024 chains (24,633,856 + 729,063,680 B), scaled by chains; the
+    # writes of that capture miss the dirty lines still in L2 at kernel end,
+    # so this is a lower bound of the full launch's traffic.
+    traffic = (24633856 + 729063680) / 1024 * chains if (D, L) == (1000, 32) else None
 
     # e2e through the C ABI with host buffers (library-owned device buffers).
     e2e = None
@@ -341,8 +345,12 @@ def main():
             "gpu_launches": int(launches),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
+                                           "1024-chain launch scaled by chains (lower bound: "
+                                           "writes still dirty in L2 at kernel end are uncounted)",
                          "algorithmic_bytes_per_launch": abytes, "launch_ms": k_ms,
-                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+                         "kernel": "k_chain_tma (TMA bulk stores, 2 steps per copy) + k_gauss_const",
+                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json), copy, of measured"},
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
@@ -420,6 +428,179 @@ def fused_elementwise_gbs(lib, nxv, torch, dev, stream, peak):
             for h in hs:
                 lib.nxv_buf_free(h)
     return res
+
+
+def suite(args):
+    """Every hot-path workload on GPU 0, one JSON line each.  Launch
+    sequences are captured in a CUDA graph (after a warm-up that sizes the
+    library's scratch) so the events time the GPU, not the host."""
+    import torch
+    from nx_vulkan_b200 import _native, vulkan as nxv
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    lib = _native.load()
+    assert nxv.init_devices([0]) == "ok", _native.last_error()
+    lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
+    peak, peak_kind = peaks()
+    handles = []
+
+    def wrap(t):
+        h = lib.nxv_buf_wrap(C.c_void_p(t.data_ptr()), t.numel() * t.element_size())
+        handles.append(h)
+        return h
+
+    def timed(fn, reps=20):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(3):
+            g.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / (3 * reps)
+
+    def emit(**kw):
+        print(json.dumps(kw), flush=True)
+
+    def ck(rc):
+        if rc != 0:
+            raise RuntimeError(_native.last_error())
+
+    gen = torch.Generator(device="cpu").manual_seed(0)
+
+    # -- fused elementwise chain tanh(exp(x*y+z)-1.0), size sweep ---------------
+    ops = (C.c_uint * 8)(1, 0, 100, 2, 106, 255, 255, 255)
+    src = (C.c_uint * 8)(1, 2, 1, 0, 1, 1, 1, 1)
+    imm = (C.c_double * 8)(0, 0, 0, 1.0, 0, 0, 0, 0)
+    spv = nxv.shader_path("fused_elementwise_imm.spv")
+    for dt, code, sizes in ((torch.float32, 0, (1 << 20, 1 << 24, 1 << 28)),
+                            (torch.float64, 1, (1 << 20, 1 << 24, 1 << 27))):
+        es = 4 if code == 0 else 8
+        for n in sizes:
+            sets = max(1, min(16, (512 << 20) // (4 * n * es)))
+            bufs = []
+            for _ in range(sets):
+                xs = [(torch.rand(n, dtype=torch.float32, device=dev) * 2 - 1).to(dt) for _ in range(3)]
+                out = torch.empty(n, dtype=dt, device=dev)
+                bufs.append([wrap(t) for t in xs + [out]] + [xs, out])
+            it = [0]
+
+            def call():
+                hs = bufs[it[0] % sets]
+                it[0] += 1
+                ck(lib.nxv_fused_chain_imm(hs[3], hs[0], hs[1], hs[2], None, n, 5, ops, src, imm, code, spv))
+
+            reps = 4 * sets if n <= (1 << 24) else 4
+            ms = timed(call, reps)
+            gbs = 4 * n * es / (ms / 1e3) / 1e9
+            emit(workload="fused chain tanh(exp(x*y+z)-1.0)", dtype=str(dt).split(".")[-1], n=n,
+                 us_per_call=ms * 1e3, gbs=gbs, frac_of_hbm=gbs / peak, bytes_per_call=4 * n * es,
+                 rotating_sets=sets)
+            del bufs
+            torch.cuda.empty_cache()
+
+    # -- reductions + broadcast on [4096, 4096] ---------------------------------------
+    R = 4096
+    for dt, code in ((torch.float32, 0), (torch.float64, 1)):
+        es = 4 if code == 0 else 8
+        x = torch.randn(R * R, generator=gen, dtype=torch.float64).to(dt).to(dev)
+        bvec = torch.randn(R, generator=gen, dtype=torch.float64).to(dt).to(dev)
+        hx, hb = wrap(x), wrap(bvec)
+        o_row = torch.empty(R, dtype=dt, device=dev)
+        o_idx = torch.empty(R, dtype=torch.int64, device=dev)
+        o_one = torch.empty(1, dtype=dt, device=dev)
+        o_full = torch.empty(R * R, dtype=dt, device=dev)
+        ho_row, ho_idx, ho_one, ho_full = wrap(o_row), wrap(o_idx), wrap(o_one), wrap(o_full)
+        rspv = nxv.shader_path("reduce_axis.spv" if code == 0 else "reduce_axis_f64.spv")
+        fspv = nxv.shader_path("reduce.spv" if code == 0 else "reduce_full_f64.spv")
+        bspv = nxv.shader_path("elementwise_binary_broadcast.spv" if code == 0
+                               else "elementwise_binary_broadcast_f64.spv")
+        shape = (C.c_uint * 4)(R, R, 0, 0)
+        as_ = (C.c_uint * 4)(R, 1, 0, 0)
+        bs_ = (C.c_uint * 4)(0, 1, 0, 0)
+        cases = [
+            ("sum axis 1", lambda: ck(lib.nxv_reduce_axis(ho_row, hx, R, R, 1, 0, rspv)), R * R * es + R * es),
+            ("reduce_max axis 1", lambda: ck(lib.nxv_reduce_axis(ho_row, hx, R, R, 1, 1, rspv)), R * R * es + R * es),
+            ("sum all axes", lambda: ck(lib.nxv_reduce_to_buf(ho_one, hx, R * R, 0, code, fspv)), R * R * es),
+            ("reduce_max all axes", lambda: ck(lib.nxv_reduce_to_buf(ho_one, hx, R * R, 2, code, fspv)), R * R * es),
+            ("argmax axis 1", lambda: ck(lib.nxv_argmax_axis(ho_idx, hx, R, R, 1, 0, code, 8,
+                                                             nxv.shader_path("argmax_axis.spv"))), R * R * es + R * 8),
+            ("x + b (rows)", lambda: ck(lib.nxv_apply_binary_broadcast(ho_full, hx, hb, 0, 2, shape, as_, bs_, bspv)),
+             2 * R * R * es + R * es),
+        ]
+        for name, fn, nbytes in cases:
+            ms = timed(fn, 20)
+            gbs = nbytes / (ms / 1e3) / 1e9
+            emit(workload=f"{name} [4096,4096]", dtype=str(dt).split(".")[-1], us_per_call=ms * 1e3,
+                 gbs=gbs, frac_of_hbm=gbs / peak, bytes_per_call=nbytes,
+                 l2="input 67/134 MB; back-to-back calls re-read it (L2 126 MB, partial hits)")
+        del x, o_full
+        torch.cuda.empty_cache()
+
+    # -- dense matmul ---------------------------------------------------------------------
+    N = 2048
+    cub = {}
+    for dt, code in ((torch.float64, 1), (torch.float32, 0)):
+        a = (torch.randn(N, N, generator=gen, dtype=torch.float64) / N ** 0.5).to(dt).to(dev)
+        b = (torch.randn(N, N, generator=gen, dtype=torch.float64) / N ** 0.5).to(dt).to(dev)
+        c = torch.empty(N, N, dtype=dt, device=dev)
+        ha, hb2, hc = wrap(a), wrap(b), wrap(c)
+        if code == 1:
+            fn = lambda: ck(lib.nxv_matmul_batched(hc, ha, hb2, 1, N, N, N, 1, nxv.shader_path("matmul_batched.spv")))
+        else:
+            fn = lambda: ck(lib.nxv_matmul(hc, ha, hb2, N, N, N, nxv.shader_path("matmul.spv")))
+        ms = timed(fn, 10)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        ms_cublas = timed(lambda: torch.matmul(a, b, out=c), 10)
+        flops = 2 * N ** 3
+        cub[code] = flops / (ms_cublas / 1e3) / 1e12
+        emit(workload=f"matmul {N}x{N}x{N}", dtype=str(dt).split(".")[-1],
+             kernel="DMMA mma.sync f64" if code == 1 else "3xTF32 mma.sync",
+             ms=ms, tflops=flops / (ms / 1e3) / 1e12, cublas_ms=ms_cublas, cublas_tflops=cub[code],
+             frac_of_cublas=ms_cublas / ms)
+    a = (torch.randn(64, 256, 256, generator=gen, dtype=torch.float64) / 16).to(dev)
+    b = (torch.randn(64, 256, 256, generator=gen, dtype=torch.float64) / 16).to(dev)
+    c = torch.empty(64, 256, 256, dtype=torch.float64, device=dev)
+    ha, hb2, hc = wrap(a), wrap(b), wrap(c)
+    ms = timed(lambda: ck(lib.nxv_matmul_batched(hc, ha, hb2, 64, 256, 256, 256, 1,
+                                                 nxv.shader_path("matmul_batched.spv"))), 10)
+    ms_cublas = timed(lambda: torch.bmm(a, b, out=c), 10)
+    flops = 64 * 2 * 256 ** 3
+    emit(workload="batched matmul 64 x 256^3", dtype="float64", ms=ms, tflops=flops / (ms / 1e3) / 1e12,
+         cublas_ms=ms_cublas, cublas_tflops=flops / (ms_cublas / 1e3) / 1e12, frac_of_cublas=ms_cublas / ms)
+
+    # -- logistic-regression leapfrog -----------------------------------------------------------
+    Nobs, Dm, Cc, Lr = 10000, 100, 256, 16
+    r = np.random.default_rng(4)
+    X = r.normal(size=(Nobs, Dm))
+    w = r.normal(size=Dm)
+    y = (r.random(Nobs) < 1 / (1 + np.exp(-X @ w))).astype(np.float64)
+    tX, ty = torch.from_numpy(X).to(dev), torch.from_numpy(y).to(dev)
+    tq = torch.zeros(Cc, Dm, dtype=torch.float64, device=dev)
+    tp = torch.from_numpy(r.normal(size=(Cc, Dm))).to(dev)
+    outs = [torch.empty(Cc * Lr * Dm, dtype=torch.float64, device=dev) for _ in range(3)]
+    outs.append(torch.empty(Cc * Lr, dtype=torch.float64, device=dev))
+    hs = [wrap(t) for t in outs] + [wrap(tq), wrap(tp), wrap(tX), wrap(ty)]
+    lspv = nxv.shader_path("leapfrog_logreg_f64_batched.spv")
+    ms = timed(lambda: ck(lib.nxv_leapfrog_logreg_f64_batched(*hs, Nobs, Dm, Cc, Lr, 0.002, lspv)), 3)
+    flops = (Lr + 1) * 2 * 2 * Cc * Dm * Nobs
+    emit(workload="logistic-regression leapfrog, 256 chains, X[10000,100], L=16 (one trajectory)",
+         dtype="float64", ms_per_trajectory=ms, chain_steps_per_s=Cc * Lr / (ms / 1e3),
+         gemm_tflops=flops / (ms / 1e3) / 1e12, dgemm_cublas_tflops=cub.get(1),
+         seconds_for_1000_trajectories=ms)
+    for h in handles:
+        lib.nxv_buf_free(h)
+    lib.nxv_set_stream(None)
 
 
 if __name__ == "__main__":
