@@ -337,6 +337,31 @@ int nxv_leapfrog_chain_gauss_f64_batched(void* q_chain, void* p_chain,
                                          unsigned int K, double eps, double mu,
                                          const char* spv_path);
 
+/* NEW, with no counterpart in the reference.  The batched f64 Gaussian
+ * chain above for callers that must not allocate device memory: a host
+ * that captures its sampler step into a CUDA graph (cudaMalloc is not
+ * allowed while a stream is being captured), or a framework that reserves
+ * GPU memory for its own allocator and hands its kernels raw device buffers
+ * (XLA/EXLA preallocate most of HBM, so a side allocation can fail).
+ * Arguments are raw device pointers, not nxv handles, laid out as in
+ * nxv_leapfrog_chain_gauss_f64_batched; the caller guarantees their sizes.
+ * The call allocates nothing: its scratch is a 1 MiB static device array
+ * that every GPU loading this library holds until the process exits.
+ * Limit: chains of n <= 2048 elements need only 256 bytes of it; longer
+ * chains also need n_chains * K * ceil(n / 2048) partial sums of 8 bytes,
+ * and a call needing more than 1 MiB returns -3 with a message naming the
+ * limit.  nxv_init (or nxv_init_devices) must have run.  The first call on
+ * a device looks up the array's device address and must come before any
+ * stream capture.  All calls share the array: two calls that overlap on
+ * the GPU (different streams or threads) race.  Nothing in it needs
+ * clearing between calls.  Same results as the allocating entry point. */
+int nxv_leapfrog_chain_gauss_f64_batched_noalloc(void* q_chain, void* p_chain,
+                                                 void* grad_chain, void* logp_chain,
+                                                 const void* q_init, const void* p_init,
+                                                 const void* inv_mass, const void* prec,
+                                                 unsigned int n, unsigned int n_chains,
+                                                 unsigned int K, double eps, double mu);
+
 /* NEW.  Batched f64 Bayesian logistic-regression chains (inv_mass = 1):
  * grad(q) = X^T (y - sigmoid(X q)) - q,
  * logp(q) = sum_j [y_j z_j - log(1 + e^{z_j})] - 0.5 |q|^2, z = X q.

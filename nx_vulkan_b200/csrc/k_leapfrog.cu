@@ -552,3 +552,103 @@ int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, con
 }
 
 }  // namespace nxv
+
+// ---- scratch-free entry point --------------------------------------------------
+//
+// nxv_leapfrog_chain_gauss_f64_batched_noalloc runs the same kernels as
+// nxv_leapfrog_chain_gauss_f64_batched, but its scratch (the log-density
+// constant and, for chains longer than one 2048-element tile, the per-tile
+// partial sums) lives in a file-scope device array instead of the
+// library's allocator.  Capacity: 1 MiB, i.e. 256 bytes for the constant
+// plus n_chains * K * ceil(n / 2048) partial sums of 8 bytes when n > 2048;
+// chains of n <= 2048 need only the constant.  Every GPU that loads the
+// library holds the array until the process exits.
+
+namespace nxv {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// In host code `g_noalloc_scratch` names a host-side stand-in, not device
+// memory: the device address comes from cudaGetSymbolAddress, looked up once
+// per device with that device current, and is what the kernels receive.
+int noalloc_scratch(Ctx& c, char** out) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    const int id = c.dev->id;
+    if (id < 0 || id >= 64) {
+        set_error("device id %d out of range", id);
+        return E_ARG;
+    }
+    if (!g_noalloc_addr[id]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+        g_noalloc_addr[id] = p;
+    }
+    *out = static_cast<char*>(g_noalloc_addr[id]);
+    return OK;
+}
+
+}  // namespace
+}  // namespace nxv
+
+extern "C" int nxv_leapfrog_chain_gauss_f64_batched_noalloc(
+    void* q_chain, void* p_chain, void* grad_chain, void* logp_chain, const void* q_init,
+    const void* p_init, const void* inv_mass, const void* prec, unsigned int n,
+    unsigned int n_chains, unsigned int K, double eps, double mu) {
+    using namespace nxv;
+    if (!q_chain || !p_chain || !grad_chain || !logp_chain || !q_init || !p_init || !inv_mass ||
+        !prec)
+        return E_NULL;
+    if (K == 0) {
+        set_error("K must be positive");
+        return E_ARG;
+    }
+    Ctx c;
+    int rc = begin(c, {});
+    if (rc) return rc;
+    char* base = nullptr;
+    rc = noalloc_scratch(c, &base);
+    if (rc) return rc;
+    if (n == 0 || n_chains == 0) return OK;
+    const Cfg cf = pick_cfg(c, n, n_chains, 0);
+    const size_t tile = (size_t)cf.nt * cf.vpt;
+    const size_t tiles = (n + tile - 1) / tile;
+    const size_t need = 256 + (tiles > 1 ? (size_t)n_chains * K * tiles * sizeof(double) : 0);
+    if (need > kNoAllocScratchBytes) {
+        set_error("leapfrog noalloc: %u chains x %u steps x %zu tiles of %zu elements need %zu "
+                  "bytes of scratch; the static scratch holds %zu (n_chains * K * ceil(n/%zu) "
+                  "must be <= %zu when n > %zu)",
+                  n_chains, K, tiles, tile, need, kNoAllocScratchBytes, tile,
+                  (kNoAllocScratchBytes - 256) / sizeof(double), tile);
+        return E_ARG;
+    }
+    ChainArgs<double> g{};
+    g.qc = (double*)q_chain;
+    g.pc = (double*)p_chain;
+    g.gc = (double*)grad_chain;
+    g.logp = (double*)logp_chain;
+    g.q0 = (const double*)q_init;
+    g.p0 = (const double*)p_init;
+    g.m = (const double*)inv_mass;
+    g.n = n;
+    g.chains = n_chains;
+    g.K = K;
+    g.eps = eps;
+    g.he = 0.5 * eps;
+    g.mode = 0;
+    g.scale = -0.5;
+    g.cst = 0.0;
+    g.cst_dev = (const double*)base;
+    if (tiles > 1) g.partial = (double*)(base + 256);
+    // Every slot the kernels read is written earlier in the same call (the
+    // constant by k_gauss_const, each partial by its tile), so nothing in
+    // the shared array needs clearing between calls.
+    k_gauss_const<<<1, 256, 0, c.stream>>>((const double*)prec, n, (double*)base);
+    count_launch();
+    return launch_family(c, g, FamGauss64{(const double*)prec, 0.0, mu});
+}
