@@ -57,6 +57,14 @@ def gauss_inputs(chains, d=D, seed=3):
     return prec, q0, p0, np.ones((chains, d))
 
 
+def max_over_ranks_ms(ms, dev, world):
+    """A multi-rank step takes as long as its slowest rank."""
+    if world == 1:
+        return ms
+    from nx_vulkan_b200.dist import max_over_ranks
+    return max_over_ranks(ms, device=dev)
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -119,10 +127,19 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def host_threads():
+    """Every core this process may run on (torchrun sets OMP_NUM_THREADS=1
+    for its workers, so the OpenMP default would be a single thread)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(seconds_min=10.0, seconds_max=30.0, chains=256):
     """Oracle (C restatement, all host threads) on a bounded sample."""
     from oracle import binding as orc
-    nthreads = orc.max_threads()
+    nthreads = host_threads()
     prec, q0, p0, m = gauss_inputs(chains)
     done, t0 = 0, time.perf_counter()
     while True:
@@ -142,7 +159,7 @@ def run_reference(args, rank, world):
         return
     per_step = []
     from oracle import binding as orc
-    nthreads = orc.max_threads()
+    nthreads = host_threads()
     chains = 256
     prec, q0, p0, m = gauss_inputs(chains)
     for i in range(args.warmup + args.steps):
@@ -197,6 +214,12 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
+        # The only collective is a 32 KB-per-rank diagnostics all-gather per
+        # step: latency-bound, so the low-latency protocol on two channels
+        # (measured on 2 B200s: 0.532 ms/step with NCCL defaults, 0.512 with
+        # these, 0.506 without any collective).  User settings win.
+        os.environ.setdefault("NCCL_PROTO", "LL")
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", "2")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     from nx_vulkan_b200 import _native, vulkan as nxv
@@ -211,57 +234,72 @@ def main():
 
     chains = args.chains
     prec, q0, p0, m = gauss_inputs(chains, seed=3 + 1000 * rank)
-    tq0 = torch.from_numpy(q0).to(dev)
-    tp0 = torch.from_numpy(p0).to(dev)
-    tm = torch.from_numpy(m).to(dev)
-    tprec = torch.from_numpy(prec).to(dev)
+    # Three copies of the inputs (3 x 98 MB > 2x L2) rotate between steps, so
+    # no step finds its inputs in L2; the 3.2 GB of trajectory writes per step
+    # never fit either.
+    n_sets = 3
+    in_sets = []
+    for s in range(n_sets):
+        ts = [torch.from_numpy(a).to(dev) for a in (q0, p0, m)] + [torch.from_numpy(prec).to(dev)]
+        in_sets.append(ts)
     outs = [torch.empty(chains * L * D, dtype=torch.float64, device=dev) for _ in range(3)]
     outs.append(torch.empty(chains * L, dtype=torch.float64, device=dev))
     wrap = lambda t: lib.nxv_buf_wrap(C.c_void_p(t.data_ptr()), t.numel() * t.element_size())
-    h_in = [wrap(t) for t in (tq0, tp0, tm, tprec)]
+    h_sets = [[wrap(t) for t in ts] for ts in in_sets]
+    h_in = h_sets[0]
     h_out = [wrap(t) for t in outs]
     spv = nxv.shader_path("leapfrog_chain_gauss_f64_batched.spv")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 2x L2
 
-    def step():
-        rc = lib.nxv_leapfrog_chain_gauss_f64_batched(*h_out, *h_in, D, chains, L, EPS, 0.0, spv)
+    def step(i=0):
+        rc = lib.nxv_leapfrog_chain_gauss_f64_batched(*h_out, *h_sets[i % n_sets], D, chains, L,
+                                                      EPS, 0.0, spv)
         if rc != 0:
             raise RuntimeError(f"leapfrog failed: {rc} {_native.last_error()}")
 
-    diag = torch.empty(world * chains, dtype=torch.float64, device=dev)
+    # Diagnostics exchange: the final-step logp of every chain, all-gathered
+    # on a side stream so that the collective of step i overlaps step i+1.
+    # Two buffers alternate; before buffer b is refilled the main stream waits
+    # for the collective that read it two steps earlier.
+    diags = [torch.empty(world * chains, dtype=torch.float64, device=dev) for _ in range(2)]
+    lasts = [torch.empty(chains, dtype=torch.float64, device=dev) for _ in range(2)]
+    side_done = [None, None]
+    side = torch.cuda.Stream(device=dev)
 
-    def diagnostics():
-        if world > 1:
-            last = outs[3].view(chains, L)[:, -1].contiguous()
-            dist.all_gather_into_tensor(diag, last)
+    def diagnostics(i):
+        if world == 1:
+            return
+        b = i % 2
+        if side_done[b] is not None:
+            stream.wait_event(side_done[b])
+        lasts[b].copy_(outs[3].view(chains, L)[:, -1])
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            dist.all_gather_into_tensor(diags[b], lasts[b])
+        side_done[b] = side.record_event()
 
-    for _ in range(args.warmup):
-        step()
-        diagnostics()
+    for i in range(args.warmup):
+        step(i)
+        diagnostics(i)
+    stream.wait_stream(side)
     torch.cuda.synchronize()
     n_launch0 = lib.nxv_launch_count()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
+    t0_ev, t1_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with Clocks(local) as clk:
+        t0_ev.record(stream)
         for i in range(args.steps):
-            flush.zero_()
-            evs[i][0].record(stream)
-            step()
-            diagnostics()
-            evs[i][1].record(stream)
+            step(i)
+            diagnostics(i)
+        stream.wait_stream(side)  # the final collective is inside the timed region
+        t1_ev.record(stream)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     launches = (lib.nxv_launch_count() - n_launch0) // args.steps * args.steps
-    per_ms = [a.elapsed_time(b) for a, b in evs]
-    t_ms = sum(per_ms)
-    t_all = torch.tensor([t_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
-    t_ms = float(t_all.item())
+    t_ms = max_over_ranks_ms(t0_ev.elapsed_time(t1_ev), dev, world)
     value = world * chains * L * args.steps / (t_ms / 1e3)
     clocks = clk.summary()
 
@@ -339,9 +377,13 @@ def main():
             "data": "synthetic (seeded numpy: prec~U(0.5,2) seed 3, q0,p0~N(0,1); rank r uses seed 3+1000r)",
             "config": {"workload": "anisotropic Gaussian HMC leapfrog, fused K-step chain",
                        "chains_per_gpu": chains, "d": D, "L": L, "eps": EPS, "inv_mass": 1.0,
-                       "parallelism": f"chains sharded, {world} rank(s), NCCL all-gather of final logp per step"
+                       "parallelism": f"chains sharded, {world} rank(s), NCCL all-gather of final logp per step "
+                                      f"(overlapped with the next step; NCCL_PROTO={os.environ.get('NCCL_PROTO')})"
                        if world > 1 else "1 GPU",
-                       "l2": "256 MiB buffer written between timed steps (L2 flush); per-step traffic 3.25 GB"},
+                       "l2": "inputs larger than L2: 3 rotating input sets of 98 MB (295 MB > 2x 126 MB); "
+                             "3.15 GB of trajectory writes per step",
+                       "timing": "one CUDA event pair around all timed steps on the launching stream, "
+                                 "collectives included; max over ranks"},
             "gpu_launches": int(launches),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -358,7 +400,7 @@ def main():
         if secondary:
             line["secondary"] = secondary
         print(json.dumps(line), flush=True)
-    for h in h_in + h_out:
+    for h in [h for hs in h_sets for h in hs] + h_out:
         lib.nxv_buf_free(h)
     lib.nxv_set_stream(None)
     if world > 1:
