@@ -607,7 +607,7 @@ def suite(args):
         flops = 2 * N ** 3
         cub[code] = flops / (ms_cublas / 1e3) / 1e12
         emit(workload=f"matmul {N}x{N}x{N}", dtype=str(dt).split(".")[-1],
-             kernel="DMMA mma.sync f64" if code == 1 else "3xTF32 mma.sync",
+             kernel="DMMA mma.sync f64" if code == 1 else "3xTF32 tcgen05 (TMEM accumulator, TMA 128B-swizzled tiles)",
              ms=ms, tflops=flops / (ms / 1e3) / 1e12, cublas_ms=ms_cublas, cublas_tflops=cub[code],
              frac_of_cublas=ms_cublas / ms)
     a = (torch.randn(64, 256, 256, generator=gen, dtype=torch.float64) / 16).to(dev)

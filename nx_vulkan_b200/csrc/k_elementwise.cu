@@ -287,6 +287,48 @@ k_bcast(T* __restrict__ out, const T* __restrict__ a, const T* __restrict__ b, B
     }
 }
 
+// Row-blocked variant for long inner rows (the [4096, 4096] + [4096] row
+// broadcast): grid.y walks output rows, grid.x covers the row's vectors; the
+// operand offsets of a row are decoded once per row instead of once per vector.
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+k_bcast_rows(T* __restrict__ out, const T* __restrict__ a, const T* __restrict__ b, Bcast g,
+             unsigned op, size_t rows) {
+    constexpr int W = (int)(16 / sizeof(T));
+    const unsigned last = g.ndim - 1;
+    const size_t inner = g.shape[last], nvec = inner / W;
+    const bool va = g.as[last] == 1, vb = g.bs[last] == 1;
+    for (size_t row = blockIdx.y; row < rows; row += gridDim.y) {
+        size_t oa = 0, ob = 0, rem = row;
+        for (int d = (int)last - 1; d >= 0; d--) {
+            size_t cd = rem % g.shape[d];
+            rem /= g.shape[d];
+            oa += cd * g.as[d];
+            ob += cd * g.bs[d];
+        }
+        const T* ra = a + oa;
+        const T* rb = b + ob;
+        T* ro = out + row * inner;
+        for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
+             v += (size_t)gridDim.x * blockDim.x) {
+            T xa[W], xb[W], r[W];
+            if (va) vload(ra + v * W, xa);
+            else {
+#pragma unroll
+                for (int j = 0; j < W; j++) xa[j] = ra[0];
+            }
+            if (vb) vload(rb + v * W, xb);
+            else {
+#pragma unroll
+                for (int j = 0; j < W; j++) xb[j] = rb[0];
+            }
+#pragma unroll
+            for (int j = 0; j < W; j++) r[j] = bin_op<T>(xa[j], xb[j], op);
+            vstore(ro + v * W, r);
+        }
+    }
+}
+
 // ---- transpose --------------------------------------------------------------
 
 template <typename T>
@@ -385,6 +427,22 @@ int launch_broadcast(Ctx& c, int dt, void* out, const void* a, const void* b, un
                g.as[last] <= 1 && g.bs[last] <= 1;
     for (unsigned d = 0; vec && d < last; d++)
         if ((g.as[last] == 1 && g.as[d] % W) || (g.bs[last] == 1 && g.bs[d] % W)) vec = false;
+    const size_t inner_v = g.shape[last] / W;
+    if (vec && inner_v >= 128) {
+        const size_t rows = n / g.shape[last];
+        const unsigned gx = (unsigned)((inner_v + kThreads - 1) / kThreads);
+        size_t want_y = ((size_t)c.dev->sm_count * 8 + gx - 1) / gx;
+        const unsigned gy = (unsigned)(rows < want_y ? rows : (want_y < 65535 ? want_y : 65535));
+        dim3 grid2(gx, gy);
+        if (dt == F32)
+            k_bcast_rows<float><<<grid2, kThreads, 0, c.stream>>>((float*)out, (const float*)a,
+                                                                  (const float*)b, g, op, rows);
+        else
+            k_bcast_rows<double><<<grid2, kThreads, 0, c.stream>>>((double*)out, (const double*)a,
+                                                                   (const double*)b, g, op, rows);
+        count_launch();
+        return finish(c);
+    }
     unsigned grid = grid_for(c, vec ? n / W : n, kThreads, 8);
     if (dt == F32) {
         if (vec) k_bcast<float, true><<<grid, kThreads, 0, c.stream>>>((float*)out, (const float*)a, (const float*)b, g, op, n);

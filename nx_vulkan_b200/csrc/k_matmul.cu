@@ -12,6 +12,9 @@
 // that every fragment load is bank-conflict free (A rows are BK+4 elements,
 // B rows are 128+8 elements), zero-filled out-of-range chunks, and a
 // scalar loader when a row is not 16-byte aligned.
+#include <stdlib.h>
+#include <string.h>
+
 #include "kernels.h"
 
 namespace nxv {
@@ -310,6 +313,10 @@ int launch_matmul_f64(Ctx& c, void* C, const void* A, const void* B, size_t batc
 
 int launch_matmul_f32(Ctx& c, void* C, const void* A, const void* B, size_t batch, size_t m,
                       size_t n, size_t k) {
+    // Default: tcgen05 3xTF32 (k_matmul_tc.cu).  NXV_MATMUL_F32=mma selects the
+    // warp-level mma.sync 3xTF32 kernel below.
+    const char* v = getenv("NXV_MATMUL_F32");
+    if (!(v && strcmp(v, "mma") == 0)) return launch_matmul_f32_tc(c, C, A, B, batch, m, n, k);
     return run_gemm<float, 32>(c, (float*)C, (const float*)A, (const float*)B, batch, m, n, k);
 }
 

@@ -1,0 +1,388 @@
+// k_matmul_tc.cu -- f32 GEMM as 3xTF32 on the sm_100a tensor cores (tcgen05).
+//
+// C = A . B with A [M][K], B [K][N], C [M][N] row-major f32, batched.
+// Split: x = hi + lo with hi = x with its 13 low mantissa bits cleared (an
+// exact TF32 value) and lo = x - hi (exact in f32);
+// C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi accumulated in f32 in tensor memory.
+// The dropped A_lo.B_lo term and the TF32 reading of lo are ~2^-22 relative,
+// so the result has f32 accuracy.
+//
+// Pipeline (one CTA per 128 x 128 tile of C, 4 warps):
+//   pre-pass  split A -> A_hi, A_lo [M][Kp] and B -> B^T_hi, B^T_lo [N][Kp]
+//             (K padded to a multiple of 32 with zeros): both operands
+//             K-major, every TMA box starts at an x multiple of 32.
+//   warp 0    lane 0: TMA producer -- per k-block of 32, four 2-D boxes
+//             (128 rows x 128 bytes, 128-byte swizzle) into one of 3 stages
+//             of 64 KB, completion counted on the stage's mbarrier.
+//   warp 1    lane 0: MMA issuer -- for each of the 4 K-steps of 8 in a
+//             k-block: tcgen05.mma kind::tf32 (lo.hi, hi.lo, hi.hi) into a
+//             128 x 128 f32 accumulator in TMEM; tcgen05.commit frees the
+//             stage, a last commit signals the epilogue.
+//   all       epilogue: warp q reads TMEM lanes 32q..32q+31 (its rows) with
+//             tcgen05.ld 32x32b.x8 and stores C.
+// Every mbarrier wait is bounded: on timeout the kernel records an error
+// flag, drains its own TMA loads (bounded), frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "kernels.h"
+
+namespace nxv {
+
+namespace {
+
+constexpr int TBM = 128, TBN = 128, TBK = 32, TSTAGES = 3;
+constexpr int TILE_BYTES = TBM * TBK * 4;        // 16 KB: 128 rows x 128 B
+constexpr int STAGE_BYTES = 4 * TILE_BYTES;      // A_hi, A_lo, B_hi, B_lo
+constexpr int SMEM_BYTES = TSTAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t TMEM_COLS = 128;
+
+__device__ int g_tc_error;  // 1 when a bounded wait ran out
+
+__device__ __forceinline__ uint32_t su32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait (about a second at most); false and the error flag on timeout.
+__device__ __noinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 22); i++) {
+        if (mbar_try(b, parity)) return true;
+        if (i > 128) __nanosleep(200);
+    }
+    atomicExch(&g_tc_error, 1);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(su32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(su32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand tile of rows of 128 bytes
+// with the 128-byte swizzle; 8-row groups 1024 bytes apart (SBO), version 1
+// (sm_100 format), layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::tf32: D f32 (bits 4-5 = 1), A and B TF32
+// (bits 7-9, 10-12 = 2), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TBN >> 3) << 17) |
+                           ((uint32_t)(TBM >> 4) << 24);
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(IDESC), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* b) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     su32(b))
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(128, 1)
+k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUtensorMap mA_lo,
+          const __grid_constant__ CUtensorMap mB_hi, const __grid_constant__ CUtensorMap mB_lo,
+          float* __restrict__ C, int M, int N, int Kp, long long sC) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t base = su32(smem_raw);
+    unsigned char* smem = smem_raw + ((1024 - (base & 1023)) & 1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + TSTAGES * STAGE_BYTES);
+    uint64_t* empty = full + TSTAGES;
+    uint64_t* done = empty + TSTAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    __shared__ int s_err;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.y * TBM, n0 = blockIdx.x * TBN, bz = blockIdx.z;
+    const int KB = Kp / TBK;
+
+    if (tid == 0) {
+        s_err = 0;
+        for (int s = 0; s < TSTAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         su32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    int issued = 0;  // producer: k-blocks whose loads were issued
+    if (warp == 0 && lane == 0) {
+        for (int kb = 0; kb < KB; kb++) {
+            const int s = kb % TSTAGES;
+            if (kb >= TSTAGES && !mbar_wait(&empty[s], ((kb / TSTAGES) + 1) & 1)) {
+                s_err = 1;
+                break;
+            }
+            unsigned char* st = smem + s * STAGE_BYTES;
+            mbar_expect_tx(&full[s], STAGE_BYTES);
+            tma_load_3d(st, &mA_hi, kb * TBK, m0, bz, &full[s]);
+            tma_load_3d(st + TILE_BYTES, &mA_lo, kb * TBK, m0, bz, &full[s]);
+            tma_load_3d(st + 2 * TILE_BYTES, &mB_hi, kb * TBK, n0, bz, &full[s]);
+            tma_load_3d(st + 3 * TILE_BYTES, &mB_lo, kb * TBK, n0, bz, &full[s]);
+            issued = kb + 1;
+        }
+    } else if (warp == 1 && lane == 0) {
+        bool ok = true;
+        for (int kb = 0; kb < KB; kb++) {
+            const int s = kb % TSTAGES;
+            if (!mbar_wait(&full[s], (kb / TSTAGES) & 1)) {
+                s_err = 1;
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t st = su32(smem + s * STAGE_BYTES);
+            const uint64_t ahi = sdesc(st), alo = sdesc(st + TILE_BYTES);
+            const uint64_t bhi = sdesc(st + 2 * TILE_BYTES), blo = sdesc(st + 3 * TILE_BYTES);
+#pragma unroll
+            for (int j = 0; j < TBK / 8; j++) {
+                const uint64_t adv = (uint64_t)(j * 32) >> 4;  // 8 f32 = 32 bytes along K
+                umma_tf32(tmem, alo + adv, bhi + adv, (kb | j) != 0);
+                umma_tf32(tmem, ahi + adv, blo + adv, 1);
+                umma_tf32(tmem, ahi + adv, bhi + adv, 1);
+            }
+            umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(done);
+    }
+    __syncwarp();
+    // Epilogue: wait for the accumulator, then each thread drains its row.
+    bool have = mbar_wait(done, 0);
+    if (!have) s_err = 1;
+    __syncthreads();
+    if (s_err == 0 && have) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int row = m0 + warp * 32 + lane;
+        float* crow = C + bz * sC + (size_t)row * N;
+        const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+        for (int c0 = 0; c0 < TBN; c0 += 8) {
+            uint32_t r[8];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                  "=r"(r[6]), "=r"(r[7])
+                : "r"(tl + c0));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (row < M) {
+                const int col = n0 + c0;
+                if (col + 8 <= N && (((uintptr_t)(crow + col)) & 15) == 0) {
+                    float4* d4 = reinterpret_cast<float4*>(crow + col);
+                    d4[0] = make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]),
+                                        __uint_as_float(r[2]), __uint_as_float(r[3]));
+                    d4[1] = make_float4(__uint_as_float(r[4]), __uint_as_float(r[5]),
+                                        __uint_as_float(r[6]), __uint_as_float(r[7]));
+                } else {
+                    for (int e = 0; e < 8; e++)
+                        if (col + e < N) crow[col + e] = __uint_as_float(r[e]);
+                }
+            }
+        }
+    } else if (tid == 0) {
+        // error path: let every TMA load this CTA issued land before the CTA
+        // (and its shared memory) goes away; each wait is bounded.
+        for (int kb = (issued > TSTAGES ? issued - TSTAGES : 0); kb < issued; kb++)
+            mbar_wait(&full[kb % TSTAGES], (kb / TSTAGES) & 1);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// Split A [M][K] (lda = K) into exact-TF32 hi and f32 lo parts, [M][Kp]
+// with zero padding in k in [K, Kp).
+__global__ void k_split_rows(const float* __restrict__ A, float* __restrict__ hi,
+                             float* __restrict__ lo, int M, int K, int Kp, long long sA,
+                             long long sO) {
+    const int bz = blockIdx.z;
+    A += bz * sA;
+    hi += bz * sO;
+    lo += bz * sO;
+    const size_t total = (size_t)M * Kp;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / Kp;
+        const int k = (int)(i - r * Kp);
+        const float x = k < K ? A[r * K + k] : 0.0f;
+        const float h = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+        hi[i] = h;
+        lo[i] = __fsub_rn(x, h);
+    }
+}
+
+// Split and transpose B [K][N] into B^T hi/lo [N][Kp] (32 x 32 tiles).
+__global__ void k_split_cols(const float* __restrict__ B, float* __restrict__ hi,
+                             float* __restrict__ lo, int K, int N, int Kp, long long sB,
+                             long long sO) {
+    __shared__ float t[32][33];
+    const int bz = blockIdx.z;
+    B += bz * sB;
+    hi += bz * sO;
+    lo += bz * sO;
+    const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int k = k0 + r, n = n0 + threadIdx.x;
+        t[r][threadIdx.x] = (k < K && n < N) ? B[(size_t)k * N + n] : 0.0f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int n = n0 + r, k = k0 + threadIdx.x;
+        if (n < N && k < Kp) {
+            const float x = t[threadIdx.x][r];
+            const float h = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+            hi[(size_t)n * Kp + k] = h;
+            lo[(size_t)n * Kp + k] = __fsub_rn(x, h);
+        }
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 3-D map over [batch][rows][Kp] f32, box 32 (k) x 128 (rows) x 1, 128-byte swizzle.
+int make_map(CUtensorMap* map, const float* base, int rows, int Kp, int batch) {
+    auto fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled unavailable");
+        return E_CUDA;
+    }
+    cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)Kp * 4, (cuuint64_t)Kp * 4 * (cuuint64_t)rows};
+    cuuint32_t box[3] = {(cuuint32_t)TBK, (cuuint32_t)TBM, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return E_CUDA;
+    }
+    return OK;
+}
+
+}  // namespace
+
+int tc_gemm_error() {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (v) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t batch, size_t m,
+                         size_t n, size_t k) {
+    if (batch == 0 || m == 0 || n == 0) return OK;
+    if (k == 0) {
+        cudaError_t e = cudaMemsetAsync(C, 0, batch * m * n * sizeof(float), c.stream);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+        return finish(c);
+    }
+    if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff || batch > 65535) {
+        set_error("matmul extents out of range");
+        return E_ARG;
+    }
+    const size_t Kp = (k + TBK - 1) / TBK * TBK;
+    ScratchGuard guard(c);
+    const size_t a_elems = batch * m * Kp, b_elems = batch * n * Kp;
+    float* s = (float*)scratch(c, (2 * a_elems + 2 * b_elems) * sizeof(float) + 256);
+    if (!s) return E_CUDA;
+    float* ahi = s;
+    float* alo = ahi + a_elems;
+    float* bhi = alo + a_elems;
+    float* blo = bhi + b_elems;
+    {
+        unsigned g = grid_for(c, m * Kp, 256, 8);
+        dim3 grid(g, 1, (unsigned)batch);
+        k_split_rows<<<grid, 256, 0, c.stream>>>((const float*)A, ahi, alo, (int)m, (int)k, (int)Kp,
+                                                 (long long)(m * k), (long long)(m * Kp));
+        dim3 g2((unsigned)((n + 31) / 32), (unsigned)(Kp / 32), (unsigned)batch);
+        k_split_cols<<<g2, dim3(32, 8), 0, c.stream>>>((const float*)B, bhi, blo, (int)k, (int)n,
+                                                       (int)Kp, (long long)(k * n),
+                                                       (long long)(n * Kp));
+        count_launch(2);
+    }
+    CUtensorMap mah, mal, mbh, mbl;
+    int rc;
+    if ((rc = make_map(&mah, ahi, (int)m, (int)Kp, (int)batch))) return rc;
+    if ((rc = make_map(&mal, alo, (int)m, (int)Kp, (int)batch))) return rc;
+    if ((rc = make_map(&mbh, bhi, (int)n, (int)Kp, (int)batch))) return rc;
+    if ((rc = make_map(&mbl, blo, (int)n, (int)Kp, (int)batch))) return rc;
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_gemm_tc)");
+    dim3 grid((unsigned)((n + TBN - 1) / TBN), (unsigned)((m + TBM - 1) / TBM), (unsigned)batch);
+    if (grid.y > 65535) {
+        set_error("matmul M too large");
+        return E_ARG;
+    }
+    k_gemm_tc<<<grid, 128, SMEM_BYTES, c.stream>>>(mah, mal, mbh, mbl, (float*)C, (int)m, (int)n,
+                                                    (int)Kp, (long long)(m * n));
+    count_launch();
+    return finish(c);
+}
+
+}  // namespace nxv

@@ -130,16 +130,37 @@ k_rows(const T* __restrict__ a, size_t R_, size_t L, void* out, typename R::Acc*
     const T* row = a + r * R_;
     typename R::Acc acc = R::init();
     constexpr int W = (int)(16 / sizeof(T));
+    constexpr int U = 4;  // vectors in flight per thread, one accumulator each
     // vector body when the segment start is 16-byte aligned
     size_t i = beg;
     if ((((uintptr_t)(row + beg)) & 15) == 0) {
-        size_t nv = (end - beg) / W;
-        for (size_t v = threadIdx.x; v < nv; v += blockDim.x) {
-            T x[W];
-            vload(row + beg + v * W, x);
+        const size_t nv = (end - beg) / W;
+        const size_t step = (size_t)blockDim.x * U;
+        typename R::Acc part[U];
 #pragma unroll
-            for (int j = 0; j < W; j++) acc = R::add(acc, x[j], (long long)(beg + v * W + j));
+        for (int u = 0; u < U; u++) part[u] = R::init();
+        size_t v = threadIdx.x;
+        for (; v + (U - 1) * blockDim.x < nv; v += step) {
+            T x[U][W];
+#pragma unroll
+            for (int u = 0; u < U; u++) vload(row + beg + (v + u * blockDim.x) * W, x[u]);
+#pragma unroll
+            for (int u = 0; u < U; u++)
+#pragma unroll
+                for (int j = 0; j < W; j++)
+                    part[u] = R::add(part[u], x[u][j], (long long)(beg + (v + u * blockDim.x) * W + j));
         }
+        for (int u = 0; u < U; u++, v += blockDim.x) {
+            if (v < nv) {
+                T x[W];
+                vload(row + beg + v * W, x);
+#pragma unroll
+                for (int j = 0; j < W; j++) part[u] = R::add(part[u], x[j], (long long)(beg + v * W + j));
+            }
+        }
+        acc = part[0];
+#pragma unroll
+        for (int u = 1; u < U; u++) acc = R::combine(acc, part[u]);
         i = beg + nv * W;
     }
     for (size_t e = i + threadIdx.x; e < end; e += blockDim.x) acc = R::add(acc, row[e], (long long)e);
@@ -161,6 +182,18 @@ __global__ void k_fold(const typename R::Acc* __restrict__ partial, size_t n_out
     typename R::Acc acc = partial[(o * S) * inner + j];
     for (int s = 1; s < S; s++) acc = R::combine(acc, partial[(o * S + s) * inner + j]);
     write_out<R, T>(out, t, acc, index_bytes);
+}
+
+// Rows case: one CTA folds the S partials of one row.  Thread t combines
+// partials t, t+256, ... in order, then the fixed block tree finishes.
+template <class R, typename T>
+__global__ void __launch_bounds__(kThreads)
+k_fold_rows(const typename R::Acc* __restrict__ partial, int S, void* out, int index_bytes) {
+    const size_t o = blockIdx.x;
+    typename R::Acc acc = R::init();
+    for (int s = threadIdx.x; s < S; s += blockDim.x) acc = R::combine(acc, partial[o * S + s]);
+    acc = block_reduce<R>(acc);
+    if (threadIdx.x == 0) write_out<R, T>(out, o, acc, index_bytes);
 }
 
 // cols kernel: grid (ceil(inner/256), S, outer); thread owns column j.
@@ -226,8 +259,8 @@ int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* 
         k_rows<R, T><<<grid, kThreads, 0, c.stream>>>(a, R_, L, out, part, (int)S, index_bytes);
         count_launch();
         if (S > 1) {
-            k_fold<R, T><<<(unsigned)((outer + 127) / 128), 128, 0, c.stream>>>(part, outer, (int)S, 1,
-                                                                               out, index_bytes);
+            k_fold_rows<R, T><<<(unsigned)outer, kThreads, 0, c.stream>>>(part, (int)S, out,
+                                                                           index_bytes);
             count_launch();
         }
         return finish(c);

@@ -84,6 +84,11 @@ int launch_matmul_f64(Ctx& c, void* C, const void* A, const void* B, size_t batc
                       size_t n, size_t k);
 int launch_matmul_f32(Ctx& c, void* C, const void* A, const void* B, size_t batch, size_t m,
                       size_t n, size_t k);
+// 3xTF32 on tcgen05 (k_matmul_tc.cu); the default f32 path.
+int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t batch, size_t m,
+                         size_t n, size_t k);
+// Reads and clears the tensor-core GEMM's timeout flag (1 = a bounded wait ran out).
+int tc_gemm_error();
 
 // Grid helper: blocks for a grid-stride kernel.
 inline unsigned grid_for(Ctx& c, size_t work_items, unsigned threads, unsigned per_sm) {

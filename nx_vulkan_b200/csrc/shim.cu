@@ -672,7 +672,12 @@ int nxv_set_stream(void* cuda_stream) { return set_stream((cudaStream_t)cuda_str
 
 int nxv_synchronize(void) {
     BEGIN();
-    return sync(c);
+    int rc = sync(c);
+    if (rc == OK && tc_gemm_error()) {
+        set_error("tensor-core GEMM: a bounded pipeline wait ran out; results are invalid");
+        return E_CUDA;
+    }
+    return rc;
 }
 
 void* nxv_buf_wrap(void* device_ptr, unsigned long n_bytes) {

@@ -333,3 +333,27 @@ def test_errors_are_reported(nxv):
     # empty tensor ops are no-ops, not errors
     e = unwrap(nxv.upload_f32([]))
     assert lib.nxv_apply_unary(e.handle, e.handle, 0, 0, nxv.shader_path("elementwise_unary.spv")) == 0
+
+
+@pytest.mark.parametrize("bmnk", [(1, 1, 1, 1), (1, 128, 128, 32), (1, 129, 257, 33), (3, 130, 70, 257),
+                                  (2, 256, 384, 1000), (64, 256, 256, 256)])
+def test_matmul_f32_tensor_core_vs_oracle_and_mma(nxv, orc, monkeypatch, bmnk):
+    """tcgen05 3xTF32 (default) against the oracle and against the mma.sync
+    3xTF32 kernel; both within the f32 dot-product bound."""
+    batch, m, n, k = bmnk
+    r = np.random.default_rng(11)
+    a = r.normal(size=batch * m * k).astype(np.float32)
+    b = r.normal(size=batch * k * n).astype(np.float32)
+    ta, tb = up(nxv, a), up(nxv, b)
+    got = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f32")), np.float32)
+    monkeypatch.setenv("NXV_MATMUL_F32", "mma")
+    legacy = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f32")), np.float32)
+    want = orc.matmul(a, b, m, n, k, batch=batch)
+    bound = np.concatenate([
+        (np.abs(a.reshape(batch, m, k)[q]).astype(np.float64) @ np.abs(b.reshape(batch, k, n)[q])).reshape(-1)
+        for q in range(batch)])
+    tol = 1e-5 * np.abs(want) + 1e-6 + f32_dot_bound(k, bound)
+    assert np.all(np.abs(got - want) <= tol)
+    assert np.all(np.abs(legacy - want) <= tol)
+    from nx_vulkan_b200 import _native
+    assert _native.load().nxv_synchronize() == 0  # no pipeline timeout recorded
