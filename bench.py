@@ -7,8 +7,9 @@ anisotropic Gaussian target, d = 1000, diagonal precision prec_i ~ U(0.5, 2)
 eps = 0.01, L = 32 leapfrog steps per trajectory, f64.  Outputs are the
 reference contract's q/p/grad trajectories [chain][k][i] and logp [chain][k].
 
-  value  chain-steps/s over all ranks, inputs resident in HBM, timed per step
-         with CUDA events on the launching stream, L2 flushed between steps.
+  value  chain-steps/s over all ranks, inputs resident in HBM: one CUDA
+         event pair on the launching stream around all timed steps (and the
+         collectives), three rotating input sets larger than L2 together.
   e2e    the same metric through the C ABI with host buffers: every step
          uploads q0/p0/inv_mass/prec from pinned host memory and downloads the
          four outputs into pinned host memory (nxv_buf_upload/_download).

@@ -287,44 +287,63 @@ k_bcast(T* __restrict__ out, const T* __restrict__ a, const T* __restrict__ b, B
     }
 }
 
-// Row-blocked variant for long inner rows (the [4096, 4096] + [4096] row
-// broadcast): grid.y walks output rows, grid.x covers the row's vectors; the
-// operand offsets of a row are decoded once per row instead of once per vector.
+// Vector path for outputs of fewer than 2^32 elements: the flat vector
+// index is decoded into coordinates with exact multiply-high division
+// (Lemire, Kaser & Kurz 2019: for M = ceil(2^64 / d) and 32-bit n, d,
+// floor(n / d) = umulhi64(M, n)), and each thread keeps 4 vectors in flight.
+struct FastDiv {
+    unsigned long long m[4];  // ceil(2^64 / shape[d]); 0 when shape[d] == 1
+};
+
+__device__ __forceinline__ unsigned fdiv(unsigned x, unsigned long long m) {
+    return m ? (unsigned)__umul64hi(m, (unsigned long long)x) : x;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-k_bcast_rows(T* __restrict__ out, const T* __restrict__ a, const T* __restrict__ b, Bcast g,
-             unsigned op, size_t rows) {
+k_bcast_fast(T* __restrict__ out, const T* __restrict__ a, const T* __restrict__ b, Bcast g,
+             FastDiv fd, unsigned op, unsigned nv) {
     constexpr int W = (int)(16 / sizeof(T));
-    const unsigned last = g.ndim - 1;
-    const size_t inner = g.shape[last], nvec = inner / W;
+    constexpr int U = 4;
+    const int last = (int)g.ndim - 1;
     const bool va = g.as[last] == 1, vb = g.bs[last] == 1;
-    for (size_t row = blockIdx.y; row < rows; row += gridDim.y) {
-        size_t oa = 0, ob = 0, rem = row;
-        for (int d = (int)last - 1; d >= 0; d--) {
-            size_t cd = rem % g.shape[d];
-            rem /= g.shape[d];
-            oa += cd * g.as[d];
-            ob += cd * g.bs[d];
+    const unsigned stride = gridDim.x * blockDim.x;
+    for (unsigned v0 = blockIdx.x * blockDim.x + threadIdx.x; v0 < nv; v0 += stride * U) {
+        T xa[U][W], xb[U][W];
+        unsigned ev[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const unsigned v = v0 + u * stride;
+            ev[u] = v;
+            if (v >= nv) continue;
+            unsigned rem = v * W, oa = 0, ob = 0;
+#pragma unroll
+            for (int d = 3; d >= 0; d--) {
+                if (d > last) continue;
+                const unsigned q = fdiv(rem, fd.m[d]);
+                const unsigned cd = rem - q * g.shape[d];
+                rem = q;
+                oa += cd * g.as[d];
+                ob += cd * g.bs[d];
+            }
+            if (va) vload(a + oa, xa[u]);
+            else {
+#pragma unroll
+                for (int j = 0; j < W; j++) xa[u][j] = a[oa];
+            }
+            if (vb) vload(b + ob, xb[u]);
+            else {
+#pragma unroll
+                for (int j = 0; j < W; j++) xb[u][j] = b[ob];
+            }
         }
-        const T* ra = a + oa;
-        const T* rb = b + ob;
-        T* ro = out + row * inner;
-        for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
-             v += (size_t)gridDim.x * blockDim.x) {
-            T xa[W], xb[W], r[W];
-            if (va) vload(ra + v * W, xa);
-            else {
 #pragma unroll
-                for (int j = 0; j < W; j++) xa[j] = ra[0];
-            }
-            if (vb) vload(rb + v * W, xb);
-            else {
+        for (int u = 0; u < U; u++) {
+            if (ev[u] >= nv) continue;
+            T r[W];
 #pragma unroll
-                for (int j = 0; j < W; j++) xb[j] = rb[0];
-            }
-#pragma unroll
-            for (int j = 0; j < W; j++) r[j] = bin_op<T>(xa[j], xb[j], op);
-            vstore(ro + v * W, r);
+            for (int j = 0; j < W; j++) r[j] = bin_op<T>(xa[u][j], xb[u][j], op);
+            vstore(out + (size_t)ev[u] * W, r);
         }
     }
 }
@@ -427,19 +446,26 @@ int launch_broadcast(Ctx& c, int dt, void* out, const void* a, const void* b, un
                g.as[last] <= 1 && g.bs[last] <= 1;
     for (unsigned d = 0; vec && d < last; d++)
         if ((g.as[last] == 1 && g.as[d] % W) || (g.bs[last] == 1 && g.bs[d] % W)) vec = false;
-    const size_t inner_v = g.shape[last] / W;
-    if (vec && inner_v >= 128) {
-        const size_t rows = n / g.shape[last];
-        const unsigned gx = (unsigned)((inner_v + kThreads - 1) / kThreads);
-        size_t want_y = ((size_t)c.dev->sm_count * 8 + gx - 1) / gx;
-        const unsigned gy = (unsigned)(rows < want_y ? rows : (want_y < 65535 ? want_y : 65535));
-        dim3 grid2(gx, gy);
+    // Fast vector path when every index fits 32 bits.
+    size_t amax = 0, bmax = 0;
+    for (unsigned d = 0; d < ndim; d++) {
+        amax += (size_t)(g.shape[d] - 1) * g.as[d];
+        bmax += (size_t)(g.shape[d] - 1) * g.bs[d];
+    }
+    if (vec && n < (1ull << 32) && amax + W < (1ull << 32) && bmax + W < (1ull << 32)) {
+        FastDiv fd{};
+        for (unsigned d = 0; d < 4; d++) {
+            const unsigned long long sd = g.shape[d];
+            fd.m[d] = (sd <= 1) ? 0ull : (~0ull) / sd + 1ull;  // ceil(2^64 / sd), sd >= 2
+        }
+        const unsigned nv = (unsigned)(n / W);
+        unsigned grid = grid_for(c, (nv + 3) / 4, kThreads, 8);
         if (dt == F32)
-            k_bcast_rows<float><<<grid2, kThreads, 0, c.stream>>>((float*)out, (const float*)a,
-                                                                  (const float*)b, g, op, rows);
+            k_bcast_fast<float><<<grid, kThreads, 0, c.stream>>>((float*)out, (const float*)a,
+                                                                 (const float*)b, g, fd, op, nv);
         else
-            k_bcast_rows<double><<<grid2, kThreads, 0, c.stream>>>((double*)out, (const double*)a,
-                                                                   (const double*)b, g, op, rows);
+            k_bcast_fast<double><<<grid, kThreads, 0, c.stream>>>((double*)out, (const double*)a,
+                                                                  (const double*)b, g, fd, op, nv);
         count_launch();
         return finish(c);
     }

@@ -12,6 +12,7 @@
 // that every fragment load is bank-conflict free (A rows are BK+4 elements,
 // B rows are 128+8 elements), zero-filled out-of-range chunks, and a
 // scalar loader when a row is not 16-byte aligned.
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -107,6 +108,30 @@ __device__ __forceinline__ void dmma_16x8x4(double (&d)[4], double a0, double a1
         : "d"(a0), "d"(a1), "d"(b0));
 }
 
+template <int MK>
+__device__ __forceinline__ void dmma(double (&d)[4], const double* a, const double* b);
+template <>
+__device__ __forceinline__ void dmma<4>(double (&d)[4], const double* a, const double* b) {
+    dmma_16x8x4(d, a[0], a[1], b[0]);
+}
+template <>
+__device__ __forceinline__ void dmma<8>(double (&d)[4], const double* a, const double* b) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+        : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(b[0]), "d"(b[1]));
+}
+template <>
+__device__ __forceinline__ void dmma<16>(double (&d)[4], const double* a, const double* b) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, "
+        "{%4,%5,%6,%7,%8,%9,%10,%11}, {%12,%13,%14,%15}, {%0,%1,%2,%3};\n"
+        : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+        : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(a[4]), "d"(a[5]), "d"(a[6]), "d"(a[7]),
+          "d"(b[0]), "d"(b[1]), "d"(b[2]), "d"(b[3]));
+}
+
 __device__ __forceinline__ unsigned f2tf32_rz(float x) { return __float_as_uint(x) & 0xFFFFE000u; }
 __device__ __forceinline__ unsigned f2tf32_rn(float x) {
     unsigned r;
@@ -123,7 +148,7 @@ __device__ __forceinline__ void tmma_16x8x8(float (&d)[4], const unsigned (&a)[4
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-template <typename T, int BK>
+template <typename T, int BK, int MK = 4>
 __global__ void __launch_bounds__(NTH, 1) k_gemm(GemmP<T> P) {
     using S = Smem<T, BK>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -181,21 +206,26 @@ __global__ void __launch_bounds__(NTH, 1) k_gemm(GemmP<T> P) {
         const T* sA = smem + (kt % STAGES) * S::STAGE;
         const T* sB = sA + S::A_ELEMS;
         if constexpr (sizeof(T) == 8) {
+            // DMMA m16n8kMK: A fragment register r holds (row g + 8*(r%2),
+            // col tig + 4*(r/2)); B register r holds (row tig + 4r, col g).
+            constexpr int AR = MK / 2, BR = MK / 4;
 #pragma unroll
-            for (int kk = 0; kk < BK; kk += 4) {
-                double af[4][2], bf[4];
+            for (int kk = 0; kk < BK; kk += MK) {
+                double af[4][AR], bf[4][BR];
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    af[i][0] = sA[(wm + i * 16 + g) * S::AS + kk + tig];
-                    af[i][1] = sA[(wm + i * 16 + g + 8) * S::AS + kk + tig];
-                }
+                for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) bf[j] = sB[(kk + tig) * S::BS + wn + j * 8 + g];
+                    for (int r = 0; r < AR; r++)
+                        af[i][r] = sA[(wm + i * 16 + g + 8 * (r % 2)) * S::AS + kk + tig + 4 * (r / 2)];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+#pragma unroll
+                    for (int r = 0; r < BR; r++) bf[j][r] = sB[(kk + tig + 4 * r) * S::BS + wn + j * 8 + g];
 #pragma unroll
                 for (int i = 0; i < 4; i++)
 #pragma unroll
                     for (int j = 0; j < 4; j++)
-                        dmma_16x8x4(*reinterpret_cast<double(*)[4]>(acc[i][j]), af[i][0], af[i][1], bf[j]);
+                        dmma<MK>(*reinterpret_cast<double(*)[4]>(acc[i][j]), af[i], bf[j]);
             }
         } else {
 #pragma unroll
@@ -255,13 +285,13 @@ __global__ void __launch_bounds__(NTH, 1) k_gemm(GemmP<T> P) {
         }
 }
 
-template <typename T, int BK>
+template <typename T, int BK, int MK = 4>
 int run_gemm_p(Ctx& c, GemmP<T> P) {
     constexpr int EPC = 16 / sizeof(T);
     P.vecA = ((uintptr_t)P.A % 16 == 0) && (P.lda % EPC == 0) && (P.ksplit % EPC == 0);
     P.vecB = ((uintptr_t)P.B % 16 == 0) && (P.ldb % EPC == 0);
     size_t smem = Smem<T, BK>::BYTES;
-    cudaError_t e = cudaFuncSetAttribute(k_gemm<T, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_gemm<T, BK, MK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
     dim3 grid((unsigned)((P.N + BN - 1) / BN), (unsigned)((P.M + BM - 1) / BM), (unsigned)P.batch);
@@ -269,24 +299,20 @@ int run_gemm_p(Ctx& c, GemmP<T> P) {
         set_error("matmul grid out of range");
         return E_ARG;
     }
-    k_gemm<T, BK><<<grid, NTH, smem, c.stream>>>(P);
+    k_gemm<T, BK, MK><<<grid, NTH, smem, c.stream>>>(P);
     count_launch();
     return finish(c);
 }
 
-template <typename T, int BK>
-int run_gemm(Ctx& c, T* C, const T* A, const T* B, size_t batch, size_t m, size_t n, size_t k) {
-    if (batch == 0 || m == 0 || n == 0) return OK;
-    if (k == 0) {
-        cudaError_t e = cudaMemsetAsync(C, 0, batch * m * n * sizeof(T), c.stream);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
-        return finish(c);
-    }
+// Fills the GEMM parameters of a plain (batched, dense) product.
+template <typename T>
+int plain_params(GemmP<T>& P, T* C, const T* A, const T* B, size_t batch, size_t m, size_t n,
+                 size_t k) {
     if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff || batch > 65535) {
         set_error("matmul extents out of range");
         return E_ARG;
     }
-    GemmP<T> P{};
+    P = GemmP<T>{};
     P.A = A;
     P.B = B;
     P.C = C;
@@ -301,6 +327,42 @@ int run_gemm(Ctx& c, T* C, const T* A, const T* B, size_t batch, size_t m, size_
     P.sC = (long long)(m * n);
     P.ksplit = 0;
     P.batch = (int)batch;
+    return OK;
+}
+
+// f64 configuration: BK x MMA-K.  NXV_DMMA="BKxMK" (16x4, 16x8, 16x16,
+// 32x8, 32x16) overrides the default.
+int dmma_cfg() {
+    const char* v = getenv("NXV_DMMA");
+    if (v && *v) {
+        int bk = 0, mk = 0;
+        if (sscanf(v, "%dx%d", &bk, &mk) == 2) return bk * 100 + mk;
+    }
+    return 1604;
+}
+
+int gemm_f64_dispatch(Ctx& c, const GemmP<double>& P) {
+    switch (dmma_cfg()) {
+        case 1608: return run_gemm_p<double, 16, 8>(c, P);
+        case 1616: return run_gemm_p<double, 16, 16>(c, P);
+        case 3208: return run_gemm_p<double, 32, 8>(c, P);
+        case 3216: return run_gemm_p<double, 32, 16>(c, P);
+        default: return run_gemm_p<double, 16, 4>(c, P);
+    }
+}
+
+template <typename T, int BK>
+int run_gemm(Ctx& c, T* C, const T* A, const T* B, size_t batch, size_t m, size_t n, size_t k) {
+    if (batch == 0 || m == 0 || n == 0) return OK;
+    if (k == 0) {
+        cudaError_t e = cudaMemsetAsync(C, 0, batch * m * n * sizeof(T), c.stream);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+        return finish(c);
+    }
+    GemmP<T> P;
+    int rc = plain_params(P, C, A, B, batch, m, n, k);
+    if (rc) return rc;
+    if constexpr (sizeof(T) == 8) return gemm_f64_dispatch(c, P);
     return run_gemm_p<T, BK>(c, P);
 }
 
@@ -320,6 +382,6 @@ int launch_matmul_f32(Ctx& c, void* C, const void* A, const void* B, size_t batc
     return run_gemm<float, 32>(c, (float*)C, (const float*)A, (const float*)B, batch, m, n, k);
 }
 
-int gemm_f64(Ctx& c, const GemmP<double>& P) { return run_gemm_p<double, 16>(c, P); }
+int gemm_f64(Ctx& c, const GemmP<double>& P) { return gemm_f64_dispatch(c, P); }
 
 }  // namespace nxv

@@ -66,12 +66,19 @@ template <typename T, bool MAX> struct MaxR {
 
 template <typename T> struct ArgAcc {
     T v;
-    long long i;
+    int i;  // index along the reduced axis (R < 2^31), -1 = empty
 };
 template <typename T, bool MIN> struct ArgR {
     using Acc = ArgAcc<T>;
     using Out = long long;
     __device__ static Acc init() { return Acc{MIN ? (T)INFINITY : (T)-INFINITY, -1}; }
+    // Per-element update.  Every accumulator sees its elements in increasing
+    // index order, so a strict comparison keeps the lowest index on ties, and
+    // a NaN replaces only a non-NaN (the first NaN wins).
+    __device__ static Acc add(Acc a, T x, long long idx) {
+        const bool take = (a.i < 0) || (MIN ? (x < a.v) : (x > a.v)) || (x != x && a.v == a.v);
+        return take ? Acc{x, (int)idx} : a;
+    }
     // true when b should replace a
     __device__ static bool better(Acc a, Acc b) {
         if (b.i < 0) return false;
@@ -85,7 +92,6 @@ template <typename T, bool MIN> struct ArgR {
         return MIN ? (b.v < a.v) : (b.v > a.v);
     }
     __device__ static Acc combine(Acc a, Acc b) { return better(a, b) ? b : a; }
-    __device__ static Acc add(Acc a, T x, long long idx) { return combine(a, Acc{x, idx}); }
     __device__ static Acc shfl(Acc a, int off) {
         return Acc{__shfl_down_sync(0xffffffffu, a.v, off), __shfl_down_sync(0xffffffffu, a.i, off)};
     }
@@ -385,6 +391,10 @@ int launch_argmax(Ctx& c, int dt, void* out, const void* a, size_t outer, size_t
                   size_t inner, int is_min, int index_bytes) {
     if (R == 0) {
         set_error("argmax over an empty axis");
+        return E_ARG;
+    }
+    if (R > 0x7fffffffull) {
+        set_error("argmax axis of %zu elements exceeds 2^31 - 1", R);
         return E_ARG;
     }
     if (dt == F32) {

@@ -77,7 +77,11 @@ def test_unary_specials(nxv, orc):
 def test_broadcast_shapes(nxv, orc, dt):
     r = np.random.default_rng(5)
     cases = [((3, 5), (5,)), ((3, 5), (3, 1)), ((2, 3, 4), (3, 1)), ((2, 1, 4, 3), (5, 1, 1)),
-             ((4, 8), (1, 8)), ((7,), ()), ((64, 256), (256,)), ((3, 1, 5), (1, 4, 1))]
+             ((4, 8), (1, 8)), ((7,), ()), ((64, 256), (256,)), ((3, 1, 5), (1, 4, 1)),
+             # vector path with 32-bit index decoding: large and odd outer dims,
+             # broadcast on either side and on middle dims
+             ((3, 70001, 4), (70001, 1)), ((8,), (6, 8)), ((2, 3, 5, 8), (3, 1, 8)),
+             ((1000, 12), (1000, 1)), ((5, 131072), (5, 1)), ((6, 1, 16), (7, 1))]
     spv = nxv.shader_path("elementwise_binary_broadcast.spv" if dt == np.float32
                           else "elementwise_binary_broadcast_f64.spv")
     for sa, sb in cases:
@@ -357,3 +361,19 @@ def test_matmul_f32_tensor_core_vs_oracle_and_mma(nxv, orc, monkeypatch, bmnk):
     assert np.all(np.abs(legacy - want) <= tol)
     from nx_vulkan_b200 import _native
     assert _native.load().nxv_synchronize() == 0  # no pipeline timeout recorded
+
+
+@pytest.mark.parametrize("cfg", ["16x4", "16x8", "16x16", "32x8", "32x16"])
+@pytest.mark.parametrize("bmnk", [(1, 130, 70, 257), (2, 256, 256, 100), (1, 33, 200, 17)])
+def test_matmul_f64_dmma_shapes(nxv, orc, monkeypatch, cfg, bmnk):
+    """Every DMMA configuration (k-tile x MMA K-shape) against the oracle."""
+    monkeypatch.setenv("NXV_DMMA", cfg)
+    batch, m, n, k = bmnk
+    r = np.random.default_rng(12)
+    a, b = r.normal(size=batch * m * k), r.normal(size=batch * k * n)
+    got = down(nxv, unwrap(nxv.matmul_batched(up(nxv, a), up(nxv, b), batch, m, n, k, "f64")), np.float64)
+    want = orc.matmul(a, b, m, n, k, batch=batch)
+    bound = np.concatenate([
+        (np.abs(a.reshape(batch, m, k)[q]) @ np.abs(b.reshape(batch, k, n)[q])).reshape(-1)
+        for q in range(batch)])
+    assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 2 * k * 2.2e-16 * bound)
