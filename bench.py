@@ -198,6 +198,8 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--suite", action="store_true",
                     help="measure every hot-path workload (one JSON line each) instead of the headline")
+    ap.add_argument("--only", default="fused,reduce,matmul,logreg",
+                    help="suite sections to run, comma separated: fused, reduce, matmul, logreg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -521,13 +523,15 @@ def suite(args):
 
     gen = torch.Generator(device="cpu").manual_seed(0)
 
+    want = set(args.only.split(","))
+
     # -- fused elementwise chain tanh(exp(x*y+z)-1.0), size sweep ---------------
     ops = (C.c_uint * 8)(1, 0, 100, 2, 106, 255, 255, 255)
     src = (C.c_uint * 8)(1, 2, 1, 0, 1, 1, 1, 1)
     imm = (C.c_double * 8)(0, 0, 0, 1.0, 0, 0, 0, 0)
     spv = nxv.shader_path("fused_elementwise_imm.spv")
     for dt, code, sizes in ((torch.float32, 0, (1 << 20, 1 << 24, 1 << 28)),
-                            (torch.float64, 1, (1 << 20, 1 << 24, 1 << 27))):
+                            (torch.float64, 1, (1 << 20, 1 << 24, 1 << 27))) if "fused" in want else ():
         es = 4 if code == 0 else 8
         for n in sizes:
             sets = max(1, min(16, (512 << 20) // (4 * n * es)))
@@ -554,7 +558,7 @@ def suite(args):
 
     # -- reductions + broadcast on [4096, 4096] ---------------------------------------
     R = 4096
-    for dt, code in ((torch.float32, 0), (torch.float64, 1)):
+    for dt, code in ((torch.float32, 0), (torch.float64, 1)) if "reduce" in want else ():
         es = 4 if code == 0 else 8
         x = torch.randn(R * R, generator=gen, dtype=torch.float64).to(dt).to(dev)
         bvec = torch.randn(R, generator=gen, dtype=torch.float64).to(dt).to(dev)
@@ -593,7 +597,7 @@ def suite(args):
     # -- dense matmul ---------------------------------------------------------------------
     N = 2048
     cub = {}
-    for dt, code in ((torch.float64, 1), (torch.float32, 0)):
+    for dt, code in ((torch.float64, 1), (torch.float32, 0)) if "matmul" in want else ():
         a = (torch.randn(N, N, generator=gen, dtype=torch.float64) / N ** 0.5).to(dt).to(dev)
         b = (torch.randn(N, N, generator=gen, dtype=torch.float64) / N ** 0.5).to(dt).to(dev)
         c = torch.empty(N, N, dtype=dt, device=dev)
@@ -611,36 +615,38 @@ def suite(args):
              kernel="DMMA mma.sync f64" if code == 1 else "3xTF32 tcgen05 (TMEM accumulator, TMA 128B-swizzled tiles)",
              ms=ms, tflops=flops / (ms / 1e3) / 1e12, cublas_ms=ms_cublas, cublas_tflops=cub[code],
              frac_of_cublas=ms_cublas / ms)
-    a = (torch.randn(64, 256, 256, generator=gen, dtype=torch.float64) / 16).to(dev)
-    b = (torch.randn(64, 256, 256, generator=gen, dtype=torch.float64) / 16).to(dev)
-    c = torch.empty(64, 256, 256, dtype=torch.float64, device=dev)
-    ha, hb2, hc = wrap(a), wrap(b), wrap(c)
-    ms = timed(lambda: ck(lib.nxv_matmul_batched(hc, ha, hb2, 64, 256, 256, 256, 1,
-                                                 nxv.shader_path("matmul_batched.spv"))), 10)
-    ms_cublas = timed(lambda: torch.bmm(a, b, out=c), 10)
-    flops = 64 * 2 * 256 ** 3
-    emit(workload="batched matmul 64 x 256^3", dtype="float64", ms=ms, tflops=flops / (ms / 1e3) / 1e12,
-         cublas_ms=ms_cublas, cublas_tflops=flops / (ms_cublas / 1e3) / 1e12, frac_of_cublas=ms_cublas / ms)
+    if "matmul" in want:
+        a = (torch.randn(64, 256, 256, generator=gen, dtype=torch.float64) / 16).to(dev)
+        b = (torch.randn(64, 256, 256, generator=gen, dtype=torch.float64) / 16).to(dev)
+        c = torch.empty(64, 256, 256, dtype=torch.float64, device=dev)
+        ha, hb2, hc = wrap(a), wrap(b), wrap(c)
+        ms = timed(lambda: ck(lib.nxv_matmul_batched(hc, ha, hb2, 64, 256, 256, 256, 1,
+                                                     nxv.shader_path("matmul_batched.spv"))), 10)
+        ms_cublas = timed(lambda: torch.bmm(a, b, out=c), 10)
+        flops = 64 * 2 * 256 ** 3
+        emit(workload="batched matmul 64 x 256^3", dtype="float64", ms=ms, tflops=flops / (ms / 1e3) / 1e12,
+             cublas_ms=ms_cublas, cublas_tflops=flops / (ms_cublas / 1e3) / 1e12, frac_of_cublas=ms_cublas / ms)
 
     # -- logistic-regression leapfrog -----------------------------------------------------------
-    Nobs, Dm, Cc, Lr = 10000, 100, 256, 16
-    r = np.random.default_rng(4)
-    X = r.normal(size=(Nobs, Dm))
-    w = r.normal(size=Dm)
-    y = (r.random(Nobs) < 1 / (1 + np.exp(-X @ w))).astype(np.float64)
-    tX, ty = torch.from_numpy(X).to(dev), torch.from_numpy(y).to(dev)
-    tq = torch.zeros(Cc, Dm, dtype=torch.float64, device=dev)
-    tp = torch.from_numpy(r.normal(size=(Cc, Dm))).to(dev)
-    outs = [torch.empty(Cc * Lr * Dm, dtype=torch.float64, device=dev) for _ in range(3)]
-    outs.append(torch.empty(Cc * Lr, dtype=torch.float64, device=dev))
-    hs = [wrap(t) for t in outs] + [wrap(tq), wrap(tp), wrap(tX), wrap(ty)]
-    lspv = nxv.shader_path("leapfrog_logreg_f64_batched.spv")
-    ms = timed(lambda: ck(lib.nxv_leapfrog_logreg_f64_batched(*hs, Nobs, Dm, Cc, Lr, 0.002, lspv)), 3)
-    flops = (Lr + 1) * 2 * 2 * Cc * Dm * Nobs
-    emit(workload="logistic-regression leapfrog, 256 chains, X[10000,100], L=16 (one trajectory)",
-         dtype="float64", ms_per_trajectory=ms, chain_steps_per_s=Cc * Lr / (ms / 1e3),
-         gemm_tflops=flops / (ms / 1e3) / 1e12, dgemm_cublas_tflops=cub.get(1),
-         seconds_for_1000_trajectories=ms)
+    if "logreg" in want:
+        Nobs, Dm, Cc, Lr = 10000, 100, 256, 16
+        r = np.random.default_rng(4)
+        X = r.normal(size=(Nobs, Dm))
+        w = r.normal(size=Dm)
+        y = (r.random(Nobs) < 1 / (1 + np.exp(-X @ w))).astype(np.float64)
+        tX, ty = torch.from_numpy(X).to(dev), torch.from_numpy(y).to(dev)
+        tq = torch.zeros(Cc, Dm, dtype=torch.float64, device=dev)
+        tp = torch.from_numpy(r.normal(size=(Cc, Dm))).to(dev)
+        outs = [torch.empty(Cc * Lr * Dm, dtype=torch.float64, device=dev) for _ in range(3)]
+        outs.append(torch.empty(Cc * Lr, dtype=torch.float64, device=dev))
+        hs = [wrap(t) for t in outs] + [wrap(tq), wrap(tp), wrap(tX), wrap(ty)]
+        lspv = nxv.shader_path("leapfrog_logreg_f64_batched.spv")
+        ms = timed(lambda: ck(lib.nxv_leapfrog_logreg_f64_batched(*hs, Nobs, Dm, Cc, Lr, 0.002, lspv)), 3)
+        flops = (Lr + 1) * 2 * 2 * Cc * Dm * Nobs
+        emit(workload="logistic-regression leapfrog, 256 chains, X[10000,100], L=16 (one trajectory)",
+             dtype="float64", ms_per_trajectory=ms, chain_steps_per_s=Cc * Lr / (ms / 1e3),
+             gemm_tflops=flops / (ms / 1e3) / 1e12, dgemm_cublas_tflops=cub.get(1),
+             seconds_for_1000_trajectories=ms)
     for h in handles:
         lib.nxv_buf_free(h)
     lib.nxv_set_stream(None)

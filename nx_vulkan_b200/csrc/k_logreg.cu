@@ -5,25 +5,286 @@
 //   z = X q,  r = y - sigmoid(z),  grad(q) = X^T r - q,
 //   logp(q) = sum_j [y_j z_j - softplus(z_j)] - 0.5 |q|^2,
 // batched over C chains: Z = Q . X^T (C x N_obs, K = D) and G = R . X - Q
-// (C x D, K = N_obs).  Both products run on the f64 DMMA GEMM; the second is
-// split along N_obs into S slices whose partials are folded in slice order
-// (deterministic).  The leapfrog update is fused into that fold.
-// Per step: drift (1 launch), GEMM Z, residual+softplus, GEMM G (split-K),
-// fold+kick+write (1 launch).  X^T is materialised once per call.
+// (C x D, K = N_obs).
+//
+// Fused path (D <= 104): one kernel per gradient.  CTA (s, b) owns chains
+// [128 b, 128 b + 128) and observations [L s, L s + L).  Its Q block stays in
+// shared memory; X streams through in tiles of 32 observations (cp.async,
+// double-buffered).  Per tile, each warp (16 chains) computes its 16 x 32
+// block of Z with DMMA (m16n8k4 f64), turns it into R = y - sigmoid(Z) and
+// the logp terms in registers, parks R in shared memory and accumulates its
+// 16 x D block of G += R . X_tile with DMMA.  Z never leaves the SM; each
+// CTA writes one G partial and one logp partial per chain.  A fold kernel
+// (one CTA per chain) sums the partials in slice order (deterministic),
+// subtracts q, completes the step (final half-kick, trajectory writes,
+// logp) and performs the next step's half-kick and drift.  Two launches
+// per leapfrog step; X is read from L2 (8 MB at the benchmark size).
+//
+// General path (D > 104): Z and G on the DMMA GEMM, G split along N_obs,
+// the same fold.
 #include "kernels.h"
 #include "ops_common.cuh"
 
 #include <math.h>
 
+#include <algorithm>
+#include <functional>
+
 namespace nxv {
 
 namespace {
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// D += A(16x4) . B(4x8), f64.  A register r: (row g + 8r, col tig);
+// B: (row tig, col g); D registers: (g, 2tig), (g, 2tig+1), (g+8, 2tig),
+// (g+8, 2tig+1), with g = lane / 4, tig = lane % 4.
+__device__ __forceinline__ void dmma4(double (&d)[4], double a0, double a1, double b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+        "{%0,%1,%2,%3};\n"
+        : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+        : "d"(a0), "d"(a1), "d"(b0));
+}
+
+// Residual and logp term of one observation: r = y - sigmoid(z),
+// t = y z - softplus(z), softplus(z) = max(z, 0) + log1p(exp(-|z|)).
+__device__ __forceinline__ double lr_resid(double z, double yj, double& t) {
+    double s = div_(1.0, add_(1.0, exp(-z)));
+    double sp = add_((z > 0.0 ? z : 0.0), log1p(exp(-fabs(z))));
+    t = sub_(mul_(yj, z), sp);
+    return sub_(yj, s);
+}
+
+// ---- fused gradient ---------------------------------------------------------------
+
+// DT: 8-wide tiles over the padded model dimension DP = 8 DT >= D.
+template <int DT> struct LrCfg {
+    static constexpr int NW = 8;          // warps; warp w owns chains [16w, 16w + 16)
+    static constexpr int BC = 16 * NW;    // chains per CTA
+    static constexpr int BN = 32;         // observations per X tile
+    static constexpr int DP = 8 * DT;
+    // Row strides (doubles) == 4 or 12 mod 16: every fragment load below hits
+    // 16 distinct 8-byte bank pairs per half-warp.
+    static constexpr int DS = DP + 4;
+    static constexpr int RS = BN + 4;
+    static constexpr int Q_OFF = 0;
+    static constexpr int X_OFF = BC * DS;
+    static constexpr int R_OFF = X_OFF + 2 * BN * DS;
+    static constexpr int Y_OFF = R_OFF + BC * RS;  // y tiles, 2 x BN
+    static constexpr int TOTAL = Y_OFF + 2 * BN;
+    static constexpr size_t BYTES = (size_t)TOTAL * 8;
+    static_assert(DS % 16 == 4 || DS % 16 == 12, "DS bank layout");
+    static_assert(RS % 16 == 4 || RS % 16 == 12, "RS bank layout");
+    static_assert((X_OFF * 8) % 16 == 0 && (DS * 8) % 16 == 0, "cp.async alignment");
+};
+
+// part[s][c][d] = sum over j in slice s of R[c][j] X[j][d];
+// lpart[c][s] = sum over j in slice s of (y_j z_cj - softplus(z_cj)).
+// vecX: X rows are 16-byte aligned (D even, X aligned) and use cp.async.
+template <int DT>
+__global__ void __launch_bounds__(256, 1)
+k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
+          const double* __restrict__ y, double* __restrict__ part, double* __restrict__ lpart,
+          unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S, int vecX) {
+    using G = LrCfg<DT>;
+    constexpr int BN = G::BN, DS = G::DS, RS = G::RS, DP = G::DP;
+    constexpr int NZ = BN / 8;  // 8-observation tiles of Z per warp
+    extern __shared__ __align__(16) double lr_smem[];
+    double* Qs = lr_smem + G::Q_OFF;
+    double* Xs = lr_smem + G::X_OFF;
+    double* Rs = lr_smem + G::R_OFF;
+    double* Ys = lr_smem + G::Y_OFF;
+    const unsigned s = blockIdx.x;
+    const unsigned c0 = blockIdx.y * G::BC;
+    const unsigned j0 = s * L;
+    const unsigned j1 = min(n_obs, j0 + L);
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
+
+    // Both X buffers start as zeros: the padded columns [D, DP) stay zero and
+    // rows past a partial tile hold finite values (R is zero there).
+    for (int i = tid; i < 2 * BN * DS; i += 256) Xs[i] = 0.0;
+    for (int i = tid; i < G::BC * DS; i += 256) {
+        const int r = i / DS, col = i - r * DS;
+        const unsigned c = c0 + r;
+        Qs[i] = (c < C && col < (int)D) ? q[(size_t)c * D + col] : 0.0;
+    }
+    __syncthreads();
+
+    const unsigned ntile = (j1 - j0 + BN - 1) / BN;
+    const unsigned hd = D >> 1;  // 16-byte chunks per row on the vector path
+    auto load_x = [&](unsigned t, int buf) {
+        const unsigned jt = j0 + t * BN;
+        const unsigned rows = min((unsigned)BN, j1 - jt);
+        double* dst = Xs + buf * BN * DS;
+        const double* src = X + (size_t)jt * D;
+        if (tid < (int)rows) cp_async8(Ys + buf * BN + tid, y + jt + tid);
+        if (vecX) {
+            const unsigned total = rows * hd;
+            for (unsigned ch = tid; ch < total; ch += 256) {
+                const unsigned r = ch / hd, cc = (ch - r * hd) * 2;
+                cp_async16(dst + r * DS + cc, src + (size_t)r * D + cc);
+            }
+        } else {
+            const unsigned total = rows * D;
+            for (unsigned i = tid; i < total; i += 256) {
+                const unsigned r = i / D, col = i - r * D;
+                dst[r * DS + col] = src[i];
+            }
+        }
+    };
+
+    double gacc[DT][4];
+#pragma unroll
+    for (int t = 0; t < DT; t++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) gacc[t][e] = 0.0;
+    // logp of rows g and g + 8: sum of y z - max(z, 0), running product of
+    // den and the sum of its flushed logs
+    double lsum[2] = {0.0, 0.0}, lprod[2] = {1.0, 1.0}, llog[2] = {0.0, 0.0};
+    const double* qa = Qs + (warp * 16 + g) * DS + tig;
+    double* rw = Rs + warp * 16 * RS;
+
+    load_x(0, 0);
+    cp_commit();
+    for (unsigned t = 0; t < ntile; t++) {
+        if (t + 1 < ntile) load_x(t + 1, (t + 1) & 1);
+        cp_commit();
+        cp_wait<1>();
+        __syncthreads();
+        const double* xb = Xs + (t & 1) * BN * DS;
+        const unsigned jt = j0 + t * BN;
+        const unsigned valid = min((unsigned)BN, j1 - jt);
+        const unsigned ntz = (valid + 7) >> 3;  // 8-observation tiles holding data
+
+        // Z block (16 chains x 32 observations) = Q . X_tile^T over DP.
+        double z[NZ][4];
+#pragma unroll
+        for (int n = 0; n < NZ; n++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) z[n][e] = 0.0;
+#pragma unroll
+        for (int kk = 0; kk < DP; kk += 4) {
+            const double a0 = qa[kk], a1 = qa[kk + 8 * DS];
+#pragma unroll
+            for (int n = 0; n < NZ; n++)
+                if (n < (int)ntz) dmma4(z[n], a0, a1, xb[(n * 8 + g) * DS + kk + tig]);
+        }
+
+        // R = y - sigmoid(Z) into this warp's rows of Rs (zero past the slice),
+        // with e = exp(-|z|), den = 1 + e in [1, 2], sigmoid(z) = (z >= 0 ? 1 : e)
+        // / den.  The 8 reciprocals of a row come from one division (batch
+        // inversion: prefix products, one reciprocal, back-substitution).  The
+        // logp term y z - softplus(z) = y z - max(z, 0) - log(den): the first
+        // part is summed, den enters a running product whose log is taken
+        // once per 64 tiles.
+        const double* yb = Ys + (t & 1) * BN;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            double ev[2 * NZ], dn[2 * NZ], pf[2 * NZ], rc[2 * NZ];
+#pragma unroll
+            for (int n = 0; n < NZ; n++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int i = 2 * n + e;
+                    const bool ok = (unsigned)(n * 8 + 2 * tig + e) < valid;
+                    ev[i] = ok ? exp(-fabs(z[n][2 * h + e])) : 0.0;
+                    dn[i] = add_(1.0, ev[i]);
+                }
+            pf[0] = dn[0];
+#pragma unroll
+            for (int i = 1; i < 2 * NZ; i++) pf[i] = mul_(pf[i - 1], dn[i]);
+            double inv = div_(1.0, pf[2 * NZ - 1]);
+#pragma unroll
+            for (int i = 2 * NZ - 1; i > 0; i--) {
+                rc[i] = mul_(inv, pf[i - 1]);
+                inv = mul_(inv, dn[i]);
+            }
+            rc[0] = inv;
+            lprod[h] = mul_(lprod[h], pf[2 * NZ - 1]);
+#pragma unroll
+            for (int n = 0; n < NZ; n++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int i = 2 * n + e;
+                    const unsigned col = n * 8 + 2 * tig + e;
+                    double r = 0.0;
+                    if (col < valid) {
+                        const double zz = z[n][2 * h + e], yj = yb[col];
+                        r = sub_(yj, mul_(zz >= 0.0 ? 1.0 : ev[i], rc[i]));
+                        lsum[h] = add_(lsum[h], sub_(mul_(yj, zz), zz > 0.0 ? zz : 0.0));
+                    }
+                    rw[(g + 8 * h) * RS + col] = r;
+                }
+            if ((t & 63) == 63) {
+                llog[h] = add_(llog[h], log(lprod[h]));
+                lprod[h] = 1.0;
+            }
+        }
+        __syncwarp();
+
+        // G block (16 chains x DP) += R . X_tile over the tile's observations.
+        const int kv = (int)((valid + 3) >> 2) << 2;
+#pragma unroll
+        for (int kk = 0; kk < BN; kk += 4) {
+            if (kk < kv) {
+                const double a0 = rw[g * RS + kk + tig], a1 = rw[(g + 8) * RS + kk + tig];
+                const double* xr = xb + (kk + tig) * DS + g;
+#pragma unroll
+                for (int n = 0; n < DT; n++) dmma4(gacc[n], a0, a1, xr[n * 8]);
+            }
+        }
+        __syncthreads();  // buffer t & 1 and Rs are rewritten next iteration
+    }
+    cp_wait<0>();
+
+    // Partials out.
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const unsigned c = c0 + warp * 16 + g + 8 * h;
+        if (c >= C) continue;
+        double* dst = part + ((size_t)s * C + c) * D;
+#pragma unroll
+        for (int n = 0; n < DT; n++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const unsigned d = n * 8 + 2 * tig + e;
+                if (d < D) dst[d] = gacc[n][2 * h + e];
+            }
+    }
+    // logp partial per chain: sum over the four lanes of a row (tig), a fixed
+    // pairing so the result is identical on every lane.
+    double lp0 = sub_(lsum[0], add_(llog[0], log(lprod[0])));
+    double lp1 = sub_(lsum[1], add_(llog[1], log(lprod[1])));
+    lp0 = add_(lp0, __shfl_xor_sync(0xffffffffu, lp0, 1));
+    lp0 = add_(lp0, __shfl_xor_sync(0xffffffffu, lp0, 2));
+    lp1 = add_(lp1, __shfl_xor_sync(0xffffffffu, lp1, 1));
+    lp1 = add_(lp1, __shfl_xor_sync(0xffffffffu, lp1, 2));
+    if (tig == 0) {
+        const unsigned ca = c0 + warp * 16 + g, cb = ca + 8;
+        if (ca < C) lpart[(size_t)ca * S + s] = lp0;
+        if (cb < C) lpart[(size_t)cb * S + s] = lp1;
+    }
+}
+
+// ---- general path: residual over Z from the GEMM -------------------------------------
 
 constexpr int kRT = 256;  // residual kernel threads
 constexpr int kRE = 4;    // observations per residual thread
 
 // R = y - sigmoid(Z) in place; lpart[c][blk] = sum over the block's j of
-// y z - softplus(z), softplus(z) = max(z, 0) + log1p(exp(-|z|)).
+// y z - softplus(z).
 __global__ void __launch_bounds__(kRT)
 k_lr_resid(double* __restrict__ Z, const double* __restrict__ y, size_t n_obs, double* lpart,
            unsigned nblk) {
@@ -35,12 +296,9 @@ k_lr_resid(double* __restrict__ Z, const double* __restrict__ y, size_t n_obs, d
     for (int e = 0; e < kRE; e++) {
         size_t j = base + (size_t)e * kRT + threadIdx.x;
         if (j < n_obs) {
-            double z = zr[j];
-            double yj = y[j];
-            double s = div_(1.0, add_(1.0, exp(-z)));
-            zr[j] = sub_(yj, s);
-            double sp = add_((z > 0.0 ? z : 0.0), log1p(exp(-fabs(z))));
-            t = add_(t, sub_(mul_(yj, z), sp));
+            double te;
+            zr[j] = lr_resid(zr[j], y[j], te);
+            t = add_(t, te);
         }
     }
     __shared__ double sm[kRT / 32];
@@ -55,44 +313,82 @@ k_lr_resid(double* __restrict__ Z, const double* __restrict__ y, size_t n_obs, d
     }
 }
 
-// p_h = p + he*g; q = q + eps*p_h; p = p_h   (inv_mass = 1)
-__global__ void k_lr_drift(double* __restrict__ q, double* __restrict__ p,
-                           const double* __restrict__ g, size_t total, double eps, double he) {
-    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= total) return;
-    double ph = add_(p[i], mul_(he, g[i]));
-    q[i] = add_(q[i], mul_(eps, ph));
-    p[i] = ph;
+// ---- fold + leapfrog update ----------------------------------------------------------
+
+constexpr int kFT = 512;  // fold threads per chain
+
+// In-order sum of a[t * stride] for t in [t0, t1), t1 > t0, with 8 loads in
+// flight (the partials come from L2; a dependent chain of loads would leave
+// the fold latency-bound).
+__device__ __forceinline__ double sum_rows(const double* __restrict__ a, size_t stride, int t0,
+                                           int t1) {
+    double s = a[(size_t)t0 * stride];
+    int t = t0 + 1;
+    for (; t + 8 <= t1; t += 8) {
+        double v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = a[(size_t)(t + u) * stride];
+#pragma unroll
+        for (int u = 0; u < 8; u++) s = add_(s, v[u]);
+    }
+    for (; t < t1; t++) s = add_(s, a[(size_t)t * stride]);
+    return s;
 }
 
-// One CTA per chain: g = sum_s part[s] - q; then (step) p = p + he*g and
-// write q/p/g rows of step k and logp[c][k] = sum lpart - 0.5 |q|^2.
-__global__ void __launch_bounds__(128)
-k_lr_fold(const double* __restrict__ part, int S, size_t CD, double* __restrict__ q,
-          double* __restrict__ p, double* __restrict__ g, const double* __restrict__ lpart,
-          unsigned nblk, size_t D, double he, int write_step, unsigned k, unsigned K,
-          double* qc, double* pc, double* gc, double* logp) {
+// One CTA per chain: g = sum_s part[s] - q.  With H > 1 the S slices are cut
+// into H contiguous groups, thread (h, i) sums group h of element i in slice
+// order and the H group sums are added in group order (a fixed order, so the
+// result is deterministic).  With write_step: p = p + he*g, rows of step k
+// written to the trajectories and logp[c][k] = sum lpart - 0.5 |q|^2.  With
+// drift: the next step's half-kick and drift, p_h = p + he*g;
+// q = q + eps*p_h; p = p_h  (inverse mass 1).
+__global__ void __launch_bounds__(kFT)
+k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __restrict__ q,
+          double* __restrict__ p, const double* __restrict__ lpart, unsigned nblk, size_t D,
+          double eps, double he, int write_step, int drift, unsigned k, unsigned K, double* qc,
+          double* pc, double* gc, double* logp) {
+    extern __shared__ double fold_sm[];  // [H][D] group sums when H > 1
     const unsigned c = blockIdx.x;
+    const double* pc0 = part + (size_t)c * D;
+    if (H > 1) {
+        const unsigned tid = threadIdx.x;
+        if (tid < (unsigned)H * D) {
+            const unsigned h = tid / (unsigned)D, i = tid - h * (unsigned)D;
+            const int t0 = (int)((size_t)h * S / H), t1 = (int)((size_t)(h + 1) * S / H);
+            fold_sm[tid] = sum_rows(pc0 + i, CD, t0, t1);
+        }
+        __syncthreads();
+    }
     double qq = 0.0;
     for (size_t i = threadIdx.x; i < D; i += blockDim.x) {
-        size_t o = (size_t)c * D + i;
-        double s = part[o];
-        for (int t = 1; t < S; t++) s = add_(s, part[(size_t)t * CD + o]);
+        const size_t o = (size_t)c * D + i;
+        double s;
+        if (H > 1) {
+            s = fold_sm[i];
+            for (int h = 1; h < H; h++) s = add_(s, fold_sm[(size_t)h * D + i]);
+        } else {
+            s = sum_rows(pc0 + i, CD, 0, S);
+        }
         double qi = q[o];
         double gi = sub_(s, qi);
-        g[o] = gi;
         qq = add_(qq, mul_(qi, qi));
+        double pi = p[o];
         if (write_step) {
-            double pi = add_(p[o], mul_(he, gi));
-            p[o] = pi;
+            pi = add_(pi, mul_(he, gi));
             size_t row = ((size_t)c * K + k) * D + i;
             qc[row] = qi;
             pc[row] = pi;
             gc[row] = gi;
         }
+        if (drift) {
+            double ph = add_(pi, mul_(he, gi));
+            q[o] = add_(qi, mul_(eps, ph));
+            pi = ph;
+        }
+        p[o] = pi;
     }
     if (!write_step) return;
-    __shared__ double sm[4];
+    __shared__ double sm[kFT / 32];
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) qq = add_(qq, __shfl_down_sync(0xffffffffu, qq, off));
     if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = qq;
@@ -100,10 +396,23 @@ k_lr_fold(const double* __restrict__ part, int S, size_t CD, double* __restrict_
     if (threadIdx.x == 0) {
         double sq = sm[0];
         for (int w = 1; w < (int)(blockDim.x >> 5); w++) sq = add_(sq, sm[w]);
-        double l = lpart[(size_t)c * nblk];
-        for (unsigned b = 1; b < nblk; b++) l = add_(l, lpart[(size_t)c * nblk + b]);
+        const double l = sum_rows(lpart + (size_t)c * nblk, 1, 0, (int)nblk);
         logp[(size_t)c * K + k] = sub_(l, mul_(0.5, sq));
     }
+}
+
+template <int DT>
+int launch_lr_grad(Ctx& c, const double* q, const double* X, const double* y, double* part,
+                   double* lpart, unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S,
+                   int vecX) {
+    const size_t smem = LrCfg<DT>::BYTES;
+    cudaError_t e = cudaFuncSetAttribute(k_lr_grad<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_lr_grad)");
+    dim3 grid(S, (C + LrCfg<DT>::BC - 1) / LrCfg<DT>::BC);
+    k_lr_grad<DT><<<grid, 256, smem, c.stream>>>(q, X, y, part, lpart, C, D, n_obs, L, S, vecX);
+    count_launch();
+    return OK;
 }
 
 }  // namespace
@@ -121,72 +430,97 @@ int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, co
         return E_ARG;
     }
     const size_t CD = C * D;
-    // split-K slices for G = R . X: enough CTAs to cover the SMs.
-    const size_t ctas_mn = ((C + 127) / 128) * ((D + 127) / 128);
-    size_t S = (2 * (size_t)c.dev->sm_count + ctas_mn - 1) / ctas_mn;
-    size_t L = (n_obs + S - 1) / S;
-    L = (L + 15) & ~(size_t)15;  // keep slice starts 16-byte aligned, BK multiple
-    S = (n_obs + L - 1) / L;
-    const unsigned nblk = (unsigned)((n_obs + kRT * kRE - 1) / (kRT * kRE));
-    // scratch: Xt [D][N] | q | p | g [C][D] | Z [C][N] | lpart [C][nblk] | part [S][C][D]
+    const bool fused = D <= 104;
+    const double he = 0.5 * eps;
+    size_t S, L;
+    unsigned nblk;
+    if (fused) {
+        // Slices: enough CTAs to cover the SMs once; L a multiple of 8.
+        const size_t cblk = (C + 127) / 128;
+        S = ((size_t)c.dev->sm_count + cblk - 1) / cblk;
+        L = ((n_obs + S - 1) / S + 7) & ~(size_t)7;
+        S = (n_obs + L - 1) / L;
+        nblk = (unsigned)S;
+    } else {
+        // split-K slices for G = R . X: enough CTAs to cover the SMs.
+        const size_t ctas_mn = ((C + 127) / 128) * ((D + 127) / 128);
+        S = (2 * (size_t)c.dev->sm_count + ctas_mn - 1) / ctas_mn;
+        L = (n_obs + S - 1) / S;
+        L = (L + 15) & ~(size_t)15;  // keep slice starts 16-byte aligned, BK multiple
+        S = (n_obs + L - 1) / L;
+        nblk = (unsigned)((n_obs + kRT * kRE - 1) / (kRT * kRE));
+    }
+    // scratch: q | p [C][D] | lpart [C][nblk] | part [S][C][D] | (general) Xt [D][N], Z [C][N]
     size_t off = 0;
     auto take = [&](size_t bytes) {
         size_t o = off;
         off += (bytes + 255) & ~(size_t)255;
         return o;
     };
-    size_t oXt = take(D * n_obs * 8), oq = take(CD * 8), op = take(CD * 8), og = take(CD * 8),
-           oZ = take(C * n_obs * 8), oL = take(C * nblk * 8), oP = take(S * CD * 8);
+    size_t oq = take(CD * 8), op = take(CD * 8), oL = take(C * nblk * 8), oP = take(S * CD * 8);
+    size_t oXt = fused ? 0 : take(D * n_obs * 8), oZ = fused ? 0 : take(C * n_obs * 8);
     ScratchGuard guard(c);
     char* base = (char*)scratch(c, off);
     if (!base) return E_CUDA;
-    double* Xt = (double*)(base + oXt);
     double* q = (double*)(base + oq);
     double* p = (double*)(base + op);
-    double* g = (double*)(base + og);
-    double* Z = (double*)(base + oZ);
     double* lp = (double*)(base + oL);
     double* part = (double*)(base + oP);
-
-    int rc = enqueue_transpose(c, F64, Xt, X, (unsigned)n_obs, (unsigned)D);
-    if (rc) return rc;
     NXV_CK(cudaMemcpyAsync(q, q0, CD * 8, cudaMemcpyDeviceToDevice, c.stream));
     NXV_CK(cudaMemcpyAsync(p, p0, CD * 8, cudaMemcpyDeviceToDevice, c.stream));
 
-    GemmP<double> G1{};  // Z = Q . Xt
-    G1.A = q; G1.B = Xt; G1.C = Z;
-    G1.M = (int)C; G1.N = (int)n_obs; G1.K = (int)D;
-    G1.lda = (int)D; G1.ldb = (int)n_obs; G1.ldc = (int)n_obs;
-    G1.batch = 1;
-    GemmP<double> G2{};  // part[s] = R[:, slice s] . X[slice s, :]
-    G2.A = Z; G2.B = (const double*)X; G2.C = part;
-    G2.M = (int)C; G2.N = (int)D; G2.K = (int)n_obs;
-    G2.lda = (int)n_obs; G2.ldb = (int)D; G2.ldc = (int)D;
-    G2.sC = (long long)CD; G2.ksplit = (int)L; G2.batch = (int)S;
-
-    const double he = 0.5 * eps;
-    auto gradient = [&](int write_step, unsigned k) -> int {
-        int r = gemm_f64(c, G1);
-        if (r) return r;
-        dim3 rg(nblk, (unsigned)C);
-        k_lr_resid<<<rg, kRT, 0, c.stream>>>(Z, (const double*)y, n_obs, lp, nblk);
-        count_launch();
-        r = gemm_f64(c, G2);
-        if (r) return r;
-        k_lr_fold<<<(unsigned)C, 128, 0, c.stream>>>(part, (int)S, CD, q, p, g, lp, nblk, D, he,
-                                                      write_step, k, K, (double*)qc, (double*)pc,
-                                                      (double*)gc, (double*)logp);
-        count_launch();
-        return OK;
-    };
-    rc = gradient(0, 0);
-    if (rc) return rc;
-    for (unsigned k = 0; k < K; k++) {
-        unsigned blocks = (unsigned)((CD + 255) / 256);
-        k_lr_drift<<<blocks, 256, 0, c.stream>>>(q, p, g, CD, eps, he);
-        count_launch();
-        rc = gradient(1, k);
+    std::function<int()> grad;
+    GemmP<double> G1{}, G2{};
+    if (fused) {
+        const int vecX = (D % 2 == 0) && ((uintptr_t)X % 16 == 0);
+        const unsigned Cu = (unsigned)C, Du = (unsigned)D, Nu = (unsigned)n_obs,
+                       Lu = (unsigned)L, Su = (unsigned)S;
+        const double* Xd = (const double*)X;
+        const double* yd = (const double*)y;
+        grad = [=, &c]() -> int {
+            if (D <= 32) return launch_lr_grad<4>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+            if (D <= 64) return launch_lr_grad<8>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+            return launch_lr_grad<13>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+        };
+    } else {
+        double* Xt = (double*)(base + oXt);
+        double* Z = (double*)(base + oZ);
+        int rc = enqueue_transpose(c, F64, Xt, X, (unsigned)n_obs, (unsigned)D);
         if (rc) return rc;
+        G1.A = q; G1.B = Xt; G1.C = Z;  // Z = Q . Xt
+        G1.M = (int)C; G1.N = (int)n_obs; G1.K = (int)D;
+        G1.lda = (int)D; G1.ldb = (int)n_obs; G1.ldc = (int)n_obs;
+        G1.batch = 1;
+        G2.A = Z; G2.B = (const double*)X; G2.C = part;  // part[s] = R[:, s] . X[s, :]
+        G2.M = (int)C; G2.N = (int)D; G2.K = (int)n_obs;
+        G2.lda = (int)n_obs; G2.ldb = (int)D; G2.ldc = (int)D;
+        G2.sC = (long long)CD; G2.ksplit = (int)L; G2.batch = (int)S;
+        grad = [&, Z, nblk]() -> int {
+            int r = gemm_f64(c, G1);
+            if (r) return r;
+            dim3 rg(nblk, (unsigned)C);
+            k_lr_resid<<<rg, kRT, 0, c.stream>>>(Z, (const double*)y, n_obs, lp, nblk);
+            count_launch();
+            return gemm_f64(c, G2);
+        };
+    }
+    // slice groups of the fold: as many as fit kFT threads, at most S
+    const int H = (D <= (size_t)kFT / 2) ? (int)std::min<size_t>(S, kFT / D) : 1;
+    const size_t fold_smem = H > 1 ? (size_t)H * D * 8 : 0;
+    auto fold = [&](int write_step, int drift, unsigned k) {
+        k_lr_fold<<<(unsigned)C, kFT, fold_smem, c.stream>>>(
+            part, (int)S, H, CD, q, p, lp, nblk, D, eps, he, write_step, drift, k, K, (double*)qc,
+            (double*)pc, (double*)gc, (double*)logp);
+        count_launch();
+    };
+    // gradient at q0, then step 0's half-kick and drift
+    int rc = grad();
+    if (rc) return rc;
+    fold(0, 1, 0);
+    for (unsigned k = 0; k < K; k++) {
+        rc = grad();
+        if (rc) return rc;
+        fold(1, k + 1 < K, k);
     }
     return finish(c);
 }

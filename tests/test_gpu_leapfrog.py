@@ -175,7 +175,14 @@ def test_gauss_full_config(nxv, orc):
     assert np.max(np.abs(h1 - h0) / h0) < 1e-3
 
 
-@pytest.mark.parametrize("N,D,C,K", [(50, 3, 2, 2), (1000, 20, 5, 4), (10000, 100, 16, 3)])
+@pytest.mark.parametrize("N,D,C,K", [
+    (50, 3, 2, 2), (1000, 20, 5, 4), (10000, 100, 16, 3),
+    # two chain blocks with a partial one; the benchmark's X shape and chain count
+    (10000, 100, 256, 2), (997, 7, 130, 3),
+    # fewer observations than one tile, model dims at each tile-width boundary
+    (5, 2, 1, 1), (333, 32, 3, 2), (333, 33, 3, 2), (777, 64, 9, 2), (777, 104, 9, 2),
+    # general (two-GEMM) path
+    (300, 120, 4, 2)])
 def test_logreg_vs_oracle(nxv, orc, N, D, C, K):
     r = np.random.default_rng(4)
     X = r.normal(size=(N, D))
