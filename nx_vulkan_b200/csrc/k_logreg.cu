@@ -69,10 +69,13 @@ __device__ __forceinline__ double lr_resid(double z, double yj, double& t) {
 // ---- fused gradient ---------------------------------------------------------------
 
 // DT: 8-wide tiles over the padded model dimension DP = 8 DT >= D.
-template <int DT> struct LrCfg {
-    static constexpr int NW = 8;          // warps; warp w owns chains [16w, 16w + 16)
+// NW: warps per CTA, warp w owns chains [16w, 16w + 16).  BN: observations
+// per X tile.
+template <int DT, int NW_, int BN_> struct LrCfg {
+    static constexpr int NW = NW_;
+    static constexpr int NT = 32 * NW;    // threads
     static constexpr int BC = 16 * NW;    // chains per CTA
-    static constexpr int BN = 32;         // observations per X tile
+    static constexpr int BN = BN_;
     static constexpr int DP = 8 * DT;
     // Row strides (doubles) == 4 or 12 mod 16: every fragment load below hits
     // 16 distinct 8-byte bank pairs per half-warp.
@@ -89,16 +92,48 @@ template <int DT> struct LrCfg {
     static_assert((X_OFF * 8) % 16 == 0 && (DS * 8) % 16 == 0, "cp.async alignment");
 };
 
+// Z block of one warp: z[n] (16 x 8) += Q rows . X_tile rows n*8 .. n*8+7 over
+// k in [0, DP).  qa: this lane's A element (row g, col tig); xb: this lane's B
+// element (tile row g, col tig).  FULL: all NZ observation groups hold data
+// (no per-MMA guard); otherwise only the first ntz.
+template <int NZ, int DP, int DS, bool FULL>
+__device__ __forceinline__ void z_block(double (&z)[NZ][4], const double* qa, const double* xb,
+                                        unsigned ntz) {
+#pragma unroll
+    for (int kk = 0; kk < DP; kk += 4) {
+        const double a0 = qa[kk], a1 = qa[kk + 8 * DS];
+#pragma unroll
+        for (int n = 0; n < NZ; n++)
+            if (FULL || n < (int)ntz) dmma4(z[n], a0, a1, xb[n * 8 * DS + kk]);
+    }
+}
+
+// G block of one warp: gacc[n] (16 x 8) += R rows . X_tile columns n*8 ..
+// n*8+7 over the tile's observations k in [0, kv).  rw: this lane's A element
+// (row g, col tig); xr: this lane's B element (tile row tig, col g).
+template <int DT, int BN, int DS, int RS, bool FULL>
+__device__ __forceinline__ void g_block(double (&gacc)[DT][4], const double* rw, const double* xr,
+                                        int kv) {
+#pragma unroll
+    for (int kk = 0; kk < BN; kk += 4) {
+        if (FULL || kk < kv) {
+            const double a0 = rw[kk], a1 = rw[8 * RS + kk];
+#pragma unroll
+            for (int n = 0; n < DT; n++) dmma4(gacc[n], a0, a1, xr[kk * DS + n * 8]);
+        }
+    }
+}
+
 // part[s][c][d] = sum over j in slice s of R[c][j] X[j][d];
 // lpart[c][s] = sum over j in slice s of (y_j z_cj - softplus(z_cj)).
 // vecX: X rows are 16-byte aligned (D even, X aligned) and use cp.async.
-template <int DT>
-__global__ void __launch_bounds__(256, 1)
+template <int DT, int NW, int BN_>
+__global__ void __launch_bounds__(32 * NW, 8 / NW)
 k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
           const double* __restrict__ y, double* __restrict__ part, double* __restrict__ lpart,
           unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S, int vecX) {
-    using G = LrCfg<DT>;
-    constexpr int BN = G::BN, DS = G::DS, RS = G::RS, DP = G::DP;
+    using G = LrCfg<DT, NW, BN_>;
+    constexpr int BN = G::BN, DS = G::DS, RS = G::RS, DP = G::DP, NT = G::NT;
     constexpr int NZ = BN / 8;  // 8-observation tiles of Z per warp
     extern __shared__ __align__(16) double lr_smem[];
     double* Qs = lr_smem + G::Q_OFF;
@@ -114,16 +149,30 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
 
     // Both X buffers start as zeros: the padded columns [D, DP) stay zero and
     // rows past a partial tile hold finite values (R is zero there).
-    for (int i = tid; i < 2 * BN * DS; i += 256) Xs[i] = 0.0;
-    for (int i = tid; i < G::BC * DS; i += 256) {
+    for (int i = tid; i < 2 * BN * DS; i += NT) Xs[i] = 0.0;
+    // Q block: zeros outside [c0, C) x [0, D); the rest by cp.async (with the
+    // first X tile) when rows are 16-byte aligned, else by plain loads.
+    const bool vq = (D & 1) == 0;
+    const unsigned hd = D >> 1;  // 16-byte chunks per row on the vector paths
+    const unsigned crows = min((unsigned)G::BC, C - c0);
+    for (int i = tid; i < G::BC * DS; i += NT) {
         const int r = i / DS, col = i - r * DS;
-        const unsigned c = c0 + r;
-        Qs[i] = (c < C && col < (int)D) ? q[(size_t)c * D + col] : 0.0;
+        if ((unsigned)r < crows && col < (int)D) {
+            if (!vq) Qs[i] = q[(size_t)(c0 + r) * D + col];
+        } else {
+            Qs[i] = 0.0;
+        }
     }
     __syncthreads();
+    if (vq) {
+        const unsigned total = crows * hd;
+        for (unsigned ch = tid; ch < total; ch += NT) {
+            const unsigned r = ch / hd, cc = (ch - r * hd) * 2;
+            cp_async16(Qs + r * DS + cc, q + (size_t)(c0 + r) * D + cc);
+        }
+    }
 
     const unsigned ntile = (j1 - j0 + BN - 1) / BN;
-    const unsigned hd = D >> 1;  // 16-byte chunks per row on the vector path
     auto load_x = [&](unsigned t, int buf) {
         const unsigned jt = j0 + t * BN;
         const unsigned rows = min((unsigned)BN, j1 - jt);
@@ -132,13 +181,13 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
         if (tid < (int)rows) cp_async8(Ys + buf * BN + tid, y + jt + tid);
         if (vecX) {
             const unsigned total = rows * hd;
-            for (unsigned ch = tid; ch < total; ch += 256) {
+            for (unsigned ch = tid; ch < total; ch += NT) {
                 const unsigned r = ch / hd, cc = (ch - r * hd) * 2;
                 cp_async16(dst + r * DS + cc, src + (size_t)r * D + cc);
             }
         } else {
             const unsigned total = rows * D;
-            for (unsigned i = tid; i < total; i += 256) {
+            for (unsigned i = tid; i < total; i += NT) {
                 const unsigned r = i / D, col = i - r * D;
                 dst[r * DS + col] = src[i];
             }
@@ -174,13 +223,10 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
         for (int n = 0; n < NZ; n++)
 #pragma unroll
             for (int e = 0; e < 4; e++) z[n][e] = 0.0;
-#pragma unroll
-        for (int kk = 0; kk < DP; kk += 4) {
-            const double a0 = qa[kk], a1 = qa[kk + 8 * DS];
-#pragma unroll
-            for (int n = 0; n < NZ; n++)
-                if (n < (int)ntz) dmma4(z[n], a0, a1, xb[(n * 8 + g) * DS + kk + tig]);
-        }
+        if (ntz == NZ)
+            z_block<NZ, DP, DS, true>(z, qa, xb + g * DS + tig, ntz);
+        else
+            z_block<NZ, DP, DS, false>(z, qa, xb + g * DS + tig, ntz);
 
         // R = y - sigmoid(Z) into this warp's rows of Rs (zero past the slice),
         // with e = exp(-|z|), den = 1 + e in [1, 2], sigmoid(z) = (z >= 0 ? 1 : e)
@@ -236,32 +282,46 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
 
         // G block (16 chains x DP) += R . X_tile over the tile's observations.
         const int kv = (int)((valid + 3) >> 2) << 2;
-#pragma unroll
-        for (int kk = 0; kk < BN; kk += 4) {
-            if (kk < kv) {
-                const double a0 = rw[g * RS + kk + tig], a1 = rw[(g + 8) * RS + kk + tig];
-                const double* xr = xb + (kk + tig) * DS + g;
-#pragma unroll
-                for (int n = 0; n < DT; n++) dmma4(gacc[n], a0, a1, xr[n * 8]);
-            }
-        }
+        if (kv == BN)
+            g_block<DT, BN, DS, RS, true>(gacc, rw + g * RS + tig, xb + tig * DS + g, kv);
+        else
+            g_block<DT, BN, DS, RS, false>(gacc, rw + g * RS + tig, xb + tig * DS + g, kv);
         __syncthreads();  // buffer t & 1 and Rs are rewritten next iteration
     }
     cp_wait<0>();
 
-    // Partials out.
+    // Partials out: the G block goes through shared memory (the Q block's
+    // space, free after the last tile's barrier) as a dense [crows][D] array,
+    // which is also the layout of part[s][c0 .. c0 + crows) -- one contiguous
+    // range written with coalesced 16-byte stores.
+    double* Gs = Qs;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        const unsigned c = c0 + warp * 16 + g + 8 * h;
-        if (c >= C) continue;
-        double* dst = part + ((size_t)s * C + c) * D;
+        const int row = warp * 16 + g + 8 * h;
 #pragma unroll
-        for (int n = 0; n < DT; n++)
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const unsigned d = n * 8 + 2 * tig + e;
-                if (d < D) dst[d] = gacc[n][2 * h + e];
+        for (int n = 0; n < DT; n++) {
+            const unsigned d = n * 8 + 2 * tig;
+            if (vq) {
+                if (d < D)
+                    *reinterpret_cast<double2*>(Gs + row * D + d) =
+                        make_double2(gacc[n][2 * h], gacc[n][2 * h + 1]);
+            } else {
+                if (d < D) Gs[row * D + d] = gacc[n][2 * h];
+                if (d + 1 < D) Gs[row * D + d + 1] = gacc[n][2 * h + 1];
             }
+        }
+    }
+    __syncthreads();
+    {
+        double* dst = part + ((size_t)s * C + c0) * D;
+        if (vq) {
+            const unsigned total = crows * hd;
+            for (unsigned k = tid; k < total; k += NT)
+                reinterpret_cast<double2*>(dst)[k] = reinterpret_cast<const double2*>(Gs)[k];
+        } else {
+            const unsigned total = crows * D;
+            for (unsigned k = tid; k < total; k += NT) dst[k] = Gs[k];
+        }
     }
     // logp partial per chain: sum over the four lanes of a row (tig), a fixed
     // pairing so the result is identical on every lane.
@@ -401,16 +461,18 @@ k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __re
     }
 }
 
-template <int DT>
+template <int DT, int NW, int BN>
 int launch_lr_grad(Ctx& c, const double* q, const double* X, const double* y, double* part,
                    double* lpart, unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S,
                    int vecX) {
-    const size_t smem = LrCfg<DT>::BYTES;
-    cudaError_t e = cudaFuncSetAttribute(k_lr_grad<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    using G = LrCfg<DT, NW, BN>;
+    const size_t smem = G::BYTES;
+    cudaError_t e = cudaFuncSetAttribute(k_lr_grad<DT, NW, BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_lr_grad)");
-    dim3 grid(S, (C + LrCfg<DT>::BC - 1) / LrCfg<DT>::BC);
-    k_lr_grad<DT><<<grid, 256, smem, c.stream>>>(q, X, y, part, lpart, C, D, n_obs, L, S, vecX);
+    dim3 grid(S, (C + G::BC - 1) / G::BC);
+    k_lr_grad<DT, NW, BN><<<grid, G::NT, smem, c.stream>>>(q, X, y, part, lpart, C, D, n_obs, L, S,
+                                                          vecX);
     count_launch();
     return OK;
 }
@@ -478,9 +540,11 @@ int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, co
         const double* Xd = (const double*)X;
         const double* yd = (const double*)y;
         grad = [=, &c]() -> int {
-            if (D <= 32) return launch_lr_grad<4>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
-            if (D <= 64) return launch_lr_grad<8>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
-            return launch_lr_grad<13>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+            if (D <= 32)
+                return launch_lr_grad<4, 8, 32>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+            if (D <= 64)
+                return launch_lr_grad<8, 8, 32>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+            return launch_lr_grad<13, 8, 32>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
         };
     } else {
         double* Xt = (double*)(base + oXt);
