@@ -9,12 +9,15 @@
 //
 // Both kernels: CTA tile 128x128, 8 warps in a 2 (M) x 4 (N) grid with a
 // 64x32 warp tile, a 3-stage cp.async pipeline, shared-memory rows padded so
-// that every fragment load is bank-conflict free (A rows are BK+4 elements,
-// B rows are 128+8 elements), zero-filled out-of-range chunks, and a
+// that every fragment load is bank-conflict free (A rows are BK+4 elements;
+// B rows are 128+4 doubles -- 4 mod 16 in 8-byte bank pairs -- or 128+8
+// floats -- 8 mod 32 in 4-byte banks), zero-filled out-of-range chunks, and a
 // scalar loader when a row is not 16-byte aligned.
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+
+#include <algorithm>
 
 #include "kernels.h"
 
@@ -40,7 +43,7 @@ namespace {
 template <typename T, int BK>
 struct Smem {
     static constexpr int AS = BK + 4;      // A row stride (elements)
-    static constexpr int BS = BN + 8;      // B row stride (elements)
+    static constexpr int BS = BN + (sizeof(T) == 8 ? 4 : 8);  // B row stride (elements)
     static constexpr int A_ELEMS = BM * AS;
     static constexpr int B_ELEMS = BK * BS;
     static constexpr int STAGE = A_ELEMS + B_ELEMS;
@@ -148,62 +151,96 @@ __device__ __forceinline__ void tmma_16x8x8(float (&d)[4], const unsigned (&a)[4
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-template <typename T, int BK, int MK = 4>
-__global__ void __launch_bounds__(NTH, 1) k_gemm(GemmP<T> P) {
+// Interior tile: every 16-byte chunk of the A and B tiles is in range and
+// aligned, so the loads need no guards.
+template <typename T, int BK>
+__device__ __forceinline__ void load_tile_fast(T* sA, T* sB, const T* A, const T* B, int lda,
+                                               int ldb, int m0, int n0, int k0) {
+    constexpr int EPC = 16 / sizeof(T);
     using S = Smem<T, BK>;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    T* smem = reinterpret_cast<T*>(smem_raw);
-    const int bz = blockIdx.z;
-    const T* __restrict__ A = P.A;
-    const T* __restrict__ B = P.B;
-    T* __restrict__ C = P.C + bz * P.sC;
-    const int M = P.M, N = P.N, lda = P.lda, ldb = P.ldb, ldc = P.ldc;
-    int K = P.K;
+    const int tid = threadIdx.x;
+    constexpr int A_CHUNKS = BM * BK / EPC;
+#pragma unroll
+    for (int ch = tid; ch < A_CHUNKS; ch += NTH) {
+        const int r = ch / (BK / EPC), cc = (ch % (BK / EPC)) * EPC;
+        cp_async16(sA + r * S::AS + cc, A + (size_t)(m0 + r) * lda + k0 + cc, true);
+    }
+    constexpr int B_CHUNKS = BK * BN / EPC;
+#pragma unroll
+    for (int ch = tid; ch < B_CHUNKS; ch += NTH) {
+        const int r = ch / (BN / EPC), cc = (ch % (BN / EPC)) * EPC;
+        cp_async16(sB + r * S::BS + cc, B + (size_t)(k0 + r) * ldb + n0 + cc, true);
+    }
+}
+
+// Tile coordinates of linear tile `lin`: z (batch or K slice), m0, n0.
+struct TileAt {
+    int z, m0, n0;
+};
+template <typename T>
+__device__ __forceinline__ TileAt tile_at(const GemmP<T>& P, long long lin) {
+    const int tm = (P.M + BM - 1) / BM, tn = (P.N + BN - 1) / BN;
+    const long long per_z = (long long)tm * tn;
+    const int z = (int)(lin / per_z);
+    const int r = (int)(lin - (long long)z * per_z);
+    return TileAt{z, (r / tn) * BM, (r % tn) * BN};
+}
+
+// Operands of slice/batch z: A, B advanced and the K extent of the slice.
+template <typename T>
+__device__ __forceinline__ void operands_at(const GemmP<T>& P, int z, const T*& A, const T*& B,
+                                            int& K) {
+    A = P.A;
+    B = P.B;
+    K = P.K;
     if (P.ksplit > 0) {
-        // split-K: slice bz covers k in [bz*ksplit, min(K, (bz+1)*ksplit))
-        int kb = bz * P.ksplit;
+        // split-K: slice z covers k in [z*ksplit, min(K, (z+1)*ksplit))
+        const int kb = z * P.ksplit;
         K = (K - kb) < P.ksplit ? (K - kb) : P.ksplit;
         A += kb;
-        B += (size_t)kb * ldb;
+        B += (size_t)kb * P.ldb;
     } else {
-        A += bz * P.sA;
-        B += bz * P.sB;
+        A += z * P.sA;
+        B += z * P.sB;
     }
+}
+
+// acc += A[m0.., k] . B[k, n0..] over k-tiles [kt0, kt1) of this operand pair,
+// through the STAGES-deep cp.async pipeline in `smem`.
+template <typename T, int BK, int MK>
+__device__ __forceinline__ void gemm_mainloop(const GemmP<T>& P, const T* __restrict__ A,
+                                              const T* __restrict__ B, int K, int m0, int n0,
+                                              int kt0, int kt1, T* smem, T (&acc)[4][4][4]) {
+    using S = Smem<T, BK>;
+    const int M = P.M, N = P.N, lda = P.lda, ldb = P.ldb;
     const bool vecA = P.vecA, vecB = P.vecB;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const bool inner_mn = vecA && vecB && m0 + BM <= M && n0 + BN <= N;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, tig = lane & 3;
     const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
-
-    constexpr int NACC = sizeof(T) == 8 ? 4 : 4;
-    T acc[4][4][NACC];
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-#pragma unroll
-            for (int e = 0; e < NACC; e++) acc[i][j][e] = T(0);
-
-    const int KT = (K + BK - 1) / BK;
+    auto load = [&](int st, int kt) {
+        T* sA = smem + st * S::STAGE;
+        T* sB = sA + S::A_ELEMS;
+        const int k0 = kt * BK;
+        if (inner_mn && k0 + BK <= K)
+            load_tile_fast<T, BK>(sA, sB, A, B, lda, ldb, m0, n0, k0);
+        else
+            load_tile<T, BK>(sA, sB, A, B, M, N, K, lda, ldb, m0, n0, k0, vecA, vecB);
+    };
 #pragma unroll
     for (int s = 0; s < STAGES - 1; s++) {
-        if (s < KT) load_tile<T, BK>(smem + s * S::STAGE, smem + s * S::STAGE + S::A_ELEMS, A, B, M,
-                                     N, K, lda, ldb, m0, n0, s * BK, vecA, vecB);
+        if (kt0 + s < kt1) load(s, kt0 + s);
         cp_commit();
     }
-    for (int kt = 0; kt < KT; kt++) {
+    for (int kt = kt0; kt < kt1; kt++) {
         cp_wait<STAGES - 2>();
         __syncthreads();
         {
-            int nk = kt + STAGES - 1;
-            if (nk < KT) {
-                int st = nk % STAGES;
-                load_tile<T, BK>(smem + st * S::STAGE, smem + st * S::STAGE + S::A_ELEMS, A, B, M, N,
-                                 K, lda, ldb, m0, n0, nk * BK, vecA, vecB);
-            }
+            const int nk = kt + STAGES - 1;
+            if (nk < kt1) load((nk - kt0) % STAGES, nk);
             cp_commit();
         }
-        const T* sA = smem + (kt % STAGES) * S::STAGE;
+        const T* sA = smem + ((kt - kt0) % STAGES) * S::STAGE;
         const T* sB = sA + S::A_ELEMS;
         if constexpr (sizeof(T) == 8) {
             // DMMA m16n8kMK: A fragment register r holds (row g + 8*(r%2),
@@ -264,15 +301,47 @@ __global__ void __launch_bounds__(NTH, 1) k_gemm(GemmP<T> P) {
         }
     }
     cp_wait<0>();
-    // epilogue: c0,c1 at (g, 2tig..2tig+1), c2,c3 at (g+8, 2tig..)
+    __syncthreads();  // the caller may reuse smem or start another tile
+}
+
+template <typename T>
+__device__ __forceinline__ void zero_acc(T (&acc)[4][4][4]) {
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[i][j][e] = T(0);
+}
+
+// Data-parallel kernel: CTA b computes linear tile tile_base + b over its
+// whole K and writes C (bounds-checked).
+template <typename T, int BK, int MK = 4>
+__global__ void __launch_bounds__(NTH, 1) k_gemm(GemmP<T> P, long long tile_base) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T* smem = reinterpret_cast<T*>(smem_raw);
+    const TileAt ta = tile_at(P, tile_base + blockIdx.x);
+    const T* A;
+    const T* B;
+    int K;
+    operands_at(P, ta.z, A, B, K);
+    T* __restrict__ C = P.C + ta.z * P.sC;
+    T acc[4][4][4];
+    zero_acc(acc);
+    gemm_mainloop<T, BK, MK>(P, A, B, K, ta.m0, ta.n0, 0, (K + BK - 1) / BK, smem, acc);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, tig = lane & 3;
+    const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
+    const int M = P.M, N = P.N, ldc = P.ldc;
+    // accumulator (i, j): c0,c1 at (g, 2tig..2tig+1), c2,c3 at (g+8, 2tig..)
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            int col = n0 + wn + j * 8 + 2 * tig;
+            const int col = ta.n0 + wn + j * 8 + 2 * tig;
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-                int row = m0 + wm + i * 16 + g + h * 8;
+                const int row = ta.m0 + wm + i * 16 + g + h * 8;
                 if (row >= M) continue;
                 T* dst = C + (size_t)row * ldc + col;
                 if (col + 1 < N) {
@@ -285,21 +354,182 @@ __global__ void __launch_bounds__(NTH, 1) k_gemm(GemmP<T> P) {
         }
 }
 
+// ---- stream-K tail --------------------------------------------------------------------
+//
+// The tiles after the last full wave (tile_base .. tile_base + tail) would
+// leave SMs idle.  Their tail * KT k-tile iterations are cut into G equal
+// contiguous ranges, range p = [W p / G, W (p+1) / G) with W = tail * KT.  A
+// range is shorter than KT (tail < G), so it touches at most two tiles; CTA p
+// writes the partial sum of each touched tile to workspace slot 2p or 2p+1
+// (dense BM x BN).  k_gemm_fix then adds each tile's partials in range order
+// -- that is, in k order -- and writes C: the result does not depend on
+// timing.
+
+__host__ __device__ inline long long sk_lo(long long p, long long W, int G) { return p * W / G; }
+
+template <typename T, int BK, int MK = 4>
+__global__ void __launch_bounds__(NTH, 1)
+k_gemm_sk(GemmP<T> P, long long tile_base, long long W, int G, int KT, T* __restrict__ ws) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T* smem = reinterpret_cast<T*>(smem_raw);
+    const int p = blockIdx.x;
+    const long long hi = sk_lo(p + 1, W, G);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, tig = lane & 3;
+    const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
+    int slot = 0;
+    for (long long it = sk_lo(p, W, G); it < hi && slot < 2; slot++) {
+        const long long t = it / KT;
+        const int kt0 = (int)(it - t * KT);
+        const int kt1 = (int)((hi - it) < (long long)(KT - kt0) ? kt0 + (hi - it) : KT);
+        const TileAt ta = tile_at(P, tile_base + t);
+        const T* A;
+        const T* B;
+        int K;
+        operands_at(P, ta.z, A, B, K);
+        T acc[4][4][4];
+        zero_acc(acc);
+        gemm_mainloop<T, BK, MK>(P, A, B, K, ta.m0, ta.n0, kt0, kt1, smem, acc);
+        T* dst = ws + ((size_t)p * 2 + slot) * (BM * BN);
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int row = wm + i * 16 + g + h * 8, col = wn + j * 8 + 2 * tig;
+                    dst[row * BN + col] = acc[i][j][2 * h];
+                    dst[row * BN + col + 1] = acc[i][j][2 * h + 1];
+                }
+        it += kt1 - kt0;
+    }
+}
+
+// CTA (t, f) of the fix-up sums part f of tail tile t's elements over the
+// tile's partials in range order.  The contributing ranges (at most G) are
+// listed once in shared memory; four partials are loaded per step.
+constexpr int kMaxSkRanges = 1024;
+
+template <typename T> struct alignas(16) V16 {
+    T x[16 / sizeof(T)];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(NTH)
+k_gemm_fix(GemmP<T> P, long long tile_base, long long W, int G, int KT,
+           const T* __restrict__ ws) {
+    __shared__ int src_slot[kMaxSkRanges];  // workspace slot of each contributor, in k order
+    __shared__ int n_src;
+    const long long t = blockIdx.x;
+    const int per = (BM * BN) / gridDim.y;  // elements of this CTA
+    const int e0 = blockIdx.y * per;
+    if (threadIdx.x == 0) {
+        const long long i0 = t * KT, i1 = i0 + KT;
+        int p0 = (int)(i0 * G / W);  // first range holding iteration i0
+        while (p0 + 1 < G && sk_lo(p0 + 1, W, G) <= i0) p0++;
+        while (p0 > 0 && sk_lo(p0, W, G) > i0) p0--;
+        int n = 0;
+        for (int q = p0; q < G && n < kMaxSkRanges; q++) {
+            const long long lo = sk_lo(q, W, G);
+            if (lo >= i1) break;
+            src_slot[n++] = q * 2 + ((lo / KT == t) ? 0 : 1);
+        }
+        n_src = n;
+    }
+    __syncthreads();
+    const int n = n_src;
+    const TileAt ta = tile_at(P, tile_base + t);
+    T* __restrict__ C = P.C + ta.z * P.sC;
+    const int M = P.M, N = P.N, ldc = P.ldc;
+    constexpr int V = 16 / sizeof(T);  // elements per 16-byte vector
+    for (int e = e0 + threadIdx.x * V; e < e0 + per; e += NTH * V) {
+        auto at = [&](int q) {
+            return *reinterpret_cast<const V16<T>*>(ws + (size_t)src_slot[q] * (BM * BN) + e);
+        };
+        T sum[V];
+        {
+            const V16<T> v = at(0);
+#pragma unroll
+            for (int u = 0; u < V; u++) sum[u] = v.x[u];
+        }
+        int q = 1;
+        for (; q + 4 <= n; q += 4) {
+            const V16<T> v0 = at(q), v1 = at(q + 1), v2 = at(q + 2), v3 = at(q + 3);
+#pragma unroll
+            for (int u = 0; u < V; u++) sum[u] = (((sum[u] + v0.x[u]) + v1.x[u]) + v2.x[u]) + v3.x[u];
+        }
+        for (; q < n; q++) {
+            const V16<T> v = at(q);
+#pragma unroll
+            for (int u = 0; u < V; u++) sum[u] = sum[u] + v.x[u];
+        }
+        const int row = ta.m0 + e / BN, col0 = ta.n0 + e % BN;
+        if (row >= M) continue;
+#pragma unroll
+        for (int u = 0; u < V; u++)
+            if (col0 + u < N) C[(size_t)row * ldc + col0 + u] = sum[u];
+    }
+}
+
+// Stream-K is used for plain products (no K slicing) whose last wave leaves
+// SMs idle for at least 6 k-tile times in total per SM -- the fix-up costs
+// about that much.  NXV_GEMM_SK=0 disables it.
+bool sk_enabled() {
+    const char* v = getenv("NXV_GEMM_SK");
+    return !(v && strcmp(v, "0") == 0);
+}
+
 template <typename T, int BK, int MK = 4>
 int run_gemm_p(Ctx& c, GemmP<T> P) {
     constexpr int EPC = 16 / sizeof(T);
     P.vecA = ((uintptr_t)P.A % 16 == 0) && (P.lda % EPC == 0) && (P.ksplit % EPC == 0);
     P.vecB = ((uintptr_t)P.B % 16 == 0) && (P.ldb % EPC == 0);
     size_t smem = Smem<T, BK>::BYTES;
-    cudaError_t e = cudaFuncSetAttribute(k_gemm<T, BK, MK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
-    dim3 grid((unsigned)((P.N + BN - 1) / BN), (unsigned)((P.M + BM - 1) / BM), (unsigned)P.batch);
-    if (grid.y > 65535 || grid.z > 65535) {
+    const long long tiles = (long long)((P.M + BM - 1) / BM) * ((P.N + BN - 1) / BN) * P.batch;
+    if (tiles <= 0) return finish(c);
+    if (tiles > 0x7fffffffLL) {
         set_error("matmul grid out of range");
         return E_ARG;
     }
-    k_gemm<T, BK, MK><<<grid, NTH, smem, c.stream>>>(P);
+    const int KT = (P.K + BK - 1) / BK;
+    const int sms = c.dev->sm_count;
+    const long long tail = tiles % sms;
+    const bool sk = sk_enabled() && P.ksplit == 0 && tail > 0 && (sms - tail) * KT >= 6LL * sms;
+    if (!sk) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm<T, BK, MK>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+        k_gemm<T, BK, MK><<<(unsigned)tiles, NTH, smem, c.stream>>>(P, 0);
+        count_launch();
+        return finish(c);
+    }
+    const long long dp = tiles - tail;
+    const long long W = tail * KT;
+    // G ranges: one per SM, at most 32 per tail tile (the fix-up reads every
+    // partial) and at most W; G >= tail, so a range is at most KT long and
+    // touches at most two tiles.
+    const int G = (int)std::min<long long>(std::min<long long>(std::min<long long>(W, sms), 32 * tail),
+                                           kMaxSkRanges);
+    ScratchGuard guard(c);
+    T* ws = (T*)scratch(c, (size_t)G * 2 * BM * BN * sizeof(T), kScratchGemm);
+    if (!ws) return E_CUDA;
+    cudaError_t e = cudaFuncSetAttribute(k_gemm<T, BK, MK>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemm_sk<T, BK, MK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+    if (dp > 0) {
+        k_gemm<T, BK, MK><<<(unsigned)dp, NTH, smem, c.stream>>>(P, 0);
+        count_launch();
+    }
+    k_gemm_sk<T, BK, MK><<<G, NTH, smem, c.stream>>>(P, dp, W, G, KT, ws);
+    count_launch();
+    // fix-up: split each tile's elements over f CTAs so that about 2 CTAs per
+    // SM run (f divides BM*BN / (NTH * 16 bytes) evenly for f <= 16, a power of 2)
+    int f = 1;
+    while (f < 16 && tail * f < 2LL * sms) f *= 2;
+    k_gemm_fix<T><<<dim3((unsigned)tail, f), NTH, 0, c.stream>>>(P, dp, W, G, KT, ws);
     count_launch();
     return finish(c);
 }
@@ -330,24 +560,25 @@ int plain_params(GemmP<T>& P, T* C, const T* A, const T* B, size_t batch, size_t
     return OK;
 }
 
-// f64 configuration: BK x MMA-K.  NXV_DMMA="BKxMK" (16x4, 16x8, 16x16,
-// 32x8, 32x16) overrides the default.
+// f64 configuration: BK x MMA-K, default 32x4.  NXV_DMMA="BKxMK" (16x4,
+// 16x8, 16x16, 32x8, 32x16) overrides it.
 int dmma_cfg() {
     const char* v = getenv("NXV_DMMA");
     if (v && *v) {
         int bk = 0, mk = 0;
         if (sscanf(v, "%dx%d", &bk, &mk) == 2) return bk * 100 + mk;
     }
-    return 1604;
+    return 3204;
 }
 
 int gemm_f64_dispatch(Ctx& c, const GemmP<double>& P) {
     switch (dmma_cfg()) {
         case 1608: return run_gemm_p<double, 16, 8>(c, P);
         case 1616: return run_gemm_p<double, 16, 16>(c, P);
+        case 1604: return run_gemm_p<double, 16, 4>(c, P);
         case 3208: return run_gemm_p<double, 32, 8>(c, P);
         case 3216: return run_gemm_p<double, 32, 16>(c, P);
-        default: return run_gemm_p<double, 16, 4>(c, P);
+        default: return run_gemm_p<double, 32, 4>(c, P);
     }
 }
 

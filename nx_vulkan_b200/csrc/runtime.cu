@@ -7,6 +7,9 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <map>
+#include <tuple>
+
 namespace nxv {
 
 std::atomic<unsigned long> g_launches{0};
@@ -31,7 +34,8 @@ thread_local int tl_cuda_current = -1;
 thread_local char tl_err[512] = {0};
 
 std::mutex g_scratch_mu;
-std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> g_scratch;
+// (device, stream, slot) -> (region, bytes)
+std::map<std::tuple<int, cudaStream_t, int>, std::pair<void*, size_t>> g_scratch;
 
 int init_one(int id) {
     if (id < 0 || id >= kMaxDevices) {
@@ -149,7 +153,7 @@ void destroy_all() {
     {
         std::lock_guard<std::mutex> sk(g_scratch_mu);
         for (auto& kv : g_scratch) {
-            cudaSetDevice(kv.first.first);
+            cudaSetDevice(std::get<0>(kv.first));
             cudaFree(kv.second.first);
         }
         g_scratch.clear();
@@ -249,10 +253,10 @@ int sync(Ctx& c) {
     return OK;
 }
 
-void* scratch(Ctx& c, size_t bytes) {
+void* scratch(Ctx& c, size_t bytes, int slot) {
     if (bytes == 0) bytes = 256;
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    auto key = std::make_pair(c.dev->id, c.stream);
+    auto key = std::make_tuple(c.dev->id, c.stream, slot);
     auto it = g_scratch.find(key);
     if (it != g_scratch.end() && it->second.second >= bytes) return it->second.first;
     if (it != g_scratch.end()) {

@@ -83,9 +83,12 @@ inline void* dptr(const void* h) { return h ? static_cast<const Buf*>(h)->ptr : 
 inline size_t nbytes(const void* h) { return h ? static_cast<const Buf*>(h)->n_bytes : 0; }
 
 // Scratch memory: returns a device region of at least `bytes`, valid for
-// work queued on c.stream until the next scratch() call on this device.
-// Callers hold a ScratchGuard for the whole op (see Device::scratch_mu).
-void* scratch(Ctx& c, size_t bytes);
+// work queued on c.stream until the next scratch() call with the same slot
+// on this device.  Callers hold a ScratchGuard for the whole op (see
+// Device::scratch_mu).  Slot 0 belongs to the op entry points; slot 1 to the
+// GEMM (its stream-K workspace), which ops holding slot 0 may call.
+enum { kScratchOp = 0, kScratchGemm = 1 };
+void* scratch(Ctx& c, size_t bytes, int slot = kScratchOp);
 struct ScratchGuard {
     std::lock_guard<std::recursive_mutex> lk;
     explicit ScratchGuard(Ctx& c) : lk(c.dev->scratch_mu) {}

@@ -363,7 +363,7 @@ def test_matmul_f32_tensor_core_vs_oracle_and_mma(nxv, orc, monkeypatch, bmnk):
     assert _native.load().nxv_synchronize() == 0  # no pipeline timeout recorded
 
 
-@pytest.mark.parametrize("cfg", ["16x4", "16x8", "16x16", "32x8", "32x16"])
+@pytest.mark.parametrize("cfg", ["16x4", "16x8", "16x16", "32x4", "32x8", "32x16"])
 @pytest.mark.parametrize("bmnk", [(1, 130, 70, 257), (2, 256, 256, 100), (1, 33, 200, 17)])
 def test_matmul_f64_dmma_shapes(nxv, orc, monkeypatch, cfg, bmnk):
     """Every DMMA configuration (k-tile x MMA K-shape) against the oracle."""
@@ -377,3 +377,28 @@ def test_matmul_f64_dmma_shapes(nxv, orc, monkeypatch, cfg, bmnk):
         (np.abs(a.reshape(batch, m, k)[q]) @ np.abs(b.reshape(batch, k, n)[q])).reshape(-1)
         for q in range(batch)])
     assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 2 * k * 2.2e-16 * bound)
+
+
+@pytest.mark.parametrize("bmnk", [(1, 1000, 700, 513), (3, 300, 260, 700), (1, 1100, 1300, 640),
+                                  (1, 2304, 1152, 320), (1, 100, 120, 3000)])
+def test_matmul_f64_stream_k(nxv, orc, monkeypatch, bmnk):
+    """Tile counts that leave a partial last wave run their tail as stream-K
+    (k-ranges split evenly over the SMs, partials summed in k order).  The
+    result is within the f64 bound, identical bit for bit on a second call,
+    and within the bound of the plain data-parallel schedule (NXV_GEMM_SK=0)."""
+    batch, m, n, k = bmnk
+    r = np.random.default_rng(13)
+    a, b = r.normal(size=batch * m * k), r.normal(size=batch * k * n)
+    ta, tb = up(nxv, a), up(nxv, b)
+    got = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f64")), np.float64)
+    again = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f64")), np.float64)
+    assert np.array_equal(got, again)
+    monkeypatch.setenv("NXV_GEMM_SK", "0")
+    plain = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f64")), np.float64)
+    want = orc.matmul(a, b, m, n, k, batch=batch)
+    bound = np.concatenate([
+        (np.abs(a.reshape(batch, m, k)[q]) @ np.abs(b.reshape(batch, k, n)[q])).reshape(-1)
+        for q in range(batch)])
+    tol = 1e-12 * np.abs(want) + 2 * k * 2.2e-16 * bound
+    assert np.all(np.abs(got - want) <= tol)
+    assert np.all(np.abs(plain - want) <= tol)
