@@ -198,8 +198,9 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--suite", action="store_true",
                     help="measure every hot-path workload (one JSON line each) instead of the headline")
-    ap.add_argument("--only", default="fused,reduce,matmul,logreg",
-                    help="suite sections to run, comma separated: fused, reduce, matmul, logreg")
+    ap.add_argument("--only", default="fused,reduce,random,matmul,logreg",
+                    help="suite sections to run, comma separated: fused, reduce, random, matmul, "
+                         "logreg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -593,6 +594,33 @@ def suite(args):
                  l2="input 67/134 MB; back-to-back calls re-read it (L2 126 MB, partial hits)")
         del x, o_full
         torch.cuda.empty_cache()
+
+    # -- Philox random streams (write-bound) -------------------------------------------------
+    if "random" in want:
+        n = 1 << 26
+        for code, name in ((0, "f32"), (1, "f64")):
+            es = 4 if code == 0 else 8
+            outs = [torch.empty(n * es // 4, dtype=torch.float32, device=dev) for _ in range(2)]
+            hs = [wrap(t) for t in outs]
+            spv_r = nxv.shader_path("random_philox.spv" if code == 0 else "random_philox_f64.spv")
+            for dist, dname in ((0, "uniform"), (1, "normal")):
+                it = [0]
+
+                def call():
+                    h = hs[it[0] % 2]
+                    it[0] += 1
+                    if code == 0:
+                        ck(lib.nxv_random(h, n, 7, dist, spv_r))
+                    else:
+                        ck(lib.nxv_random_f64(h, n, 7, dist, spv_r))
+
+                ms = timed(call, 8)
+                gbs = n * es / (ms / 1e3) / 1e9
+                emit(workload=f"philox random {dname}", dtype=name, n=n, us_per_call=ms * 1e3,
+                     gbs=gbs, frac_of_hbm=gbs / peak, bytes_per_call=n * es,
+                     l2="two alternating outputs of 256/512 MB (larger than L2)")
+            del outs
+            torch.cuda.empty_cache()
 
     # -- dense matmul ---------------------------------------------------------------------
     N = 2048

@@ -399,7 +399,10 @@ int nxv_set_stream(void* cuda_stream);
 int nxv_synchronize(void);
 
 /* Non-owning handle over existing device memory of n_bytes (e.g. a tensor
- * of another framework); nxv_buf_free releases only the handle record. */
+ * of another framework); nxv_buf_free releases only the handle record.  The
+ * caller keeps that memory allocated for as long as work using the handle
+ * can run -- including CUDA graphs captured with it, which keep its raw
+ * address. */
 void* nxv_buf_wrap(void* device_ptr, unsigned long n_bytes);
 
 /* Device address and byte size behind a handle (NULL / 0 for NULL). */
