@@ -561,38 +561,59 @@ def suite(args):
     R = 4096
     for dt, code in ((torch.float32, 0), (torch.float64, 1)) if "reduce" in want else ():
         es = 4 if code == 0 else 8
+        # Rotating copies of x (and of the broadcast output) so that one call's
+        # input is not still in the 126 MB L2 from the previous call.
+        nset = 3 if code == 0 else 2
         x = torch.randn(R * R, generator=gen, dtype=torch.float64).to(dt).to(dev)
+        xs = [x] + [x.clone() for _ in range(nset - 1)]
         bvec = torch.randn(R, generator=gen, dtype=torch.float64).to(dt).to(dev)
-        hx, hb = wrap(x), wrap(bvec)
+        hxs, hb = [wrap(t) for t in xs], wrap(bvec)
         o_row = torch.empty(R, dtype=dt, device=dev)
         o_idx = torch.empty(R, dtype=torch.int64, device=dev)
         o_one = torch.empty(1, dtype=dt, device=dev)
-        o_full = torch.empty(R * R, dtype=dt, device=dev)
-        ho_row, ho_idx, ho_one, ho_full = wrap(o_row), wrap(o_idx), wrap(o_one), wrap(o_full)
+        o_fulls = [torch.empty(R * R, dtype=dt, device=dev) for _ in range(nset)]
+        ho_row, ho_idx, ho_one = wrap(o_row), wrap(o_idx), wrap(o_one)
+        ho_fulls = [wrap(t) for t in o_fulls]
         rspv = nxv.shader_path("reduce_axis.spv" if code == 0 else "reduce_axis_f64.spv")
         fspv = nxv.shader_path("reduce.spv" if code == 0 else "reduce_full_f64.spv")
+        aspv = nxv.shader_path("argmax_axis.spv")
         bspv = nxv.shader_path("elementwise_binary_broadcast.spv" if code == 0
                                else "elementwise_binary_broadcast_f64.spv")
         shape = (C.c_uint * 4)(R, R, 0, 0)
         as_ = (C.c_uint * 4)(R, 1, 0, 0)
         bs_ = (C.c_uint * 4)(0, 1, 0, 0)
+        k = [0]
+
+        def rot(f):
+            def call():
+                i = k[0] % nset
+                k[0] += 1
+                f(i)
+            return call
+
         cases = [
-            ("sum axis 1", lambda: ck(lib.nxv_reduce_axis(ho_row, hx, R, R, 1, 0, rspv)), R * R * es + R * es),
-            ("reduce_max axis 1", lambda: ck(lib.nxv_reduce_axis(ho_row, hx, R, R, 1, 1, rspv)), R * R * es + R * es),
-            ("sum all axes", lambda: ck(lib.nxv_reduce_to_buf(ho_one, hx, R * R, 0, code, fspv)), R * R * es),
-            ("reduce_max all axes", lambda: ck(lib.nxv_reduce_to_buf(ho_one, hx, R * R, 2, code, fspv)), R * R * es),
-            ("argmax axis 1", lambda: ck(lib.nxv_argmax_axis(ho_idx, hx, R, R, 1, 0, code, 8,
-                                                             nxv.shader_path("argmax_axis.spv"))), R * R * es + R * 8),
-            ("x + b (rows)", lambda: ck(lib.nxv_apply_binary_broadcast(ho_full, hx, hb, 0, 2, shape, as_, bs_, bspv)),
+            ("sum axis 1", rot(lambda i: ck(lib.nxv_reduce_axis(ho_row, hxs[i], R, R, 1, 0, rspv))),
+             R * R * es + R * es),
+            ("reduce_max axis 1", rot(lambda i: ck(lib.nxv_reduce_axis(ho_row, hxs[i], R, R, 1, 1, rspv))),
+             R * R * es + R * es),
+            ("sum all axes", rot(lambda i: ck(lib.nxv_reduce_to_buf(ho_one, hxs[i], R * R, 0, code, fspv))),
+             R * R * es),
+            ("reduce_max all axes", rot(lambda i: ck(lib.nxv_reduce_to_buf(ho_one, hxs[i], R * R, 2, code, fspv))),
+             R * R * es),
+            ("argmax axis 1", rot(lambda i: ck(lib.nxv_argmax_axis(ho_idx, hxs[i], R, R, 1, 0, code, 8, aspv))),
+             R * R * es + R * 8),
+            ("x + b (rows)", rot(lambda i: ck(lib.nxv_apply_binary_broadcast(ho_fulls[i], hxs[i], hb, 0, 2, shape,
+                                                                              as_, bs_, bspv))),
              2 * R * R * es + R * es),
         ]
         for name, fn, nbytes in cases:
-            ms = timed(fn, 20)
+            ms = timed(fn, 10 * nset)
             gbs = nbytes / (ms / 1e3) / 1e9
             emit(workload=f"{name} [4096,4096]", dtype=str(dt).split(".")[-1], us_per_call=ms * 1e3,
                  gbs=gbs, frac_of_hbm=gbs / peak, bytes_per_call=nbytes,
-                 l2="input 67/134 MB; back-to-back calls re-read it (L2 126 MB, partial hits)")
-        del x, o_full
+                 l2=f"{nset} rotating copies of the {R * R * es >> 20} MiB input (and output): "
+                    "each call's data is out of L2")
+        del x, xs, o_fulls
         torch.cuda.empty_cache()
 
     # -- Philox random streams (write-bound) -------------------------------------------------
