@@ -337,6 +337,21 @@ int nxv_leapfrog_chain_gauss_f64_batched(void* q_chain, void* p_chain,
                                          unsigned int K, double eps, double mu,
                                          const char* spv_path);
 
+/* NEW.  nxv_leapfrog_chain_gauss_f64_batched that also writes the kinetic
+ * energy of every step, ke_chain[chain][k] = 0.5 * sum_i p_i^2 * inv_mass_i
+ * (the reference's kinetic_energy.spv formula, shim.h:169-173, fused into
+ * the chain's epilogue so a NUTS caller gets the Hamiltonian -logp + KE of
+ * every trajectory point without another pass).  ke_chain holds
+ * n_chains * K doubles.  spv: leapfrog_chain_gauss_f64_batched.spv. */
+int nxv_leapfrog_chain_gauss_f64_batched_ke(void* q_chain, void* p_chain,
+                                            void* grad_chain, void* logp_chain,
+                                            void* ke_chain,
+                                            void* q_init, void* p_init, void* inv_mass,
+                                            void* prec,
+                                            unsigned int n, unsigned int n_chains,
+                                            unsigned int K, double eps, double mu,
+                                            const char* spv_path);
+
 /* NEW, with no counterpart in the reference.  The batched f64 Gaussian
  * chain above for callers that must not allocate device memory: a host
  * that captures its sampler step into a CUDA graph (cudaMalloc is not

@@ -69,6 +69,7 @@ SIGNATURES: dict[str, tuple] = {
     "nxv_leapfrog_chain_weibull": (C.c_int, CHAIN7 + [u32, u32, f32, f32, f32, f32, cstr]),
     "nxv_leapfrog_chain_normal_f64": (C.c_int, CHAIN7 + [u32, u32, f64, f64, f64, cstr]),
     "nxv_leapfrog_chain_gauss_f64_batched": (C.c_int, CHAIN7 + [vp, u32, u32, u32, f64, f64, cstr]),
+    "nxv_leapfrog_chain_gauss_f64_batched_ke": (C.c_int, [vp] * 9 + [u32, u32, u32, f64, f64, cstr]),
     "nxv_leapfrog_chain_gauss_f64_batched_noalloc": (C.c_int, [vp] * 8 + [u32, u32, u32, f64, f64]),
     "nxv_leapfrog_logreg_f64_batched": (C.c_int, [vp] * 8 + [u32, u32, u32, u32, f64, cstr]),
     "nxv_init_devices": (C.c_int, [intp, C.c_int]),

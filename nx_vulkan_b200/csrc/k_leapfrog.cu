@@ -135,15 +135,20 @@ struct ChainArgs {
     double scale, cst;
     const double* cst_dev;  // added to cst when non-null
     int mode;               // 0: per-chain logp; 1: per-256-group partials (_lg)
+    T* ke;                  // [chain][k] kinetic energy 0.5 * sum(p*p*m) (KE kernels only)
+    double* ke_partial;     // [chain][k][tile] when tiles > 1 (KE kernels only)
 };
 
 template <typename T>
 __device__ __forceinline__ void st_stream(T* p, T v) { __stcs(p, v); }
 
-template <typename T, class Fam, int NT, int VPT>
+// KE: also reduce the kinetic energy 0.5 * sum_i (p_i * p_i) * m_i of every
+// step, in the same fixed tree as logp, into g.ke (or g.ke_partial).
+template <typename T, class Fam, int NT, int VPT, bool KE>
 __global__ void __launch_bounds__(NT) k_chain(ChainArgs<T> g, Fam fam) {
     constexpr int NW = NT / 32;
     __shared__ double red[KC][NW];
+    __shared__ double redk[KE ? KC : 1][NW];
     const unsigned tile = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const double cst = g.cst + (g.cst_dev ? *g.cst_dev : 0.0);
@@ -169,7 +174,7 @@ __global__ void __launch_bounds__(NT) k_chain(ChainArgs<T> g, Fam fam) {
             for (unsigned kk = 0; kk < kn; kk++) {
                 const unsigned k = k0 + kk;
                 const size_t row = ((size_t)chain * g.K + k) * g.n;
-                double t = 0.0;
+                double t = 0.0, tk = 0.0;
 #pragma unroll
                 for (int v = 0; v < VPT; v++) {
                     T ph = add_(p[v], mul_(he, gr[v]));
@@ -182,11 +187,18 @@ __global__ void __launch_bounds__(NT) k_chain(ChainArgs<T> g, Fam fam) {
                         st_stream(g.pc + row + i, p[v]);
                         st_stream(g.gc + row + i, gr[v]);
                         t = __dadd_rn(t, fam.term(q[v], ep[v]));
+                        if constexpr (KE) tk = __dadd_rn(tk, (double)mul_(mul_(p[v], p[v]), em[v]));
                     }
                 }
 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1)
                     t = __dadd_rn(t, __shfl_down_sync(0xffffffffu, t, off));
+                if constexpr (KE) {
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1)
+                        tk = __dadd_rn(tk, __shfl_down_sync(0xffffffffu, tk, off));
+                    if (lane == 0) redk[kk][warp] = tk;
+                }
                 if (lane == 0) red[kk][warp] = t;
             }
             __syncthreads();
@@ -202,6 +214,13 @@ __global__ void __launch_bounds__(NT) k_chain(ChainArgs<T> g, Fam fam) {
                     g.logp[(size_t)chain * g.K + k] = (T)(g.scale * s + cst);
                 } else {
                     g.partial[((size_t)chain * g.K + k) * g.tiles + tile] = s;
+                }
+                if constexpr (KE) {
+                    double sk = redk[tid][0];
+#pragma unroll
+                    for (int w = 1; w < NW; w++) sk = __dadd_rn(sk, redk[tid][w]);
+                    if (g.tiles == 1) g.ke[(size_t)chain * g.K + k] = (T)(0.5 * sk);
+                    else g.ke_partial[((size_t)chain * g.K + k) * g.tiles + tile] = sk;
                 }
             }
             __syncthreads();
@@ -235,11 +254,12 @@ __device__ __forceinline__ void bulk_wait_read1() {
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 
-template <typename T, class Fam, int NT, int VPT, int S>
+template <typename T, class Fam, int NT, int VPT, int S, bool KE>
 __global__ void __launch_bounds__(NT) k_chain_tma(ChainArgs<T> g, Fam fam) {
     static_assert(KC % S == 0, "S must divide KC");
     constexpr int NW = NT / 32;
     __shared__ double red[KC][NW];
+    __shared__ double redk[KE ? KC : 1][NW];
     extern __shared__ __align__(128) unsigned char dsm[];
     T* sbuf = reinterpret_cast<T*>(dsm);  // [2][3][S][n]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -270,7 +290,7 @@ __global__ void __launch_bounds__(NT) k_chain_tma(ChainArgs<T> g, Fam fam) {
             __syncthreads();
             T* b = sbuf + (size_t)bsel * bufsz;
             for (unsigned kk = 0; kk < kn; kk++) {
-                double t = 0.0;
+                double t = 0.0, tk = 0.0;
 #pragma unroll
                 for (int v = 0; v < VPT; v++) {
                     T ph = add_(p[v], mul_(he, gr[v]));
@@ -283,11 +303,18 @@ __global__ void __launch_bounds__(NT) k_chain_tma(ChainArgs<T> g, Fam fam) {
                         b[arr + kk * n + i] = p[v];
                         b[2 * arr + kk * n + i] = gr[v];
                         t = __dadd_rn(t, fam.term(q[v], ep[v]));
+                        if constexpr (KE) tk = __dadd_rn(tk, (double)mul_(mul_(p[v], p[v]), em[v]));
                     }
                 }
 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1)
                     t = __dadd_rn(t, __shfl_down_sync(0xffffffffu, t, off));
+                if constexpr (KE) {
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1)
+                        tk = __dadd_rn(tk, __shfl_down_sync(0xffffffffu, tk, off));
+                    if (lane == 0) redk[(k0 + kk) % KC][warp] = tk;
+                }
                 if (lane == 0) red[(k0 + kk) % KC][warp] = t;
             }
             fence_proxy_async_smem();
@@ -308,6 +335,12 @@ __global__ void __launch_bounds__(NT) k_chain_tma(ChainArgs<T> g, Fam fam) {
 #pragma unroll
                     for (int w = 1; w < NW; w++) s = __dadd_rn(s, red[tid][w]);
                     g.logp[(size_t)chain * g.K + kbase + tid] = (T)(g.scale * s + cst);
+                    if constexpr (KE) {
+                        double sk = redk[tid][0];
+#pragma unroll
+                        for (int w = 1; w < NW; w++) sk = __dadd_rn(sk, redk[tid][w]);
+                        g.ke[(size_t)chain * g.K + kbase + tid] = (T)(0.5 * sk);
+                    }
                 }
             }
         }
@@ -326,6 +359,12 @@ __global__ void k_chain_fold(ChainArgs<T> g) {
     double s = pp[0];
     for (unsigned i = 1; i < g.tiles; i++) s = __dadd_rn(s, pp[i]);
     g.logp[t] = (T)(g.scale * s + cst);
+    if (g.ke) {
+        const double* pk = g.ke_partial + t * g.tiles;
+        double sk = pk[0];
+        for (unsigned i = 1; i < g.tiles; i++) sk = __dadd_rn(sk, pk[i]);
+        g.ke[t] = (T)(0.5 * sk);
+    }
 }
 
 // 0.5 * sum_i log prec_i - n * log sqrt(2 pi), fixed-order block tree.
@@ -381,7 +420,7 @@ size_t occupancy_smem(Ctx& c) {
     return want > 4096 ? want - 4096 : 0;
 }
 
-template <typename T, class Fam, int NT, int VPT>
+template <typename T, class Fam, int NT, int VPT, bool KE>
 int launch_cfg(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
     g.tiles = (unsigned)((g.n + NT * VPT - 1) / (NT * VPT));
     if (g.mode == 0 && g.tiles > 1 && !g.partial) {
@@ -396,11 +435,15 @@ int launch_cfg(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
     dim3 grid(g.tiles, gy);
     size_t dyn = occupancy_smem(c);
     if (dyn > 0) {
-        cudaError_t e = cudaFuncSetAttribute(k_chain<T, Fam, NT, VPT>,
+        cudaError_t e = cudaFuncSetAttribute(k_chain<T, Fam, NT, VPT, KE>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_chain)");
     }
-    k_chain<T, Fam, NT, VPT><<<grid, NT, dyn, c.stream>>>(g, fam);
+    if (KE && g.tiles > 1 && !g.ke_partial) {
+        set_error("kinetic-energy partials need scratch");
+        return E_ARG;
+    }
+    k_chain<T, Fam, NT, VPT, KE><<<grid, NT, dyn, c.stream>>>(g, fam);
     count_launch();
     if (g.mode == 0 && g.tiles > 1) {
         size_t total = (size_t)g.chains * g.K;
@@ -422,46 +465,47 @@ int tma_steps() {
     return (s == 1 || s == 2 || s == 4) ? s : 0;
 }
 
-template <typename T, class Fam, int VPT, int S>
+template <typename T, class Fam, int VPT, int S, bool KE>
 int launch_tma(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
     size_t smem = 2 * 3 * (size_t)S * g.n * sizeof(T);
     int per_block = 0;
     cudaDeviceGetAttribute(&per_block, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.dev->id);
-    if (smem + KC * 8 * 8 > (size_t)per_block) return E_KERNEL;  // caller falls back
-    cudaError_t e = cudaFuncSetAttribute(k_chain_tma<T, Fam, 256, VPT, S>,
+    if (smem + (KE ? 2 : 1) * KC * 8 * 8 > (size_t)per_block) return E_KERNEL;  // caller falls back
+    cudaError_t e = cudaFuncSetAttribute(k_chain_tma<T, Fam, 256, VPT, S, KE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_chain_tma)");
     g.tiles = 1;
     unsigned grid = g.chains < 0x7fffffffu ? g.chains : 0x7fffffffu;
-    k_chain_tma<T, Fam, 256, VPT, S><<<grid, 256, smem, c.stream>>>(g, fam);
+    k_chain_tma<T, Fam, 256, VPT, S, KE><<<grid, 256, smem, c.stream>>>(g, fam);
     count_launch();
     return finish(c);
 }
 
-template <typename T, class Fam, int VPT>
+template <typename T, class Fam, int VPT, bool KE>
 int launch_tma_s(Ctx& c, ChainArgs<T>& g, const Fam& fam, int s) {
-    if (s == 1) return launch_tma<T, Fam, VPT, 1>(c, g, fam);
-    if (s == 2) return launch_tma<T, Fam, VPT, 2>(c, g, fam);
-    return launch_tma<T, Fam, VPT, 4>(c, g, fam);
+    if (s == 1) return launch_tma<T, Fam, VPT, 1, KE>(c, g, fam);
+    if (s == 2) return launch_tma<T, Fam, VPT, 2, KE>(c, g, fam);
+    return launch_tma<T, Fam, VPT, 4, KE>(c, g, fam);
 }
 
-template <typename T, class Fam>
+// KE: the kernels also write g.ke (instantiated for the f64 Gaussian only).
+template <typename T, class Fam, bool KE = false>
 int launch_family(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
     if (g.n == 0 || g.K == 0 || g.chains == 0) return OK;
     ScratchGuard guard(c);
     int s = tma_steps();
     if (s && g.mode == 0 && g.n <= 2048 && (g.n * sizeof(T)) % 16 == 0) {
-        int rc = g.n <= 1024 ? launch_tma_s<T, Fam, 4>(c, g, fam, s)
-                             : launch_tma_s<T, Fam, 8>(c, g, fam, s);
+        int rc = g.n <= 1024 ? launch_tma_s<T, Fam, 4, KE>(c, g, fam, s)
+                             : launch_tma_s<T, Fam, 8, KE>(c, g, fam, s);
         if (rc != E_KERNEL) return rc;
     }
     Cfg cf = pick_cfg(c, g.n, g.chains, g.mode);
-    if (cf.nt == 128) return launch_cfg<T, Fam, 128, 8>(c, g, fam);
+    if (cf.nt == 128) return launch_cfg<T, Fam, 128, 8, KE>(c, g, fam);
     switch (cf.vpt) {
-        case 1: return launch_cfg<T, Fam, 256, 1>(c, g, fam);
-        case 2: return launch_cfg<T, Fam, 256, 2>(c, g, fam);
-        case 4: return launch_cfg<T, Fam, 256, 4>(c, g, fam);
-        default: return launch_cfg<T, Fam, 256, 8>(c, g, fam);
+        case 1: return launch_cfg<T, Fam, 256, 1, KE>(c, g, fam);
+        case 2: return launch_cfg<T, Fam, 256, 2, KE>(c, g, fam);
+        case 4: return launch_cfg<T, Fam, 256, 4, KE>(c, g, fam);
+        default: return launch_cfg<T, Fam, 256, 8, KE>(c, g, fam);
     }
 }
 
@@ -511,7 +555,7 @@ int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void
 
 int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                            const void* p0, const void* m, const void* prec, double prec_scalar,
-                           double mu, size_t n, size_t chains, unsigned K, double eps) {
+                           double mu, size_t n, size_t chains, unsigned K, double eps, void* ke) {
     ChainArgs<double> g{};
     g.qc = (double*)qc;
     g.pc = (double*)pc;
@@ -527,28 +571,38 @@ int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, con
     g.he = 0.5 * eps;
     g.mode = 0;
     g.scale = -0.5;
+    g.ke = (double*)ke;
     if (n == 0 || K == 0 || chains == 0) return OK;
     ScratchGuard guard(c);
+    // Scratch: [256 B: the log-density constant][tile partials of logp][tile
+    // partials of the kinetic energy], partials only when a chain spans
+    // several tiles.
+    Cfg cf = pick_cfg(c, n, chains, 0);
+    size_t tiles = (n + (size_t)cf.nt * cf.vpt - 1) / ((size_t)cf.nt * cf.vpt);
+    size_t part = tiles > 1 ? chains * (size_t)K * tiles * sizeof(double) : 0;
+    size_t need = 256 + part * (ke ? 2 : 1);
+    char* base = (char*)scratch(c, need);
+    if (!base) return E_CUDA;
+    if (tiles > 1) {
+        g.partial = (double*)(base + 256);
+        if (ke) g.ke_partial = (double*)(base + 256 + part);
+    }
+    FamGauss64 fam{(const double*)prec, prec_scalar, mu};
     if (prec) {
         // The constant needs sum(log prec): one tiny launch ahead of the
-        // chain writes it to scratch[0]; tile partials (if any) follow at
-        // byte offset 256 of the same scratch region.
-        Cfg cf = pick_cfg(c, n, chains, 0);
-        size_t tiles = (n + (size_t)cf.nt * cf.vpt - 1) / ((size_t)cf.nt * cf.vpt);
-        size_t need = 256 + (tiles > 1 ? chains * (size_t)K * tiles * sizeof(double) : 0);
-        char* base = (char*)scratch(c, need);
-        if (!base) return E_CUDA;
+        // chain writes it to the first 256 bytes of scratch.
         k_gauss_const<<<1, 256, 0, c.stream>>>((const double*)prec, n, (double*)base);
         count_launch();
         g.cst = 0.0;
         g.cst_dev = (const double*)base;
-        if (tiles > 1) g.partial = (double*)(base + 256);
-        return launch_family(c, g, FamGauss64{(const double*)prec, 0.0, mu});
+        fam.prec_s = 0.0;
+    } else {
+        // scalar precision: the reference's Normal(mu, sigma) f64 chain with
+        // prec = 1/sigma^2; the constant is -n (log sigma + log sqrt(2 pi)).
+        g.cst = 0.5 * (double)n * log(prec_scalar) - (double)n * 0.91893853320467274178;
     }
-    // scalar precision: the reference's Normal(mu, sigma) f64 chain with
-    // prec = 1/sigma^2; the constant is -n (log sigma + log sqrt(2 pi)).
-    g.cst = 0.5 * (double)n * log(prec_scalar) - (double)n * 0.91893853320467274178;
-    return launch_family(c, g, FamGauss64{nullptr, prec_scalar, mu});
+    if (ke) return launch_family<double, FamGauss64, true>(c, g, fam);
+    return launch_family(c, g, fam);
 }
 
 }  // namespace nxv

@@ -59,9 +59,11 @@ int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void
                      void* logp, const void* q0, const void* p0, const void* m, size_t n,
                      size_t chains, unsigned K, float eps, int logp_mode);
 // f64 Gaussian: prec == nullptr means prec_i = prec_scalar for all i.
+// ke: optional [chain][k] kinetic energy 0.5 * sum(p*p*inv_mass) per step.
 int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                            const void* p0, const void* m, const void* prec, double prec_scalar,
-                           double mu, size_t n, size_t chains, unsigned K, double eps);
+                           double mu, size_t n, size_t chains, unsigned K, double eps,
+                           void* ke = nullptr);
 int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                             const void* p0, const void* X, const void* y, size_t n_obs,
                             size_t n_dim, size_t chains, unsigned K, double eps);

@@ -635,6 +635,36 @@ int nxv_leapfrog_chain_gauss_f64_batched(void* q_chain, void* p_chain, void* gra
                                   dptr(prec), 0.0, mu, n, n_chains, K, eps);
 }
 
+int nxv_leapfrog_chain_gauss_f64_batched_ke(void* q_chain, void* p_chain, void* grad_chain,
+                                            void* logp_chain, void* ke_chain, void* q_init,
+                                            void* p_init, void* inv_mass, void* prec,
+                                            unsigned int n, unsigned int n_chains, unsigned int K,
+                                            double eps, double mu, const char* spv_path) {
+    if (!q_chain || !p_chain || !grad_chain || !logp_chain || !ke_chain || !q_init || !p_init ||
+        !inv_mass || !prec || !spv_path)
+        return E_NULL;
+    std::string k = spv_base(spv_path);
+    if (k != "leapfrog_chain_gauss_f64_batched.spv") return bad_kernel(k);
+    if (K == 0) {
+        set_error("K must be positive");
+        return E_ARG;
+    }
+    BEGIN(q_chain, p_chain, grad_chain, logp_chain, ke_chain, q_init, p_init, inv_mass, prec);
+    size_t vec = (size_t)n * 8 * n_chains, chain = vec * K;
+    NEED(q_init, vec, "q_init");
+    NEED(p_init, vec, "p_init");
+    NEED(inv_mass, vec, "inv_mass");
+    NEED(prec, (size_t)n * 8, "prec");
+    NEED(q_chain, chain, "q_chain");
+    NEED(p_chain, chain, "p_chain");
+    NEED(grad_chain, chain, "grad_chain");
+    NEED(logp_chain, (size_t)K * n_chains * 8, "logp_chain");
+    NEED(ke_chain, (size_t)K * n_chains * 8, "ke_chain");
+    return launch_chain_gauss_f64(c, dptr(q_chain), dptr(p_chain), dptr(grad_chain),
+                                  dptr(logp_chain), dptr(q_init), dptr(p_init), dptr(inv_mass),
+                                  dptr(prec), 0.0, mu, n, n_chains, K, eps, dptr(ke_chain));
+}
+
 int nxv_leapfrog_logreg_f64_batched(void* q_chain, void* p_chain, void* grad_chain,
                                     void* logp_chain, void* q_init, void* p_init, void* X,
                                     void* y, unsigned int n_obs, unsigned int n_dim,

@@ -695,8 +695,10 @@ def leapfrog_chain_normal_f64(q, p, m, k, eps, mu, sigma):
                   [eps, mu, sigma], elt=8)
 
 
-def leapfrog_chain_gauss_f64_batched(q, p, m, prec, n_chains, k, eps, mu=0.0):
-    """Batched anisotropic Gaussian chains: q, p, m are [chain][n] f64, prec [n]."""
+def leapfrog_chain_gauss_f64_batched(q, p, m, prec, n_chains, k, eps, mu=0.0, kinetic=False):
+    """Batched anisotropic Gaussian chains: q, p, m are [chain][n] f64, prec [n].
+    Returns q, p, grad trajectories [chain][k][n] and logp [chain][k]; with
+    kinetic=True also the kinetic energy 0.5 * sum(p^2 m) [chain][k]."""
     if not (q.n_bytes == p.n_bytes == m.n_bytes) or k <= 0 or n_chains <= 0:
         return (ERROR, "size_mismatch" if k > 0 else "bad_op")
     n = q.n_bytes // 8 // n_chains
@@ -704,11 +706,19 @@ def leapfrog_chain_gauss_f64_batched(q, p, m, prec, n_chains, k, eps, mu=0.0):
         return (ERROR, "size_mismatch")
     outs = [_alloc(q.n_bytes * k), _alloc(q.n_bytes * k), _alloc(q.n_bytes * k),
             _alloc(n_chains * k * 8)]
+    if kinetic:
+        outs.append(_alloc(n_chains * k * 8))
     if any(o is None for o in outs):
         return (ERROR, "alloc_failed")
-    rc = _lib().nxv_leapfrog_chain_gauss_f64_batched(
-        *(o.handle for o in outs), q.handle, p.handle, m.handle, prec.handle, n, n_chains, k,
-        eps, mu, shader_path("leapfrog_chain_gauss_f64_batched.spv"))
+    spv = shader_path("leapfrog_chain_gauss_f64_batched.spv")
+    if kinetic:
+        rc = _lib().nxv_leapfrog_chain_gauss_f64_batched_ke(
+            *(o.handle for o in outs), q.handle, p.handle, m.handle, prec.handle, n, n_chains, k,
+            eps, mu, spv)
+    else:
+        rc = _lib().nxv_leapfrog_chain_gauss_f64_batched(
+            *(o.handle for o in outs), q.handle, p.handle, m.handle, prec.handle, n, n_chains, k,
+            eps, mu, spv)
     return _dispatch(outs, rc)
 
 

@@ -129,6 +129,30 @@ def test_gauss_batched_tma_staged(nxv, orc, monkeypatch, stages, chains, d, K):
     close(down(nxv, outs[3], np.float64), want[3], 1e-12, 1e-12)
 
 
+@pytest.mark.parametrize("stages", ["2", "0"])
+@pytest.mark.parametrize("chains,d,K", [(1, 1, 1), (64, 1000, 32), (7, 17, 5), (5, 4000, 9), (3, 998, 33)])
+def test_gauss_batched_kinetic_energy(nxv, orc, monkeypatch, stages, chains, d, K):
+    """The chain with the fused kinetic energy: trajectories and logp as the
+    plain chain; ke[chain][k] = 0.5 * sum(p^2 m) of the oracle's p within
+    1e-12 relative (tree vs sequential order).  Covers the staged-store
+    kernel, the register-store kernel and multi-tile chains (d = 4000)."""
+    monkeypatch.setenv("NXV_LF_TMA", stages)
+    prec, q0, p0, m = gauss_config(chains, d)
+    m = m * np.random.default_rng(1).uniform(0.5, 1.5, m.shape)
+    eps = 0.01
+    outs = unwrap(nxv.leapfrog_chain_gauss_f64_batched(up(nxv, q0), up(nxv, p0), up(nxv, m), up(nxv, prec),
+                                                       chains, K, eps, kinetic=True))
+    assert len(outs) == 5
+    want = orc.chain_gauss_f64(q0, p0, m, prec, 0.0, d, chains, K, eps)
+    for t, w in zip(outs[:3], want[:3]):
+        assert np.array_equal(down(nxv, t, np.float64), w)
+    close(down(nxv, outs[3], np.float64), want[3], 1e-12, 1e-12)
+    pc = want[1].reshape(chains, K, d)
+    ke_want = np.array([[sum(((pc[c, k] * pc[c, k]) * m[c]).tolist()) * 0.5 for k in range(K)]
+                        for c in range(chains)])
+    close(down(nxv, outs[4], np.float64).reshape(chains, K), ke_want, 1e-12, 1e-12)
+
+
 @pytest.mark.parametrize("family", ["normal", "weibull"])
 def test_chain_families_tma_staged(nxv, orc, monkeypatch, family):
     monkeypatch.setenv("NXV_LF_TMA", "2")
