@@ -198,8 +198,9 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--suite", action="store_true",
                     help="measure every hot-path workload (one JSON line each) instead of the headline")
-    ap.add_argument("--only", default="fused,reduce,random,matmul,logreg",
-                    help="suite sections to run, comma separated: fused, reduce, random, matmul, "
+    ap.add_argument("--only", default="fused,reduce,random,misc,matmul,logreg",
+                    help="suite sections to run, comma separated: fused, reduce, random, misc "
+                         "(transpose, cast, logsumexp, HMC primitives, host transfers), matmul, "
                          "logreg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -642,6 +643,90 @@ def suite(args):
                      l2="two alternating outputs of 256/512 MB (larger than L2)")
             del outs
             torch.cuda.empty_cache()
+
+    # -- transpose, cast, logsumexp, HMC primitives, host transfers ---------------------------
+    if "misc" in want:
+        def hbm_line(name, dtype, fn, nbytes, reps=10, **extra):
+            ms = timed(fn, reps)
+            gbs = nbytes / (ms / 1e3) / 1e9
+            emit(workload=name, dtype=dtype, us_per_call=ms * 1e3, gbs=gbs, frac_of_hbm=gbs / peak,
+                 bytes_per_call=nbytes, **extra)
+
+        # 2-D transpose, 256 MiB in and out
+        for dt, name, spv_t, (m, n) in ((torch.float32, "float32", "transpose.spv", (8192, 8192)),
+                                        (torch.float64, "float64", "transpose_f64.spv", (4096, 8192))):
+            es = 4 if dt == torch.float32 else 8
+            a = torch.randn(m * n, dtype=dt, device=dev)
+            o = torch.empty(m * n, dtype=dt, device=dev)
+            ha, ho = wrap(a), wrap(o)
+            sp = nxv.shader_path(spv_t)
+            hbm_line(f"transpose [{m},{n}]", name,
+                     lambda: ck(lib.nxv_transpose(ho, ha, m, n, sp)), 2 * m * n * es)
+            del a, o
+        # casts, 2^26 elements
+        n = 1 << 26
+        a32 = torch.randn(n, dtype=torch.float32, device=dev)
+        a64 = torch.empty(n, dtype=torch.float64, device=dev)
+        h32, h64 = wrap(a32), wrap(a64)
+        up_spv, down_spv = nxv.shader_path("cast_f32_to_f64.spv"), nxv.shader_path("cast_f64_to_f32.spv")
+        hbm_line("cast f32 -> f64 [2^26]", "float32", lambda: ck(lib.nxv_cast(h64, h32, n, up_spv)), n * 12)
+        hbm_line("cast f64 -> f32 [2^26]", "float64", lambda: ck(lib.nxv_cast(h32, h64, n, down_spv)), n * 12)
+        del a32, a64
+        # logsumexp over axis 1 of [4096, 4096] f32, 3 rotating copies (out of L2)
+        R = 4096
+        xs = [torch.randn(R * R, dtype=torch.float32, device=dev) for _ in range(3)]
+        hxs = [wrap(t) for t in xs]
+        o = torch.empty(R, dtype=torch.float32, device=dev)
+        ho = wrap(o)
+        lse_spv = nxv.shader_path("logsumexp.spv")
+        k = [0]
+
+        def lse():
+            i = k[0] % 3
+            k[0] += 1
+            ck(lib.nxv_reduce_axis(ho, hxs[i], R, R, 1, 0, lse_spv))
+
+        hbm_line("logsumexp axis 1 [4096,4096]", "float32", lse, R * R * 4 + R * 4, reps=30,
+                 math="f64 exp/log per element")
+        del xs
+        # HMC primitives (f32, the reference's kinetic_energy.spv / normal_logpdf.spv)
+        n = 1 << 26
+        pv = torch.randn(n, dtype=torch.float32, device=dev)
+        mv = torch.rand(n, dtype=torch.float32, device=dev) + 0.5
+        part = torch.empty((n + 255) // 256, dtype=torch.float32, device=dev)
+        hp, hm, hpart = wrap(pv), wrap(mv), wrap(part)
+        ke_spv = nxv.shader_path("kinetic_energy.spv")
+        hbm_line("kinetic_energy [2^26] (per-256 partials)", "float32",
+                 lambda: ck(lib.nxv_kinetic_energy(hpart, hp, hm, n, ke_spv)), 2 * n * 4 + (n // 256) * 4)
+        n2 = 1 << 24
+        xv, muv, sv, ov = (torch.rand(n2, dtype=torch.float32, device=dev) + 0.5 for _ in range(4))
+        hx2, hmu, hs2, ho2 = wrap(xv), wrap(muv), wrap(sv), wrap(ov)
+        lp_spv = nxv.shader_path("normal_logpdf.spv")
+        hbm_line("normal_logpdf [2^24]", "float32",
+                 lambda: ck(lib.nxv_normal_logpdf(ho2, hx2, hmu, hs2, n2, lp_spv)), 4 * n2 * 4)
+        del pv, mv, part, xv, muv, sv, ov
+        torch.cuda.empty_cache()
+        # host <-> device through the C ABI (256 MiB): pinned copies directly,
+        # pageable through the library's pinned staging ring
+        nb = 256 << 20
+        buf = lib.nxv_buf_alloc(nb)
+        pinned = torch.empty(nb, dtype=torch.uint8, pin_memory=True)
+        pageable = np.ones(nb, dtype=np.uint8)
+        for kind, host in (("pinned", pinned.data_ptr()), ("pageable", pageable.ctypes.data)):
+            for direction in ("upload", "download"):
+                f = lib.nxv_buf_upload if direction == "upload" else lib.nxv_buf_download
+                ck(f(buf, C.c_void_p(host), nb))
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                reps = 5
+                for _ in range(reps):
+                    ck(f(buf, C.c_void_p(host), nb))
+                lib.nxv_synchronize()
+                torch.cuda.synchronize()
+                sec = (time.perf_counter() - t0) / reps
+                emit(workload=f"host {direction} 256 MiB ({kind})", us_per_call=sec * 1e6,
+                     gbs=nb / sec / 1e9, timing="host wall clock around synchronous calls")
+        lib.nxv_buf_free(buf)
 
     # -- dense matmul ---------------------------------------------------------------------
     N = 2048

@@ -223,12 +223,50 @@ int fused_typed(Ctx& c, T* out, const T* a, const T* b, const T* cc, const T* d,
 
 // ---- cast -------------------------------------------------------------------
 
+// f32 <-> f64.  Vector path (both pointers 16-byte aligned): a thread
+// converts groups of 4 elements -- one float4 and two double2 -- with
+// kUnroll groups in flight; the n % 4 tail is scalar.
 template <typename To, typename From>
 __global__ void __launch_bounds__(kThreads) k_cast(To* __restrict__ out,
-                                                  const From* __restrict__ a, size_t n) {
-    size_t stride = (size_t)gridDim.x * blockDim.x;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-        out[i] = (To)a[i];
+                                                  const From* __restrict__ a, size_t n, int vec) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    size_t done = 0;
+    if (vec) {
+        const size_t ng = n / 4;
+        for (; t + (kUnroll - 1) * stride < ng; t += kUnroll * stride) {
+            From x[kUnroll][4];
+#pragma unroll
+            for (int u = 0; u < kUnroll; u++) {
+                const From* src = a + (t + u * stride) * 4;
+                if constexpr (sizeof(From) == 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(src);
+                    x[u][0] = v.x, x[u][1] = v.y, x[u][2] = v.z, x[u][3] = v.w;
+                } else {
+                    const double2 v0 = reinterpret_cast<const double2*>(src)[0];
+                    const double2 v1 = reinterpret_cast<const double2*>(src)[1];
+                    x[u][0] = v0.x, x[u][1] = v0.y, x[u][2] = v1.x, x[u][3] = v1.y;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; u++) {
+                To* dst = out + (t + u * stride) * 4;
+                if constexpr (sizeof(To) == 8) {
+                    reinterpret_cast<double2*>(dst)[0] = make_double2((double)x[u][0], (double)x[u][1]);
+                    reinterpret_cast<double2*>(dst)[1] = make_double2((double)x[u][2], (double)x[u][3]);
+                } else {
+                    *reinterpret_cast<float4*>(dst) = make_float4((float)x[u][0], (float)x[u][1],
+                                                                  (float)x[u][2], (float)x[u][3]);
+                }
+            }
+        }
+        for (; t < ng; t += stride)
+#pragma unroll
+            for (int e = 0; e < 4; e++) out[t * 4 + e] = (To)a[t * 4 + e];
+        done = ng * 4;
+        t = done + (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    }
+    for (; t < n; t += stride) out[t] = (To)a[t];
 }
 
 // ---- broadcast --------------------------------------------------------------
@@ -350,27 +388,40 @@ k_bcast_fast(T* __restrict__ out, const T* __restrict__ a, const T* __restrict__
 
 // ---- transpose --------------------------------------------------------------
 
+// 32 x 32 tile through shared memory, 32 x 8 threads, 4 elements each:
+// coalesced row reads of A and row writes of the output.
 template <typename T>
-__global__ void __launch_bounds__(1024) k_transpose(T* __restrict__ out, const T* __restrict__ a,
-                                                    unsigned m, unsigned n) {
+__global__ void __launch_bounds__(256) k_transpose(T* __restrict__ out, const T* __restrict__ a,
+                                                   unsigned m, unsigned n) {
     __shared__ T tile[32][33];
-    unsigned bx = blockIdx.x * 32, by = blockIdx.y * 32;
-    unsigned x = bx + threadIdx.x, y = by + threadIdx.y;
-    if (x < n && y < m) tile[threadIdx.y][threadIdx.x] = a[(size_t)y * n + x];
+    const unsigned bx = blockIdx.x * 32, by = blockIdx.y * 32;
+    const unsigned x = bx + threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+        const unsigned y = by + threadIdx.y + j;
+        if (x < n && y < m) tile[threadIdx.y + j][threadIdx.x] = a[(size_t)y * n + x];
+    }
     __syncthreads();
-    unsigned ox = by + threadIdx.x, oy = bx + threadIdx.y;  // out is n x m
-    if (ox < m && oy < n) out[(size_t)oy * m + ox] = tile[threadIdx.x][threadIdx.y];
+    const unsigned ox = by + threadIdx.x;  // out is n x m
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+        const unsigned oy = bx + threadIdx.y + j;
+        if (ox < m && oy < n) out[(size_t)oy * m + ox] = tile[threadIdx.x][threadIdx.y + j];
+    }
 }
 
 // ---- HMC elementwise helpers (f32) ---------------------------------------------
 
 // normal_logpdf.spv: ((z*z)*-0.5 - log sigma) - log sqrt(2 pi), z = (x-mu)/sigma
 // (op order from lib/nx_vulkan/fast.ex:153-161).
-struct NormalLogpdfF {
+// EX: log sigma in f64 rounded once (the oracle's evaluation,
+// NXV_EXACT_F32=1), else logf (within 1 ulp).
+template <bool EX> struct NormalLogpdfF {
     __device__ float operator()(const float* x) const {
         float z = div_(sub_(x[0], x[1]), x[2]);
         float z2 = mul_(z, z);
-        return sub_(sub_(mul_(z2, -0.5f), (float)log((double)x[2])), 0.918938533204672742f);
+        const float ls = EX ? (float)log((double)x[2]) : logf(x[2]);
+        return sub_(sub_(mul_(z2, -0.5f), ls), 0.918938533204672742f);
     }
 };
 
@@ -417,11 +468,12 @@ int launch_unary(Ctx& c, int dt, void* out, const void* a, size_t n, unsigned op
 
 int launch_cast(Ctx& c, int to_f64, void* out, const void* a, size_t n) {
     if (n == 0) return OK;
-    unsigned g = grid_for(c, n, kThreads, 8);
+    const int vec = al16(out) && al16(a);
+    unsigned g = grid_for(c, vec ? (n / 4 + kUnroll - 1) / kUnroll : n, kThreads, 8);
     if (to_f64)
-        k_cast<double, float><<<g, kThreads, 0, c.stream>>>((double*)out, (const float*)a, n);
+        k_cast<double, float><<<g, kThreads, 0, c.stream>>>((double*)out, (const float*)a, n, vec);
     else
-        k_cast<float, double><<<g, kThreads, 0, c.stream>>>((float*)out, (const double*)a, n);
+        k_cast<float, double><<<g, kThreads, 0, c.stream>>>((float*)out, (const double*)a, n, vec);
     count_launch();
     return finish(c);
 }
@@ -500,7 +552,7 @@ int launch_transpose(Ctx& c, int dt, void* out, const void* a, unsigned m, unsig
 
 int enqueue_transpose(Ctx& c, int dt, void* out, const void* a, unsigned m, unsigned n) {
     if (m == 0 || n == 0) return OK;
-    dim3 grid((n + 31) / 32, (m + 31) / 32), block(32, 32);
+    dim3 grid((n + 31) / 32, (m + 31) / 32), block(32, 8);
     if (dt == F32) k_transpose<float><<<grid, block, 0, c.stream>>>((float*)out, (const float*)a, m, n);
     else k_transpose<double><<<grid, block, 0, c.stream>>>((double*)out, (const double*)a, m, n);
     count_launch();
@@ -509,8 +561,11 @@ int enqueue_transpose(Ctx& c, int dt, void* out, const void* a, unsigned m, unsi
 
 int launch_normal_logpdf(Ctx& c, void* out, const void* x, const void* mu, const void* sigma,
                          size_t n) {
+    if (fast_f32())
+        return run_map<float, 3>(c, (float*)out, (const float*)x, (const float*)mu,
+                                 (const float*)sigma, nullptr, n, NormalLogpdfF<false>{});
     return run_map<float, 3>(c, (float*)out, (const float*)x, (const float*)mu,
-                             (const float*)sigma, nullptr, n, NormalLogpdfF{});
+                             (const float*)sigma, nullptr, n, NormalLogpdfF<true>{});
 }
 
 int launch_leapfrog_step_f32(Ctx& c, void* qn, void* pn, const void* q, const void* p,

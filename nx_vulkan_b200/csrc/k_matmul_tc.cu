@@ -27,6 +27,8 @@
 
 #include "kernels.h"
 
+#include <algorithm>
+
 namespace nxv {
 
 namespace {
@@ -237,24 +239,44 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUt
     }
 }
 
+__device__ __forceinline__ float tf32_hi(float x) {
+    return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
+
 // Split A [M][K] (lda = K) into exact-TF32 hi and f32 lo parts, [M][Kp]
-// with zero padding in k in [K, Kp).
-__global__ void k_split_rows(const float* __restrict__ A, float* __restrict__ hi,
-                             float* __restrict__ lo, int M, int K, int Kp, long long sA,
-                             long long sO) {
-    const int bz = blockIdx.z;
+// with zero padding in k in [K, Kp).  Grid (row blocks, batch); each warp
+// walks rows, lane l covering 4-column groups l, l+32, ... of a row with
+// 16-byte loads when the row is 16-byte aligned (K % 4 == 0).
+__global__ void __launch_bounds__(256)
+k_split_rows(const float* __restrict__ A, float* __restrict__ hi, float* __restrict__ lo, int M,
+             int K, int Kp, long long sA, long long sO) {
+    const int bz = blockIdx.y;
     A += bz * sA;
     hi += bz * sO;
     lo += bz * sO;
-    const size_t total = (size_t)M * Kp;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (size_t)gridDim.x * blockDim.x) {
-        const size_t r = i / Kp;
-        const int k = (int)(i - r * Kp);
-        const float x = k < K ? A[r * K + k] : 0.0f;
-        const float h = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-        hi[i] = h;
-        lo[i] = __fsub_rn(x, h);
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    const bool vec = (K & 3) == 0 && (((uintptr_t)A) & 15) == 0;
+    for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < M; r += warps) {
+        const float* src = A + (size_t)r * K;
+        float* h = hi + (size_t)r * Kp;
+        float* l = lo + (size_t)r * Kp;
+        for (int k = lane * 4; k < Kp; k += 128) {  // Kp % 32 == 0: groups never straddle Kp
+            float x[4];
+            if (vec && k + 4 <= K) {
+                const float4 v = *reinterpret_cast<const float4*>(src + k);
+                x[0] = v.x, x[1] = v.y, x[2] = v.z, x[3] = v.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++) x[e] = k + e < K ? src[k + e] : 0.0f;
+            }
+            float4 vh, vl;
+            vh.x = tf32_hi(x[0]), vh.y = tf32_hi(x[1]), vh.z = tf32_hi(x[2]), vh.w = tf32_hi(x[3]);
+            vl.x = __fsub_rn(x[0], vh.x), vl.y = __fsub_rn(x[1], vh.y);
+            vl.z = __fsub_rn(x[2], vh.z), vl.w = __fsub_rn(x[3], vh.w);
+            *reinterpret_cast<float4*>(h + k) = vh;
+            *reinterpret_cast<float4*>(l + k) = vl;
+        }
     }
 }
 
@@ -277,7 +299,7 @@ __global__ void k_split_cols(const float* __restrict__ B, float* __restrict__ hi
         const int n = n0 + r, k = k0 + threadIdx.x;
         if (n < N && k < Kp) {
             const float x = t[threadIdx.x][r];
-            const float h = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+            const float h = tf32_hi(x);
             hi[(size_t)n * Kp + k] = h;
             lo[(size_t)n * Kp + k] = __fsub_rn(x, h);
         }
@@ -355,10 +377,12 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
     float* bhi = alo + a_elems;
     float* blo = bhi + b_elems;
     {
-        unsigned g = grid_for(c, m * Kp, 256, 8);
-        dim3 grid(g, 1, (unsigned)batch);
-        k_split_rows<<<grid, 256, 0, c.stream>>>((const float*)A, ahi, alo, (int)m, (int)k, (int)Kp,
-                                                 (long long)(m * k), (long long)(m * Kp));
+        // rows: 8 warps (rows) per CTA, enough CTAs for 8 per SM
+        const size_t row_ctas = (m + 7) / 8;
+        const unsigned gr = (unsigned)std::min<size_t>(row_ctas, (size_t)c.dev->sm_count * 8);
+        k_split_rows<<<dim3(gr, (unsigned)batch), 256, 0, c.stream>>>(
+            (const float*)A, ahi, alo, (int)m, (int)k, (int)Kp, (long long)(m * k),
+            (long long)(m * Kp));
         dim3 g2((unsigned)((n + 31) / 32), (unsigned)(Kp / 32), (unsigned)batch);
         k_split_cols<<<g2, dim3(32, 8), 0, c.stream>>>((const float*)B, bhi, blo, (int)k, (int)n,
                                                        (int)Kp, (long long)(k * n),

@@ -7,9 +7,12 @@
 //   f32 uniform:  element i <- word (i & 1) of philox(ctr = (i >> 1, 0), key = seed),
 //                 u = (w >> 8) * 2^-24 in [0, 1)
 //   f32 normal:   pair c <- u1 = ((w0 >> 8) + 1) * 2^-24, u2 = (w1 >> 8) * 2^-24,
-//                 r = sqrt(-2 ln u1): (r cos 2 pi u2, r sin 2 pi u2) in f64, rounded
+//                 r = sqrt(-2 ln u1): (r cos 2 pi u2, r sin 2 pi u2) -- in f32
+//                 (logf, sqrtf, sincospif: within 4 ulp) by default, in f64 and
+//                 rounded once with NXV_EXACT_F32=1
 //   f64 uniform:  element i <- philox((i, 1), seed): (((w0 << 32) | w1) >> 11) * 2^-53
-//   f64 normal:   pair c <- u1 = philox((2c, 1)) + 2^-53, u2 = philox((2c + 1, 1))
+//   f64 normal:   pair c <- u1 = philox((2c, 1)) + 2^-53, u2 = philox((2c + 1, 1)),
+//                 (r cos 2 pi u2, r sin 2 pi u2) through sincospi(2 u2)
 // Write-bound: one thread per pair, vector stores when aligned.
 #include "kernels.h"
 
@@ -35,6 +38,7 @@ __device__ __forceinline__ void philox2x32(uint32_t x0, uint32_t x1, uint32_t ke
 
 constexpr double kTwoPi = 6.283185307179586476925286766559;
 
+template <bool EX>
 __global__ void k_random_f32(float* __restrict__ out, size_t n, uint32_t seed, unsigned dist) {
     size_t pairs = (n + 1) / 2;
     size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -45,13 +49,21 @@ __global__ void k_random_f32(float* __restrict__ out, size_t n, uint32_t seed, u
         if (dist == 0) {
             v0 = (float)(w0 >> 8) * 0x1.0p-24f;
             v1 = (float)(w1 >> 8) * 0x1.0p-24f;
-        } else {
+        } else if (EX) {
             double u1 = ((double)(w0 >> 8) + 1.0) * 0x1.0p-24;
             double u2 = (double)(w1 >> 8) * 0x1.0p-24;
             double r = sqrt(-2.0 * log(u1));
             double a = kTwoPi * u2;
             v0 = (float)(r * cos(a));
             v1 = (float)(r * sin(a));
+        } else {
+            const float u1 = (float)((w0 >> 8) + 1u) * 0x1.0p-24f;  // exact: <= 2^24
+            const float u2 = (float)(w1 >> 8) * 0x1.0p-24f;
+            const float r = sqrtf(-2.0f * logf(u1));
+            float sn, cs;
+            sincospif(2.0f * u2, &sn, &cs);  // sin, cos of 2 pi u2 (2 u2 exact)
+            v0 = r * cs;
+            v1 = r * sn;
         }
         if (2 * c + 1 < n) {
             if ((((uintptr_t)(out + 2 * c)) & 7) == 0) {
@@ -85,9 +97,10 @@ __global__ void k_random_f64(double* __restrict__ out, size_t n, uint32_t seed, 
         double u1 = u53((uint32_t)(2 * c), seed) + 0x1.0p-53;
         double u2 = u53((uint32_t)(2 * c + 1), seed);
         double r = sqrt(-2.0 * log(u1));
-        double a = kTwoPi * u2;
-        out[2 * c] = r * cos(a);
-        if (2 * c + 1 < n) out[2 * c + 1] = r * sin(a);
+        double sn, cs;
+        sincospi(2.0 * u2, &sn, &cs);  // sin, cos of 2 pi u2 in one call (2 u2 exact)
+        out[2 * c] = r * cs;
+        if (2 * c + 1 < n) out[2 * c + 1] = r * sn;
     }
 }
 
@@ -100,7 +113,10 @@ int launch_random(Ctx& c, int dt, void* out, size_t n, uint32_t seed, unsigned d
         return E_ARG;
     }
     unsigned g = grid_for(c, (n + 1) / 2, 256, 8);
-    if (dt == F32) k_random_f32<<<g, 256, 0, c.stream>>>((float*)out, n, seed, dist);
+    if (dt == F32) {
+        if (fast_f32()) k_random_f32<false><<<g, 256, 0, c.stream>>>((float*)out, n, seed, dist);
+        else k_random_f32<true><<<g, 256, 0, c.stream>>>((float*)out, n, seed, dist);
+    }
     else k_random_f64<<<g, 256, 0, c.stream>>>((double*)out, n, seed, dist);
     count_launch();
     return finish(c);

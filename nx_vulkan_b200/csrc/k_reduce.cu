@@ -385,21 +385,62 @@ int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* 
 
 // ---- logsumexp (f32 in/out, f64 math) --------------------------------------------
 
+// One warp per row: pass 1 the row max, pass 2 sum exp(x - max) in double
+// (the row is read again, mostly from L1), then log(sum) + max.  EX: exp in
+// f64 (the oracle's evaluation; NXV_EXACT_F32=1), else expf of the f32
+// difference.  Shuffle trees in a fixed order.
+template <bool EX>
 __global__ void __launch_bounds__(kThreads)
-k_lse_rows(const float* __restrict__ a, size_t R_, float* out) {
-    const float* row = a + (size_t)blockIdx.x * R_;
+k_lse_rows(const float* __restrict__ a, size_t outer, unsigned R_, float* __restrict__ out) {
+    const size_t r = (size_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+    const unsigned lane = threadIdx.x & 31;
+    if (r >= outer) return;
+    const float* row = a + r * R_;
+    const bool vec = (((uintptr_t)row) & 15) == 0;
+    const unsigned nv = vec ? R_ / 4 : 0;
+    const float4* rv = reinterpret_cast<const float4*>(row);
+    constexpr int U = 4;  // 16-byte loads in flight per lane
     float mx = -INFINITY;
-    for (size_t e = threadIdx.x; e < R_; e += blockDim.x) mx = fmaxf(mx, row[e]);
-    mx = block_reduce<MaxR<float, true>>(mx);
-    __shared__ float s_mx;
-    if (threadIdx.x == 0) s_mx = mx;
-    __syncthreads();
-    double m = (double)s_mx;
+    {
+        unsigned v = lane;
+        for (; v + (U - 1) * 32 < nv; v += 32 * U) {
+            float4 x[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) x[u] = rv[v + u * 32];
+#pragma unroll
+            for (int u = 0; u < U; u++) mx = fmaxf(mx, fmaxf(fmaxf(x[u].x, x[u].y), fmaxf(x[u].z, x[u].w)));
+        }
+        for (; v < nv; v += 32) {
+            const float4 x = rv[v];
+            mx = fmaxf(mx, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
+        }
+    }
+    for (unsigned e = nv * 4 + lane; e < R_; e += 32) mx = fmaxf(mx, row[e]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    auto term = [&](float x) -> double {
+        if constexpr (EX) return exp((double)x - (double)mx);
+        else return (double)expf(x - mx);
+    };
+    auto term4 = [&](float4 x) -> double {
+        return __dadd_rn(__dadd_rn(term(x.x), term(x.y)), __dadd_rn(term(x.z), term(x.w)));
+    };
     double s = 0.0;
-    for (size_t e = threadIdx.x; e < R_; e += blockDim.x) s += exp((double)row[e] - m);
-    __syncthreads();
-    s = block_reduce<SumR<float>>(s);
-    if (threadIdx.x == 0) out[blockIdx.x] = (float)(log(s) + m);
+    {
+        unsigned v = lane;
+        for (; v + (U - 1) * 32 < nv; v += 32 * U) {
+            float4 x[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) x[u] = rv[v + u * 32];
+#pragma unroll
+            for (int u = 0; u < U; u++) s = __dadd_rn(s, term4(x[u]));
+        }
+        for (; v < nv; v += 32) s = __dadd_rn(s, term4(rv[v]));
+    }
+    for (unsigned e = nv * 4 + lane; e < R_; e += 32) s = __dadd_rn(s, term(row[e]));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s = __dadd_rn(s, __shfl_down_sync(0xffffffffu, s, off));
+    if (lane == 0) out[r] = (float)(log(s) + (double)mx);
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -420,13 +461,36 @@ k_lse_cols(const float* __restrict__ a, size_t R_, size_t inner, float* out) {
 
 // ---- kinetic energy partials -------------------------------------------------------
 
+// out[g] = 0.5 * sum over the 256 elements of group g of (p*p)*m (the
+// reference's per-workgroup partials).  One warp per group: lane l takes
+// elements 8l .. 8l+7 (two 16-byte loads of p and of m when aligned),
+// terms in f32 as (p*p)*m, sums in double, then a fixed shuffle tree.
 __global__ void __launch_bounds__(kThreads)
 k_kinetic(const float* __restrict__ p, const float* __restrict__ m, size_t n, float* out) {
-    size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x;
+    const size_t grp = (size_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+    const unsigned lane = threadIdx.x & 31;
+    const size_t ngrp = (n + 255) / 256;
+    if (grp >= ngrp) return;
+    const size_t i0 = grp * 256 + (size_t)lane * 8;
     double t = 0.0;
-    if (i < n) t = (double)mul_(mul_(p[i], p[i]), m[i]);
-    t = block_reduce<SumR<float>>(t);
-    if (threadIdx.x == 0) out[blockIdx.x] = (float)(0.5 * t);
+    if (i0 + 8 <= n && (((uintptr_t)(p + i0)) & 15) == 0 && (((uintptr_t)(m + i0)) & 15) == 0) {
+        const float4 p0 = *reinterpret_cast<const float4*>(p + i0);
+        const float4 p1 = *reinterpret_cast<const float4*>(p + i0 + 4);
+        const float4 m0 = *reinterpret_cast<const float4*>(m + i0);
+        const float4 m1 = *reinterpret_cast<const float4*>(m + i0 + 4);
+        const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) t = __dadd_rn(t, (double)mul_(mul_(pv[e], pv[e]), mv[e]));
+    } else {
+        for (int e = 0; e < 8; e++) {
+            const size_t i = i0 + e;
+            if (i < n) t = __dadd_rn(t, (double)mul_(mul_(p[i], p[i]), m[i]));
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) t = __dadd_rn(t, __shfl_down_sync(0xffffffffu, t, off));
+    if (lane == 0) out[grp] = (float)(0.5 * t);
 }
 
 }  // namespace
@@ -487,8 +551,17 @@ int launch_argmax(Ctx& c, int dt, void* out, const void* a, size_t outer, size_t
 int launch_logsumexp(Ctx& c, void* out, const void* a, size_t outer, size_t R, size_t inner) {
     if (R == 0 || outer == 0 || inner == 0) return OK;
     if (inner == 1) {
-        if (outer > 0x7fffffff) return E_ARG;
-        k_lse_rows<<<(unsigned)outer, kThreads, 0, c.stream>>>((const float*)a, R, (float*)out);
+        const size_t ctas = (outer + kThreads / 32 - 1) / (kThreads / 32);
+        if (ctas > 0x7fffffff || R > 0xffffffffull) {
+            set_error("logsumexp extents out of range");
+            return E_ARG;
+        }
+        if (fast_f32())
+            k_lse_rows<false><<<(unsigned)ctas, kThreads, 0, c.stream>>>((const float*)a, outer,
+                                                                         (unsigned)R, (float*)out);
+        else
+            k_lse_rows<true><<<(unsigned)ctas, kThreads, 0, c.stream>>>((const float*)a, outer,
+                                                                        (unsigned)R, (float*)out);
     } else {
         if (outer > 65535) return E_ARG;
         dim3 grid((unsigned)((inner + kThreads - 1) / kThreads), (unsigned)outer);
@@ -500,9 +573,10 @@ int launch_logsumexp(Ctx& c, void* out, const void* a, size_t outer, size_t R, s
 
 int launch_kinetic_energy(Ctx& c, void* out, const void* p, const void* m, size_t n) {
     if (n == 0) return OK;
-    size_t groups = (n + kThreads - 1) / kThreads;
-    k_kinetic<<<(unsigned)groups, kThreads, 0, c.stream>>>((const float*)p, (const float*)m, n,
-                                                           (float*)out);
+    const size_t groups = (n + 255) / 256;
+    const size_t ctas = (groups + kThreads / 32 - 1) / (kThreads / 32);
+    k_kinetic<<<(unsigned)ctas, kThreads, 0, c.stream>>>((const float*)p, (const float*)m, n,
+                                                         (float*)out);
     count_launch();
     return finish(c);
 }

@@ -218,8 +218,14 @@ def test_argmax_ties_and_nan(nxv, orc):
     assert list(got) == [1, 2, 0]
 
 
-def test_logsumexp(nxv, orc):
-    for shape in [(64, 1000, 1), (3, 50, 17)]:
+@pytest.mark.parametrize("exact", ["0", "1"])
+def test_logsumexp(nxv, orc, monkeypatch, exact):
+    """f32 in/out within 1e-5 relative; exp in f32 (default) or f64
+    (NXV_EXACT_F32=1), sums in double.  Rows of 1..4096+ elements, odd and
+    unaligned lengths, the cols kernel."""
+    monkeypatch.setenv("NXV_EXACT_F32", exact)
+    for shape in [(64, 1000, 1), (3, 50, 17), (4096, 4096, 1), (1, 100003, 1), (5000, 7, 1),
+                  (9, 1, 1), (33, 4097, 1)]:
         x = np.random.default_rng(2).normal(size=int(np.prod(shape))).astype(np.float32) * 10
         got = down(nxv, unwrap(nxv.logsumexp(up(nxv, x), *shape)), np.float32)
         close(got, orc.logsumexp(x, *shape), 1e-5, 1e-6)
@@ -285,8 +291,12 @@ def test_matmul_config_sizes(nxv, orc):
     assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 2 * 256 * 2.2e-16 * bound)
 
 
+@pytest.mark.parametrize("exact", ["0", "1"])
 @pytest.mark.parametrize("n", [1, 2, 7, 1024, 1000001])
-def test_philox_matches_oracle(nxv, orc, n):
+def test_philox_matches_oracle(nxv, orc, monkeypatch, n, exact):
+    """Uniforms bit-exact; f32 normals within 1e-6 (f32 math by default,
+    f64 math rounded once with NXV_EXACT_F32=1); f64 normals within 1e-12."""
+    monkeypatch.setenv("NXV_EXACT_F32", exact)
     for seed in (0, 42, 0xDEADBEEF):
         u = down(nxv, unwrap(nxv.uniform(n, seed)), np.float32)
         assert np.array_equal(u, orc.random_f32(n, seed, 0))  # bit-exact
@@ -298,7 +308,7 @@ def test_philox_matches_oracle(nxv, orc, n):
         close(g64, orc.random_f64(n, seed, 1), 1e-12, 1e-14)
 
 
-@pytest.mark.parametrize("mn", [(1, 1), (3, 5), (33, 65), (1000, 17), (4096, 4096)])
+@pytest.mark.parametrize("mn", [(1, 1), (3, 5), (33, 65), (1000, 17), (4096, 4096), (8, 3000), (3000, 9)])
 def test_transpose_and_cast(nxv, orc, mn):
     m, n = mn
     a = np.random.default_rng(4).normal(size=m * n).astype(np.float32)
@@ -309,6 +319,39 @@ def test_transpose_and_cast(nxv, orc, mn):
     b = np.random.default_rng(5).normal(size=m * n) * 1e3
     f = down(nxv, unwrap(nxv.cast_f64_to_f32(up(nxv, b), m * n)), np.float32)
     assert np.array_equal(f, b.astype(np.float32))
+
+
+@pytest.mark.parametrize("n", [1, 255, 256, 257, 100003, 1 << 20])
+def test_kinetic_energy_partials(nxv, orc, n):
+    """One partial per 256-element group: 0.5 * sum((p*p)*m) of the group,
+    the f32 products summed in double (within 1e-6 of numpy per group)."""
+    r = np.random.default_rng(n)
+    p, m = r.normal(size=n).astype(np.float32), r.uniform(0.5, 2, n).astype(np.float32)
+    parts = down(nxv, unwrap(nxv.kinetic_energy(up(nxv, p), up(nxv, m))), np.float32)
+    assert parts.size == (n + 255) // 256
+    terms = ((p * p) * m).astype(np.float64)
+    pad = np.zeros(parts.size * 256)
+    pad[:n] = terms
+    want = 0.5 * pad.reshape(-1, 256).sum(axis=1)
+    close(parts, want, 1e-6, 1e-6)
+    # an unaligned p (offset by one element) takes the scalar path
+    if n > 1:
+        p2, m2 = p[1:].copy(), m[1:].copy()
+        pt = unwrap(nxv.upload_f32(np.concatenate([[0.0], p2]).astype(np.float32)))
+        from nx_vulkan_b200 import _native
+        lib = _native.load()
+        base = lib.nxv_buf_device_ptr(pt.handle)
+        hp = lib.nxv_buf_wrap(base + 4, (n - 1) * 4)
+        hm = up(nxv, m2)
+        out = unwrap(nxv.upload_f32(np.zeros((n - 1 + 255) // 256, np.float32)))
+        assert lib.nxv_kinetic_energy(out.handle, hp, hm.handle, n - 1,
+                                      nxv.shader_path("kinetic_energy.spv")) == 0
+        lib.nxv_buf_free(hp)
+        got2 = down(nxv, out, np.float32)
+        t2 = ((p2 * p2) * m2).astype(np.float64)
+        pad2 = np.zeros(got2.size * 256)
+        pad2[:n - 1] = t2
+        close(got2, 0.5 * pad2.reshape(-1, 256).sum(axis=1), 1e-6, 1e-6)
 
 
 def test_kinetic_energy_and_logpdf_large(nxv, orc):
