@@ -527,6 +527,25 @@ def suite(args):
 
     want = set(args.only.split(","))
 
+    # CPU path beside each GPU line: the oracle (the C restatement of the
+    # reference's semantics) timed on a bounded sample of the same workload on
+    # this host, scaled to the full workload by its size.
+    from oracle import binding as orc
+    nthr = host_threads()
+    crng = np.random.default_rng(11)
+
+    def cpu_est(fn, scale, cores, sample, min_s=0.2):
+        fn()
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= min_s or reps >= 20:
+                break
+        return {"us_per_call": el / reps * scale * 1e6, "kind": "port", "cores": cores,
+                "sample": sample}
+
     # -- fused elementwise chain tanh(exp(x*y+z)-1.0), size sweep ---------------
     ops = (C.c_uint * 8)(1, 0, 100, 2, 106, 255, 255, 255)
     src = (C.c_uint * 8)(1, 2, 1, 0, 1, 1, 1, 1)
@@ -552,9 +571,15 @@ def suite(args):
             reps = 4 * sets if n <= (1 << 24) else 4
             ms = timed(call, reps)
             gbs = 4 * n * es / (ms / 1e3) / 1e9
+            ns = min(n, 1 << 22)
+            npdt = np.float32 if code == 0 else np.float64
+            cx = [crng.uniform(-1, 1, ns).astype(npdt) for _ in range(3)]
+            cpu = cpu_est(lambda: orc.fused(cx[0], [cx[1], cx[2]], [1, 0, 100, 2, 106], [1, 2, 1, 0, 1],
+                                            [0, 0, 0, 1.0, 0], nthreads=nthr),
+                          n / ns, nthr, f"{ns} elements, scaled x{n // ns}")
             emit(workload="fused chain tanh(exp(x*y+z)-1.0)", dtype=str(dt).split(".")[-1], n=n,
                  us_per_call=ms * 1e3, gbs=gbs, frac_of_hbm=gbs / peak, bytes_per_call=4 * n * es,
-                 rotating_sets=sets)
+                 rotating_sets=sets, cpu_baseline=cpu)
             del bufs
             torch.cuda.empty_cache()
 
@@ -607,13 +632,25 @@ def suite(args):
                                                                               as_, bs_, bspv))),
              2 * R * R * es + R * es),
         ]
+        rs = 256  # CPU sample: 256 of the 4096 rows, scaled x16
+        xc = x[: rs * R].cpu().numpy()
+        bc = bvec.cpu().numpy()
+        cpu_fns = {
+            "sum axis 1": lambda: orc.reduce_axis(xc, rs, R, 1, 0),
+            "reduce_max axis 1": lambda: orc.reduce_axis(xc, rs, R, 1, 1),
+            "sum all axes": lambda: orc.reduce_full(xc, 0),
+            "reduce_max all axes": lambda: orc.reduce_full(xc, 2),
+            "argmax axis 1": lambda: orc.argmax_axis(xc, rs, R, 1),
+            "x + b (rows)": lambda: orc.broadcast(xc, bc, 0, 2, [rs, R], [R, 1], [0, 1]),
+        }
         for name, fn, nbytes in cases:
             ms = timed(fn, 10 * nset)
             gbs = nbytes / (ms / 1e3) / 1e9
+            cpu = cpu_est(cpu_fns[name], R / rs, 1, f"{rs} of {R} rows, scaled x{R // rs}")
             emit(workload=f"{name} [4096,4096]", dtype=str(dt).split(".")[-1], us_per_call=ms * 1e3,
                  gbs=gbs, frac_of_hbm=gbs / peak, bytes_per_call=nbytes,
                  l2=f"{nset} rotating copies of the {R * R * es >> 20} MiB input (and output): "
-                    "each call's data is out of L2")
+                    "each call's data is out of L2", cpu_baseline=cpu)
         del x, xs, o_fulls
         torch.cuda.empty_cache()
 
@@ -638,19 +675,22 @@ def suite(args):
 
                 ms = timed(call, 8)
                 gbs = n * es / (ms / 1e3) / 1e9
+                ns = 1 << 22
+                cfn = orc.random_f32 if code == 0 else orc.random_f64
+                cpu = cpu_est(lambda: cfn(ns, 7, dist), n / ns, 1, f"{ns} elements, scaled x{n // ns}")
                 emit(workload=f"philox random {dname}", dtype=name, n=n, us_per_call=ms * 1e3,
                      gbs=gbs, frac_of_hbm=gbs / peak, bytes_per_call=n * es,
-                     l2="two alternating outputs of 256/512 MB (larger than L2)")
+                     l2="two alternating outputs of 256/512 MB (larger than L2)", cpu_baseline=cpu)
             del outs
             torch.cuda.empty_cache()
 
     # -- transpose, cast, logsumexp, HMC primitives, host transfers ---------------------------
     if "misc" in want:
-        def hbm_line(name, dtype, fn, nbytes, reps=10, **extra):
+        def hbm_line(name, dtype, fn, nbytes, cpu, reps=10, **extra):
             ms = timed(fn, reps)
             gbs = nbytes / (ms / 1e3) / 1e9
             emit(workload=name, dtype=dtype, us_per_call=ms * 1e3, gbs=gbs, frac_of_hbm=gbs / peak,
-                 bytes_per_call=nbytes, **extra)
+                 bytes_per_call=nbytes, cpu_baseline=cpu, **extra)
 
         # 2-D transpose, 256 MiB in and out
         for dt, name, spv_t, (m, n) in ((torch.float32, "float32", "transpose.spv", (8192, 8192)),
@@ -660,8 +700,10 @@ def suite(args):
             o = torch.empty(m * n, dtype=dt, device=dev)
             ha, ho = wrap(a), wrap(o)
             sp = nxv.shader_path(spv_t)
+            tc = crng.normal(size=(m // 4) * n).astype(np.float32 if es == 4 else np.float64)
+            cpu = cpu_est(lambda: orc.transpose(tc, m // 4, n), 4, 1, f"{m // 4} x {n}, scaled x4")
             hbm_line(f"transpose [{m},{n}]", name,
-                     lambda: ck(lib.nxv_transpose(ho, ha, m, n, sp)), 2 * m * n * es)
+                     lambda: ck(lib.nxv_transpose(ho, ha, m, n, sp)), 2 * m * n * es, cpu)
             del a, o
         # casts, 2^26 elements
         n = 1 << 26
@@ -669,8 +711,12 @@ def suite(args):
         a64 = torch.empty(n, dtype=torch.float64, device=dev)
         h32, h64 = wrap(a32), wrap(a64)
         up_spv, down_spv = nxv.shader_path("cast_f32_to_f64.spv"), nxv.shader_path("cast_f64_to_f32.spv")
-        hbm_line("cast f32 -> f64 [2^26]", "float32", lambda: ck(lib.nxv_cast(h64, h32, n, up_spv)), n * 12)
-        hbm_line("cast f64 -> f32 [2^26]", "float64", lambda: ck(lib.nxv_cast(h32, h64, n, down_spv)), n * 12)
+        c32 = crng.normal(size=1 << 22).astype(np.float32)
+        c64 = c32.astype(np.float64)
+        hbm_line("cast f32 -> f64 [2^26]", "float32", lambda: ck(lib.nxv_cast(h64, h32, n, up_spv)), n * 12,
+                 cpu_est(lambda: c32.astype(np.float64), 16, 1, "numpy astype of 2^22 elements, scaled x16"))
+        hbm_line("cast f64 -> f32 [2^26]", "float64", lambda: ck(lib.nxv_cast(h32, h64, n, down_spv)), n * 12,
+                 cpu_est(lambda: c64.astype(np.float32), 16, 1, "numpy astype of 2^22 elements, scaled x16"))
         del a32, a64
         # logsumexp over axis 1 of [4096, 4096] f32, 3 rotating copies (out of L2)
         R = 4096
@@ -686,8 +732,10 @@ def suite(args):
             k[0] += 1
             ck(lib.nxv_reduce_axis(ho, hxs[i], R, R, 1, 0, lse_spv))
 
-        hbm_line("logsumexp axis 1 [4096,4096]", "float32", lse, R * R * 4 + R * 4, reps=30,
-                 math="f64 exp/log per element")
+        lc = xs[0][: 256 * R].cpu().numpy()
+        hbm_line("logsumexp axis 1 [4096,4096]", "float32", lse, R * R * 4 + R * 4,
+                 cpu_est(lambda: orc.logsumexp(lc, 256, R, 1), 16, 1, "256 of 4096 rows, scaled x16"),
+                 reps=30, math="f32 exp, double sums (NXV_EXACT_F32=1: f64 exp)")
         del xs
         # HMC primitives (f32, the reference's kinetic_energy.spv / normal_logpdf.spv)
         n = 1 << 26
@@ -696,14 +744,19 @@ def suite(args):
         part = torch.empty((n + 255) // 256, dtype=torch.float32, device=dev)
         hp, hm, hpart = wrap(pv), wrap(mv), wrap(part)
         ke_spv = nxv.shader_path("kinetic_energy.spv")
+        kp = crng.normal(size=1 << 22).astype(np.float32)
+        km = (crng.random(1 << 22) + 0.5).astype(np.float32)
         hbm_line("kinetic_energy [2^26] (per-256 partials)", "float32",
-                 lambda: ck(lib.nxv_kinetic_energy(hpart, hp, hm, n, ke_spv)), 2 * n * 4 + (n // 256) * 4)
+                 lambda: ck(lib.nxv_kinetic_energy(hpart, hp, hm, n, ke_spv)), 2 * n * 4 + (n // 256) * 4,
+                 cpu_est(lambda: orc.kinetic_energy(kp, km), 16, 1, "2^22 elements, scaled x16"))
         n2 = 1 << 24
         xv, muv, sv, ov = (torch.rand(n2, dtype=torch.float32, device=dev) + 0.5 for _ in range(4))
         hx2, hmu, hs2, ho2 = wrap(xv), wrap(muv), wrap(sv), wrap(ov)
         lp_spv = nxv.shader_path("normal_logpdf.spv")
+        lx, lmu, ls = ((crng.random(1 << 22) + 0.5).astype(np.float32) for _ in range(3))
         hbm_line("normal_logpdf [2^24]", "float32",
-                 lambda: ck(lib.nxv_normal_logpdf(ho2, hx2, hmu, hs2, n2, lp_spv)), 4 * n2 * 4)
+                 lambda: ck(lib.nxv_normal_logpdf(ho2, hx2, hmu, hs2, n2, lp_spv)), 4 * n2 * 4,
+                 cpu_est(lambda: orc.normal_logpdf(lx, lmu, ls), 4, 1, "2^22 elements, scaled x4"))
         del pv, mv, part, xv, muv, sv, ov
         torch.cuda.empty_cache()
         # host <-> device through the C ABI (256 MiB): pinned copies directly,
@@ -745,7 +798,11 @@ def suite(args):
         ms_cublas = timed(lambda: torch.matmul(a, b, out=c), 10)
         flops = 2 * N ** 3
         cub[code] = flops / (ms_cublas / 1e3) / 1e12
-        emit(workload=f"matmul {N}x{N}x{N}", dtype=str(dt).split(".")[-1],
+        ms_ = 512
+        ca = crng.normal(size=ms_ * ms_).astype(np.float32 if code == 0 else np.float64)
+        cpu = cpu_est(lambda: orc.matmul(ca, ca, ms_, ms_, ms_), (N / ms_) ** 3, nthr,
+                      f"{ms_}^3 (OpenMP), scaled by flops x{(N // ms_) ** 3}")
+        emit(cpu_baseline=cpu, workload=f"matmul {N}x{N}x{N}", dtype=str(dt).split(".")[-1],
              kernel="DMMA mma.sync f64" if code == 1 else "3xTF32 tcgen05 (TMEM accumulator, TMA 128B-swizzled tiles)",
              ms=ms, tflops=flops / (ms / 1e3) / 1e12, cublas_ms=ms_cublas, cublas_tflops=cub[code],
              frac_of_cublas=ms_cublas / ms)
@@ -758,7 +815,10 @@ def suite(args):
                                                      nxv.shader_path("matmul_batched.spv"))), 10)
         ms_cublas = timed(lambda: torch.bmm(a, b, out=c), 10)
         flops = 64 * 2 * 256 ** 3
-        emit(workload="batched matmul 64 x 256^3", dtype="float64", ms=ms, tflops=flops / (ms / 1e3) / 1e12,
+        cb = crng.normal(size=4 * 256 * 256)
+        cpu = cpu_est(lambda: orc.matmul(cb, cb, 256, 256, 256, batch=4), 16, nthr,
+                      "4 of 64 batches (OpenMP), scaled x16")
+        emit(cpu_baseline=cpu, workload="batched matmul 64 x 256^3", dtype="float64", ms=ms, tflops=flops / (ms / 1e3) / 1e12,
              cublas_ms=ms_cublas, cublas_tflops=flops / (ms_cublas / 1e3) / 1e12, frac_of_cublas=ms_cublas / ms)
 
     # -- logistic-regression leapfrog -----------------------------------------------------------
@@ -777,7 +837,11 @@ def suite(args):
         lspv = nxv.shader_path("leapfrog_logreg_f64_batched.spv")
         ms = timed(lambda: ck(lib.nxv_leapfrog_logreg_f64_batched(*hs, Nobs, Dm, Cc, Lr, 0.002, lspv)), 3)
         flops = (Lr + 1) * 2 * 2 * Cc * Dm * Nobs
-        emit(workload="logistic-regression leapfrog, 256 chains, X[10000,100], L=16 (one trajectory)",
+        qs, ps = np.zeros((16, Dm)), r.normal(size=(16, Dm))
+        cpu = cpu_est(lambda: orc.chain_logreg_f64(qs, ps, X, y, Nobs, Dm, 16, 1, 0.002, nthreads=nthr),
+                      (Cc / 16) * (Lr + 1) / 2, nthr,
+                      "16 chains x 1 step (2 gradients, OpenMP over chains), scaled to 256 chains x 17 gradients")
+        emit(cpu_baseline=cpu, workload="logistic-regression leapfrog, 256 chains, X[10000,100], L=16 (one trajectory)",
              dtype="float64", ms_per_trajectory=ms, chain_steps_per_s=Cc * Lr / (ms / 1e3),
              gemm_tflops=flops / (ms / 1e3) / 1e12, dgemm_cublas_tflops=cub.get(1),
              seconds_for_1000_trajectories=ms)
