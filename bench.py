@@ -11,8 +11,12 @@ reference contract's q/p/grad trajectories [chain][k][i] and logp [chain][k].
          event pair on the launching stream around all timed steps (and the
          collectives), three rotating input sets larger than L2 together.
   e2e    the same metric through the C ABI with host buffers: every step
-         uploads q0/p0/inv_mass/prec from pinned host memory and downloads the
-         four outputs into pinned host memory (nxv_buf_upload/_download).
+         uploads q0/p0/inv_mass/prec from pinned host memory, runs the chain
+         and reads the step's result -- the per-step logp of every chain --
+         back into pinned host memory (nxv_buf_upload/_download); the
+         trajectories stay in their device buffers, as the reference API
+         returns them.  `e2e_full_download` also brings the q/p/grad
+         trajectories (3.2 GB per step) to the host: PCIe-bound.
   roofline  algorithmic bytes of one call / its measured duration, against
          the measured HBM copy bandwidth (MEASURED_PEAKS.json).
   cpu_baseline  the oracle (C restatement, OpenMP over all host cores) on a
@@ -75,8 +79,17 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """SM clock and clock-event reasons sampled during the timed region.
 
+    NVML (nvidia_ml_py) is read from a background thread every 2 ms -- the
+    timed region can be a few milliseconds, shorter than nvidia-smi's
+    sampling interval -- with one sample on entry and one on exit.  Without
+    NVML, nvidia-smi -lms 200 is the fallback.  Read-only: no setting of the
+    GPU is changed."""
+
+    # NVML clocks-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -84,9 +97,48 @@ class Clocks:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.nvml = None
+        self.samples = []  # (sm_mhz, reason bits)
+        self.smax = None
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"nxv_clocks_{os.getpid()}.csv"
 
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:  # the CUDA device's own GPU, whatever CUDA_VISIBLE_DEVICES maps
+            import torch
+            u = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + u).encode())
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _sample(self):
+        nv, h = self.nvml
+        clk = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        try:
+            rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        except AttributeError:
+            rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+        self.samples.append((float(clk), int(rs)))
+
     def __enter__(self):
+        import threading
+        try:
+            self.nvml = self._nvml_handle()
+            nv, h = self.nvml
+            self.smax = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._sample()
+            self.stop = threading.Event()
+
+            def run():
+                while not self.stop.wait(0.002):
+                    self._sample()
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
@@ -98,6 +150,11 @@ class Clocks:
         return self
 
     def __exit__(self, *a):
+        if self.nvml:
+            self.stop.set()
+            self.thread.join()
+            self._sample()
+            return
         if self.proc:
             self.proc.terminate()
             try:
@@ -107,6 +164,11 @@ class Clocks:
             self.f.close()
 
     def summary(self):
+        if self.nvml:
+            sm = [c for c, _ in self.samples]
+            reasons = sorted({nm for _, r in self.samples for nm, bit in self.REASONS.items() if r & bit})
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
+                    "reasons": reasons, "samples": len(sm), "source": "NVML every 2 ms"}
         if not self.path.exists():
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, smax, reasons = [], None, set()
@@ -125,7 +187,7 @@ class Clocks:
                     reasons.add(nm)
         self.path.unlink(missing_ok=True)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi -lms 200"}
 
 
 def host_threads():
@@ -329,7 +391,7 @@ def main():
     traffic = (24633856 + 729063680) / 1024 * chains if (D, L) == (1000, 32) else None
 
     # e2e through the C ABI with host buffers (library-owned device buffers).
-    e2e = None
+    e2e = e2e_full = None
     if not args.no_e2e:
         lib.nxv_set_stream(None)
         hb_in = [torch.from_numpy(a.reshape(-1)).pin_memory() for a in (q0, p0, m, prec)]
@@ -337,33 +399,42 @@ def main():
         d_in = [lib.nxv_buf_alloc(t.numel() * 8) for t in hb_in]
         d_out = [lib.nxv_buf_alloc(t.numel() * 8) for t in hb_out]
 
-        def e2e_step():
+        def e2e_step(full):
             for h, t in zip(d_in, hb_in):
                 assert lib.nxv_buf_upload(h, C.c_void_p(t.data_ptr()), t.numel() * 8) == 0
             rc = lib.nxv_leapfrog_chain_gauss_f64_batched(*d_out, *d_in, D, chains, L, EPS, 0.0, spv)
             assert rc == 0, _native.last_error()
-            for h, t in zip(d_out, hb_out):
+            pairs = list(zip(d_out, hb_out)) if full else [(d_out[3], hb_out[3])]  # [3] = logp
+            for h, t in pairs:
                 assert lib.nxv_buf_download(h, C.c_void_p(t.data_ptr()), t.numel() * 8) == 0
 
-        for _ in range(2):
-            e2e_step()
-        n_e2e = max(3, min(args.steps, 5))
-        if world > 1:
-            dist.barrier()
-        t0 = time.perf_counter()
-        for _ in range(n_e2e):
-            e2e_step()
-        el = time.perf_counter() - t0
-        el_t = torch.tensor([el], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(el_t, op=dist.ReduceOp.MAX)
-        el = float(el_t.item())
+        def e2e_run(full):
+            for _ in range(2):
+                e2e_step(full)
+            n_e2e = max(3, min(args.steps, 5)) if full else max(5, args.steps)
+            if world > 1:
+                dist.barrier()
+            t0 = time.perf_counter()
+            for _ in range(n_e2e):
+                e2e_step(full)
+            el = time.perf_counter() - t0
+            el_t = torch.tensor([el], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(el_t, op=dist.ReduceOp.MAX)
+            el = float(el_t.item())
+            down = hb_out if full else [hb_out[3]]
+            return {"value": world * chains * L * n_e2e / el, "unit": UNIT,
+                    "h2d_bytes_per_step": sum(t.numel() * 8 for t in hb_in),
+                    "d2h_bytes_per_step": sum(t.numel() * 8 for t in down),
+                    "steps": n_e2e,
+                    "timing": "host wall clock around synchronous C-ABI calls, max over ranks"}
+
+        e2e = e2e_run(False)
+        e2e["result_read"] = "per-step logp [chain][k] (the metric); trajectories stay on the device"
+        e2e_full = e2e_run(True)
+        e2e_full["result_read"] = "all four outputs: q/p/grad trajectories and logp"
         for h in d_in + d_out:
             lib.nxv_buf_free(h)
-        e2e = {"value": world * chains * L * n_e2e / el, "unit": UNIT,
-               "h2d_bytes_per_step": sum(t.numel() * 8 for t in hb_in),
-               "d2h_bytes_per_step": sum(t.numel() * 8 for t in hb_out),
-               "steps": n_e2e, "timing": "host wall clock around synchronous C-ABI calls, max over ranks"}
         lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
 
     secondary = None
@@ -400,6 +471,7 @@ def main():
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json), copy, of measured"},
             "clocks": clocks,
             "e2e": e2e,
+            "e2e_full_download": e2e_full,
             "cpu_baseline": cpu,
         }
         if secondary:
