@@ -113,13 +113,14 @@ __device__ __forceinline__ void z_block(double (&z)[NZ][4], const double* qa, co
 // (row g, col tig); xr: this lane's B element (tile row tig, col g).
 template <int DT, int BN, int DS, int RS, bool FULL>
 __device__ __forceinline__ void g_block(double (&gacc)[DT][4], const double* rw, const double* xr,
-                                        int kv) {
+                                        int kv, int ncnt) {
 #pragma unroll
     for (int kk = 0; kk < BN; kk += 4) {
         if (FULL || kk < kv) {
             const double a0 = rw[kk], a1 = rw[8 * RS + kk];
 #pragma unroll
-            for (int n = 0; n < DT; n++) dmma4(gacc[n], a0, a1, xr[kk * DS + n * 8]);
+            for (int n = 0; n < DT; n++)
+                if (n < ncnt) dmma4(gacc[n], a0, a1, xr[kk * DS + n * 8]);
         }
     }
 }
@@ -127,14 +128,21 @@ __device__ __forceinline__ void g_block(double (&gacc)[DT][4], const double* rw,
 // part[s][c][d] = sum over j in slice s of R[c][j] X[j][d];
 // lpart[c][s] = sum over j in slice s of (y_j z_cj - softplus(z_cj)).
 // vecX: X rows are 16-byte aligned (D even, X aligned) and use cp.async.
-template <int DT, int NW, int BN_>
-__global__ void __launch_bounds__(32 * NW, 8 / NW)
+// SPLIT warps share each 16-chain block: warp w serves block w % NW as part
+// wh = w / NW, taking observation tiles [wh NZW, wh NZW + NZW) of Z and
+// model-dimension tiles [wh DTW, ...) of G; with SPLIT = 2 a named barrier
+// per block orders the two warps' R writes before either reads R.
+template <int DT, int NW, int BN_, int SPLIT>
+__global__ void __launch_bounds__(32 * NW * SPLIT, SPLIT == 1 ? 8 / NW : 1)
 k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
           const double* __restrict__ y, double* __restrict__ part, double* __restrict__ lpart,
           unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S, int vecX) {
     using G = LrCfg<DT, NW, BN_>;
-    constexpr int BN = G::BN, DS = G::DS, RS = G::RS, DP = G::DP, NT = G::NT;
-    constexpr int NZ = BN / 8;  // 8-observation tiles of Z per warp
+    constexpr int BN = G::BN, DS = G::DS, RS = G::RS, DP = G::DP, NT = G::NT * SPLIT;
+    constexpr int NZ = BN / 8;              // 8-observation tiles of Z per chain block
+    constexpr int NZW = NZ / SPLIT;         // ... per warp
+    constexpr int DTW = (DT + SPLIT - 1) / SPLIT;  // 8-wide tiles of G per warp
+    static_assert(NZ % SPLIT == 0, "SPLIT must divide the Z tiles");
     extern __shared__ __align__(16) double lr_smem[];
     double* Qs = lr_smem + G::Q_OFF;
     double* Xs = lr_smem + G::X_OFF;
@@ -146,6 +154,10 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
     const unsigned j1 = min(n_obs, j0 + L);
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
+    const int pr = warp % NW, wh = warp / NW;    // chain block, part
+    const int zoff = wh * NZW;                   // first Z observation tile
+    const int nbase = wh * DTW;                  // first G tile
+    const int ncnt = DT - nbase < DTW ? DT - nbase : DTW;
 
     // Both X buffers start as zeros: the padded columns [D, DP) stay zero and
     // rows past a partial tile hold finite values (R is zero there).
@@ -194,16 +206,16 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
         }
     };
 
-    double gacc[DT][4];
+    double gacc[DTW][4];
 #pragma unroll
-    for (int t = 0; t < DT; t++)
+    for (int t = 0; t < DTW; t++)
 #pragma unroll
         for (int e = 0; e < 4; e++) gacc[t][e] = 0.0;
     // logp of rows g and g + 8: sum of y z - max(z, 0), running product of
     // den and the sum of its flushed logs
     double lsum[2] = {0.0, 0.0}, lprod[2] = {1.0, 1.0}, llog[2] = {0.0, 0.0};
-    const double* qa = Qs + (warp * 16 + g) * DS + tig;
-    double* rw = Rs + warp * 16 * RS;
+    const double* qa = Qs + (pr * 16 + g) * DS + tig;
+    double* rw = Rs + pr * 16 * RS;
 
     load_x(0, 0);
     cp_commit();
@@ -217,16 +229,17 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
         const unsigned valid = min((unsigned)BN, j1 - jt);
         const unsigned ntz = (valid + 7) >> 3;  // 8-observation tiles holding data
 
-        // Z block (16 chains x 32 observations) = Q . X_tile^T over DP.
-        double z[NZ][4];
+        // Z block (16 chains x this warp's observation tiles) = Q . X_tile^T.
+        double z[NZW][4];
 #pragma unroll
-        for (int n = 0; n < NZ; n++)
+        for (int n = 0; n < NZW; n++)
 #pragma unroll
             for (int e = 0; e < 4; e++) z[n][e] = 0.0;
-        if (ntz == NZ)
-            z_block<NZ, DP, DS, true>(z, qa, xb + g * DS + tig, ntz);
+        const int ntzw = min(max((int)ntz - zoff, 0), NZW);
+        if (ntzw == NZW)
+            z_block<NZW, DP, DS, true>(z, qa, xb + (zoff * 8 + g) * DS + tig, ntzw);
         else
-            z_block<NZ, DP, DS, false>(z, qa, xb + g * DS + tig, ntz);
+            z_block<NZW, DP, DS, false>(z, qa, xb + (zoff * 8 + g) * DS + tig, ntzw);
 
         // R = y - sigmoid(Z) into this warp's rows of Rs (zero past the slice),
         // with e = exp(-|z|), den = 1 + e in [1, 2], sigmoid(z) = (z >= 0 ? 1 : e)
@@ -238,33 +251,33 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
         const double* yb = Ys + (t & 1) * BN;
 #pragma unroll
         for (int h = 0; h < 2; h++) {
-            double ev[2 * NZ], dn[2 * NZ], pf[2 * NZ], rc[2 * NZ];
+            double ev[2 * NZW], dn[2 * NZW], pf[2 * NZW], rc[2 * NZW];
 #pragma unroll
-            for (int n = 0; n < NZ; n++)
+            for (int n = 0; n < NZW; n++)
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
                     const int i = 2 * n + e;
-                    const bool ok = (unsigned)(n * 8 + 2 * tig + e) < valid;
+                    const bool ok = (unsigned)((zoff + n) * 8 + 2 * tig + e) < valid;
                     ev[i] = ok ? exp(-fabs(z[n][2 * h + e])) : 0.0;
                     dn[i] = add_(1.0, ev[i]);
                 }
             pf[0] = dn[0];
 #pragma unroll
-            for (int i = 1; i < 2 * NZ; i++) pf[i] = mul_(pf[i - 1], dn[i]);
-            double inv = div_(1.0, pf[2 * NZ - 1]);
+            for (int i = 1; i < 2 * NZW; i++) pf[i] = mul_(pf[i - 1], dn[i]);
+            double inv = div_(1.0, pf[2 * NZW - 1]);
 #pragma unroll
-            for (int i = 2 * NZ - 1; i > 0; i--) {
+            for (int i = 2 * NZW - 1; i > 0; i--) {
                 rc[i] = mul_(inv, pf[i - 1]);
                 inv = mul_(inv, dn[i]);
             }
             rc[0] = inv;
-            lprod[h] = mul_(lprod[h], pf[2 * NZ - 1]);
+            lprod[h] = mul_(lprod[h], pf[2 * NZW - 1]);
 #pragma unroll
-            for (int n = 0; n < NZ; n++)
+            for (int n = 0; n < NZW; n++)
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
                     const int i = 2 * n + e;
-                    const unsigned col = n * 8 + 2 * tig + e;
+                    const unsigned col = (zoff + n) * 8 + 2 * tig + e;
                     double r = 0.0;
                     if (col < valid) {
                         const double zz = z[n][2 * h + e], yj = yb[col];
@@ -278,14 +291,18 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
                 lprod[h] = 1.0;
             }
         }
-        __syncwarp();
-
-        // G block (16 chains x DP) += R . X_tile over the tile's observations.
-        const int kv = (int)((valid + 3) >> 2) << 2;
-        if (kv == BN)
-            g_block<DT, BN, DS, RS, true>(gacc, rw + g * RS + tig, xb + tig * DS + g, kv);
+        if constexpr (SPLIT == 2)  // both warps of the block have written their R columns
+            asm volatile("bar.sync %0, %1;" ::"r"(pr + 1), "r"(64) : "memory");
         else
-            g_block<DT, BN, DS, RS, false>(gacc, rw + g * RS + tig, xb + tig * DS + g, kv);
+            __syncwarp();
+
+        // G block (16 chains x this warp's model tiles) += R . X_tile.
+        const int kv = (int)((valid + 3) >> 2) << 2;
+        const double* xr = xb + tig * DS + g + nbase * 8;
+        if (kv == BN)
+            g_block<DTW, BN, DS, RS, true>(gacc, rw + g * RS + tig, xr, kv, ncnt);
+        else
+            g_block<DTW, BN, DS, RS, false>(gacc, rw + g * RS + tig, xr, kv, ncnt);
         __syncthreads();  // buffer t & 1 and Rs are rewritten next iteration
     }
     cp_wait<0>();
@@ -297,10 +314,11 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
     double* Gs = Qs;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        const int row = warp * 16 + g + 8 * h;
+        const int row = pr * 16 + g + 8 * h;
 #pragma unroll
-        for (int n = 0; n < DT; n++) {
-            const unsigned d = n * 8 + 2 * tig;
+        for (int n = 0; n < DTW; n++) {
+            if (n >= ncnt) continue;
+            const unsigned d = (nbase + n) * 8 + 2 * tig;
             if (vq) {
                 if (d < D)
                     *reinterpret_cast<double2*>(Gs + row * D + d) =
@@ -331,8 +349,19 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
     lp0 = add_(lp0, __shfl_xor_sync(0xffffffffu, lp0, 2));
     lp1 = add_(lp1, __shfl_xor_sync(0xffffffffu, lp1, 1));
     lp1 = add_(lp1, __shfl_xor_sync(0xffffffffu, lp1, 2));
+    if constexpr (SPLIT == 2) {  // part 0 + part 1, in that order
+        __shared__ double lpx[NW][16];
+        if (wh == 1 && tig == 0) {
+            lpx[pr][g] = lp0;
+            lpx[pr][g + 8] = lp1;
+        }
+        __syncthreads();
+        if (wh == 1) return;
+        lp0 = add_(lp0, lpx[pr][g]);
+        lp1 = add_(lp1, lpx[pr][g + 8]);
+    }
     if (tig == 0) {
-        const unsigned ca = c0 + warp * 16 + g, cb = ca + 8;
+        const unsigned ca = c0 + pr * 16 + g, cb = ca + 8;
         if (ca < C) lpart[(size_t)ca * S + s] = lp0;
         if (cb < C) lpart[(size_t)cb * S + s] = lp1;
     }
@@ -461,18 +490,18 @@ k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __re
     }
 }
 
-template <int DT, int NW, int BN>
+template <int DT, int NW, int BN, int SPLIT>
 int launch_lr_grad(Ctx& c, const double* q, const double* X, const double* y, double* part,
                    double* lpart, unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S,
                    int vecX) {
     using G = LrCfg<DT, NW, BN>;
     const size_t smem = G::BYTES;
-    cudaError_t e = cudaFuncSetAttribute(k_lr_grad<DT, NW, BN>,
+    cudaError_t e = cudaFuncSetAttribute(k_lr_grad<DT, NW, BN, SPLIT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_lr_grad)");
     dim3 grid(S, (C + G::BC - 1) / G::BC);
-    k_lr_grad<DT, NW, BN><<<grid, G::NT, smem, c.stream>>>(q, X, y, part, lpart, C, D, n_obs, L, S,
-                                                          vecX);
+    k_lr_grad<DT, NW, BN, SPLIT><<<grid, G::NT * SPLIT, smem, c.stream>>>(
+        q, X, y, part, lpart, C, D, n_obs, L, S, vecX);
     count_launch();
     return OK;
 }
@@ -539,12 +568,16 @@ int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, co
                        Lu = (unsigned)L, Su = (unsigned)S;
         const double* Xd = (const double*)X;
         const double* yd = (const double*)y;
+        const char* sv = getenv("NXV_LR_SPLIT");  // warps per 16-chain block: 1 or 2
+        const int split = (sv && atoi(sv) == 2) ? 2 : 1;
         grad = [=, &c]() -> int {
             if (D <= 32)
-                return launch_lr_grad<4, 8, 32>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+                return launch_lr_grad<4, 8, 32, 1>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
             if (D <= 64)
-                return launch_lr_grad<8, 8, 32>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
-            return launch_lr_grad<13, 8, 32>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+                return launch_lr_grad<8, 8, 32, 1>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+            if (split == 2)
+                return launch_lr_grad<13, 8, 32, 2>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+            return launch_lr_grad<13, 8, 32, 1>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
         };
     } else {
         double* Xt = (double*)(base + oXt);

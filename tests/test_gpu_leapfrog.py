@@ -207,7 +207,9 @@ def test_gauss_full_config(nxv, orc):
     (5, 2, 1, 1), (333, 32, 3, 2), (333, 33, 3, 2), (777, 64, 9, 2), (777, 104, 9, 2),
     # general (two-GEMM) path
     (300, 120, 4, 2)])
-def test_logreg_vs_oracle(nxv, orc, N, D, C, K):
+@pytest.mark.parametrize("split", ["1", "2"])
+def test_logreg_vs_oracle(nxv, orc, monkeypatch, N, D, C, K, split):
+    monkeypatch.setenv("NXV_LR_SPLIT", split)  # warps per 16-chain block in the fused kernel
     r = np.random.default_rng(4)
     X = r.normal(size=(N, D))
     w = r.normal(size=D)
