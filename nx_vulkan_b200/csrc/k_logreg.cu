@@ -10,10 +10,12 @@
 // Fused path (D <= 104): one kernel per gradient.  CTA (s, b) owns chains
 // [128 b, 128 b + 128) and observations [L s, L s + L).  Its Q block stays in
 // shared memory; X streams through in tiles of 32 observations (cp.async,
-// double-buffered).  Per tile, each warp (16 chains) computes its 16 x 32
-// block of Z with DMMA (m16n8k4 f64), turns it into R = y - sigmoid(Z) and
-// the logp terms in registers, parks R in shared memory and accumulates its
-// 16 x D block of G += R . X_tile with DMMA.  Z never leaves the SM; each
+// double-buffered).  Two warps serve each block of 16 chains (16 warps per
+// CTA, at most 128 registers each).  Per tile, each computes a 16 x 16 half
+// of the block's Z with DMMA (m16n8k4 f64), turns it into R = y - sigmoid(Z)
+// and the logp terms in registers and parks R in shared memory; after a
+// named barrier of the pair each accumulates half of the block's 16 x D
+// G += R . X_tile with DMMA.  Z never leaves the SM; each
 // CTA writes one G partial and one logp partial per chain.  A fold kernel
 // (one CTA per chain) sums the partials in slice order (deterministic),
 // subtracts q, completes the step (final half-kick, trajectory writes,
@@ -568,15 +570,23 @@ int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, co
                        Lu = (unsigned)L, Su = (unsigned)S;
         const double* Xd = (const double*)X;
         const double* yd = (const double*)y;
-        const char* sv = getenv("NXV_LR_SPLIT");  // warps per 16-chain block: 1 or 2
-        const int split = (sv && atoi(sv) == 2) ? 2 : 1;
+        // warps per 16-chain block: 2 by default (0.955 vs 1.042 ms per
+        // trajectory of the 256-chain X[10000,100] workload); NXV_LR_SPLIT=1
+        // selects one warp per block.
+        const char* sv = getenv("NXV_LR_SPLIT");
+        const int split = (sv && atoi(sv) == 1) ? 1 : 2;
         grad = [=, &c]() -> int {
+            if (split == 2) {
+                if (D <= 32)
+                    return launch_lr_grad<4, 8, 32, 2>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+                if (D <= 64)
+                    return launch_lr_grad<8, 8, 32, 2>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+                return launch_lr_grad<13, 8, 32, 2>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
+            }
             if (D <= 32)
                 return launch_lr_grad<4, 8, 32, 1>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
             if (D <= 64)
                 return launch_lr_grad<8, 8, 32, 1>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
-            if (split == 2)
-                return launch_lr_grad<13, 8, 32, 2>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
             return launch_lr_grad<13, 8, 32, 1>(c, q, Xd, yd, part, lp, Cu, Du, Nu, Lu, Su, vecX);
         };
     } else {
