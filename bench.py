@@ -260,10 +260,10 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--suite", action="store_true",
                     help="measure every hot-path workload (one JSON line each) instead of the headline")
-    ap.add_argument("--only", default="fused,reduce,random,misc,matmul,logreg",
+    ap.add_argument("--only", default="fused,reduce,random,misc,matmul,logreg,nuts",
                     help="suite sections to run, comma separated: fused, reduce, random, misc "
                          "(transpose, cast, logsumexp, HMC primitives, host transfers), matmul, "
-                         "logreg")
+                         "logreg, nuts")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -917,6 +917,57 @@ def suite(args):
              dtype="float64", ms_per_trajectory=ms, chain_steps_per_s=Cc * Lr / (ms / 1e3),
              gemm_tflops=flops / (ms / 1e3) / 1e12, dgemm_cublas_tflops=cub.get(1),
              seconds_for_1000_trajectories=ms)
+    # -- NUTS over the speculative chain (the tree builder's call site) --------------------
+    if "nuts" in want:
+        from nx_vulkan_b200 import nuts
+        lib.nxv_set_stream(None)
+
+        class Timed:
+            """Wraps a trajectory source and accumulates the wall time of its calls."""
+
+            def __init__(self, src):
+                self.src, self.sec, self.steps = src, 0.0, 0
+                self.calls = src.calls
+
+            def extend(self, q, p, K):
+                t0 = time.perf_counter()
+                out = self.src.extend(q, p, K)
+                self.sec += time.perf_counter() - t0
+                self.steps += q.shape[0] * K
+                return out
+
+        def run_nuts(src_cls, chains, transitions, d=100, eps=0.05):
+            r = np.random.default_rng(3)
+            prec = r.uniform(0.5, 2.0, d)
+            tg = nuts.GaussianTarget(prec)
+            m = np.ones(d)
+            src = Timed(src_cls(tg, m, eps))
+            q = r.normal(size=(chains, d)) / np.sqrt(prec)
+            rng = np.random.default_rng(4)
+            q, _ = nuts.nuts_transition(src, tg, q, m, rng, max_depth=8)  # warm-up
+            src.sec, src.steps = 0.0, 0
+            depths, t0 = [], time.perf_counter()
+            for _ in range(transitions):
+                q, st = nuts.nuts_transition(src, tg, q, m, rng, max_depth=8)
+                depths.append(float(st.depth.mean()))
+            el = time.perf_counter() - t0
+            return el, src, statistics.mean(depths)
+
+        Cn, Tn = 256, 5
+        el, src, dep = run_nuts(nuts.GpuChain, Cn, Tn)
+        cel, csrc, _ = run_nuts(nuts.OracleChain, 32, 2)
+        cpu_us = cel / 2 * (Cn / 32) * 1e6
+        emit(workload="NUTS transitions, 256 chains, Gaussian d=100, eps=0.05, max depth 8",
+             dtype="float64", us_per_call=el / Tn * 1e6, transitions_per_s=Cn * Tn / el,
+             mean_tree_depth=dep, chain_call_share=src.sec / el,
+             speculative_steps_per_s=src.steps / src.sec if src.sec else None,
+             note="tree logic on the host (numpy), trajectories from the GPU chain with fused KE; "
+                  "call share = fraction of wall time in the chain calls (kernel + transfers)",
+             cpu_baseline={"us_per_call": cpu_us, "kind": "port", "cores": 1,
+                           "sample": "same NUTS driven by the oracle chain, 32 chains x 2 transitions, "
+                                     "scaled to 256 chains"})
+        lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
+
     for h in handles:
         lib.nxv_buf_free(h)
     lib.nxv_set_stream(None)

@@ -132,18 +132,34 @@ def _uturn_free(rho, ps_begin, ps_end):
 def subtree_check(P, PS):
     """Balanced-tree U-turn check over leaves in time order (len a power of
     two).  P: momenta [n, d]; PS: velocities inv_mass * P.  Returns
-    (ok, rho) with rho the summed momentum."""
-    n = P.shape[0]
-    if n == 1:
-        return True, P[0].copy()
-    h = n // 2
-    ok, rho_a = subtree_check(P[:h], PS[:h])
-    if not ok:
-        return False, None
-    ok, rho_b = subtree_check(P[h:], PS[h:])
-    if not ok:
-        return False, None
-    return merge_check(rho_a, rho_b, P[h - 1], PS[0], PS[h - 1], P[h], PS[h], PS[-1])
+    (ok, rho) with rho the summed momentum.  Evaluated level by level: at
+    level j every node of 2^j leaves is the merge of two children A, B, and
+    all of a level's merge tests (merge_check) run as one array operation;
+    the sums pair children exactly as a recursive evaluation would."""
+    n, d = P.shape
+    rho = P
+    size = 1
+    while size < n:
+        size *= 2
+        h = size // 2
+        pair = rho.reshape(-1, 2, d)
+        ra, rb = pair[:, 0], pair[:, 1]
+        first = np.arange(0, n, size)
+        last, a_last, b_first = first + size - 1, first + h - 1, first + h
+        r = ra + rb
+        ea = ra + P[b_first]
+        eb = rb + P[a_last]
+
+        def dot(x, y):
+            return np.einsum("ij,ij->i", x, y)
+
+        ok = ((dot(PS[first], r) > 0) & (dot(PS[last], r) > 0)
+              & (dot(PS[first], ea) > 0) & (dot(PS[b_first], ea) > 0)
+              & (dot(PS[a_last], eb) > 0) & (dot(PS[last], eb) > 0))
+        if not ok.all():
+            return False, None
+        rho = r
+    return True, rho[0].copy()
 
 
 def merge_check(rho_a, rho_b, p_a_last, ps_a_first, ps_a_last, p_b_first, ps_b_first, ps_b_last):
