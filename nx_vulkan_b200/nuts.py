@@ -125,53 +125,48 @@ class GpuChain:
                 self._down(lh, c * K).reshape(c, K), self._down(kh, c * K).reshape(c, K))
 
 
-def _uturn_free(rho, ps_begin, ps_end):
-    return float(ps_begin @ rho) > 0.0 and float(ps_end @ rho) > 0.0
+def _dot(x, y):
+    return np.einsum("...i,...i->...", x, y)
+
+
+def _free(rho, ps_begin, ps_end):
+    """No U-turn: both end velocities have a positive projection on rho."""
+    return (_dot(ps_begin, rho) > 0) & (_dot(ps_end, rho) > 0)
+
+
+def merge_check(rho_a, rho_b, p_a_last, ps_a_first, ps_a_last, p_b_first, ps_b_first, ps_b_last):
+    """U-turn tests when subtree A (earlier in time) and B merge; every
+    argument may carry leading batch axes.  Returns (ok, rho_a + rho_b)."""
+    rho = rho_a + rho_b
+    ok = (_free(rho, ps_a_first, ps_b_last) & _free(rho_a + p_b_first, ps_a_first, ps_b_first)
+          & _free(rho_b + p_a_last, ps_a_last, ps_b_last))
+    return ok, rho
 
 
 def subtree_check(P, PS):
-    """Balanced-tree U-turn check over leaves in time order (len a power of
-    two).  P: momenta [n, d]; PS: velocities inv_mass * P.  Returns
-    (ok, rho) with rho the summed momentum.  Evaluated level by level: at
-    level j every node of 2^j leaves is the merge of two children A, B, and
-    all of a level's merge tests (merge_check) run as one array operation;
-    the sums pair children exactly as a recursive evaluation would."""
-    n, d = P.shape
+    """Balanced-tree U-turn check over leaves in time order.  P: momenta
+    [..., n, d] with n a power of two; PS: velocities inv_mass * P.  Returns
+    (ok [...], rho [..., d]), rho the summed momentum.  Evaluated level by
+    level: at level j every node of 2^j leaves is the merge of its two
+    children, and all of a level's merge tests run as one array operation;
+    the sums pair children as a recursive evaluation would."""
+    P, PS = np.asarray(P), np.asarray(PS)
+    n, d = P.shape[-2:]
+    lead = P.shape[:-2]
+    ok = np.ones(lead, bool)
     rho = P
     size = 1
     while size < n:
         size *= 2
         h = size // 2
-        pair = rho.reshape(-1, 2, d)
-        ra, rb = pair[:, 0], pair[:, 1]
+        pair = rho.reshape(lead + (n // size, 2, d))
+        ra, rb = pair[..., 0, :], pair[..., 1, :]
         first = np.arange(0, n, size)
         last, a_last, b_first = first + size - 1, first + h - 1, first + h
-        r = ra + rb
-        ea = ra + P[b_first]
-        eb = rb + P[a_last]
-
-        def dot(x, y):
-            return np.einsum("ij,ij->i", x, y)
-
-        ok = ((dot(PS[first], r) > 0) & (dot(PS[last], r) > 0)
-              & (dot(PS[first], ea) > 0) & (dot(PS[b_first], ea) > 0)
-              & (dot(PS[a_last], eb) > 0) & (dot(PS[last], eb) > 0))
-        if not ok.all():
-            return False, None
-        rho = r
-    return True, rho[0].copy()
-
-
-def merge_check(rho_a, rho_b, p_a_last, ps_a_first, ps_a_last, p_b_first, ps_b_first, ps_b_last):
-    """U-turn tests when subtree A (earlier in time) and B merge."""
-    rho = rho_a + rho_b
-    if not _uturn_free(rho, ps_a_first, ps_b_last):
-        return False, None
-    if not _uturn_free(rho_a + p_b_first, ps_a_first, ps_b_first):
-        return False, None
-    if not _uturn_free(rho_b + p_a_last, ps_a_last, ps_b_last):
-        return False, None
-    return True, rho
+        good, rho = merge_check(ra, rb, P[..., a_last, :], PS[..., first, :], PS[..., a_last, :],
+                                P[..., b_first, :], PS[..., b_first, :], PS[..., last, :])
+        ok &= good.all(axis=-1)
+    return ok, rho[..., 0, :]
 
 
 @dataclass
@@ -182,30 +177,27 @@ class Stats:
     energy: np.ndarray       # H of the initial point
 
 
-def _logsumexp(v):
-    m = float(np.max(v))
-    return m + math.log(float(np.exp(v - m).sum()))
-
-
 def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth=10):
     """One NUTS transition for every chain of q0 [C, d]; returns (q, Stats).
 
     Leaves are drawn from `source` with speculative extension: all chains that
     need more steps at a tree level share one batched call of
-    speculative_steps(2^depth) steps."""
+    speculative_steps(2^depth) steps.  The tree logic is vectorized over the
+    chains that are still building."""
     q0 = np.asarray(q0, np.float64)
     C, d = q0.shape
     m = np.asarray(inv_mass, np.float64)
     p0 = rng.standard_normal((C, d)) / np.sqrt(m)
     H0 = -target.logp(q0) + 0.5 * ((p0 * p0) * m).sum(axis=-1)
-    # per chain: cached leaves beyond the initial point, index 0 = first step
+    # per chain and direction: leaves beyond the initial point, index 0 = first step
     cache = {+1: [None] * C, -1: [None] * C}   # dict of arrays q, p, logp, ke
     used = {+1: np.zeros(C, np.int64), -1: np.zeros(C, np.int64)}
-    # tree state
     sample = q0.copy()
     logw = -H0.copy()
     rho = p0.copy()
-    ends = {+1: (p0.copy(), p0 * m), -1: (p0.copy(), p0 * m)}  # (p, p#) at each end
+    # momentum and velocity at the tree's left (-1) and right (+1) ends
+    end_p = {+1: p0.copy(), -1: p0.copy()}
+    end_ps = {+1: p0 * m, -1: p0 * m}
     active = np.ones(C, bool)
     depth = np.zeros(C, np.int64)
     divergent = np.zeros(C, bool)
@@ -215,9 +207,10 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
         n_new = 1 << level
         dirs = np.where(rng.random(C) < 0.5, -1, 1)
         # speculative extension: one batched call for every chain short of leaves
-        need = [c for c in range(C) if active[c]
-                and (0 if cache[dirs[c]][c] is None else cache[dirs[c]][c]["q"].shape[0])
-                < used[dirs[c]][c] + n_new]
+        def have(c):
+            cc = cache[dirs[c]][c]
+            return 0 if cc is None else cc["q"].shape[0]
+        need = [c for c in range(C) if active[c] and have(c) < used[dirs[c]][c] + n_new]
         if need:
             K = speculative_steps(n_new)
             qs, ps = np.empty((len(need), d)), np.empty((len(need), d))
@@ -232,48 +225,59 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
                 new = {"q": qk[i], "p": dd * pk[i], "logp": lk[i], "ke": kk[i]}
                 cc = cache[dd][c]
                 cache[dd][c] = new if cc is None else {k: np.concatenate([cc[k], new[k]]) for k in cc}
-        for c in range(C):
-            if not active[c]:
-                continue
+        # the level's new leaves of every active chain, in time order
+        act = np.flatnonzero(active)
+        A = act.size
+        Q, P = np.empty((A, n_new, d)), np.empty((A, n_new, d))
+        H = np.empty((A, n_new))
+        for i, c in enumerate(act):
             dd = dirs[c]
             cc = cache[dd][c]
             a, b = used[dd][c], used[dd][c] + n_new
-            Q, P = cc["q"][a:b], cc["p"][a:b]
-            H = -cc["logp"][a:b] + cc["ke"][a:b]
+            sl = slice(None) if dd > 0 else slice(None, None, -1)  # backward leaves run leftward
+            Q[i], P[i] = cc["q"][a:b][sl], cc["p"][a:b][sl]
+            H[i] = (-cc["logp"][a:b] + cc["ke"][a:b])[sl]
             used[dd][c] = b
-            depth[c] = level + 1
-            if np.any(~(H - H0[c] <= MAX_DELTA_H)):  # also catches NaN
-                divergent[c], active[c] = True, False
-                continue
-            # time order: backward leaves run away from the tree's left end
-            if dd < 0:
-                Q, P, H = Q[::-1], P[::-1], H[::-1]
-            PS = P * m
-            ok, rho_sub = subtree_check(P, PS)
-            if not ok:
-                active[c] = False
-                continue
-            w = -H
-            logw_sub = _logsumexp(w)
-            # leaf of the subtree, proportional to exp(-H); then biased move
-            prob = np.exp(w - logw_sub)
-            j = int(rng.choice(n_new, p=prob / prob.sum()))
-            if rng.random() < min(1.0, math.exp(logw_sub - logw[c])):
-                sample[c] = Q[j]
-            logw[c] = float(np.logaddexp(logw[c], logw_sub))
-            # merge with the old tree (A earlier in time, B later)
-            old_p, old_ps = ends[-dd]  # far end of the old tree
-            near_p, near_ps = ends[dd]  # end the subtree attaches to
-            if dd > 0:
-                ok, rho_new = merge_check(rho[c], rho_sub, near_p[c], old_ps[c], near_ps[c],
-                                          P[0], PS[0], PS[-1])
-            else:
-                ok, rho_new = merge_check(rho_sub, rho[c], P[-1], PS[0], PS[-1],
-                                          near_p[c], near_ps[c], old_ps[c])
-            ends[dd][0][c], ends[dd][1][c] = (P[-1], PS[-1]) if dd > 0 else (P[0], PS[0])
-            if not ok:
-                active[c] = False
-                continue
-            rho[c] = rho_new
+        depth[act] = level + 1
+        fwd = dirs[act] > 0
+        # divergence (also NaN): the subtree is discarded and the tree stops
+        div = ~np.all(H - H0[act, None] <= MAX_DELTA_H, axis=1)
+        divergent[act] |= div
+        PS = P * m
+        ok_sub, rho_sub = subtree_check(P, PS)
+        ok_sub &= ~div
+        # a leaf of each subtree with probability proportional to exp(-H),
+        # then the biased move into the subtree with min(1, W_sub / W_tree)
+        w = -np.where(div[:, None], 0.0, H)
+        wmax = w.max(axis=1)
+        ew = np.exp(w - wmax[:, None])
+        tot = ew.sum(axis=1)
+        logw_sub = wmax + np.log(tot)
+        cdf = np.cumsum(ew, axis=1)
+        u = rng.random(A) * tot
+        j = np.minimum((cdf < u[:, None]).sum(axis=1), n_new - 1)
+        move = rng.random(A) < np.exp(np.minimum(0.0, logw_sub - logw[act]))
+        take = ok_sub & move
+        sample[act[take]] = Q[take, j[take]]
+        logw[act] = np.where(ok_sub, np.logaddexp(logw[act], logw_sub), logw[act])
+        # merge with the old tree: A is the earlier of (old tree, subtree) in time
+        first_p, first_ps = P[:, 0], PS[:, 0]
+        last_p, last_ps = P[:, -1], PS[:, -1]
+        lp, lps = end_p[-1][act], end_ps[-1][act]   # old tree, left end
+        rp, rps = end_p[+1][act], end_ps[+1][act]   # old tree, right end
+        f = fwd[:, None]
+        ok_m, rho_new = merge_check(
+            np.where(f, rho[act], rho_sub), np.where(f, rho_sub, rho[act]),
+            np.where(f, rp, last_p), np.where(f, lps, first_ps), np.where(f, rps, last_ps),
+            np.where(f, first_p, lp), np.where(f, first_ps, lps), np.where(f, last_ps, rps))
+        cont = ok_sub & ok_m
+        rho[act] = np.where(cont[:, None], rho_new, rho[act])
+        # the subtree's far end becomes the tree's end on its side
+        for sgn, sel in ((+1, fwd), (-1, ~fwd)):
+            idx = act[sel & ok_sub]
+            src = (last_p, last_ps) if sgn > 0 else (first_p, first_ps)
+            end_p[sgn][idx] = src[0][sel & ok_sub]
+            end_ps[sgn][idx] = src[1][sel & ok_sub]
+        active[act] = cont
     n_leap = used[+1] + used[-1]
     return sample, Stats(depth=depth, n_leapfrog=n_leap, divergent=divergent, energy=H0)
