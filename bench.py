@@ -955,8 +955,8 @@ def suite(args):
 
         Cn, Tn = 256, 5
         el, src, dep = run_nuts(nuts.GpuChain, Cn, Tn)
-        cel, csrc, _ = run_nuts(nuts.OracleChain, 32, 2)
-        cpu_us = cel / 2 * (Cn / 32) * 1e6
+        cel, csrc, _ = run_nuts(nuts.OracleChain, Cn, 2)
+        cpu_us = cel / 2 * 1e6
         emit(workload="NUTS transitions, 256 chains, Gaussian d=100, eps=0.05, max depth 8",
              dtype="float64", us_per_call=el / Tn * 1e6, transitions_per_s=Cn * Tn / el,
              mean_tree_depth=dep, chain_call_share=src.sec / el,
@@ -964,8 +964,8 @@ def suite(args):
              note="tree logic on the host (numpy), trajectories from the GPU chain with fused KE; "
                   "call share = fraction of wall time in the chain calls (kernel + transfers)",
              cpu_baseline={"us_per_call": cpu_us, "kind": "port", "cores": 1,
-                           "sample": "same NUTS driven by the oracle chain, 32 chains x 2 transitions, "
-                                     "scaled to 256 chains"})
+                           "sample": "same NUTS (same host tree logic) driven by the oracle chain, "
+                                     "256 chains x 2 transitions"})
         lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
 
     for h in handles:

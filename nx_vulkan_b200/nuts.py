@@ -89,15 +89,27 @@ class OracleChain:
 class GpuChain:
     """Trajectory source on the GPU: nxv_leapfrog_chain_gauss_f64_batched_ke
     through the Nx.Vulkan mirror; q, p, logp and kinetic energy of every step
-    come back to the host (the tree builder's view of the call)."""
+    come back to the host (the tree builder's view of the call), downloaded
+    into reused page-locked buffers (direct DMA, no staging copy)."""
 
     def __init__(self, target: GaussianTarget, inv_mass, eps: float):
+        from nx_vulkan_b200 import _native
         from nx_vulkan_b200 import vulkan as nxv
-        self.nxv, self.t, self.m, self.eps = nxv, target, np.asarray(inv_mass, np.float64), eps
+        self.nxv, self.lib = nxv, _native.load()
+        self.t, self.m, self.eps = target, np.asarray(inv_mass, np.float64), eps
         ok, self.prec_h = nxv.upload_binary(self.t.prec.tobytes())
         if ok != "ok":
             raise RuntimeError(f"upload failed: {self.prec_h}")
         self.calls = []
+        self.pinned = {}  # slot -> page-locked float64 array
+
+    def _host(self, slot, n):
+        a = self.pinned.get(slot)
+        if a is None or a.size < n:
+            import torch
+            a = torch.empty(max(n, 1 << 16), dtype=torch.float64, pin_memory=True).numpy()
+            self.pinned[slot] = a
+        return a[:n]
 
     def _up(self, a):
         ok, h = self.nxv.upload_binary(np.ascontiguousarray(a, np.float64).tobytes())
@@ -105,11 +117,12 @@ class GpuChain:
             raise RuntimeError(f"upload failed: {h}")
         return h
 
-    def _down(self, h, n):
-        ok, b = self.nxv.download_binary(h, n * 8)
-        if ok != "ok":
-            raise RuntimeError(f"download failed: {b}")
-        return np.frombuffer(b, dtype=np.float64).copy()
+    def _down(self, h, n, slot):
+        import ctypes
+        a = self._host(slot, n)
+        if self.lib.nxv_buf_download(h.handle, ctypes.c_void_p(a.ctypes.data), n * 8) != 0:
+            raise RuntimeError("download failed")
+        return a.copy()
 
     def extend(self, q, p, K):
         c, d = q.shape
@@ -121,8 +134,8 @@ class GpuChain:
             raise RuntimeError(f"chain call failed: {outs}")
         qh, ph, _gh, lh, kh = outs
         self.calls.append((c, K))
-        return (self._down(qh, c * K * d).reshape(c, K, d), self._down(ph, c * K * d).reshape(c, K, d),
-                self._down(lh, c * K).reshape(c, K), self._down(kh, c * K).reshape(c, K))
+        return (self._down(qh, c * K * d, 0).reshape(c, K, d), self._down(ph, c * K * d, 1).reshape(c, K, d),
+                self._down(lh, c * K, 2).reshape(c, K), self._down(kh, c * K, 3).reshape(c, K))
 
 
 def _dot(x, y):
