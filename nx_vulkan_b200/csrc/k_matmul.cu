@@ -492,10 +492,8 @@ int run_gemm_p(Ctx& c, GemmP<T> P) {
         return E_ARG;
     }
     const int KT = (P.K + BK - 1) / BK;
-    const int sms = c.dev->sm_count;
-    const long long tail = tiles % sms;
-    const bool sk = sk_enabled() && P.ksplit == 0 && tail > 0 && (sms - tail) * KT >= 6LL * sms;
-    if (!sk) {
+    const SkPlan pl = P.ksplit == 0 ? gemm_sk_plan(tiles, KT, c.dev->sm_count, 6) : SkPlan{};
+    if (pl.tail == 0) {
         cudaError_t e = cudaFuncSetAttribute(k_gemm<T, BK, MK>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
@@ -503,13 +501,8 @@ int run_gemm_p(Ctx& c, GemmP<T> P) {
         count_launch();
         return finish(c);
     }
-    const long long dp = tiles - tail;
-    const long long W = tail * KT;
-    // G ranges: one per SM, at most 32 per tail tile (the fix-up reads every
-    // partial) and at most W; G >= tail, so a range is at most KT long and
-    // touches at most two tiles.
-    const int G = (int)std::min<long long>(std::min<long long>(std::min<long long>(W, sms), 32 * tail),
-                                           kMaxSkRanges);
+    const long long dp = pl.dp, tail = pl.tail, W = pl.W;
+    const int G = pl.G;
     ScratchGuard guard(c);
     T* ws = (T*)scratch(c, (size_t)G * 2 * BM * BN * sizeof(T), kScratchGemm);
     if (!ws) return E_CUDA;
@@ -528,7 +521,7 @@ int run_gemm_p(Ctx& c, GemmP<T> P) {
     // fix-up: split each tile's elements over f CTAs so that about 2 CTAs per
     // SM run (f divides BM*BN / (NTH * 16 bytes) evenly for f <= 16, a power of 2)
     int f = 1;
-    while (f < 16 && tail * f < 2LL * sms) f *= 2;
+    while (f < 16 && tail * f < 2LL * c.dev->sm_count) f *= 2;
     k_gemm_fix<T><<<dim3((unsigned)tail, f), NTH, 0, c.stream>>>(P, dp, W, G, KT, ws);
     count_launch();
     return finish(c);
@@ -614,5 +607,37 @@ int launch_matmul_f32(Ctx& c, void* C, const void* A, const void* B, size_t batc
 }
 
 int gemm_f64(Ctx& c, const GemmP<double>& P) { return gemm_f64_dispatch(c, P); }
+
+bool gemm_sk_enabled() { return sk_enabled(); }
+
+SkPlan gemm_sk_plan(long long tiles, int KT, int sms, int min_idle) {
+    SkPlan pl{};
+    pl.tail = tiles % sms;
+    if (!(sk_enabled() && pl.tail > 0 && (sms - pl.tail) * (long long)KT >= (long long)min_idle * sms)) {
+        pl.tail = 0;
+        return pl;
+    }
+    pl.dp = tiles - pl.tail;
+    pl.W = pl.tail * KT;
+    pl.G = (int)std::min<long long>(std::min<long long>(std::min<long long>(pl.W, sms), 32 * pl.tail),
+                                    kMaxSkRanges);
+    return pl;
+}
+
+int launch_gemm_fix_f32(Ctx& c, float* C, int M, int N, int batch, const SkPlan& pl, int KT,
+                        const float* ws) {
+    GemmP<float> P{};
+    P.C = C;
+    P.M = M;
+    P.N = N;
+    P.ldc = N;
+    P.sC = (long long)M * N;
+    P.batch = batch;
+    int f = 1;
+    while (f < 16 && pl.tail * f < 2LL * c.dev->sm_count) f *= 2;
+    k_gemm_fix<float><<<dim3((unsigned)pl.tail, f), NTH, 0, c.stream>>>(P, pl.dp, pl.W, pl.G, KT, ws);
+    count_launch();
+    return OK;
+}
 
 }  // namespace nxv

@@ -7,7 +7,8 @@
 // The dropped A_lo.B_lo term and the TF32 reading of lo are ~2^-22 relative,
 // so the result has f32 accuracy.
 //
-// Pipeline (one CTA per 128 x 128 tile of C, 4 warps):
+// Pipeline (one CTA per 128 x 128 tile of C, 4 warps; the tiles after the
+// last full wave of SMs run stream-K, see k_gemm_tc):
 //   pre-pass  split A -> A_hi, A_lo [M][Kp] and B -> B^T_hi, B^T_lo [N][Kp]
 //             (K padded to a multiple of 32 with zeros): both operands
 //             K-major, every TMA box starts at an x multiple of 32.
@@ -112,10 +113,23 @@ __device__ __forceinline__ void umma_commit(uint64_t* b) {
                  : "memory");
 }
 
+// One CTA computes up to two work items, each a 128 x 128 tile of C over a
+// range of k-blocks:
+//   mode 0 (data-parallel): tile tile_base + blockIdx.x over all KB k-blocks,
+//            written to C;
+//   mode 1 (stream-K tail): CTA p takes k-block iterations
+//            [W p / G, W (p+1) / G) of the tiles after tile_base (KB
+//            iterations per tile), at most two tiles, and writes each
+//            partial sum to workspace slot 2p or 2p+1 (dense 128 x 128 f32);
+//            a fix-up adds every tile's slots in order.
+// The producer and the MMA issuer count pipeline iterations across the items
+// (stage = it % TSTAGES, parity from it / TSTAGES); the accumulator is
+// drained between items behind a block barrier.
 __global__ void __launch_bounds__(128, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUtensorMap mA_lo,
           const __grid_constant__ CUtensorMap mB_hi, const __grid_constant__ CUtensorMap mB_lo,
-          float* __restrict__ C, int M, int N, int Kp, long long sC) {
+          float* __restrict__ C, int M, int N, int Kp, long long sC, long long tile_base, int mode,
+          long long W, int G, float* __restrict__ ws) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t base = su32(smem_raw);
     unsigned char* smem = smem_raw + ((1024 - (base & 1023)) & 1023);
@@ -126,8 +140,32 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUt
     __shared__ int s_err;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.y * TBM, n0 = blockIdx.x * TBN, bz = blockIdx.z;
     const int KB = Kp / TBK;
+    const int tm = (M + TBM - 1) / TBM, tn = (N + TBN - 1) / TBN;
+
+    // work items: (linear tile, first k-block, end k-block, workspace slot)
+    long long it_tile[2];
+    int it_k0[2], it_k1[2], n_items = 0;
+    if (mode == 0) {
+        it_tile[0] = tile_base + blockIdx.x;
+        it_k0[0] = 0;
+        it_k1[0] = KB;
+        n_items = 1;
+    } else {
+        const long long p = blockIdx.x;
+        long long it = p * W / G;
+        const long long hi = (p + 1) * W / G;
+        while (it < hi && n_items < 2) {
+            const long long t = it / KB;
+            const int k0 = (int)(it - t * KB);
+            const int k1 = (int)((hi - it) < (long long)(KB - k0) ? k0 + (hi - it) : KB);
+            it_tile[n_items] = tile_base + t;
+            it_k0[n_items] = k0;
+            it_k1[n_items] = k1;
+            n_items++;
+            it += k1 - k0;
+        }
+    }
 
     if (tid == 0) {
         s_err = 0;
@@ -151,55 +189,68 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUt
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    int issued = 0;  // producer: k-blocks whose loads were issued
-    if (warp == 0 && lane == 0) {
-        for (int kb = 0; kb < KB; kb++) {
-            const int s = kb % TSTAGES;
-            if (kb >= TSTAGES && !mbar_wait(&empty[s], ((kb / TSTAGES) + 1) & 1)) {
-                s_err = 1;
-                break;
+    int issued = 0;    // producer: pipeline iterations whose loads were issued
+    int pipe_it = 0;   // pipeline iterations of the items before this one
+    for (int item = 0; item < n_items; item++) {
+        const long long lin = it_tile[item];
+        const int bz = (int)(lin / ((long long)tm * tn));
+        const int rr = (int)(lin - (long long)bz * tm * tn);
+        const int m0 = (rr / tn) * TBM, n0 = (rr % tn) * TBN;
+        const int k0 = it_k0[item], k1 = it_k1[item];
+        if (warp == 0 && lane == 0) {
+            for (int kb = k0; kb < k1; kb++) {
+                const int it = pipe_it + (kb - k0);
+                const int s = it % TSTAGES;
+                if (it >= TSTAGES && !mbar_wait(&empty[s], ((it / TSTAGES) + 1) & 1)) {
+                    s_err = 1;
+                    break;
+                }
+                unsigned char* st = smem + s * STAGE_BYTES;
+                mbar_expect_tx(&full[s], STAGE_BYTES);
+                tma_load_3d(st, &mA_hi, kb * TBK, m0, bz, &full[s]);
+                tma_load_3d(st + TILE_BYTES, &mA_lo, kb * TBK, m0, bz, &full[s]);
+                tma_load_3d(st + 2 * TILE_BYTES, &mB_hi, kb * TBK, n0, bz, &full[s]);
+                tma_load_3d(st + 3 * TILE_BYTES, &mB_lo, kb * TBK, n0, bz, &full[s]);
+                issued = it + 1;
             }
-            unsigned char* st = smem + s * STAGE_BYTES;
-            mbar_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_3d(st, &mA_hi, kb * TBK, m0, bz, &full[s]);
-            tma_load_3d(st + TILE_BYTES, &mA_lo, kb * TBK, m0, bz, &full[s]);
-            tma_load_3d(st + 2 * TILE_BYTES, &mB_hi, kb * TBK, n0, bz, &full[s]);
-            tma_load_3d(st + 3 * TILE_BYTES, &mB_lo, kb * TBK, n0, bz, &full[s]);
-            issued = kb + 1;
-        }
-    } else if (warp == 1 && lane == 0) {
-        bool ok = true;
-        for (int kb = 0; kb < KB; kb++) {
-            const int s = kb % TSTAGES;
-            if (!mbar_wait(&full[s], (kb / TSTAGES) & 1)) {
-                s_err = 1;
-                ok = false;
-                break;
-            }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t st = su32(smem + s * STAGE_BYTES);
-            const uint64_t ahi = sdesc(st), alo = sdesc(st + TILE_BYTES);
-            const uint64_t bhi = sdesc(st + 2 * TILE_BYTES), blo = sdesc(st + 3 * TILE_BYTES);
+        } else if (warp == 1 && lane == 0) {
+            bool ok = true;
+            for (int kb = k0; kb < k1; kb++) {
+                const int it = pipe_it + (kb - k0);
+                const int s = it % TSTAGES;
+                if (!mbar_wait(&full[s], (it / TSTAGES) & 1)) {
+                    s_err = 1;
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t st = su32(smem + s * STAGE_BYTES);
+                const uint64_t ahi = sdesc(st), alo = sdesc(st + TILE_BYTES);
+                const uint64_t bhi = sdesc(st + 2 * TILE_BYTES), blo = sdesc(st + 3 * TILE_BYTES);
 #pragma unroll
-            for (int j = 0; j < TBK / 8; j++) {
-                const uint64_t adv = (uint64_t)(j * 32) >> 4;  // 8 f32 = 32 bytes along K
-                umma_tf32(tmem, alo + adv, bhi + adv, (kb | j) != 0);
-                umma_tf32(tmem, ahi + adv, blo + adv, 1);
-                umma_tf32(tmem, ahi + adv, bhi + adv, 1);
+                for (int j = 0; j < TBK / 8; j++) {
+                    const uint64_t adv = (uint64_t)(j * 32) >> 4;  // 8 f32 = 32 bytes along K
+                    umma_tf32(tmem, alo + adv, bhi + adv, (kb != k0 || j != 0) ? 1u : 0u);
+                    umma_tf32(tmem, ahi + adv, blo + adv, 1);
+                    umma_tf32(tmem, ahi + adv, bhi + adv, 1);
+                }
+                umma_commit(&empty[s]);
             }
-            umma_commit(&empty[s]);
+            if (ok) umma_commit(done);
         }
-        if (ok) umma_commit(done);
-    }
-    __syncwarp();
-    // Epilogue: wait for the accumulator, then each thread drains its row.
-    bool have = mbar_wait(done, 0);
-    if (!have) s_err = 1;
-    __syncthreads();
-    if (s_err == 0 && have) {
+        __syncwarp();
+        pipe_it += k1 - k0;
+        // Epilogue: wait for the accumulator (done completes once per item),
+        // then each thread drains its row to C or to the workspace slot.
+        bool have = mbar_wait(done, item & 1);
+        if (!have) s_err = 1;
+        __syncthreads();
+        if (s_err != 0 || !have) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int row = m0 + warp * 32 + lane;
-        float* crow = C + bz * sC + (size_t)row * N;
+        const int lrow = warp * 32 + lane;
+        const int row = m0 + lrow;
+        float* crow = (mode == 0) ? C + bz * sC + (size_t)row * N
+                                  : ws + ((size_t)blockIdx.x * 2 + item) * (TBM * TBN) + (size_t)lrow * TBN;
         const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
         for (int c0 = 0; c0 < TBN; c0 += 8) {
@@ -210,7 +261,13 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUt
                   "=r"(r[6]), "=r"(r[7])
                 : "r"(tl + c0));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (row < M) {
+            if (mode == 1) {  // dense slot, every element
+                float4* d4 = reinterpret_cast<float4*>(crow + c0);
+                d4[0] = make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]),
+                                    __uint_as_float(r[2]), __uint_as_float(r[3]));
+                d4[1] = make_float4(__uint_as_float(r[4]), __uint_as_float(r[5]),
+                                    __uint_as_float(r[6]), __uint_as_float(r[7]));
+            } else if (row < M) {
                 const int col = n0 + c0;
                 if (col + 8 <= N && (((uintptr_t)(crow + col)) & 15) == 0) {
                     float4* d4 = reinterpret_cast<float4*>(crow + col);
@@ -224,11 +281,16 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUt
                 }
             }
         }
-    } else if (tid == 0) {
+        // the next item's MMAs overwrite the accumulator: every read is done
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    }
+    if (s_err != 0 && tid == 0) {
         // error path: let every TMA load this CTA issued land before the CTA
         // (and its shared memory) goes away; each wait is bounded.
-        for (int kb = (issued > TSTAGES ? issued - TSTAGES : 0); kb < issued; kb++)
-            mbar_wait(&full[kb % TSTAGES], (kb / TSTAGES) & 1);
+        for (int it = (issued > TSTAGES ? issued - TSTAGES : 0); it < issued; it++)
+            mbar_wait(&full[it % TSTAGES], (it / TSTAGES) & 1);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -398,14 +460,34 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
     cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          SMEM_BYTES);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_gemm_tc)");
-    dim3 grid((unsigned)((n + TBN - 1) / TBN), (unsigned)((m + TBM - 1) / TBM), (unsigned)batch);
-    if (grid.y > 65535) {
-        set_error("matmul M too large");
+    const long long tiles = (long long)((m + TBM - 1) / TBM) * ((n + TBN - 1) / TBN) * batch;
+    if (tiles > 0x7fffffffLL) {
+        set_error("matmul grid out of range");
         return E_ARG;
     }
-    k_gemm_tc<<<grid, 128, SMEM_BYTES, c.stream>>>(mah, mal, mbh, mbl, (float*)C, (int)m, (int)n,
-                                                    (int)Kp, (long long)(m * n));
-    count_launch();
+    const int KB = (int)(Kp / TBK);
+    // A 32-deep k-block takes ~0.7 us here: stream-K needs ~24 idle k-blocks
+    // per SM to repay its fix-up (2048^3 with a 73 % last wave does not).
+    const SkPlan pl = gemm_sk_plan(tiles, KB, c.dev->sm_count, 24);
+    const long long dp = pl.tail ? pl.dp : tiles;
+    if (dp > 0) {
+        k_gemm_tc<<<(unsigned)dp, 128, SMEM_BYTES, c.stream>>>(
+            mah, mal, mbh, mbl, (float*)C, (int)m, (int)n, (int)Kp, (long long)(m * n), 0, 0, 0, 1,
+            nullptr);
+        count_launch();
+    }
+    if (pl.tail) {
+        // workspace: 2 slots of 128 x 128 f32 per range, in the GEMM's own
+        // scratch slot (the split planes above hold the op scratch)
+        float* wsp = (float*)scratch(c, (size_t)pl.G * 2 * TBM * TBN * sizeof(float), kScratchGemm);
+        if (!wsp) return E_CUDA;
+        k_gemm_tc<<<(unsigned)pl.G, 128, SMEM_BYTES, c.stream>>>(
+            mah, mal, mbh, mbl, (float*)C, (int)m, (int)n, (int)Kp, (long long)(m * n), pl.dp, 1,
+            pl.W, pl.G, wsp);
+        count_launch();
+        int rc2 = launch_gemm_fix_f32(c, (float*)C, (int)m, (int)n, (int)batch, pl, KB, wsp);
+        if (rc2) return rc2;
+    }
     return finish(c);
 }
 

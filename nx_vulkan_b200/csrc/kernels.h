@@ -92,6 +92,22 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
 // Reads and clears the tensor-core GEMM's timeout flag (1 = a bounded wait ran out).
 int tc_gemm_error();
 
+// Stream-K schedule for 128 x 128 tiles (k_matmul.cu): tiles [0, dp) run
+// data-parallel; the k-tile iterations of tiles [dp, dp + tail) are cut into
+// G equal ranges (W = tail * KT iterations); tail == 0: no stream-K.  The
+// fix-up adds each tail tile's partials (workspace slots of 128 x 128, two
+// per range) in range order into C.
+struct SkPlan {
+    long long dp, tail, W;
+    int G;
+};
+// min_idle: stream-K pays when the last wave's idle SMs add up to at least
+// min_idle k-tile times per SM (its fix-up and extra launches cost about that).
+bool gemm_sk_enabled();
+SkPlan gemm_sk_plan(long long tiles, int KT, int sms, int min_idle);
+int launch_gemm_fix_f32(Ctx& c, float* C, int M, int N, int batch, const SkPlan& pl, int KT,
+                        const float* ws);
+
 // Grid helper: blocks for a grid-stride kernel.
 inline unsigned grid_for(Ctx& c, size_t work_items, unsigned threads, unsigned per_sm) {
     size_t want = (work_items + threads - 1) / threads;

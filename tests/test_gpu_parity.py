@@ -445,3 +445,31 @@ def test_matmul_f64_stream_k(nxv, orc, monkeypatch, bmnk):
     tol = 1e-12 * np.abs(want) + 2 * k * 2.2e-16 * bound
     assert np.all(np.abs(got - want) <= tol)
     assert np.all(np.abs(plain - want) <= tol)
+
+
+@pytest.mark.parametrize("bmnk", [(1, 100, 120, 3000), (1, 500, 400, 4000), (2, 256, 256, 2048),
+                                  (1, 2560, 1024, 2048)])
+def test_matmul_f32_stream_k(nxv, orc, monkeypatch, bmnk):
+    """tcgen05 3xTF32 with a stream-K tail (few tiles over a deep K, and a
+    full wave plus 12 tail tiles): within the f32 dot-product bound,
+    identical bit for bit on a second call, and within the bound of the
+    data-parallel schedule (NXV_GEMM_SK=0)."""
+    batch, m, n, k = bmnk
+    r = np.random.default_rng(14)
+    a = r.normal(size=batch * m * k).astype(np.float32)
+    b = r.normal(size=batch * k * n).astype(np.float32)
+    ta, tb = up(nxv, a), up(nxv, b)
+    got = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f32")), np.float32)
+    again = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f32")), np.float32)
+    assert np.array_equal(got, again)
+    monkeypatch.setenv("NXV_GEMM_SK", "0")
+    plain = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f32")), np.float32)
+    want = orc.matmul(a, b, m, n, k, batch=batch)
+    bound = np.concatenate([
+        (np.abs(a.reshape(batch, m, k)[q]).astype(np.float64) @ np.abs(b.reshape(batch, k, n)[q])).reshape(-1)
+        for q in range(batch)])
+    tol = 1e-5 * np.abs(want) + 1e-6 + f32_dot_bound(k, bound)
+    assert np.all(np.abs(got - want) <= tol)
+    assert np.all(np.abs(plain - want) <= tol)
+    from nx_vulkan_b200 import _native
+    assert _native.load().nxv_synchronize() == 0  # no pipeline timeout recorded
