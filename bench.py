@@ -893,6 +893,29 @@ def suite(args):
         emit(cpu_baseline=cpu, workload="batched matmul 64 x 256^3", dtype="float64", ms=ms, tflops=flops / (ms / 1e3) / 1e12,
              cublas_ms=ms_cublas, cublas_tflops=flops / (ms_cublas / 1e3) / 1e12, frac_of_cublas=ms_cublas / ms)
 
+        # stream-K vs data-parallel schedule on shapes whose tile count leaves SMs idle
+        bspv = nxv.shader_path("matmul_batched.spv")
+        for code, shapes in ((1, [(1, 1024, 1024, 1024), (1, 4096, 4096, 4096), (1, 3000, 3000, 512)]),
+                             (0, [(1, 128, 128, 4096), (1, 500, 400, 4000), (2, 256, 256, 2048),
+                                  (1, 2560, 1024, 2048)])):
+            tdt = torch.float64 if code == 1 else torch.float32
+            for bt, m_, n_, k_ in shapes:
+                a = torch.randn(bt, m_, k_, dtype=tdt, device=dev)
+                b = torch.randn(bt, k_, n_, dtype=tdt, device=dev)
+                c = torch.empty(bt, m_, n_, dtype=tdt, device=dev)
+                ha, hb2, hc = wrap(a), wrap(b), wrap(c)
+                res = {}
+                for sk in ("1", "0"):
+                    os.environ["NXV_GEMM_SK"] = sk
+                    res[sk] = timed(lambda: ck(lib.nxv_matmul_batched(hc, ha, hb2, bt, m_, n_, k_, code, bspv)), 10)
+                os.environ.pop("NXV_GEMM_SK", None)
+                fl = 2.0 * bt * m_ * n_ * k_
+                emit(workload=f"matmul {bt}x{m_}x{n_}x{k_} schedules", dtype="float64" if code else "float32",
+                     ms=res["1"], tflops=fl / (res["1"] / 1e3) / 1e12, ms_data_parallel_only=res["0"],
+                     tflops_data_parallel_only=fl / (res["0"] / 1e3) / 1e12,
+                     note="default schedule (stream-K tail where it pays) vs NXV_GEMM_SK=0")
+                del a, b, c
+
     # -- logistic-regression leapfrog -----------------------------------------------------------
     if "logreg" in want:
         Nobs, Dm, Cc, Lr = 10000, 100, 256, 16
