@@ -15,7 +15,9 @@ reference contract's q/p/grad trajectories [chain][k][i] and logp [chain][k].
          and reads the step's result -- the per-step logp of every chain --
          back into pinned host memory (nxv_buf_upload/_download); the
          trajectories stay in their device buffers, as the reference API
-         returns them.  `e2e_full_download` also brings the q/p/grad
+         returns them.  Step i+1's upload runs on a copy stream while step i
+         computes (nxv_set_stream, two input sets).  `e2e_serial` is the same
+         without the overlap; `e2e_full_download` also brings the q/p/grad
          trajectories (3.2 GB per step) to the host: PCIe-bound.
   roofline  algorithmic bytes of one call / its measured duration, against
          the measured HBM copy bandwidth (MEASURED_PEAKS.json).
@@ -391,7 +393,7 @@ def main():
     traffic = (24633856 + 729063680) / 1024 * chains if (D, L) == (1000, 32) else None
 
     # e2e through the C ABI with host buffers (library-owned device buffers).
-    e2e = e2e_full = None
+    e2e = e2e_full = e2e_serial = None
     if not args.no_e2e:
         lib.nxv_set_stream(None)
         hb_in = [torch.from_numpy(a.reshape(-1)).pin_memory() for a in (q0, p0, m, prec)]
@@ -429,11 +431,74 @@ def main():
                     "steps": n_e2e,
                     "timing": "host wall clock around synchronous C-ABI calls, max over ranks"}
 
-        e2e = e2e_run(False)
-        e2e["result_read"] = "per-step logp [chain][k] (the metric); trajectories stay on the device"
+        # Pipelined through the same public calls: step i+1's inputs upload on a
+        # copy stream (nxv_set_stream) while step i runs on a compute stream,
+        # two device input sets alternating, events ordering the two streams.
+        s_copy, s_comp = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        d_sets = [d_in, [lib.nxv_buf_alloc(t.numel() * 8) for t in hb_in]]
+        up_ev = [torch.cuda.Event(), torch.cuda.Event()]
+        used_ev = [torch.cuda.Event(), torch.cuda.Event()]
+
+        def p_upload(i):
+            b = i % 2
+            s_copy.wait_event(used_ev[b])  # the chain of step i-2 read this set
+            lib.nxv_set_stream(C.c_void_p(s_copy.cuda_stream))
+            for h, t in zip(d_sets[b], hb_in):
+                assert lib.nxv_buf_upload(h, C.c_void_p(t.data_ptr()), t.numel() * 8) == 0
+            up_ev[b].record(s_copy)
+
+        def p_launch(i):
+            b = i % 2
+            s_comp.wait_event(up_ev[b])
+            lib.nxv_set_stream(C.c_void_p(s_comp.cuda_stream))
+            rc = lib.nxv_leapfrog_chain_gauss_f64_batched(*d_out, *d_sets[b], D, chains, L, EPS, 0.0, spv)
+            assert rc == 0, _native.last_error()
+            used_ev[b].record(s_comp)
+
+        def p_result(i):
+            # the step's result to the host (waits for the chain)
+            lib.nxv_set_stream(C.c_void_p(s_comp.cuda_stream))
+            assert lib.nxv_buf_download(d_out[3], C.c_void_p(hb_out[3].data_ptr()), hb_out[3].numel() * 8) == 0
+
+        def e2e_pipelined():
+            n_e2e = max(5, args.steps)
+
+            def run(n):
+                # nxv_buf_upload returns once the copy is done (the caller may
+                # reuse its buffer), so step i is launched first and step
+                # i+1's upload runs while it computes
+                p_upload(0)
+                for i in range(n):
+                    p_launch(i)
+                    if i + 1 < n:
+                        p_upload(i + 1)
+                    p_result(i)
+
+            run(3)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            t0 = time.perf_counter()
+            run(n_e2e)
+            el = time.perf_counter() - t0
+            el_t = torch.tensor([el], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(el_t, op=dist.ReduceOp.MAX)
+            el = float(el_t.item())
+            return {"value": world * chains * L * n_e2e / el, "unit": UNIT,
+                    "h2d_bytes_per_step": sum(t.numel() * 8 for t in hb_in),
+                    "d2h_bytes_per_step": hb_out[3].numel() * 8, "steps": n_e2e,
+                    "timing": "host wall clock from the first upload to the last result, max over ranks",
+                    "result_read": "per-step logp [chain][k] (the metric); trajectories stay on the device",
+                    "pipelined": "inputs of step i+1 upload on a copy stream while step i computes"}
+
+        e2e_serial = e2e_run(False)
+        e2e_serial["result_read"] = "per-step logp [chain][k] (the metric); trajectories stay on the device"
+        e2e = e2e_pipelined()
         e2e_full = e2e_run(True)
         e2e_full["result_read"] = "all four outputs: q/p/grad trajectories and logp"
-        for h in d_in + d_out:
+        torch.cuda.synchronize()
+        for h in d_sets[0] + d_sets[1] + d_out:
             lib.nxv_buf_free(h)
         lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
 
@@ -471,6 +536,7 @@ def main():
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json), copy, of measured"},
             "clocks": clocks,
             "e2e": e2e,
+            "e2e_serial": e2e_serial,
             "e2e_full_download": e2e_full,
             "cpu_baseline": cpu,
         }
