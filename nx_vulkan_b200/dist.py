@@ -1,11 +1,19 @@
-"""Multi-GPU plumbing for the batched leapfrog chains (one process per GPU).
+"""Multi-GPU plumbing (one process per GPU).
 
-HMC chains are independent, so a batch of chains is partitioned into
-contiguous per-rank blocks with no data-path exchange; each rank integrates
-its block with the fused chain kernel on its own GPU.  The only collective is
-one all-gather of per-chain diagnostics (the final-step log density), the
-exchange a sampler needs to compare chains.  Timing of a multi-rank step is
-the maximum over ranks.
+Leapfrog: HMC chains are independent, so a batch of chains is partitioned
+into contiguous per-rank blocks with no data-path exchange; each rank
+integrates its block with the fused chain kernel on its own GPU.  The only
+collective is one all-gather of per-chain diagnostics (the final-step log
+density), the exchange a sampler needs to compare chains.  Timing of a
+multi-rank step is the maximum over ranks.
+
+Large elementwise, broadcast, reduction and batched-matmul calls shard the
+same way: contiguous 1/G slices of the flattened tensor (whole rows for
+row-wise ops, whole batch entries for batched matmul), each rank running the
+single-GPU kernel on its slice.  Elementwise and broadcast results need no
+exchange.  A full reduction gathers the G per-rank partials and folds them in
+rank order on every rank, so every rank gets the same value and the value
+does not depend on timing; row-wise results are all-gathered in row order.
 
 The functions take `torch.distributed` tensors and work with any backend:
 NCCL over NVLink on the GPUs, gloo on CPU for the host-side tests.
@@ -76,3 +84,160 @@ def max_over_ranks(value: float, device=None, group=None) -> float:
     if dist.is_available() and dist.is_initialized():
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+def element_shard(n: int, rank: int, world: int, align: int = 1) -> Shard:
+    """Contiguous slice of n elements for `rank`, with boundaries on
+    multiples of `align` (e.g. the row length, so that no row is split)."""
+    if align <= 0 or n % align:
+        raise ValueError(f"{n} elements do not split into units of {align}")
+    sh = chain_shard(n // align, rank, world)
+    return Shard(rank, world, sh.start * align, sh.count * align)
+
+
+# identities of the full reductions (nxv_reduce op codes: 0 sum, 1 min, 2 max)
+REDUCE_IDENTITY = {0: 0.0, 1: float("inf"), 2: float("-inf")}
+
+
+def fold_in_rank_order(partials, op: int) -> float:
+    """Fold per-rank partials left to right in rank order (sum in double;
+    min/max propagate NaN like the single-GPU kernels)."""
+    if op not in REDUCE_IDENTITY:
+        raise ValueError(f"reduce op {op} outside 0..2")
+    acc = REDUCE_IDENTITY[op]
+    for v in partials:
+        v = float(v)
+        if op == 0:
+            acc = acc + v
+        elif v != v or acc != acc:
+            acc = float("nan")
+        elif op == 1:
+            acc = v if v < acc else acc
+        else:
+            acc = v if v > acc else acc
+    return acc
+
+
+def fold_partials(local: float, op: int, group=None, device=None) -> float:
+    """Full reduction across ranks: one all-gather of every rank's partial
+    (float64), then the same rank-order fold on every rank.  A rank whose
+    slice is empty passes the op's identity."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    t = torch.tensor([float(local)], dtype=torch.float64, device=device)
+    out = torch.empty(world, dtype=torch.float64, device=device)
+    dist.all_gather_into_tensor(out, t, group=group)
+    return fold_in_rank_order(out.cpu().tolist(), op)
+
+
+def gather_rows(local, group=None):
+    """All-gather a row-sharded result: local is [rows_r, ...] on every rank
+    (row counts may differ by rank); returns [sum rows_r, ...] in rank order."""
+    tail = tuple(local.shape[1:])
+    flat = gather_diagnostics(local.reshape(-1), group=group)
+    return flat.reshape((-1,) + tail)
+
+
+def _coll_device():
+    """Tensors for collectives live on the GPU under NCCL, on the host else."""
+    import torch
+    import torch.distributed as dist
+
+    if dist.get_backend() == "nccl":
+        return torch.device("cuda", torch.cuda.current_device())
+    return torch.device("cpu")
+
+
+def reduce_full(nxv, x_slice, op: int, dtype: str = "f64", group=None) -> float:
+    """Sum (0), min (1) or max (2) of a tensor stored as contiguous per-rank
+    slices: the rank's slice through nxv_reduce / nxv_reduce_f64 on its GPU,
+    then the rank-order fold.  `x_slice` is the rank's device buffer (None
+    or empty for an empty slice).  f32 partials are folded in double and the
+    result rounded to f32 once, like the single-GPU f32 reduce."""
+    import numpy as np
+
+    if op not in REDUCE_IDENTITY:
+        raise ValueError(f"reduce op {op} outside 0..2")
+    if x_slice is None or x_slice.n_bytes == 0:
+        local = REDUCE_IDENTITY[op]
+    else:
+        if dtype == "f64":
+            r = nxv.reduce_f64(x_slice, op)
+        else:
+            r = (nxv.sum, nxv.reduce_min, nxv.reduce_max)[op](x_slice)
+        if r[0] != "ok":
+            raise RuntimeError(f"reduce failed on this rank: {r[1]}")
+        local = r[1]
+    v = fold_partials(local, op, group=group, device=_coll_device())
+    return float(np.float32(v)) if dtype == "f32" else v
+
+
+def _gather_host(arr, group):
+    import numpy as np
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(arr)).to(_coll_device())
+    return gather_rows(t, group=group).cpu().numpy()
+
+
+def reduce_rows(nxv, x_rows, n_rows: int, row_len: int, op: int, dtype: str = "f64",
+                group=None):
+    """Per-row sum/max/min (nxv_reduce_axis op codes 0/1/2) of a row-sharded
+    matrix: each rank reduces its n_rows rows on its GPU, and the results are
+    all-gathered in row order.  Returns the full [total rows] vector (numpy)."""
+    import numpy as np
+
+    elt, np_t = (8, np.float64) if dtype == "f64" else (4, np.float32)
+    if n_rows == 0:
+        local = np.zeros(0, np_t)
+    else:
+        fn = nxv.reduce_axis_f64 if dtype == "f64" else nxv.reduce_axis
+        ok, out = fn(x_rows, n_rows, row_len, 1, op)
+        if ok != "ok":
+            raise RuntimeError(f"reduce_axis failed on this rank: {out}")
+        ok, b = nxv.download_binary(out, n_rows * elt)
+        if ok != "ok":
+            raise RuntimeError(f"download failed on this rank: {b}")
+        local = np.frombuffer(b, np_t)
+    return _gather_host(local, group)
+
+
+def argmax_rows(nxv, x_rows, n_rows: int, row_len: int, dtype: str = "f64", group=None):
+    """Per-row argmax (lowest index on ties) of a row-sharded matrix; indices
+    are within the row, so sharding by rows leaves them unchanged."""
+    import numpy as np
+
+    if n_rows == 0:
+        local = np.zeros(0, np.int64)
+    else:
+        ok, out = nxv.argmax_axis(x_rows, n_rows, row_len, 1, dtype=dtype)
+        if ok != "ok":
+            raise RuntimeError(f"argmax failed on this rank: {out}")
+        ok, b = nxv.download_binary(out, n_rows * 8)
+        if ok != "ok":
+            raise RuntimeError(f"download failed on this rank: {b}")
+        local = np.frombuffer(b, np.int64)
+    return _gather_host(local, group)
+
+
+def matmul_batched(nxv, a, b, n_batch: int, m: int, n: int, k: int, dtype: str = "f64",
+                   group=None):
+    """Batched matmul sharded by batch entry: each rank multiplies its
+    n_batch entries on its GPU; the products are all-gathered in batch
+    order.  Returns [total batch, m, n] (numpy)."""
+    import numpy as np
+
+    elt, np_t = (8, np.float64) if dtype == "f64" else (4, np.float32)
+    if n_batch == 0:
+        local = np.zeros((0, m, n), np_t)
+    else:
+        ok, out = nxv.matmul_batched(a, b, n_batch, m, n, k, dtype=dtype)
+        if ok != "ok":
+            raise RuntimeError(f"matmul failed on this rank: {out}")
+        ok, raw = nxv.download_binary(out, n_batch * m * n * elt)
+        if ok != "ok":
+            raise RuntimeError(f"download failed on this rank: {raw}")
+        local = np.frombuffer(raw, np_t).reshape(n_batch, m, n)
+    return _gather_host(local, group)

@@ -82,3 +82,158 @@ def test_two_rank_gather_matches_single_process(n_chains):
     for rank, diag, t in results:
         assert np.array_equal(diag, want)  # every rank sees every chain, in chain order
         assert t == 2.0  # max over ranks of 1 + rank
+
+
+# ---- sharded elementwise / reduction / batched matmul (host logic) ------------
+
+class _Buf:
+    def __init__(self, arr):
+        self.arr = np.ascontiguousarray(arr)
+        self.n_bytes = self.arr.nbytes
+
+
+class FakeNxv:
+    """Stands in for the Nx.Vulkan mirror on a machine without a GPU: the same
+    call signatures and ("ok", value) results, computed with numpy."""
+
+    def reduce_f64(self, t, op):
+        return ("ok", float((np.sum, np.min, np.max)[op](t.arr)))
+
+    def sum(self, t):
+        return ("ok", float(np.float32(np.sum(t.arr, dtype=np.float64))))
+
+    def reduce_min(self, t):
+        return ("ok", float(np.min(t.arr)))
+
+    def reduce_max(self, t):
+        return ("ok", float(np.max(t.arr)))
+
+    def reduce_axis_f64(self, t, outer, r, inner, op):
+        x = t.arr.reshape(outer, r, inner)
+        return ("ok", _Buf((np.sum, np.max, np.min)[op](x, axis=1).reshape(-1)))
+
+    def argmax_axis(self, t, outer, r, inner, dtype="f32"):
+        return ("ok", _Buf(np.argmax(t.arr.reshape(outer, r, inner), axis=1).astype(np.int64)))
+
+    def matmul_batched(self, a, b, batch, m, n, k, dtype="f64"):
+        return ("ok", _Buf(np.matmul(a.arr.reshape(batch, m, k), b.arr.reshape(batch, k, n))))
+
+    def download_binary(self, t, n_bytes):
+        assert n_bytes == t.n_bytes
+        return ("ok", t.arr.tobytes())
+
+
+def test_element_shard_keeps_rows_whole():
+    from nx_vulkan_b200.dist import element_shard
+    for rows, world in ((10, 3), (1, 4), (4096, 8)):
+        shards = [element_shard(rows * 7, r, world, 7) for r in range(world)]
+        assert shards[0].start == 0 and shards[-1].stop == rows * 7
+        assert all(s.start % 7 == 0 and s.count % 7 == 0 for s in shards)
+    with pytest.raises(ValueError):
+        element_shard(10, 0, 2, 3)
+
+
+def test_fold_in_rank_order():
+    from nx_vulkan_b200.dist import fold_in_rank_order
+    assert fold_in_rank_order([1e16, 1.0, -1e16], 0) == 0.0   # left to right, in rank order
+    assert fold_in_rank_order([3.0, -1.0, 2.0], 1) == -1.0
+    assert fold_in_rank_order([3.0, float("inf"), 2.0], 2) == float("inf")
+    assert fold_in_rank_order([], 2) == float("-inf")
+    assert np.isnan(fold_in_rank_order([1.0, float("nan"), 2.0], 2))
+    with pytest.raises(ValueError):
+        fold_in_rank_order([1.0], 3)
+
+
+def _sharded_worker(rank, world, port, result_q, use_gpu):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from nx_vulkan_b200 import dist as nd
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        if use_gpu:
+            from nx_vulkan_b200 import vulkan as nxv
+            assert nxv.init() == "ok"
+
+            def buf(a):
+                if a.size == 0:
+                    return None
+                ok, t = nxv.upload_binary(np.ascontiguousarray(a).tobytes())
+                assert ok == "ok", t
+                return t
+        else:
+            nxv = FakeNxv()
+            buf = _Buf
+        rows, row_len, batch, m, n, k = 9, 37, 2, 6, 7, 8
+        r = np.random.default_rng(11)
+        x = r.normal(size=(rows, row_len))
+        a, b = r.normal(size=(batch, m, k)), r.normal(size=(batch, k, n))
+        sh = nd.element_shard(rows * row_len, rank, world, row_len)
+        xs = x.reshape(-1)[sh.start:sh.stop]
+        rs = nd.chain_shard(rows, rank, world)
+        bs = nd.chain_shard(batch, rank, world)
+        out = {
+            "sum": nd.reduce_full(nxv, buf(xs), 0, "f64"),
+            "min": nd.reduce_full(nxv, buf(xs), 1, "f64"),
+            "max": nd.reduce_full(nxv, buf(xs), 2, "f64"),
+            "sum32": nd.reduce_full(nxv, buf(xs.astype(np.float32)), 0, "f32"),
+            "row_sum": nd.reduce_rows(nxv, buf(x[rs.start:rs.stop]), rs.count, row_len, 0),
+            "row_max": nd.reduce_rows(nxv, buf(x[rs.start:rs.stop]), rs.count, row_len, 1),
+            "argmax": nd.argmax_rows(nxv, buf(x[rs.start:rs.stop]), rs.count, row_len),
+            "bmm": nd.matmul_batched(nxv, buf(a[bs.start:bs.stop]), buf(b[bs.start:bs.stop]),
+                                     bs.count, m, n, k),
+            "partials": [float(np.sum(x.reshape(-1)[s.start:s.stop]))
+                         for s in (nd.element_shard(rows * row_len, q, world, row_len)
+                                   for q in range(world))],
+        }
+        result_q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def run_sharded(world, use_gpu=False):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, world, port, q, use_gpu))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=180) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return [o for _, o in sorted(results, key=lambda t: t[0])]
+
+
+def check_sharded(results, world, exact_rows):
+    """Every rank holds the same gathered results, equal to the unsharded
+    computation; the full sum is the rank-order fold of the slice sums."""
+    rows, row_len, batch, m, n, k = 9, 37, 2, 6, 7, 8
+    r = np.random.default_rng(11)
+    x = r.normal(size=(rows, row_len))
+    a, b = r.normal(size=(batch, m, k)), r.normal(size=(batch, k, n))
+    from nx_vulkan_b200.dist import fold_in_rank_order
+    for o in results:
+        assert o["min"] == x.min() and o["max"] == x.max()
+        want_sum = fold_in_rank_order(o["partials"], 0)
+        assert abs(o["sum"] - want_sum) <= 1e-12 * np.abs(x).sum()
+        assert abs(o["sum"] - x.sum()) <= 1e-12 * np.abs(x).sum()
+        assert abs(o["sum32"] - x.astype(np.float32).astype(np.float64).sum()) <= 1e-5 * np.abs(x).sum()
+        assert np.array_equal(o["argmax"], np.argmax(x, axis=1))
+        assert np.array_equal(o["row_max"], x.max(axis=1))
+        if exact_rows:
+            assert np.array_equal(o["row_sum"], x.sum(axis=1))
+        assert np.allclose(o["row_sum"], x.sum(axis=1), rtol=1e-12, atol=1e-12 * row_len)
+        bound = 2 * k * np.finfo(np.float64).eps * np.matmul(np.abs(a), np.abs(b))
+        assert np.all(np.abs(o["bmm"] - np.matmul(a, b)) <= 1e-12 * np.abs(np.matmul(a, b)) + bound)
+        for key in ("sum", "sum32", "row_sum", "argmax", "bmm"):   # identical on every rank
+            assert np.array_equal(np.asarray(o[key]), np.asarray(results[0][key]))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_ops_over_gloo(world):
+    # world 3: one rank gets no batch entry (2 entries over 3 ranks)
+    check_sharded(run_sharded(world), world, exact_rows=True)
