@@ -269,6 +269,32 @@ __global__ void __launch_bounds__(kThreads) k_cast(To* __restrict__ out,
     for (; t < n; t += stride) out[t] = (To)a[t];
 }
 
+// f32 -> f64 with every warp-wide store covering one contiguous span: a lane
+// converts one float2 into one double2 (the warp reads 256 B and writes
+// 512 B per vector), 8 pairs in flight per lane; the odd last element is
+// scalar.  Needs out 16-byte and a 8-byte aligned.
+__global__ void __launch_bounds__(kThreads) k_cast_up(double* __restrict__ out,
+                                                     const float* __restrict__ a, size_t n) {
+    constexpr int U = 8;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t np = n / 2;
+    const float2* a2 = reinterpret_cast<const float2*>(a);
+    double2* o2 = reinterpret_cast<double2*>(out);
+    size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; t + (U - 1) * stride < np; t += U * stride) {
+        float2 x[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) x[u] = __ldcs(a2 + t + u * stride);
+#pragma unroll
+        for (int u = 0; u < U; u++) __stcs(o2 + t + u * stride, make_double2((double)x[u].x, (double)x[u].y));
+    }
+    for (; t < np; t += stride) {
+        const float2 x = a2[t];
+        o2[t] = make_double2((double)x.x, (double)x.y);
+    }
+    if ((n & 1) && blockIdx.x == 0 && threadIdx.x == 0) out[n - 1] = (double)a[n - 1];
+}
+
 // ---- broadcast --------------------------------------------------------------
 
 struct Bcast {
@@ -329,6 +355,12 @@ k_bcast(T* __restrict__ out, const T* __restrict__ a, const T* __restrict__ b, B
 // index is decoded into coordinates with exact multiply-high division
 // (Lemire, Kaser & Kurz 2019: for M = ceil(2^64 / d) and 32-bit n, d,
 // floor(n / d) = umulhi64(M, n)), and each thread keeps 4 vectors in flight.
+// NXV_BCAST_ROWS=0: every vector broadcast on the flat-index kernel.
+bool bcast_rows_enabled() {
+    const char* e = getenv("NXV_BCAST_ROWS");
+    return !(e && e[0] == '0');
+}
+
 struct FastDiv {
     unsigned long long m[4];  // ceil(2^64 / shape[d]); 0 when shape[d] == 1
 };
@@ -386,27 +418,120 @@ k_bcast_fast(T* __restrict__ out, const T* __restrict__ a, const T* __restrict__
     }
 }
 
+// Row path (same conditions as the vector path): the innermost dimension, of
+// Lv vectors, is contiguous in the output and has stride 1 or 0 in each
+// operand.  A task is one chunk of kThreads * 4 vectors of one row; the row's
+// operand offsets are decoded once per task, so per element only the loads,
+// the op (a template constant) and the store remain.
+template <typename T, int OP>
+__global__ void __launch_bounds__(kThreads)
+k_bcast_rows(T* __restrict__ out, const T* __restrict__ a, const T* __restrict__ b, Bcast g,
+             FastDiv fd, unsigned rows, unsigned Lv, unsigned chunks) {
+    constexpr int W = (int)(16 / sizeof(T));
+    constexpr int U = 4;
+    const int last = (int)g.ndim - 1;
+    const bool va = g.as[last] == 1, vb = g.bs[last] == 1;
+    const unsigned ntask = rows * chunks;
+    for (unsigned task = blockIdx.x; task < ntask; task += gridDim.x) {
+        const unsigned r = task / chunks, ch = task - r * chunks;
+        unsigned rem = r, oa = 0, ob = 0;
+#pragma unroll
+        for (int d = 2; d >= 0; d--) {
+            if (d >= last) continue;
+            const unsigned q = fdiv(rem, fd.m[d]);
+            const unsigned cd = rem - q * g.shape[d];
+            rem = q;
+            oa += cd * g.as[d];
+            ob += cd * g.bs[d];
+        }
+        const T* ar = a + oa;
+        const T* br = b + ob;
+        T* orow = out + (size_t)r * Lv * W;
+        const unsigned v0 = ch * (kThreads * U) + threadIdx.x;
+        T xa[U][W], xb[U][W];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const unsigned v = v0 + u * kThreads;
+            if (v >= Lv) continue;
+            if (va) vload(ar + (size_t)v * W, xa[u]);
+            else {
+#pragma unroll
+                for (int j = 0; j < W; j++) xa[u][j] = ar[0];
+            }
+            if (vb) vload(br + (size_t)v * W, xb[u]);
+            else {
+#pragma unroll
+                for (int j = 0; j < W; j++) xb[u][j] = br[0];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const unsigned v = v0 + u * kThreads;
+            if (v >= Lv) continue;
+            T r2[W];
+#pragma unroll
+            for (int j = 0; j < W; j++) r2[j] = bin_op<T>(xa[u][j], xb[u][j], OP);
+            vstore(orow + (size_t)v * W, r2);
+        }
+    }
+}
+
+template <typename T, int OP>
+void launch_bcast_rows(Ctx& c, T* out, const T* a, const T* b, const Bcast& g, const FastDiv& fd,
+                       unsigned rows, unsigned Lv) {
+    const unsigned chunks = (Lv + kThreads * 4 - 1) / (kThreads * 4);
+    const size_t tasks = (size_t)rows * chunks;
+    const size_t cap = (size_t)c.dev->sm_count * 8;
+    const unsigned grid = (unsigned)(tasks < cap ? tasks : cap);
+    k_bcast_rows<T, OP><<<grid, kThreads, 0, c.stream>>>(out, a, b, g, fd, rows, Lv, chunks);
+}
+
+template <typename T>
+void bcast_rows_op(Ctx& c, unsigned op, T* out, const T* a, const T* b, const Bcast& g,
+                   const FastDiv& fd, unsigned rows, unsigned Lv) {
+    switch (op) {
+        case 0: return launch_bcast_rows<T, 0>(c, out, a, b, g, fd, rows, Lv);
+        case 1: return launch_bcast_rows<T, 1>(c, out, a, b, g, fd, rows, Lv);
+        case 2: return launch_bcast_rows<T, 2>(c, out, a, b, g, fd, rows, Lv);
+        case 3: return launch_bcast_rows<T, 3>(c, out, a, b, g, fd, rows, Lv);
+        case 4: return launch_bcast_rows<T, 4>(c, out, a, b, g, fd, rows, Lv);
+        case 5: return launch_bcast_rows<T, 5>(c, out, a, b, g, fd, rows, Lv);
+        case 6: return launch_bcast_rows<T, 6>(c, out, a, b, g, fd, rows, Lv);
+        case 7: return launch_bcast_rows<T, 7>(c, out, a, b, g, fd, rows, Lv);
+        case 8: return launch_bcast_rows<T, 8>(c, out, a, b, g, fd, rows, Lv);
+        default: return launch_bcast_rows<T, 9>(c, out, a, b, g, fd, rows, Lv);
+    }
+}
+
 // ---- transpose --------------------------------------------------------------
 
-// 32 x 32 tile through shared memory, 32 x 8 threads, 4 elements each:
-// coalesced row reads of A and row writes of the output.
-template <typename T>
+// TS x TS tile through shared memory (padded rows: conflict-free column
+// reads), 32 x 8 threads, each moving (TS/32) x (TS/8) elements: coalesced
+// row reads of A and row writes of the output.  TS = 64 for f32 (16 KB per
+// CTA in flight), 32 for f64 (8 KB).
+template <typename T, int TS>
 __global__ void __launch_bounds__(256) k_transpose(T* __restrict__ out, const T* __restrict__ a,
                                                    unsigned m, unsigned n) {
-    __shared__ T tile[32][33];
-    const unsigned bx = blockIdx.x * 32, by = blockIdx.y * 32;
-    const unsigned x = bx + threadIdx.x;
+    __shared__ T tile[TS][TS + 1];
+    const unsigned bx = blockIdx.x * TS, by = blockIdx.y * TS;
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
+    for (int j = 0; j < TS; j += 8) {
         const unsigned y = by + threadIdx.y + j;
-        if (x < n && y < m) tile[threadIdx.y + j][threadIdx.x] = a[(size_t)y * n + x];
+#pragma unroll
+        for (int i = 0; i < TS; i += 32) {
+            const unsigned x = bx + threadIdx.x + i;
+            if (x < n && y < m) tile[threadIdx.y + j][threadIdx.x + i] = a[(size_t)y * n + x];
+        }
     }
     __syncthreads();
-    const unsigned ox = by + threadIdx.x;  // out is n x m
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-        const unsigned oy = bx + threadIdx.y + j;
-        if (ox < m && oy < n) out[(size_t)oy * m + ox] = tile[threadIdx.x][threadIdx.y + j];
+    for (int j = 0; j < TS; j += 8) {
+        const unsigned oy = bx + threadIdx.y + j;  // out is n x m
+#pragma unroll
+        for (int i = 0; i < TS; i += 32) {
+            const unsigned ox = by + threadIdx.x + i;
+            if (ox < m && oy < n) out[(size_t)oy * m + ox] = tile[threadIdx.x + i][threadIdx.y + j];
+        }
     }
 }
 
@@ -470,7 +595,10 @@ int launch_cast(Ctx& c, int to_f64, void* out, const void* a, size_t n) {
     if (n == 0) return OK;
     const int vec = al16(out) && al16(a);
     unsigned g = grid_for(c, vec ? (n / 4 + kUnroll - 1) / kUnroll : n, kThreads, 8);
-    if (to_f64)
+    if (to_f64 && al16(out) && (((uintptr_t)a) & 7) == 0) {
+        const unsigned g2 = grid_for(c, (n / 2 + 7) / 8, kThreads, 8);
+        k_cast_up<<<g2, kThreads, 0, c.stream>>>((double*)out, (const float*)a, n);
+    } else if (to_f64)
         k_cast<double, float><<<g, kThreads, 0, c.stream>>>((double*)out, (const float*)a, n, vec);
     else
         k_cast<float, double><<<g, kThreads, 0, c.stream>>>((float*)out, (const double*)a, n, vec);
@@ -511,6 +639,18 @@ int launch_broadcast(Ctx& c, int dt, void* out, const void* a, const void* b, un
             fd.m[d] = (sd <= 1) ? 0ull : (~0ull) / sd + 1ull;  // ceil(2^64 / sd), sd >= 2
         }
         const unsigned nv = (unsigned)(n / W);
+        const unsigned Lv = g.shape[last] / W;
+        if (Lv >= 64 && bcast_rows_enabled()) {
+            const unsigned rows = (unsigned)(n / g.shape[last]);
+            if (dt == F32)
+                bcast_rows_op<float>(c, op, (float*)out, (const float*)a, (const float*)b, g, fd,
+                                     rows, Lv);
+            else
+                bcast_rows_op<double>(c, op, (double*)out, (const double*)a, (const double*)b, g, fd,
+                                      rows, Lv);
+            count_launch();
+            return finish(c);
+        }
         unsigned grid = grid_for(c, (nv + 3) / 4, kThreads, 8);
         if (dt == F32)
             k_bcast_fast<float><<<grid, kThreads, 0, c.stream>>>((float*)out, (const float*)a,
@@ -552,9 +692,14 @@ int launch_transpose(Ctx& c, int dt, void* out, const void* a, unsigned m, unsig
 
 int enqueue_transpose(Ctx& c, int dt, void* out, const void* a, unsigned m, unsigned n) {
     if (m == 0 || n == 0) return OK;
-    dim3 grid((n + 31) / 32, (m + 31) / 32), block(32, 8);
-    if (dt == F32) k_transpose<float><<<grid, block, 0, c.stream>>>((float*)out, (const float*)a, m, n);
-    else k_transpose<double><<<grid, block, 0, c.stream>>>((double*)out, (const double*)a, m, n);
+    const dim3 block(32, 8);
+    if (dt == F32) {
+        const dim3 grid((n + 63) / 64, (m + 63) / 64);
+        k_transpose<float, 64><<<grid, block, 0, c.stream>>>((float*)out, (const float*)a, m, n);
+    } else {
+        const dim3 grid((n + 31) / 32, (m + 31) / 32);
+        k_transpose<double, 32><<<grid, block, 0, c.stream>>>((double*)out, (const double*)a, m, n);
+    }
     count_launch();
     return OK;
 }

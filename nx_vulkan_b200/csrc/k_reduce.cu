@@ -54,7 +54,7 @@ template <> struct SumR<double> {
 };
 
 template <typename T, bool MAX> struct MaxR {
-    static constexpr int kU = 4;
+    static constexpr int kU = 8;
     using Acc = T;
     using Out = T;
     __device__ static Acc init() { return MAX ? -INFINITY : INFINITY; }
@@ -192,16 +192,18 @@ k_rows(const T* __restrict__ a, size_t R_, size_t L, void* out, typename R::Acc*
     }
 }
 
-// Many rows: one warp per row, no shared memory or barrier.  Lane l takes
-// vectors l, l+32, ... into U accumulators (vector v goes to accumulator
-// (v / 32) % U, so each accumulator sees increasing indices; U = 8 for f64,
-// 4 for f32, the faster of the two for 4096-element rows); the U
-// accumulators are combined in order, then a shuffle tree (lane i takes lane
-// i + off) -- a fixed order.  Requires R_ < 2^31 (32-bit element index).
-template <class R, typename T>
-__global__ void __launch_bounds__(kThreads)
+// Many rows: one warp per row, RPC rows (warps) per CTA, no shared memory or
+// barrier.  Lane l takes vectors l, l+32, ... into U accumulators (vector v
+// goes to accumulator (v / 32) % U, so each accumulator sees increasing
+// indices; U = 8 for f64, 4 for f32); the U accumulators are combined in
+// order, then a shuffle tree (lane i takes lane i + off) -- a fixed order.
+// Small CTAs (RPC = 2) spread the rows evenly over the SMs: with 8 rows per
+// CTA, 4096 rows leave some SMs 4 CTAs and others 3.  Requires R_ < 2^31
+// (32-bit element index).
+template <class R, typename T, int RPC>
+__global__ void __launch_bounds__(32 * RPC)
 k_rows_warp(const T* __restrict__ a, size_t outer, unsigned R_, void* out, int index_bytes) {
-    const size_t r = (size_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+    const size_t r = (size_t)blockIdx.x * RPC + (threadIdx.x >> 5);
     const unsigned lane = threadIdx.x & 31;
     if (r >= outer) return;  // the whole warp leaves together
     const T* row = a + r * R_;
@@ -242,6 +244,24 @@ k_rows_warp(const T* __restrict__ a, size_t outer, unsigned R_, void* out, int i
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc = R::combine(acc, R::shfl(acc, off));
     if (lane == 0) write_out<R, T>(out, r, acc, index_bytes);
+}
+
+// Rows (warps) per CTA of the row kernels: NXV_ROW_CTA = 2, 4 or 8 (default 2).
+int rows_per_cta() {
+    if (const char* e = getenv("NXV_ROW_CTA")) {
+        const int g = atoi(e);
+        if (g == 2 || g == 4 || g == 8) return g;
+    }
+    return 2;
+}
+
+template <class R, typename T>
+void launch_rows_warp(Ctx& c, const T* a, size_t outer, unsigned R_, void* out, int index_bytes) {
+    const int rpc = rows_per_cta();
+    const unsigned ctas = (unsigned)((outer + rpc - 1) / rpc);
+    if (rpc == 8) k_rows_warp<R, T, 8><<<ctas, 256, 0, c.stream>>>(a, outer, R_, out, index_bytes);
+    else if (rpc == 4) k_rows_warp<R, T, 4><<<ctas, 128, 0, c.stream>>>(a, outer, R_, out, index_bytes);
+    else k_rows_warp<R, T, 2><<<ctas, 64, 0, c.stream>>>(a, outer, R_, out, index_bytes);
 }
 
 // Fold S partials per output in index order.
@@ -308,14 +328,11 @@ int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* 
         S = (R_ + L - 1) / L;
         if (S == 0) S = 1;
         if (S == 1 && R_ < 0x80000000ull) {
-            const size_t rows_per_cta = kThreads / 32;
-            const size_t ctas = (outer + rows_per_cta - 1) / rows_per_cta;
-            if (ctas > 0x7fffffffull) {
+            if ((outer + 1) / 2 > 0x7fffffffull) {
                 set_error("too many rows for a reduce");
                 return E_ARG;
             }
-            k_rows_warp<R, T><<<(unsigned)ctas, kThreads, 0, c.stream>>>(a, outer, (unsigned)R_, out,
-                                                                         index_bytes);
+            launch_rows_warp<R, T>(c, a, outer, (unsigned)R_, out, index_bytes);
             count_launch();
             return finish(c);
         }
@@ -385,62 +402,115 @@ int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* 
 
 // ---- logsumexp (f32 in/out, f64 math) --------------------------------------------
 
-// One warp per row: pass 1 the row max, pass 2 sum exp(x - max) in double
-// (the row is read again, mostly from L1), then log(sum) + max.  EX: exp in
-// f64 (the oracle's evaluation; NXV_EXACT_F32=1), else expf of the f32
-// difference.  Shuffle trees in a fixed order.
+// One warp per row, one pass over the row (online logsumexp).  Each lane
+// keeps a running max m and s = sum of exp(x - m) over the elements it has
+// seen (double); when a group of 16 elements raises the max, s is rescaled by
+// exp(m_old - m_new).  The 32 lane states merge in a fixed shuffle tree:
+// s = s_a exp(m_a - M) + s_b exp(m_b - M).  The special values follow the
+// two-pass definition the oracle uses (max ignoring NaN, then sum of
+// exp(x - max)): a NaN, a +inf, or a row of only -inf/NaN gives NaN (lanes
+// whose elements are all -inf, or that have none, hold m = -inf, s = 0).  NaN
+// never enters m (fmaxf ignores it); while m is -inf every element seen was
+// -inf or NaN, and terms are taken against 0 so that NaN propagates and -inf
+// adds 0.  EX: exp in f64 (the oracle's evaluation; NXV_EXACT_F32=1), else
+// expf of the f32 difference with 16 terms summed in f32 before the double
+// add.
 template <bool EX>
-__global__ void __launch_bounds__(kThreads)
+struct LseLane {
+    float m = -INFINITY;
+    double s = 0.0;
+    __device__ __forceinline__ void raise_to(float bm) {
+        if (bm > m) {
+            if constexpr (EX) s *= exp((double)m - (double)bm);
+            else s *= (double)expf(m - bm);
+            m = bm;
+        }
+    }
+    __device__ __forceinline__ float ref() const { return m == -INFINITY ? 0.f : m; }
+    __device__ __forceinline__ double term(float x, float r) const {
+        if constexpr (EX) return exp((double)x - (double)r);
+        else return (double)expf(x - r);
+    }
+};
+
+template <bool EX, int U>
+__device__ __forceinline__ void lse_group(LseLane<EX>& L, const float4 (&x)[U]) {
+    float bm = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < U; u++) bm = fmaxf(bm, fmaxf(fmaxf(x[u].x, x[u].y), fmaxf(x[u].z, x[u].w)));
+    L.raise_to(bm);
+    const float r = L.ref();
+    if constexpr (EX) {
+        double t = 0.0;
+#pragma unroll
+        for (int u = 0; u < U; u++)
+            t = __dadd_rn(t, __dadd_rn(__dadd_rn(L.term(x[u].x, r), L.term(x[u].y, r)),
+                                       __dadd_rn(L.term(x[u].z, r), L.term(x[u].w, r))));
+        L.s = __dadd_rn(L.s, t);
+    } else {
+        float t = 0.f;
+#pragma unroll
+        for (int u = 0; u < U; u++)
+            t = add_(t, add_(add_(expf(x[u].x - r), expf(x[u].y - r)),
+                             add_(expf(x[u].z - r), expf(x[u].w - r))));
+        L.s = __dadd_rn(L.s, (double)t);
+    }
+}
+
+template <bool EX>
+__device__ __forceinline__ void lse_merge(LseLane<EX>& L, float mo, double so) {
+    const float M = fmaxf(L.m, mo);
+    // factor 1 for the side that holds the max (also when both are -inf:
+    // two lanes without finite elements must not make 0 * exp(NaN))
+    const double fa = L.m == M ? 1.0 : exp((double)L.m - (double)M);
+    const double fb = mo == M ? 1.0 : exp((double)mo - (double)M);
+    L.s = __dadd_rn(__dmul_rn(L.s, fa), __dmul_rn(so, fb));
+    L.m = M;
+}
+
+// One warp per row, RPC rows per CTA (as k_rows_warp).
+template <bool EX, int RPC>
+__global__ void __launch_bounds__(32 * RPC)
 k_lse_rows(const float* __restrict__ a, size_t outer, unsigned R_, float* __restrict__ out) {
-    const size_t r = (size_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+    const size_t r = (size_t)blockIdx.x * RPC + (threadIdx.x >> 5);
     const unsigned lane = threadIdx.x & 31;
     if (r >= outer) return;
     const float* row = a + r * R_;
     const bool vec = (((uintptr_t)row) & 15) == 0;
     const unsigned nv = vec ? R_ / 4 : 0;
     const float4* rv = reinterpret_cast<const float4*>(row);
-    constexpr int U = 4;  // 16-byte loads in flight per lane
-    float mx = -INFINITY;
-    {
-        unsigned v = lane;
-        for (; v + (U - 1) * 32 < nv; v += 32 * U) {
-            float4 x[U];
+    constexpr int U = EX ? 2 : 4;  // 16-byte loads in flight per lane (EX: f64 exp is register-heavy)
+    LseLane<EX> L;
+    unsigned v = lane;
+    for (; v + (U - 1) * 32 < nv; v += 32 * U) {
+        float4 x[U];
 #pragma unroll
-            for (int u = 0; u < U; u++) x[u] = rv[v + u * 32];
-#pragma unroll
-            for (int u = 0; u < U; u++) mx = fmaxf(mx, fmaxf(fmaxf(x[u].x, x[u].y), fmaxf(x[u].z, x[u].w)));
-        }
-        for (; v < nv; v += 32) {
-            const float4 x = rv[v];
-            mx = fmaxf(mx, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
-        }
+        for (int u = 0; u < U; u++) x[u] = __ldcs(rv + v + u * 32);
+        lse_group<EX, U>(L, x);
     }
-    for (unsigned e = nv * 4 + lane; e < R_; e += 32) mx = fmaxf(mx, row[e]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    auto term = [&](float x) -> double {
-        if constexpr (EX) return exp((double)x - (double)mx);
-        else return (double)expf(x - mx);
-    };
-    auto term4 = [&](float4 x) -> double {
-        return __dadd_rn(__dadd_rn(term(x.x), term(x.y)), __dadd_rn(term(x.z), term(x.w)));
-    };
-    double s = 0.0;
-    {
-        unsigned v = lane;
-        for (; v + (U - 1) * 32 < nv; v += 32 * U) {
-            float4 x[U];
-#pragma unroll
-            for (int u = 0; u < U; u++) x[u] = rv[v + u * 32];
-#pragma unroll
-            for (int u = 0; u < U; u++) s = __dadd_rn(s, term4(x[u]));
-        }
-        for (; v < nv; v += 32) s = __dadd_rn(s, term4(rv[v]));
+    for (; v < nv; v += 32) {
+        float4 x[1] = {__ldcs(rv + v)};
+        lse_group<EX, 1>(L, x);
     }
-    for (unsigned e = nv * 4 + lane; e < R_; e += 32) s = __dadd_rn(s, term(row[e]));
+    for (unsigned e = nv * 4 + lane; e < R_; e += 32) {
+        const float x = row[e];
+        L.raise_to(x);
+        L.s = __dadd_rn(L.s, L.term(x, L.ref()));
+    }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s = __dadd_rn(s, __shfl_down_sync(0xffffffffu, s, off));
-    if (lane == 0) out[r] = (float)(log(s) + (double)mx);
+    for (int off = 16; off > 0; off >>= 1)
+        lse_merge(L, __shfl_down_sync(0xffffffffu, L.m, off), __shfl_down_sync(0xffffffffu, L.s, off));
+    if (lane == 0)
+        out[r] = L.m == -INFINITY ? __int_as_float(0x7fc00000) : (float)(log(L.s) + (double)L.m);
+}
+
+template <bool EX>
+void launch_lse_rows(Ctx& c, const float* a, size_t outer, unsigned R_, float* out) {
+    const int rpc = rows_per_cta();
+    const unsigned ctas = (unsigned)((outer + rpc - 1) / rpc);
+    if (rpc == 8) k_lse_rows<EX, 8><<<ctas, 256, 0, c.stream>>>(a, outer, R_, out);
+    else if (rpc == 4) k_lse_rows<EX, 4><<<ctas, 128, 0, c.stream>>>(a, outer, R_, out);
+    else k_lse_rows<EX, 2><<<ctas, 64, 0, c.stream>>>(a, outer, R_, out);
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -551,17 +621,12 @@ int launch_argmax(Ctx& c, int dt, void* out, const void* a, size_t outer, size_t
 int launch_logsumexp(Ctx& c, void* out, const void* a, size_t outer, size_t R, size_t inner) {
     if (R == 0 || outer == 0 || inner == 0) return OK;
     if (inner == 1) {
-        const size_t ctas = (outer + kThreads / 32 - 1) / (kThreads / 32);
-        if (ctas > 0x7fffffff || R > 0xffffffffull) {
+        if ((outer + 1) / 2 > 0x7fffffff || R > 0xffffffffull) {
             set_error("logsumexp extents out of range");
             return E_ARG;
         }
-        if (fast_f32())
-            k_lse_rows<false><<<(unsigned)ctas, kThreads, 0, c.stream>>>((const float*)a, outer,
-                                                                         (unsigned)R, (float*)out);
-        else
-            k_lse_rows<true><<<(unsigned)ctas, kThreads, 0, c.stream>>>((const float*)a, outer,
-                                                                        (unsigned)R, (float*)out);
+        if (fast_f32()) launch_lse_rows<false>(c, (const float*)a, outer, (unsigned)R, (float*)out);
+        else launch_lse_rows<true>(c, (const float*)a, outer, (unsigned)R, (float*)out);
     } else {
         if (outer > 65535) return E_ARG;
         dim3 grid((unsigned)((inner + kThreads - 1) / kThreads), (unsigned)outer);

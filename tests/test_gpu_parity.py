@@ -81,7 +81,10 @@ def test_broadcast_shapes(nxv, orc, dt):
              # vector path with 32-bit index decoding: large and odd outer dims,
              # broadcast on either side and on middle dims
              ((3, 70001, 4), (70001, 1)), ((8,), (6, 8)), ((2, 3, 5, 8), (3, 1, 8)),
-             ((1000, 12), (1000, 1)), ((5, 131072), (5, 1)), ((6, 1, 16), (7, 1))]
+             ((1000, 12), (1000, 1)), ((5, 131072), (5, 1)), ((6, 1, 16), (7, 1)),
+             # row path: innermost extent of >= 64 vectors, several chunks per row
+             ((3, 4, 512), (4, 1)), ((2, 3, 5, 1024), (3, 1, 1024)), ((7, 1032), (1032,)),
+             ((2, 4100), (4100,)), ((1, 2048), (9, 2048)), ((3, 1, 8192), (5, 1))]
     spv = nxv.shader_path("elementwise_binary_broadcast.spv" if dt == np.float32
                           else "elementwise_binary_broadcast_f64.spv")
     for sa, sb in cases:
@@ -94,6 +97,28 @@ def test_broadcast_shapes(nxv, orc, dt):
             got = down(nxv, t, dt)
             want = orc.broadcast(a.reshape(-1), b.reshape(-1), op, len(out), list(out), ast, bst)
             assert np.array_equal(got, want), (sa, sb, op)
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_broadcast_rows_all_ops(nxv, orc, dt):
+    """Every binary op on the row path (one kernel instantiation per op)."""
+    r = np.random.default_rng(6)
+    a = np.abs(r.normal(size=(33, 1536))).astype(dt) + 0.5
+    b = r.normal(size=(1536,)).astype(dt)
+    b[::7] = a[0, ::7]   # some equal pairs for the comparisons
+    out = (33, 1536)
+    ast, bst = nxv.broadcast_strides(a.shape, out), nxv.broadcast_strides(b.shape, out)
+    spv = nxv.shader_path("elementwise_binary_broadcast.spv" if dt == np.float32
+                          else "elementwise_binary_broadcast_f64.spv")
+    for op in range(10):
+        t = unwrap(nxv._broadcast(up(nxv, a.reshape(-1)), up(nxv, b), op, 2, nxv._pad4(out), ast, bst,
+                                  spv, a.itemsize))
+        got = down(nxv, t, dt)
+        want = orc.broadcast(a.reshape(-1), b, op, 2, list(out), ast, bst)
+        if op == 4:   # pow: f64 evaluation rounded once on both sides
+            close(got, want, 1e-6 if dt == np.float32 else 1e-14, 0.0)
+        else:
+            assert np.array_equal(got, want), op
 
 
 def test_broadcast_config_rows(nxv, orc):
@@ -210,6 +235,36 @@ def test_argmax_bit_exact(nxv, orc, shape, dt):
             assert np.array_equal(got.astype(np.int64), want)
 
 
+@pytest.mark.parametrize("g", ["2", "4", "8"])
+def test_row_kernels_all_cta_sizes(nxv, orc, monkeypatch, g):
+    """The row kernels (>= 296 rows; one warp per row) with 2, 4 and 8 rows per
+    CTA: max, min and argmax bit-exact, sums and logsumexp within their
+    tolerances; rows of aligned and unaligned starts, shorter than one warp
+    chunk, and long; row counts that leave the last CTA partly empty."""
+    monkeypatch.setenv("NXV_ROW_CTA", g)
+    for outer, R in ((300, 4096), (1001, 7), (5001, 1001), (333, 10003)):
+        for dt in (np.float32, np.float64):
+            x = np.random.default_rng(8).normal(size=outer * R).astype(dt)
+            x[::53] = np.round(x[::53])
+            t = up(nxv, x)
+            spv = nxv.shader_path("reduce_axis.spv" if dt == np.float32 else "reduce_axis_f64.spv")
+            for op in (0, 1, 2):
+                got = down(nxv, unwrap(nxv._reduce_axis(t, outer, R, 1, op, spv, x.itemsize)), dt)
+                want = orc.reduce_axis(x, outer, R, 1, op)
+                if op == 0:
+                    xs = np.abs(x.reshape(outer, R)).astype(np.float64).sum(axis=1)
+                    tol = 1e-5 * np.abs(want) + 1e-6 if dt == np.float32 else 1e-12 * np.abs(want) + 4 * 2.2e-16 * xs
+                    assert np.all(np.abs(got - want) <= tol)
+                else:
+                    assert np.array_equal(got, want)
+            dts = "f32" if dt == np.float32 else "f64"
+            got = down(nxv, unwrap(nxv.argmax_axis(t, outer, R, 1, dtype=dts)), np.int64)
+            assert np.array_equal(got, orc.argmax_axis(x, outer, R, 1, False))
+            if dt == np.float32:
+                got = down(nxv, unwrap(nxv.logsumexp(t, outer, R, 1)), np.float32)
+                close(got, orc.logsumexp(x, outer, R, 1), 1e-5, 1e-6)
+
+
 def test_argmax_ties_and_nan(nxv, orc):
     x = np.array([1, 3, 3, 2, 5, 5, np.nan, 5, np.nan, 0, 0, 0], np.float32)
     t = up(nxv, x)
@@ -229,6 +284,41 @@ def test_logsumexp(nxv, orc, monkeypatch, exact):
         x = np.random.default_rng(2).normal(size=int(np.prod(shape))).astype(np.float32) * 10
         got = down(nxv, unwrap(nxv.logsumexp(up(nxv, x), *shape)), np.float32)
         close(got, orc.logsumexp(x, *shape), 1e-5, 1e-6)
+
+
+@pytest.mark.parametrize("exact", ["0", "1"])
+def test_logsumexp_special_values(nxv, orc, monkeypatch, exact):
+    """IEEE specials as in the two-pass definition: -inf elements add 0,
+    a NaN or +inf gives NaN, a row of only -inf gives NaN; the max moving
+    late in a row (ascending rows) exercises the rescaling."""
+    monkeypatch.setenv("NXV_EXACT_F32", exact)
+    R = 600
+    rows = np.random.default_rng(4).normal(size=(12, R)).astype(np.float32)
+    rows[0, :500] = -np.inf               # leading -inf, finite max later
+    rows[1, :] = -np.inf                  # only -inf
+    rows[2, 17] = np.nan
+    rows[3, 599] = np.inf
+    rows[4, :] = np.nan
+    rows[5, :] = np.sort(rows[5]) * 30    # ascending: the max rises at every group
+    rows[6, :] = np.sort(rows[6])[::-1] * 30
+    rows[7, :] = 88.0                      # exp would overflow without the shift
+    rows[8, ::2] = -np.inf
+    rows[9, :300] = np.nan
+    rows[9, 300:] = -np.inf
+    rows[10, :] = -1e30
+    rows[11, 0] = 1e30
+    x = rows.reshape(-1)
+    got = down(nxv, unwrap(nxv.logsumexp(up(nxv, x), 12, R, 1)), np.float32)
+    want = orc.logsumexp(x, 12, R, 1)
+    assert np.array_equal(np.isnan(got), np.isnan(want)), (got, want)
+    ok = ~np.isnan(want)
+    close(got[ok], want[ok], 1e-5, 1e-6)
+    # one more column of -inf: rows of 601 start unaligned (scalar path) and
+    # the results do not change
+    x2 = np.concatenate([rows, np.full((12, 1), -np.inf, np.float32)], axis=1).reshape(-1)
+    got2 = down(nxv, unwrap(nxv.logsumexp(up(nxv, x2), 12, R + 1, 1)), np.float32)
+    assert np.array_equal(np.isnan(got2), np.isnan(want))
+    close(got2[ok], want[ok], 1e-5, 1e-6)
 
 
 @pytest.mark.parametrize("mnk", [(1, 1, 1), (2, 2, 2), (17, 33, 9), (128, 128, 128), (130, 70, 257),
