@@ -205,6 +205,9 @@ def test_gauss_full_config(nxv, orc):
     (10000, 100, 256, 2), (997, 7, 130, 3),
     # fewer observations than one tile, model dims at each tile-width boundary
     (5, 2, 1, 1), (333, 32, 3, 2), (333, 33, 3, 2), (777, 64, 9, 2), (777, 104, 9, 2),
+    # partial tiles; one observation; slices of more than 64 tiles (the
+    # running-product flush)
+    (1001, 50, 33, 2), (1, 2, 1, 1), (160000, 4, 4, 1),
     # general (two-GEMM) path
     (300, 120, 4, 2)])
 @pytest.mark.parametrize("split", ["1", "2"])
@@ -219,5 +222,6 @@ def test_logreg_vs_oracle(nxv, orc, monkeypatch, N, D, C, K, split):
     eps = 0.002
     outs = unwrap(nxv.leapfrog_logreg_f64_batched(up(nxv, q0), up(nxv, p0), up(nxv, X), up(nxv, y), N, D, C, K, eps))
     want = orc.chain_logreg_f64(q0, p0, X, y, N, D, C, K, eps)
+    assert nxv.synchronize() == "ok"  # no bounded pipeline wait ran out
     for t, wv in zip(outs, want):
         close(down(nxv, t, np.float64), wv, 1e-10, 1e-10)
