@@ -673,6 +673,8 @@ def suite(args):
     crng = np.random.default_rng(11)
 
     def cpu_est(fn, scale, cores, sample, min_s=0.2):
+        if args.no_cpu:
+            return None
         fn()
         reps, t0 = 0, time.perf_counter()
         while True:
