@@ -260,6 +260,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--diag-depth", type=int, default=4,
+                    help="N > 1: diagnostics buffers in flight (collective of step i waited for at step i + depth)")
     ap.add_argument("--suite", action="store_true",
                     help="measure every hot-path workload (one JSON line each) instead of the headline")
     ap.add_argument("--only", default="fused,reduce,random,misc,matmul,logreg,nuts",
@@ -327,18 +329,22 @@ def main():
             raise RuntimeError(f"leapfrog failed: {rc} {_native.last_error()}")
 
     # Diagnostics exchange: the final-step logp of every chain, all-gathered
-    # on a side stream so that the collective of step i overlaps step i+1.
-    # Two buffers alternate; before buffer b is refilled the main stream waits
-    # for the collective that read it two steps earlier.
-    diags = [torch.empty(world * chains, dtype=torch.float64, device=dev) for _ in range(2)]
-    lasts = [torch.empty(chains, dtype=torch.float64, device=dev) for _ in range(2)]
-    side_done = [None, None]
-    side = torch.cuda.Stream(device=dev)
+    # on a side stream so that the collective of step i overlaps the next
+    # steps.  `depth` buffers rotate; before buffer b is refilled the main
+    # stream waits for the collective that read it `depth` steps earlier.
+    depth = max(2, args.diag_depth)
+    diags = [torch.empty(world * chains, dtype=torch.float64, device=dev) for _ in range(depth)]
+    lasts = [torch.empty(chains, dtype=torch.float64, device=dev) for _ in range(depth)]
+    side_done = [None] * depth
+    # High priority: the collective's CTAs are dispatched ahead of the chain
+    # kernel's pending CTAs (a 4096-CTA grid), so it runs during the next
+    # step instead of after that step's last wave.
+    side = torch.cuda.Stream(device=dev, priority=-1)
 
     def diagnostics(i):
         if world == 1:
             return
-        b = i % 2
+        b = i % depth
         if side_done[b] is not None:
             stream.wait_event(side_done[b])
         lasts[b].copy_(outs[3].view(chains, L)[:, -1])
@@ -383,6 +389,17 @@ def main():
         b.record(stream)
     torch.cuda.synchronize()
     k_ms = statistics.median([a.elapsed_time(b) for a, b in kev])
+    # per-rank view of a multi-GPU run: step time, the kernel alone, SM clock
+    ranks_info = None
+    if world > 1:
+        loc = torch.tensor([t0_ev.elapsed_time(t1_ev) / args.steps, k_ms,
+                            float(clocks.get("sm_mhz") or 0.0), float(len(clocks.get("reasons") or []))],
+                           dtype=torch.float64, device=dev)
+        allr = torch.empty(world * 4, dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(allr, loc)
+        rows = allr.view(world, 4).cpu().tolist()
+        ranks_info = {"step_ms": [r[0] for r in rows], "kernel_alone_ms": [r[1] for r in rows],
+                      "sm_mhz": [r[2] for r in rows], "clock_event_reasons": [int(r[3]) for r in rows]}
     peak, peak_kind = peaks()
     abytes = algo_bytes(chains)
     achieved = abytes / (k_ms / 1e3) / 1e9
@@ -519,13 +536,15 @@ def main():
             "config": {"workload": "anisotropic Gaussian HMC leapfrog, fused K-step chain",
                        "chains_per_gpu": chains, "d": D, "L": L, "eps": EPS, "inv_mass": 1.0,
                        "parallelism": f"chains sharded, {world} rank(s), NCCL all-gather of final logp per step "
-                                      f"(overlapped with the next step; NCCL_PROTO={os.environ.get('NCCL_PROTO')})"
+                                      f"on a high-priority side stream, waited for {depth} steps later "
+                                      f"(NCCL_PROTO={os.environ.get('NCCL_PROTO')})"
                        if world > 1 else "1 GPU",
                        "l2": "inputs larger than L2: 3 rotating input sets of 98 MB (295 MB > 2x 126 MB); "
                              "3.15 GB of trajectory writes per step",
                        "timing": "one CUDA event pair around all timed steps on the launching stream, "
                                  "collectives included; max over ranks"},
             "gpu_launches": int(launches),
+            **({"ranks": ranks_info} if ranks_info else {}),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
