@@ -260,6 +260,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--diag-every", type=int, default=1,
+                    help="N > 1: steps whose final logps go out in one all-gather (default: every step)")
     ap.add_argument("--diag-depth", type=int, default=4,
                     help="N > 1: diagnostics buffers in flight (collective of step i waited for at step i + depth)")
     ap.add_argument("--suite", action="store_true",
@@ -329,33 +331,37 @@ def main():
             raise RuntimeError(f"leapfrog failed: {rc} {_native.last_error()}")
 
     # Diagnostics exchange: the final-step logp of every chain, all-gathered
-    # on a side stream so that the collective of step i overlaps the next
-    # steps.  `depth` buffers rotate; before buffer b is refilled the main
-    # stream waits for the collective that read it `depth` steps earlier.
+    # on a side stream so that the collective overlaps the next steps.  The
+    # logps of `every` consecutive steps go out in one collective (every x
+    # chains values per rank; the last group of a run is flushed even when
+    # short).  `depth` buffers rotate; before buffer b is refilled the main
+    # stream waits for the collective that read it `depth` groups earlier.
     depth = max(2, args.diag_depth)
-    diags = [torch.empty(world * chains, dtype=torch.float64, device=dev) for _ in range(depth)]
-    lasts = [torch.empty(chains, dtype=torch.float64, device=dev) for _ in range(depth)]
+    every = max(1, args.diag_every)
+    diags = [torch.empty(world * every * chains, dtype=torch.float64, device=dev) for _ in range(depth)]
+    lasts = [torch.empty(every * chains, dtype=torch.float64, device=dev) for _ in range(depth)]
     side_done = [None] * depth
     # High priority: the collective's CTAs are dispatched ahead of the chain
     # kernel's pending CTAs (a 4096-CTA grid), so it runs during the next
     # step instead of after that step's last wave.
     side = torch.cuda.Stream(device=dev, priority=-1)
 
-    def diagnostics(i):
+    def diagnostics(i, final=False):
         if world == 1:
             return
-        b = i % depth
-        if side_done[b] is not None:
+        b, j = (i // every) % depth, i % every
+        if j == 0 and side_done[b] is not None:
             stream.wait_event(side_done[b])
-        lasts[b].copy_(outs[3].view(chains, L)[:, -1])
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            dist.all_gather_into_tensor(diags[b], lasts[b])
-        side_done[b] = side.record_event()
+        lasts[b][j * chains:(j + 1) * chains].copy_(outs[3].view(chains, L)[:, -1])
+        if j == every - 1 or final:
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                dist.all_gather_into_tensor(diags[b], lasts[b])
+            side_done[b] = side.record_event()
 
     for i in range(args.warmup):
         step(i)
-        diagnostics(i)
+        diagnostics(i, final=i == args.warmup - 1)
     stream.wait_stream(side)
     torch.cuda.synchronize()
     n_launch0 = lib.nxv_launch_count()
@@ -367,7 +373,7 @@ def main():
         t0_ev.record(stream)
         for i in range(args.steps):
             step(i)
-            diagnostics(i)
+            diagnostics(i, final=i == args.steps - 1)
         stream.wait_stream(side)  # the final collective is inside the timed region
         t1_ev.record(stream)
         torch.cuda.synchronize()
@@ -535,8 +541,9 @@ def main():
             "data": "synthetic (seeded numpy: prec~U(0.5,2) seed 3, q0,p0~N(0,1); rank r uses seed 3+1000r)",
             "config": {"workload": "anisotropic Gaussian HMC leapfrog, fused K-step chain",
                        "chains_per_gpu": chains, "d": D, "L": L, "eps": EPS, "inv_mass": 1.0,
-                       "parallelism": f"chains sharded, {world} rank(s), NCCL all-gather of final logp per step "
-                                      f"on a high-priority side stream, waited for {depth} steps later "
+                       "parallelism": f"chains sharded, {world} rank(s), NCCL all-gather of every chain's "
+                                      f"final-step logp, {every} step(s) per collective, on a high-priority "
+                                      f"side stream, waited for {depth} collectives later "
                                       f"(NCCL_PROTO={os.environ.get('NCCL_PROTO')})"
                        if world > 1 else "1 GPU",
                        "l2": "inputs larger than L2: 3 rotating input sets of 98 MB (295 MB > 2x 126 MB); "
