@@ -366,10 +366,13 @@ def main():
     torch.cuda.synchronize()
     n_launch0 = lib.nxv_launch_count()
     t0_ev, t1_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    # The clock sampler starts (NVML initialisation takes milliseconds, and
+    # differently on every rank) before the barrier, so that the ranks leave
+    # the barrier together and start their timed steps at the same moment.
     with Clocks(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         t0_ev.record(stream)
         for i in range(args.steps):
             step(i)
