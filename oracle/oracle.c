@@ -369,7 +369,7 @@ void orc_matmul_batched_f32(float* c, const float* a, const float* b, size_t bat
  * (hi, lo) = mulhilo(0xD256D193, x0); x0' = hi ^ key ^ x1; x1' = lo; the key
  * is bumped by the Weyl constant 0x9E3779B9 between rounds.
  *
- * This build's documented mapping (the contract the GPU kernel must match):
+ * The library's documented mapping (the contract the GPU kernel must match):
  *   f32 uniform:  element i <- word (i & 1) of philox(ctr = (i >> 1, 0), key = seed);
  *                 u = (w >> 8) * 2^-24 in [0, 1).
  *   f32 normal:   elements 2c, 2c+1 <- both words of philox((c, 0), seed):
