@@ -413,8 +413,10 @@ int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* 
 // never enters m (fmaxf ignores it); while m is -inf every element seen was
 // -inf or NaN, and terms are taken against 0 so that NaN propagates and -inf
 // adds 0.  EX: exp in f64 (the oracle's evaluation; NXV_EXACT_F32=1), else
-// expf of the f32 difference with 16 terms summed in f32 before the double
-// add.
+// the hardware exponential __expf of the f32 difference, 16 terms summed in
+// f32 before the double add.  __expf's error grows with |x - max|, but a
+// term's weight in the sum falls as e^(x - max), so the sum stays within a
+// few ulp (13.9 us instead of 15.1 us with expf on [4096, 4096]).
 template <bool EX>
 struct LseLane {
     float m = -INFINITY;
@@ -451,8 +453,8 @@ __device__ __forceinline__ void lse_group(LseLane<EX>& L, const float4 (&x)[U]) 
         float t = 0.f;
 #pragma unroll
         for (int u = 0; u < U; u++)
-            t = add_(t, add_(add_(expf(x[u].x - r), expf(x[u].y - r)),
-                             add_(expf(x[u].z - r), expf(x[u].w - r))));
+            t = add_(t, add_(add_(__expf(x[u].x - r), __expf(x[u].y - r)),
+                             add_(__expf(x[u].z - r), __expf(x[u].w - r))));
         L.s = __dadd_rn(L.s, (double)t);
     }
 }
