@@ -382,7 +382,7 @@ def test_matmul_config_sizes(nxv, orc):
 
 
 @pytest.mark.parametrize("exact", ["0", "1"])
-@pytest.mark.parametrize("n", [1, 2, 7, 1024, 1000001])
+@pytest.mark.parametrize("n", [1, 2, 4, 6, 7, 1024, 1000001])
 def test_philox_matches_oracle(nxv, orc, monkeypatch, n, exact):
     """Uniforms bit-exact; f32 normals within 1e-6 (f32 math by default,
     f64 math rounded once with NXV_EXACT_F32=1); f64 normals within 1e-12."""
