@@ -308,7 +308,8 @@ __device__ __forceinline__ float tf32_hi(float x) {
 // Split A [M][K] (lda = K) into exact-TF32 hi and f32 lo parts, [M][Kp]
 // with zero padding in k in [K, Kp).  Grid (row blocks, batch); each warp
 // walks rows, lane l covering 4-column groups l, l+32, ... of a row with
-// 16-byte loads when the row is 16-byte aligned (K % 4 == 0).
+// 16-byte loads when the row is 16-byte aligned (K % 4 == 0), four groups in
+// flight.
 __global__ void __launch_bounds__(256)
 k_split_rows(const float* __restrict__ A, float* __restrict__ hi, float* __restrict__ lo, int M,
              int K, int Kp, long long sA, long long sO) {
@@ -323,21 +324,35 @@ k_split_rows(const float* __restrict__ A, float* __restrict__ hi, float* __restr
         const float* src = A + (size_t)r * K;
         float* h = hi + (size_t)r * Kp;
         float* l = lo + (size_t)r * Kp;
-        for (int k = lane * 4; k < Kp; k += 128) {  // Kp % 32 == 0: groups never straddle Kp
-            float x[4];
-            if (vec && k + 4 <= K) {
-                const float4 v = *reinterpret_cast<const float4*>(src + k);
-                x[0] = v.x, x[1] = v.y, x[2] = v.z, x[3] = v.w;
-            } else {
+        // U groups of 4 columns per lane in flight (loads first, then the
+        // splits and stores); Kp % 32 == 0, so groups never straddle Kp
+        constexpr int U = 4;
+        for (int k0 = lane * 4; k0 < Kp; k0 += 128 * U) {
+            float x[U][4];
 #pragma unroll
-                for (int e = 0; e < 4; e++) x[e] = k + e < K ? src[k + e] : 0.0f;
+            for (int u = 0; u < U; u++) {
+                const int k = k0 + u * 128;
+                if (k >= Kp) continue;
+                if (vec && k + 4 <= K) {
+                    const float4 v = *reinterpret_cast<const float4*>(src + k);
+                    x[u][0] = v.x, x[u][1] = v.y, x[u][2] = v.z, x[u][3] = v.w;
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) x[u][e] = k + e < K ? src[k + e] : 0.0f;
+                }
             }
-            float4 vh, vl;
-            vh.x = tf32_hi(x[0]), vh.y = tf32_hi(x[1]), vh.z = tf32_hi(x[2]), vh.w = tf32_hi(x[3]);
-            vl.x = __fsub_rn(x[0], vh.x), vl.y = __fsub_rn(x[1], vh.y);
-            vl.z = __fsub_rn(x[2], vh.z), vl.w = __fsub_rn(x[3], vh.w);
-            *reinterpret_cast<float4*>(h + k) = vh;
-            *reinterpret_cast<float4*>(l + k) = vl;
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int k = k0 + u * 128;
+                if (k >= Kp) continue;
+                float4 vh, vl;
+                vh.x = tf32_hi(x[u][0]), vh.y = tf32_hi(x[u][1]);
+                vh.z = tf32_hi(x[u][2]), vh.w = tf32_hi(x[u][3]);
+                vl.x = __fsub_rn(x[u][0], vh.x), vl.y = __fsub_rn(x[u][1], vh.y);
+                vl.z = __fsub_rn(x[u][2], vh.z), vl.w = __fsub_rn(x[u][3], vh.w);
+                *reinterpret_cast<float4*>(h + k) = vh;
+                *reinterpret_cast<float4*>(l + k) = vl;
+            }
         }
     }
 }
@@ -439,10 +454,11 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
     float* bhi = alo + a_elems;
     float* blo = bhi + b_elems;
     {
-        // rows: 8 warps (rows) per CTA, enough CTAs for 8 per SM
-        const size_t row_ctas = (m + 7) / 8;
-        const unsigned gr = (unsigned)std::min<size_t>(row_ctas, (size_t)c.dev->sm_count * 8);
-        k_split_rows<<<dim3(gr, (unsigned)batch), 256, 0, c.stream>>>(
+        // rows: 2 warps (rows) per CTA, so that a few thousand rows spread
+        // evenly over the SMs; at most 32 CTAs per SM
+        const size_t row_ctas = (m + 1) / 2;
+        const unsigned gr = (unsigned)std::min<size_t>(row_ctas, (size_t)c.dev->sm_count * 32);
+        k_split_rows<<<dim3(gr, (unsigned)batch), 64, 0, c.stream>>>(
             (const float*)A, ahi, alo, (int)m, (int)k, (int)Kp, (long long)(m * k),
             (long long)(m * Kp));
         dim3 g2((unsigned)((n + 31) / 32), (unsigned)(Kp / 32), (unsigned)batch);
