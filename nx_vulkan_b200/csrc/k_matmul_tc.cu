@@ -357,23 +357,32 @@ k_split_rows(const float* __restrict__ A, float* __restrict__ hi, float* __restr
     }
 }
 
-// Split and transpose B [K][N] into B^T hi/lo [N][Kp] (32 x 32 tiles).
+// Split and transpose B [K][N] into B^T hi/lo [N][Kp]: tiles of 32 k x 64 n,
+// 32 x 8 threads, 8 elements in flight per thread; the padded row (65) keeps
+// the column reads conflict-free.
 __global__ void k_split_cols(const float* __restrict__ B, float* __restrict__ hi,
                              float* __restrict__ lo, int K, int N, int Kp, long long sB,
                              long long sO) {
-    __shared__ float t[32][33];
+    __shared__ float t[32][65];
     const int bz = blockIdx.z;
     B += bz * sB;
     hi += bz * sO;
     lo += bz * sO;
-    const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
-    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-        const int k = k0 + r, n = n0 + threadIdx.x;
-        t[r][threadIdx.x] = (k < K && n < N) ? B[(size_t)k * N + n] : 0.0f;
+    const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 64;
+#pragma unroll
+    for (int r = threadIdx.y; r < 32; r += 8) {
+        const int k = k0 + r;
+#pragma unroll
+        for (int c = 0; c < 64; c += 32) {
+            const int n = n0 + c + threadIdx.x;
+            t[r][c + threadIdx.x] = (k < K && n < N) ? B[(size_t)k * N + n] : 0.0f;
+        }
     }
     __syncthreads();
-    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-        const int n = n0 + r, k = k0 + threadIdx.x;
+    const int k = k0 + threadIdx.x;
+#pragma unroll
+    for (int r = threadIdx.y; r < 64; r += 8) {
+        const int n = n0 + r;
         if (n < N && k < Kp) {
             const float x = t[threadIdx.x][r];
             const float h = tf32_hi(x);
@@ -461,7 +470,7 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
         k_split_rows<<<dim3(gr, (unsigned)batch), 64, 0, c.stream>>>(
             (const float*)A, ahi, alo, (int)m, (int)k, (int)Kp, (long long)(m * k),
             (long long)(m * Kp));
-        dim3 g2((unsigned)((n + 31) / 32), (unsigned)(Kp / 32), (unsigned)batch);
+        dim3 g2((unsigned)((n + 63) / 64), (unsigned)(Kp / 32), (unsigned)batch);
         k_split_cols<<<g2, dim3(32, 8), 0, c.stream>>>((const float*)B, bhi, blo, (int)k, (int)n,
                                                        (int)Kp, (long long)(k * n),
                                                        (long long)(n * Kp));
