@@ -353,11 +353,11 @@ int nxv_leapfrog_chain_gauss_f64_batched_ke(void* q_chain, void* p_chain,
                                             const char* spv_path);
 
 /* NEW, with no counterpart in the reference.  The batched f64 Gaussian
- * chain above for callers that must not allocate device memory: a host
- * that captures its sampler step into a CUDA graph (cudaMalloc is not
- * allowed while a stream is being captured), or a framework that reserves
- * GPU memory for its own allocator and hands its kernels raw device buffers
- * (XLA/EXLA preallocate most of HBM, so a side allocation can fail).
+ * chain above for callers that must not allocate device memory while they
+ * run: a framework that reserves GPU memory for its own allocator and hands
+ * its kernels raw device buffers (XLA/EXLA preallocate most of HBM, so a
+ * side allocation by this library can fail), or a service that does all of
+ * its device allocation at start-up and keeps a fixed memory budget.
  * Arguments are raw device pointers, not nxv handles, laid out as in
  * nxv_leapfrog_chain_gauss_f64_batched; the caller guarantees their sizes.
  * The call allocates nothing: its scratch is a 1 MiB static device array

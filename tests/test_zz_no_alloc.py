@@ -1,9 +1,9 @@
 """The leapfrog entry point that allocates nothing.
 
 nxv_leapfrog_chain_gauss_f64_batched_noalloc serves callers that cannot
-allocate device memory at call time: a sampler step captured into a CUDA
-graph (no cudaMalloc while a stream is captured), or a host framework that
-keeps GPU memory in its own allocator and hands raw buffers to the library.
+allocate device memory at call time: a host framework that keeps GPU memory
+in its own allocator (EXLA preallocates most of HBM) and hands raw buffers
+to the library, or a service that allocates everything at start-up.
 It runs the batched Gaussian chain with its scratch in a static device
 array.  These tests call it through the C ABI with raw device pointers and
 check that it gives the allocating entry point's results on two calls in a
