@@ -392,16 +392,20 @@ __global__ void k_split_cols(const float* __restrict__ B, float* __restrict__ hi
     }
 }
 
+// The driver's tensor-map encoder, looked up once (a function-local static:
+// initialised once even when several threads make their first GEMM call at
+// the same time).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = []() {
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
                 cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
+            return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        cudaGetLastError();
+        return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+    }();
     return fn;
 }
 
