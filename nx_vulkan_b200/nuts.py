@@ -159,27 +159,39 @@ def merge_check(rho_a, rho_b, p_a_last, ps_a_first, ps_a_last, p_b_first, ps_b_f
 def subtree_check(P, PS):
     """Balanced-tree U-turn check over leaves in time order.  P: momenta
     [..., n, d] with n a power of two; PS: velocities inv_mass * P.  Returns
-    (ok [...], rho [..., d]), rho the summed momentum.  Evaluated level by
-    level: at level j every node of 2^j leaves is the merge of its two
-    children, and all of a level's merge tests run as one array operation;
-    the sums pair children as a recursive evaluation would."""
+    (ok [...], rho [..., d]), rho the summed momentum.
+
+    Every node [a, b) of 2^j leaves is the merge of its halves [a, m) and
+    [m, b), tested as in merge_check.  The momentum sums come from prefix
+    sums S (rho of [a, b) = S[b] - S[a]), and every dot product from two
+    Gram matrices per chain: G = PS . S^T (so ps_i . rho = G[i, b] - G[i, a])
+    and H = PS . P^T (ps_i . p_j); each level's tests are then array
+    lookups.  Two matrix products replace the per-level dot products over
+    [..., n, d] arrays."""
     P, PS = np.asarray(P), np.asarray(PS)
     n, d = P.shape[-2:]
     lead = P.shape[:-2]
+    S = np.zeros(lead + (n + 1, d))
+    np.cumsum(P, axis=-2, out=S[..., 1:, :])
+    G = PS @ np.swapaxes(S, -1, -2)   # [..., n, n + 1]
+    H = PS @ np.swapaxes(P, -1, -2)   # [..., n, n]
     ok = np.ones(lead, bool)
-    rho = P
     size = 1
     while size < n:
         size *= 2
-        h = size // 2
-        pair = rho.reshape(lead + (n // size, 2, d))
-        ra, rb = pair[..., 0, :], pair[..., 1, :]
-        first = np.arange(0, n, size)
-        last, a_last, b_first = first + size - 1, first + h - 1, first + h
-        good, rho = merge_check(ra, rb, P[..., a_last, :], PS[..., first, :], PS[..., a_last, :],
-                                P[..., b_first, :], PS[..., b_first, :], PS[..., last, :])
+        a = np.arange(0, n, size)
+        m, b = a + size // 2, a + size
+        first, last, a_last, b_first = a, b - 1, m - 1, m
+        good = ((G[..., first, b] - G[..., first, a] > 0)       # whole node: ends vs rho
+                & (G[..., last, b] - G[..., last, a] > 0)
+                # rho_A + p_B,first against ps_A,first and ps_B,first
+                & (G[..., first, m] - G[..., first, a] + H[..., first, b_first] > 0)
+                & (G[..., b_first, m] - G[..., b_first, a] + H[..., b_first, b_first] > 0)
+                # rho_B + p_A,last against ps_A,last and ps_B,last
+                & (G[..., a_last, b] - G[..., a_last, m] + H[..., a_last, a_last] > 0)
+                & (G[..., last, b] - G[..., last, m] + H[..., last, a_last] > 0))
         ok &= good.all(axis=-1)
-    return ok, rho[..., 0, :]
+    return ok, S[..., n, :]
 
 
 @dataclass
