@@ -162,19 +162,18 @@ def subtree_check(P, PS):
     (ok [...], rho [..., d]), rho the summed momentum.
 
     Every node [a, b) of 2^j leaves is the merge of its halves [a, m) and
-    [m, b), tested as in merge_check.  The momentum sums come from prefix
-    sums S (rho of [a, b) = S[b] - S[a]), and every dot product from two
-    Gram matrices per chain: G = PS . S^T (so ps_i . rho = G[i, b] - G[i, a])
-    and H = PS . P^T (ps_i . p_j); each level's tests are then array
-    lookups.  Two matrix products replace the per-level dot products over
-    [..., n, d] arrays."""
+    [m, b), tested as in merge_check.  Every dot product comes from one Gram
+    matrix per chain, H = PS . P^T (ps_i . p_j), and its running sums along
+    j, G[i, b] = sum of H[i, :b] = ps_i . (p_0 + ... + p_(b-1)), so that
+    ps_i . rho of [a, b) = G[i, b] - G[i, a]; each level's tests are then
+    array lookups.  One matrix product replaces the per-level dot products
+    over [..., n, d] arrays."""
     P, PS = np.asarray(P), np.asarray(PS)
     n, d = P.shape[-2:]
     lead = P.shape[:-2]
-    S = np.zeros(lead + (n + 1, d))
-    np.cumsum(P, axis=-2, out=S[..., 1:, :])
-    G = PS @ np.swapaxes(S, -1, -2)   # [..., n, n + 1]
     H = PS @ np.swapaxes(P, -1, -2)   # [..., n, n]
+    G = np.zeros(lead + (n, n + 1))
+    np.cumsum(H, axis=-1, out=G[..., 1:])
     ok = np.ones(lead, bool)
     size = 1
     while size < n:
@@ -191,7 +190,7 @@ def subtree_check(P, PS):
                 & (G[..., a_last, b] - G[..., a_last, m] + H[..., a_last, a_last] > 0)
                 & (G[..., last, b] - G[..., last, m] + H[..., last, a_last] > 0))
         ok &= good.all(axis=-1)
-    return ok, S[..., n, :]
+    return ok, P.sum(axis=-2)
 
 
 @dataclass
@@ -200,6 +199,77 @@ class Stats:
     n_leapfrog: np.ndarray   # leaves used per chain
     divergent: np.ndarray    # a subtree diverged
     energy: np.ndarray       # H of the initial point
+
+
+class _Leaves:
+    """Leaves integrated beyond the initial point in one direction, for every
+    chain.  Rows (q, p in forward-time sign, H = -logp + KE) live in one flat
+    store that grows by doubling and is reused across transitions; each
+    extension appends one block of K leaves per extended chain.  Per chain:
+    `have` leaves stored, `used` taken into the tree, and the flat start and
+    leaf number of its current and previous blocks.
+
+    A tree level takes leaves [used, used + n) of a chain, which always lie
+    in those two blocks: a chain is extended only when fewer than n leaves
+    are left, so the leftover of the previous block is used up by the level
+    that follows the extension, and `used` never falls behind the previous
+    block's first leaf again."""
+
+    def __init__(self, C: int, d: int):
+        self.C, self.d = C, d
+        self.q = np.empty((0, d))
+        self.p = np.empty((0, d))
+        self.h = np.empty(0)
+        self.reset()
+
+    def reset(self):
+        C = self.C
+        self.size = 0
+        self.have = np.zeros(C, np.int64)
+        self.used = np.zeros(C, np.int64)
+        self.cur_start = np.zeros(C, np.int64)
+        self.cur_base = np.zeros(C, np.int64)
+        self.prev_start = np.zeros(C, np.int64)
+        self.prev_base = np.zeros(C, np.int64)
+
+    def _reserve(self, rows: int):
+        need = self.size + rows
+        if need <= self.h.shape[0]:
+            return
+        cap = max(need, 2 * self.h.shape[0])
+        for name in ("q", "p", "h"):
+            old = getattr(self, name)
+            new = np.empty((cap,) + old.shape[1:])
+            new[: self.size] = old[: self.size]
+            setattr(self, name, new)
+
+    def append(self, rows, q, p, h):
+        """Store K new leaves ([len(rows), K, ...]) after the leaves of chains `rows`."""
+        n, K = q.shape[:2]
+        self._reserve(n * K)
+        s0 = self.size
+        self.q[s0: s0 + n * K] = q.reshape(n * K, self.d)
+        self.p[s0: s0 + n * K] = p.reshape(n * K, self.d)
+        self.h[s0: s0 + n * K] = h.reshape(n * K)
+        self.size += n * K
+        self.prev_start[rows] = self.cur_start[rows]
+        self.prev_base[rows] = self.cur_base[rows]
+        self.cur_start[rows] = s0 + np.arange(n) * K
+        self.cur_base[rows] = self.have[rows]
+        self.have[rows] += K
+
+    def last(self, rows):
+        """Flat row of the last stored leaf of chains `rows` (have > 0)."""
+        return self.cur_start[rows] + (self.have[rows] - self.cur_base[rows]) - 1
+
+    def take(self, rows, n: int):
+        """The next n leaves of chains `rows` ([len(rows), n, ...]), marked used."""
+        j = self.used[rows][:, None] + np.arange(n)
+        cb = self.cur_base[rows][:, None]
+        flat = np.where(j >= cb, self.cur_start[rows][:, None] + (j - cb),
+                        self.prev_start[rows][:, None] + (j - self.prev_base[rows][:, None]))
+        self.used[rows] += n
+        return self.q[flat], self.p[flat], self.h[flat]
 
 
 def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth=10):
@@ -214,9 +284,17 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
     m = np.asarray(inv_mass, np.float64)
     p0 = rng.standard_normal((C, d)) / np.sqrt(m)
     H0 = -target.logp(q0) + 0.5 * ((p0 * p0) * m).sum(axis=-1)
-    # per chain and direction: leaves beyond the initial point, index 0 = first step
-    cache = {+1: [None] * C, -1: [None] * C}   # dict of arrays q, p, logp, ke
-    used = {+1: np.zeros(C, np.int64), -1: np.zeros(C, np.int64)}
+    # per direction: the leaves beyond the initial point (kept on the source
+    # between transitions, so the store's pages stay mapped)
+    leaves = getattr(source, "_nuts_leaves", None)
+    if leaves is None or leaves[+1].C != C or leaves[+1].d != d:
+        leaves = {+1: _Leaves(C, d), -1: _Leaves(C, d)}
+        try:
+            source._nuts_leaves = leaves
+        except AttributeError:
+            pass
+    for L in leaves.values():
+        L.reset()
     sample = q0.copy()
     logw = -H0.copy()
     rho = p0.copy()
@@ -231,40 +309,43 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
             break
         n_new = 1 << level
         dirs = np.where(rng.random(C) < 0.5, -1, 1)
-        # speculative extension: one batched call for every chain short of leaves
-        def have(c):
-            cc = cache[dirs[c]][c]
-            return 0 if cc is None else cc["q"].shape[0]
-        need = [c for c in range(C) if active[c] and have(c) < used[dirs[c]][c] + n_new]
-        if need:
+        fwd_all = dirs > 0
+        have = np.where(fwd_all, leaves[+1].have, leaves[-1].have)
+        used = np.where(fwd_all, leaves[+1].used, leaves[-1].used)
+        # speculative extension: one batched call for every chain short of
+        # leaves, in chain order; each starts from its last stored leaf in
+        # that direction (the initial point when there is none), with the
+        # momentum negated when integrating backward
+        need = np.flatnonzero(active & (have < used + n_new))
+        if need.size:
             K = speculative_steps(n_new)
-            qs, ps = np.empty((len(need), d)), np.empty((len(need), d))
-            for i, c in enumerate(need):
-                dd = dirs[c]
-                cc = cache[dd][c]
-                q_f, p_f = (q0[c], p0[c]) if cc is None else (cc["q"][-1], cc["p"][-1])
-                qs[i], ps[i] = q_f, dd * p_f
+            qs, ps = q0[need].copy(), p0[need].copy()
+            for sgn in (+1, -1):
+                L = leaves[sgn]
+                sel = (dirs[need] == sgn) & (L.have[need] > 0)
+                if sel.any():
+                    f = L.last(need[sel])
+                    qs[sel], ps[sel] = L.q[f], L.p[f]
+            ps *= dirs[need][:, None]
             qk, pk, lk, kk = source.extend(qs, ps, K)
-            for i, c in enumerate(need):
-                dd = dirs[c]
-                new = {"q": qk[i], "p": dd * pk[i], "logp": lk[i], "ke": kk[i]}
-                cc = cache[dd][c]
-                cache[dd][c] = new if cc is None else {k: np.concatenate([cc[k], new[k]]) for k in cc}
+            hk = -lk + kk
+            for sgn in (+1, -1):
+                sel = dirs[need] == sgn
+                if sel.any():
+                    leaves[sgn].append(need[sel], qk[sel], sgn * pk[sel], hk[sel])
         # the level's new leaves of every active chain, in time order
         act = np.flatnonzero(active)
         A = act.size
+        fwd = dirs[act] > 0
         Q, P = np.empty((A, n_new, d)), np.empty((A, n_new, d))
         H = np.empty((A, n_new))
-        for i, c in enumerate(act):
-            dd = dirs[c]
-            cc = cache[dd][c]
-            a, b = used[dd][c], used[dd][c] + n_new
-            sl = slice(None) if dd > 0 else slice(None, None, -1)  # backward leaves run leftward
-            Q[i], P[i] = cc["q"][a:b][sl], cc["p"][a:b][sl]
-            H[i] = (-cc["logp"][a:b] + cc["ke"][a:b])[sl]
-            used[dd][c] = b
+        for sgn, sel in ((+1, fwd), (-1, ~fwd)):
+            if sel.any():
+                q_, p_, h_ = leaves[sgn].take(act[sel], n_new)
+                if sgn < 0:  # backward leaves run leftward
+                    q_, p_, h_ = q_[:, ::-1], p_[:, ::-1], h_[:, ::-1]
+                Q[sel], P[sel], H[sel] = q_, p_, h_
         depth[act] = level + 1
-        fwd = dirs[act] > 0
         # divergence (also NaN): the subtree is discarded and the tree stops
         div = ~np.all(H - H0[act, None] <= MAX_DELTA_H, axis=1)
         divergent[act] |= div
@@ -304,5 +385,5 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
             end_p[sgn][idx] = src[0][sel & ok_sub]
             end_ps[sgn][idx] = src[1][sel & ok_sub]
         active[act] = cont
-    n_leap = used[+1] + used[-1]
+    n_leap = leaves[+1].used + leaves[-1].used
     return sample, Stats(depth=depth, n_leapfrog=n_leap, divergent=divergent, energy=H0)
