@@ -89,8 +89,11 @@ class OracleChain:
 class GpuChain:
     """Trajectory source on the GPU: nxv_leapfrog_chain_gauss_f64_batched_ke
     through the Nx.Vulkan mirror; q, p, logp and kinetic energy of every step
-    come back to the host (the tree builder's view of the call), downloaded
-    into reused page-locked buffers (direct DMA, no staging copy)."""
+    come back to the host (the tree builder's view of the call).  Transfers
+    go through reused page-locked buffers (direct DMA, no staging copy); the
+    arrays `extend` returns are views of those buffers, valid until the next
+    call.  The per-chain inverse mass (the same row for every chain) is
+    uploaded once per chain count."""
 
     def __init__(self, target: GaussianTarget, inv_mass, eps: float):
         from nx_vulkan_b200 import _native
@@ -102,6 +105,7 @@ class GpuChain:
             raise RuntimeError(f"upload failed: {self.prec_h}")
         self.calls = []
         self.pinned = {}  # slot -> page-locked float64 array
+        self.m_dev = {}   # chain count -> device buffer of inv_mass broadcast to [c, d]
 
     def _host(self, slot, n):
         a = self.pinned.get(slot)
@@ -111,8 +115,12 @@ class GpuChain:
             self.pinned[slot] = a
         return a[:n]
 
-    def _up(self, a):
-        ok, h = self.nxv.upload_binary(np.ascontiguousarray(a, np.float64).tobytes())
+    def _up(self, a, slot):
+        # staged in a page-locked buffer: the upload is a direct DMA (and
+        # returns once the copy is done, so the buffer can be reused)
+        host = self._host(slot, a.size)
+        host[:] = np.asarray(a, np.float64).reshape(-1)
+        ok, h = self.nxv.upload_binary(host)
         if ok != "ok":
             raise RuntimeError(f"upload failed: {h}")
         return h
@@ -122,13 +130,15 @@ class GpuChain:
         a = self._host(slot, n)
         if self.lib.nxv_buf_download(h.handle, ctypes.c_void_p(a.ctypes.data), n * 8) != 0:
             raise RuntimeError("download failed")
-        return a.copy()
+        return a
 
     def extend(self, q, p, K):
         c, d = q.shape
-        m = np.broadcast_to(self.m, (c, d))
+        m = self.m_dev.get(c)
+        if m is None:
+            m = self.m_dev[c] = self._up(np.broadcast_to(self.m, (c, d)), 12)
         ok, outs = self.nxv.leapfrog_chain_gauss_f64_batched(
-            self._up(q), self._up(p), self._up(m), self.prec_h, c, K, self.eps, self.t.mu,
+            self._up(q, 10), self._up(p, 11), m, self.prec_h, c, K, self.eps, self.t.mu,
             kinetic=True)
         if ok != "ok":
             raise RuntimeError(f"chain call failed: {outs}")
