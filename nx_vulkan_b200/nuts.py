@@ -211,38 +211,31 @@ class Stats:
     energy: np.ndarray       # H of the initial point
 
 
-class _Leaves:
-    """Leaves integrated beyond the initial point in one direction, for every
-    chain.  Rows (q, p in forward-time sign, H = -logp + KE) live in one flat
-    store that grows by doubling and is reused across transitions; each
-    extension appends one block of K leaves per extended chain.  Per chain:
-    `have` leaves stored, `used` taken into the tree, and the flat start and
-    leaf number of its current and previous blocks.
+class _Store:
+    """Leaf rows (q, p in the sign it was integrated with -- negated for
+    backward leaves --, H = -logp + KE) of both directions in one flat store
+    that grows by doubling and is reused across transitions."""
 
-    A tree level takes leaves [used, used + n) of a chain, which always lie
-    in those two blocks: a chain is extended only when fewer than n leaves
-    are left, so the leftover of the previous block is used up by the level
-    that follows the extension, and `used` never falls behind the previous
-    block's first leaf again."""
-
-    def __init__(self, C: int, d: int):
-        self.C, self.d = C, d
+    def __init__(self, d: int):
+        self.d = d
         self.q = np.empty((0, d))
         self.p = np.empty((0, d))
         self.h = np.empty(0)
-        self.reset()
-
-    def reset(self):
-        C = self.C
         self.size = 0
-        self.have = np.zeros(C, np.int64)
-        self.used = np.zeros(C, np.int64)
-        self.cur_start = np.zeros(C, np.int64)
-        self.cur_base = np.zeros(C, np.int64)
-        self.prev_start = np.zeros(C, np.int64)
-        self.prev_base = np.zeros(C, np.int64)
 
-    def _reserve(self, rows: int):
+    def append(self, q, p, h) -> int:
+        """Append the leaves of one chain call ([n, K, ...]); returns the
+        first flat row (chain i's leaves start at row + i K)."""
+        n, K = q.shape[:2]
+        self.reserve(n * K)
+        s0 = self.size
+        self.q[s0: s0 + n * K] = q.reshape(n * K, self.d)
+        self.p[s0: s0 + n * K] = p.reshape(n * K, self.d)
+        self.h[s0: s0 + n * K] = h.reshape(n * K)
+        self.size += n * K
+        return s0
+
+    def reserve(self, rows: int):
         need = self.size + rows
         if need <= self.h.shape[0]:
             return
@@ -253,18 +246,38 @@ class _Leaves:
             new[: self.size] = old[: self.size]
             setattr(self, name, new)
 
-    def append(self, rows, q, p, h):
-        """Store K new leaves ([len(rows), K, ...]) after the leaves of chains `rows`."""
-        n, K = q.shape[:2]
-        self._reserve(n * K)
-        s0 = self.size
-        self.q[s0: s0 + n * K] = q.reshape(n * K, self.d)
-        self.p[s0: s0 + n * K] = p.reshape(n * K, self.d)
-        self.h[s0: s0 + n * K] = h.reshape(n * K)
-        self.size += n * K
+
+class _Leaves:
+    """Leaves integrated beyond the initial point in one direction, for every
+    chain, kept in a shared _Store; each extension appends one block of K
+    leaves per extended chain.  Per chain: `have` leaves stored, `used`
+    taken into the tree, and the flat start and leaf number of its current
+    and previous blocks.
+
+    A tree level takes leaves [used, used + n) of a chain, which always lie
+    in those two blocks: a chain is extended only when fewer than n leaves
+    are left, so the leftover of the previous block is used up by the level
+    that follows the extension, and `used` never falls behind the previous
+    block's first leaf again."""
+
+    def __init__(self, store: _Store, C: int):
+        self.store, self.C = store, C
+        self.reset()
+
+    def reset(self):
+        C = self.C
+        self.have = np.zeros(C, np.int64)
+        self.used = np.zeros(C, np.int64)
+        self.cur_start = np.zeros(C, np.int64)
+        self.cur_base = np.zeros(C, np.int64)
+        self.prev_start = np.zeros(C, np.int64)
+        self.prev_base = np.zeros(C, np.int64)
+
+    def add_block(self, rows, starts, K: int):
+        """Chains `rows` got K new leaves at flat rows starts, starts + 1, ..."""
         self.prev_start[rows] = self.cur_start[rows]
         self.prev_base[rows] = self.cur_base[rows]
-        self.cur_start[rows] = s0 + np.arange(n) * K
+        self.cur_start[rows] = starts
         self.cur_base[rows] = self.have[rows]
         self.have[rows] += K
 
@@ -273,13 +286,13 @@ class _Leaves:
         return self.cur_start[rows] + (self.have[rows] - self.cur_base[rows]) - 1
 
     def take(self, rows, n: int):
-        """The next n leaves of chains `rows` ([len(rows), n, ...]), marked used."""
+        """Flat rows [len(rows), n] of the next n leaves of chains `rows`, marked used."""
         j = self.used[rows][:, None] + np.arange(n)
         cb = self.cur_base[rows][:, None]
         flat = np.where(j >= cb, self.cur_start[rows][:, None] + (j - cb),
                         self.prev_start[rows][:, None] + (j - self.prev_base[rows][:, None]))
         self.used[rows] += n
-        return self.q[flat], self.p[flat], self.h[flat]
+        return flat
 
 
 def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth=10):
@@ -297,12 +310,15 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
     # per direction: the leaves beyond the initial point (kept on the source
     # between transitions, so the store's pages stay mapped)
     leaves = getattr(source, "_nuts_leaves", None)
-    if leaves is None or leaves[+1].C != C or leaves[+1].d != d:
-        leaves = {+1: _Leaves(C, d), -1: _Leaves(C, d)}
+    if leaves is None or leaves[+1].C != C or leaves[+1].store.d != d:
+        store = _Store(d)
+        leaves = {+1: _Leaves(store, C), -1: _Leaves(store, C)}
         try:
             source._nuts_leaves = leaves
         except AttributeError:
             pass
+    store = leaves[+1].store
+    store.size = 0
     for L in leaves.values():
         L.reset()
     sample = q0.copy()
@@ -329,32 +345,34 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
         need = np.flatnonzero(active & (have < used + n_new))
         if need.size:
             K = speculative_steps(n_new)
-            qs, ps = q0[need].copy(), p0[need].copy()
+            # initial point: p0 in forward sign, negated for backward chains;
+            # stored leaves already hold p in their integration sign
+            qs, ps = q0[need].copy(), p0[need] * dirs[need][:, None]
             for sgn in (+1, -1):
                 L = leaves[sgn]
                 sel = (dirs[need] == sgn) & (L.have[need] > 0)
                 if sel.any():
                     f = L.last(need[sel])
-                    qs[sel], ps[sel] = L.q[f], L.p[f]
-            ps *= dirs[need][:, None]
+                    qs[sel], ps[sel] = store.q[f], store.p[f]
             qk, pk, lk, kk = source.extend(qs, ps, K)
-            hk = -lk + kk
+            s0 = store.append(qk, pk, -lk + kk)
+            starts = s0 + np.arange(need.size) * K
             for sgn in (+1, -1):
                 sel = dirs[need] == sgn
                 if sel.any():
-                    leaves[sgn].append(need[sel], qk[sel], sgn * pk[sel], hk[sel])
-        # the level's new leaves of every active chain, in time order
+                    leaves[sgn].add_block(need[sel], starts[sel], K)
+        # the level's new leaves of every active chain, in time order: their
+        # flat rows, then one gather of p and H (q only for the sampled leaf)
         act = np.flatnonzero(active)
         A = act.size
         fwd = dirs[act] > 0
-        Q, P = np.empty((A, n_new, d)), np.empty((A, n_new, d))
-        H = np.empty((A, n_new))
+        rows = np.empty((A, n_new), np.int64)
         for sgn, sel in ((+1, fwd), (-1, ~fwd)):
             if sel.any():
-                q_, p_, h_ = leaves[sgn].take(act[sel], n_new)
-                if sgn < 0:  # backward leaves run leftward
-                    q_, p_, h_ = q_[:, ::-1], p_[:, ::-1], h_[:, ::-1]
-                Q[sel], P[sel], H[sel] = q_, p_, h_
+                r_ = leaves[sgn].take(act[sel], n_new)
+                rows[sel] = r_ if sgn > 0 else r_[:, ::-1]  # backward leaves run leftward
+        P, H = store.p[rows], store.h[rows]
+        P[~fwd] *= -1.0  # backward leaves were integrated with negated momentum
         depth[act] = level + 1
         # divergence (also NaN): the subtree is discarded and the tree stops
         div = ~np.all(H - H0[act, None] <= MAX_DELTA_H, axis=1)
@@ -374,7 +392,7 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
         j = np.minimum((cdf < u[:, None]).sum(axis=1), n_new - 1)
         move = rng.random(A) < np.exp(np.minimum(0.0, logw_sub - logw[act]))
         take = ok_sub & move
-        sample[act[take]] = Q[take, j[take]]
+        sample[act[take]] = store.q[rows[take, j[take]]]
         logw[act] = np.where(ok_sub, np.logaddexp(logw[act], logw_sub), logw[act])
         # merge with the old tree: A is the earlier of (old tree, subtree) in time
         first_p, first_ps = P[:, 0], PS[:, 0]
