@@ -78,3 +78,48 @@ def test_nuts_samples_the_gaussian():
     se = np.sqrt(var / x.shape[0])
     assert np.all(np.abs(x.mean(axis=0)) < 5 * se)
     assert np.all(np.abs(x.var(axis=0) / var - 1) < 0.10)
+
+
+def test_leaf_store_takes_the_right_leaves():
+    """The flat leaf store under the tree builder's extension rule (extend a
+    chain by speculative_steps(n) leaves when fewer than n are left, then
+    take n): over random direction sequences, every level's rows hold leaves
+    used .. used + n - 1 of that chain and direction, in order -- the two
+    blocks a chain keeps per direction always cover them."""
+    rng = np.random.default_rng(11)
+    C, d = 7, 3
+    store = nuts._Store(d)
+    leaves = {+1: nuts._Leaves(store, C), -1: nuts._Leaves(store, C)}
+    for trial in range(20):
+        store.size = 0
+        for L in leaves.values():
+            L.reset()
+        for level in range(9):
+            n = 1 << level
+            dirs = np.where(rng.random(C) < 0.5, -1, 1)
+            have = np.where(dirs > 0, leaves[+1].have, leaves[-1].have)
+            used = np.where(dirs > 0, leaves[+1].used, leaves[-1].used)
+            need = np.flatnonzero(have < used + n)
+            if need.size:
+                K = nuts.speculative_steps(n)
+                # leaf labels: q[..., 0] = chain, q[..., 1] = direction, q[..., 2] = leaf number
+                lab = np.zeros((need.size, K, d))
+                lab[..., 0] = need[:, None]
+                lab[..., 1] = dirs[need][:, None]
+                lab[..., 2] = have[need][:, None] + np.arange(K)
+                s0 = store.append(lab, lab, lab[..., 2])
+                starts = s0 + np.arange(need.size) * K
+                for sgn in (+1, -1):
+                    sel = dirs[need] == sgn
+                    if sel.any():
+                        leaves[sgn].add_block(need[sel], starts[sel], K)
+            for sgn in (+1, -1):
+                rows_c = np.flatnonzero(dirs == sgn)
+                if rows_c.size == 0:
+                    continue
+                u0 = leaves[sgn].used[rows_c].copy()
+                rows = leaves[sgn].take(rows_c, n)
+                got = store.q[rows]
+                assert np.array_equal(got[..., 0], np.broadcast_to(rows_c[:, None], (rows_c.size, n)))
+                assert np.all(got[..., 1] == sgn)
+                assert np.array_equal(got[..., 2], u0[:, None] + np.arange(n))
