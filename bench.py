@@ -11,7 +11,8 @@ reference contract's q/p/grad trajectories [chain][k][i] and logp [chain][k].
          event pair on the launching stream around all timed steps (and the
          collectives), three rotating input sets larger than L2 together.
   e2e    the same metric through the C ABI with host buffers: every step
-         uploads q0/p0/inv_mass/prec from pinned host memory, runs the chain
+         uploads q0/p0 [chain][d] and the shared inv_mass/prec rows [d] from
+         pinned host memory, runs the chain
          and reads the step's result -- the per-step logp of every chain --
          back into pinned host memory (nxv_buf_upload/_download); the
          trajectories stay in their device buffers, as the reference API
@@ -28,6 +29,9 @@ Multi-GPU (torchrun, one process per GPU): chains are independent, so each
 rank integrates its own 4096 chains (weak scaling) and one NCCL all-gather
 collects the per-chain diagnostics (final logp) each step.
 `--impl reference` times the CPU restatement of the reference path instead.
+`--workload logreg` runs the logistic-regression HMC workload (256 chains
+split over the ranks, one trajectory with device-drawn momenta per step).
+`--suite` times every other hot-path workload on one GPU.
 """
 from __future__ import annotations
 
@@ -49,19 +53,26 @@ sys.path.insert(0, str(ROOT))
 D, CHAINS, L, EPS = 1000, 4096, 32, 0.01
 METRIC = "f64 leapfrog steps/s (chains×L)"
 UNIT = "chain-steps/s"
-# algorithmic bytes of one call: read q0, p0, inv_mass (3*d*8 per chain),
-# write q/p/grad trajectories (3*L*d*8 per chain) and logp (L*8 per chain);
-# prec (d*8) is read once.
+# algorithmic bytes of one call: read q0, p0 (2*d*8 per chain), write the
+# q/p/grad trajectories (3*L*d*8 per chain) and logp (L*8 per chain); the
+# inverse mass (one [d] row shared by the chains) and prec are read once.
 def algo_bytes(chains, d=D, steps=L):
-    return chains * (3 * d * 8 + 3 * steps * d * 8 + steps * 8) + d * 8
+    return chains * (2 * d * 8 + 3 * steps * d * 8 + steps * 8) + 2 * d * 8
 
 
 def gauss_inputs(chains, d=D, seed=3):
+    """prec [d], q0 and p0 [chains][d], inverse mass: one [d] row of ones
+    shared by every chain (the workload's m = 1)."""
     r = np.random.default_rng(seed)
     prec = r.uniform(0.5, 2.0, d)
     q0 = r.normal(size=(chains, d))
     p0 = r.normal(size=(chains, d))
-    return prec, q0, p0, np.ones((chains, d))
+    return prec, q0, p0, np.ones(d)
+
+
+def per_chain(m, chains):
+    """The shared [d] inverse-mass row as the oracle's [chain][d] array."""
+    return np.ascontiguousarray(np.broadcast_to(m, (chains, m.size)))
 
 
 def max_over_ranks_ms(ms, dev, world):
@@ -165,10 +176,15 @@ class Clocks:
                 self.proc.kill()
             self.f.close()
 
-    def summary(self):
+    def mark(self):
+        """Index of the next sample: summary(mark) covers what follows it."""
+        return len(self.samples)
+
+    def summary(self, start=0):
         if self.nvml:
-            sm = [c for c, _ in self.samples]
-            reasons = sorted({nm for _, r in self.samples for nm, bit in self.REASONS.items() if r & bit})
+            smp = self.samples[start:]
+            sm = [c for c, _ in smp]
+            reasons = sorted({nm for _, r in smp for nm, bit in self.REASONS.items() if r & bit})
             return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
                     "reasons": reasons, "samples": len(sm), "source": "NVML every 2 ms"}
         if not self.path.exists():
@@ -206,6 +222,7 @@ def cpu_sample(seconds_min=10.0, seconds_max=30.0, chains=256):
     from oracle import binding as orc
     nthreads = host_threads()
     prec, q0, p0, m = gauss_inputs(chains)
+    m = per_chain(m, chains)
     done, t0 = 0, time.perf_counter()
     while True:
         orc.chain_gauss_f64(q0, p0, m, prec, 0.0, D, chains, L, EPS, nthreads=nthreads)
@@ -225,8 +242,9 @@ def run_reference(args, rank, world):
     per_step = []
     from oracle import binding as orc
     nthreads = host_threads()
-    chains = 256
+    chains = args.chains  # the GPU arm's per-GPU batch: the same workload per step
     prec, q0, p0, m = gauss_inputs(chains)
+    m = per_chain(m, chains)
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
         orc.chain_gauss_f64(q0, p0, m, prec, 0.0, D, chains, L, EPS, nthreads=nthreads)
@@ -242,7 +260,8 @@ def run_reference(args, rank, world):
         "config": {"workload": "anisotropic Gaussian HMC leapfrog (reference path restated on CPU)",
                    "chains": chains, "d": D, "L": L, "eps": EPS},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
-                         "sample": f"{chains} chains x L={L} x d={D} per step; the reference's "
+                         "sample": f"{chains} chains x L={L} x d={D} per step (the GPU arm's "
+                                   f"per-GPU batch); the reference's "
                                    "Vulkan/Elixir stack cannot run here, so its CPU path is the "
                                    "oracle's C restatement of Nx.BinaryBackend semantics"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -264,6 +283,12 @@ def main():
                     help="N > 1: steps whose final logps go out in one all-gather (default: every step)")
     ap.add_argument("--diag-depth", type=int, default=4,
                     help="N > 1: diagnostics buffers in flight (collective of step i waited for at step i + depth)")
+    ap.add_argument("--workload", default="gauss", choices=["gauss", "logreg"],
+                    help="gauss: the headline anisotropic-Gaussian chain; logreg: the "
+                         "logistic-regression HMC workload (256 chains over all ranks, "
+                         "X[10000,100], L=16, eps=0.002, momenta drawn on the device)")
+    ap.add_argument("--repeats", type=int, default=5,
+                    help="timed regions of --steps steps each; value is their median")
     ap.add_argument("--suite", action="store_true",
                     help="measure every hot-path workload (one JSON line each) instead of the headline")
     ap.add_argument("--only", default="fused,reduce,random,misc,matmul,logreg,nuts",
@@ -280,6 +305,8 @@ def main():
         return run_reference(args, rank, world)
     if args.suite:
         return suite(args)
+    if args.workload == "logreg":
+        return logreg_main(args, rank, world, local)
 
     import torch
     import torch.distributed as dist
@@ -322,7 +349,6 @@ def main():
     h_in = h_sets[0]
     h_out = [wrap(t) for t in outs]
     spv = nxv.shader_path("leapfrog_chain_gauss_f64_batched.spv")
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 2x L2
 
     def step(i=0):
         rc = lib.nxv_leapfrog_chain_gauss_f64_batched(*h_out, *h_sets[i % n_sets], D, chains, L,
@@ -364,40 +390,49 @@ def main():
         diagnostics(i, final=i == args.warmup - 1)
     stream.wait_stream(side)
     torch.cuda.synchronize()
+    repeats = max(1, args.repeats)
+    groups = (args.steps + every - 1) // every
     n_launch0 = lib.nxv_launch_count()
     t0_ev, t1_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # per-step events around the chain call alone (no collective), in the
+    # same timed loop: the roofline's launch time
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    rep_ms, rep_clocks, k_all = [], [], []
     # The clock sampler starts (NVML initialisation takes milliseconds, and
     # differently on every rank) before the barrier, so that the ranks leave
     # the barrier together and start their timed steps at the same moment.
     with Clocks(local) as clk:
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        t0_ev.record(stream)
-        for i in range(args.steps):
-            step(i)
-            diagnostics(i, final=i == args.steps - 1)
-        stream.wait_stream(side)  # the final collective is inside the timed region
-        t1_ev.record(stream)
-        torch.cuda.synchronize()
+        for rep in range(repeats):
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            mark = clk.mark()
+            t0_ev.record(stream)
+            for i in range(args.steps):
+                kev[i][0].record(stream)
+                step(rep * args.steps + i)
+                kev[i][1].record(stream)
+                # groups of `every` steps restart with each repeat
+                diagnostics(rep * groups * every + i, final=i == args.steps - 1)
+            stream.wait_stream(side)  # the final collective is inside the timed region
+            t1_ev.record(stream)
+            torch.cuda.synchronize()
+            rep_clocks.append(clk.summary(mark))
+            rep_ms.append(max_over_ranks_ms(t0_ev.elapsed_time(t1_ev), dev, world))
+            k_all += [a.elapsed_time(b) for a, b in kev]
     if world > 1:
         dist.barrier()
-    launches = (lib.nxv_launch_count() - n_launch0) // args.steps * args.steps
-    t_ms = max_over_ranks_ms(t0_ev.elapsed_time(t1_ev), dev, world)
+    launches = (lib.nxv_launch_count() - n_launch0) // (args.steps * repeats) * args.steps
+    t_ms = statistics.median(rep_ms)
     value = world * chains * L * args.steps / (t_ms / 1e3)
+    rep_values = [world * chains * L * args.steps / (ms / 1e3) for ms in rep_ms]
     clocks = clk.summary()
-
-    # Roofline of the dominant kernel: one call (chain kernel + its tile fold),
-    # timed alone (no collective) per step with events.
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(max(3, args.steps // 2))]
-    for a, b in kev:
-        flush.zero_()
-        a.record(stream)
-        step()
-        b.record(stream)
-    torch.cuda.synchronize()
-    k_ms = statistics.median([a.elapsed_time(b) for a, b in kev])
+    clocks["per_repeat"] = [{"sm_mhz": c.get("sm_mhz"), "reasons": c.get("reasons"),
+                             "samples": c.get("samples")} for c in rep_clocks]
+    # Roofline of the dominant kernel: the chain call (chain kernel + the
+    # tiny constant kernel), median over every timed step of every repeat.
+    k_ms = statistics.median(k_all)
     # per-rank view of a multi-GPU run: step time, the kernel alone, SM clock
     ranks_info = None
     if world > 1:
@@ -511,9 +546,11 @@ def main():
             if world > 1:
                 dist.all_reduce(el_t, op=dist.ReduceOp.MAX)
             el = float(el_t.item())
+            h2d = sum(t.numel() * 8 for t in hb_in)
             return {"value": world * chains * L * n_e2e / el, "unit": UNIT,
-                    "h2d_bytes_per_step": sum(t.numel() * 8 for t in hb_in),
+                    "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": hb_out[3].numel() * 8, "steps": n_e2e,
+                    "h2d_gbs_per_rank": h2d * n_e2e / el / 1e9,
                     "timing": "host wall clock from the first upload to the last result, max over ranks",
                     "result_read": "per-step logp [chain][k] (the metric); trajectories stay on the device",
                     "pipelined": "inputs of step i+1 upload on a copy stream while step i computes"}
@@ -543,24 +580,30 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic (seeded numpy: prec~U(0.5,2) seed 3, q0,p0~N(0,1); rank r uses seed 3+1000r)",
             "config": {"workload": "anisotropic Gaussian HMC leapfrog, fused K-step chain",
-                       "chains_per_gpu": chains, "d": D, "L": L, "eps": EPS, "inv_mass": 1.0,
+                       "chains_per_gpu": chains, "d": D, "L": L, "eps": EPS,
+                       "inv_mass": "1.0, one [d] row shared by the chains",
                        "parallelism": f"chains sharded, {world} rank(s), NCCL all-gather of every chain's "
                                       f"final-step logp, {every} step(s) per collective, on a high-priority "
                                       f"side stream, waited for {depth} collectives later "
                                       f"(NCCL_PROTO={os.environ.get('NCCL_PROTO')})"
                        if world > 1 else "1 GPU",
-                       "l2": "inputs larger than L2: 3 rotating input sets of 98 MB (295 MB > 2x 126 MB); "
+                       "l2": "inputs larger than L2: 3 rotating input sets of 66 MB (197 MB > 126 MB); "
                              "3.15 GB of trajectory writes per step",
-                       "timing": "one CUDA event pair around all timed steps on the launching stream, "
-                                 "collectives included; max over ranks"},
+                       "timing": f"{repeats} timed regions of {args.steps} steps, each one CUDA event "
+                                 "pair on the launching stream around its steps, collectives included, "
+                                 "max over ranks; value is the median region"},
+            "repeats": {"n": repeats, "values": rep_values, "ms_per_step": [ms / args.steps for ms in rep_ms],
+                        "spread": (max(rep_values) - min(rep_values)) / statistics.median(rep_values)},
             "gpu_launches": int(launches),
             **({"ranks": ranks_info} if ranks_info else {}),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
-                                           "1024-chain launch scaled by chains (lower bound: "
+                         "traffic_source": "a constant, not measured in this run: ncu "
+                                           "dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                           "1024-chain launch, scaled by chains (lower bound: "
                                            "writes still dirty in L2 at kernel end are uncounted)",
                          "algorithmic_bytes_per_launch": abytes, "launch_ms": k_ms,
+                         "launch_timing": "median of per-call CUDA events inside the timed loop",
                          "kernel": "k_chain_tma (TMA bulk stores, 2 steps per copy) + k_gauss_const",
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json), copy, of measured"},
             "clocks": clocks,
@@ -577,6 +620,151 @@ def main():
     lib.nxv_set_stream(None)
     if world > 1:
         dist.destroy_process_group()
+
+
+LR_OBS, LR_DIM, LR_CHAINS, LR_STEPS, LR_EPS = 10000, 100, 256, 16, 0.002
+
+
+def logreg_data():
+    """X [10000, 100] ~ N(0, 1), w* ~ N(0, 1), y ~ Bernoulli(sigmoid(X w*)), seed 4."""
+    r = np.random.default_rng(4)
+    X = r.normal(size=(LR_OBS, LR_DIM))
+    w = r.normal(size=LR_DIM)
+    y = (r.random(LR_OBS) < 1 / (1 + np.exp(-X @ w))).astype(np.float64)
+    return X, y
+
+
+def dgemm_peak_tflops(torch, dev, n=4096, reps=10):
+    """cuBLAS DGEMM (torch.matmul f64, n^3) in this process: the FP64 tensor
+    peak the logistic gradient is held against (no FP64 figure is in the
+    measured-peaks file)."""
+    a = torch.randn(n, n, dtype=torch.float64, device=dev)
+    b = torch.randn(n, n, dtype=torch.float64, device=dev)
+    torch.matmul(a, b)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = None
+    for _ in range(reps):
+        e0.record()
+        torch.matmul(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    return 2.0 * n ** 3 / (best / 1e3) / 1e12
+
+
+def logreg_main(args, rank, world, local):
+    """The logistic-regression HMC workload: 256 chains split over the ranks
+    (contiguous blocks), X and y replicated, one step = one trajectory of
+    L = 16 leapfrog steps with fresh momenta drawn on the device (Philox key
+    seed + trajectory, counter chain * 100 + dim over the global chain
+    index), the last positions carried to the next trajectory on the device,
+    and an all-gather of every chain's final logp per trajectory (N > 1)."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("NCCL_PROTO", "LL")
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", "2")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from nx_vulkan_b200 import _native, hmc, vulkan as nxv
+    lib = _native.load()
+    assert nxv.init_devices([local]) == "ok", _native.last_error()
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
+    assert LR_CHAINS % world == 0, "the 256 chains split evenly over 1, 2, 4 or 8 ranks"
+    lo, hi = rank * LR_CHAINS // world, (rank + 1) * LR_CHAINS // world
+    cr = hi - lo
+    X, y = logreg_data()
+    ok, tX = nxv.upload_binary(X)
+    ok2, ty = nxv.upload_binary(y)
+    ok3, q0 = nxv.upload_binary(np.zeros((cr, LR_DIM)))
+    assert ok == ok2 == ok3 == "ok"
+    seed = 7
+    lps = torch.empty(cr, dtype=torch.float64, device=dev)
+    gathered = torch.empty(LR_CHAINS, dtype=torch.float64, device=dev) if world > 1 else None
+    h_lps = lib.nxv_buf_wrap(C.c_void_p(lps.data_ptr()), cr * 8)
+    spv = nxv.shader_path("leapfrog_logreg_f64_batched.spv")
+    # this rank's momenta: the rows [lo, hi) of the global [256][100] draw
+    def momenta(t):
+        ok, p = nxv.random_f64(LR_CHAINS * LR_DIM, hmc.momentum_key(seed, t), 1)
+        assert ok == "ok", _native.last_error()
+        if world == 1:
+            return p
+        mine = nxv._alloc(cr * LR_DIM * 8)
+        assert lib.nxv_buf_copy_2d(mine.handle, 0, cr * LR_DIM * 8, p.handle, lo * LR_DIM * 8,
+                                   cr * LR_DIM * 8, cr * LR_DIM * 8, 1) == 0
+        return mine
+
+    state = {"q": q0, "t": 0}
+
+    def trajectory():
+        t = state["t"]
+        p = momenta(t)
+        ok, outs = nxv.leapfrog_logreg_f64_batched(state["q"], p, tX, ty, LR_OBS, LR_DIM, cr,
+                                                   LR_STEPS, LR_EPS)
+        assert ok == "ok", _native.last_error()
+        ok, qn = hmc.last_step(outs[0], cr, LR_STEPS, LR_DIM)
+        assert ok == "ok", _native.last_error()
+        state["q"], state["t"] = qn, t + 1
+        if world > 1:  # every chain's final logp: logp[:, L-1] to lps, then all-gathered
+            assert lib.nxv_buf_copy_2d(h_lps, 0, 8, outs[3].handle, 8 * (LR_STEPS - 1),
+                                       8 * LR_STEPS, 8, cr) == 0
+            dist.all_gather_into_tensor(gathered, lps)
+
+    for _ in range(args.warmup):
+        trajectory()
+    torch.cuda.synchronize()
+    repeats = max(1, args.repeats)
+    rep_ms = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_launch0 = lib.nxv_launch_count()
+    with Clocks(local) as clk:
+        for _ in range(repeats):
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(args.steps):
+                trajectory()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            rep_ms.append(max_over_ranks_ms(e0.elapsed_time(e1), dev, world))
+    launches = (lib.nxv_launch_count() - n_launch0) // repeats
+    t_ms = statistics.median(rep_ms)
+    value = LR_CHAINS * LR_STEPS * args.steps / (t_ms / 1e3)
+    peak = dgemm_peak_tflops(torch, dev) if rank == 0 else None
+    flops = (LR_STEPS + 1) * 2 * 2 * cr * LR_DIM * LR_OBS  # per trajectory, this rank
+    achieved = flops / (t_ms / args.steps / 1e3) / 1e12
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "f64 logistic-regression leapfrog steps/s (chains×L)", "value": value,
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong (256 chains in total)", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded numpy: X~N(0,1) [10000,100], w*~N(0,1), y~Bernoulli, seed 4; "
+                    "q0=0; momenta from the device Philox generator)",
+            "config": {"workload": "Bayesian logistic-regression HMC, one trajectory per step",
+                       "chains_total": LR_CHAINS, "chains_per_gpu": cr, "n_obs": LR_OBS,
+                       "d": LR_DIM, "L": LR_STEPS, "eps": LR_EPS,
+                       "timing": f"{repeats} timed regions of {args.steps} trajectories (CUDA events "
+                                 "on the launching stream, max over ranks); value is the median"},
+            "repeats": {"n": repeats, "ms_per_step": [ms / args.steps for ms in rep_ms]},
+            "gpu_launches_per_region": int(launches),
+            "roofline": {"bound": "fp64 tensor (DMMA)", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
+                         "flops_per_step_per_gpu": flops,
+                         "peak_source": "cuBLAS DGEMM 4096^3 measured in this run (rank 0)",
+                         "note": "the step's whole time, momenta draws and carries included"},
+            "clocks": clk.summary(),
+        }), flush=True)
 
 
 def fused_elementwise_gbs(lib, nxv, torch, dev, stream, peak):

@@ -325,9 +325,13 @@ int nxv_leapfrog_chain_normal_f64(void* q_chain, void* p_chain,
 
 /* NEW.  Batched f64 Gaussian chains: n_chains independent chains, one launch.
  * grad = -prec .* (q - mu); logp = -0.5 sum prec (q-mu)^2 + 0.5 sum log prec
- * - n/2 log 2pi.  q_init, p_init, inv_mass are [chain][i]; prec is [i]
- * (shared); q/p/grad chains are [chain][k][i]; logp is [chain][k].  With
- * n_chains = 1 and prec = 1/sigma^2 this is nxv_leapfrog_chain_normal_f64.
+ * - n/2 log 2pi.  q_init, p_init are [chain][i]; inv_mass is [chain][i],
+ * or one [i] row used by every chain when its buffer holds exactly n
+ * doubles and n_chains > 1 (Nx broadcasting of an [i] mass over the chains,
+ * lib/nx_vulkan.ex:808-835; the [i] form uploads n instead of n_chains * n
+ * doubles); prec is [i] (shared); q/p/grad chains are [chain][k][i]; logp is
+ * [chain][k].  With n_chains = 1 and prec = 1/sigma^2 this is
+ * nxv_leapfrog_chain_normal_f64.
  * spv: leapfrog_chain_gauss_f64_batched.spv. */
 int nxv_leapfrog_chain_gauss_f64_batched(void* q_chain, void* p_chain,
                                          void* grad_chain, void* logp_chain,
@@ -342,7 +346,8 @@ int nxv_leapfrog_chain_gauss_f64_batched(void* q_chain, void* p_chain,
  * (the reference's kinetic_energy.spv formula, shim.h:169-173, fused into
  * the chain's epilogue so a NUTS caller gets the Hamiltonian -logp + KE of
  * every trajectory point without another pass).  ke_chain holds
- * n_chains * K doubles.  spv: leapfrog_chain_gauss_f64_batched.spv. */
+ * n_chains * K doubles; inv_mass may be [i] as above.
+ * spv: leapfrog_chain_gauss_f64_batched.spv. */
 int nxv_leapfrog_chain_gauss_f64_batched_ke(void* q_chain, void* p_chain,
                                             void* grad_chain, void* logp_chain,
                                             void* ke_chain,
@@ -363,9 +368,10 @@ int nxv_leapfrog_chain_gauss_f64_batched_ke(void* q_chain, void* p_chain,
  * The call allocates nothing: its scratch is a 1 MiB static device array
  * that every GPU loading this library holds until the process exits.
  * Limit: chains of n <= 2048 elements need only 256 bytes of it; longer
- * chains also need n_chains * K * ceil(n / 2048) partial sums of 8 bytes,
- * and a call needing more than 1 MiB returns -3 with a message naming the
- * limit.  nxv_init (or nxv_init_devices) must have run.  The first call on
+ * chains also need n_chains * K * ceil(n / 2048) partial sums of 8 bytes
+ * (2048 is the default kernel's tile; the NXV_LF_TMA and NXV_LF_CFG tuning
+ * variables can change it), and a call needing more than 1 MiB returns -3
+ * with a message naming the limit.  nxv_init (or nxv_init_devices) must have run.  The first call on
  * a device looks up the array's device address and must come before any
  * stream capture.  All calls share the array: two calls that overlap on
  * the GPU (different streams or threads) race.  Nothing in it needs
@@ -419,6 +425,20 @@ int nxv_synchronize(void);
  * can run -- including CUDA graphs captured with it, which keep its raw
  * address. */
 void* nxv_buf_wrap(void* device_ptr, unsigned long n_bytes);
+
+/* NEW.  Device-to-device copy of `rows` rows of `width` bytes: row r is read
+ * at byte src_offset + r * src_pitch of src and written at dst_offset +
+ * r * dst_pitch of dst (one cudaMemcpy2DAsync on the current stream, no
+ * kernel).  A strided slice of a device tensor without a host round trip,
+ * e.g. the last step q_chain[:, K-1, :] of a batched chain as the next
+ * trajectory's q_init.  The reference's Backend.slice downloads the tensor,
+ * walks the output coordinates on the host and uploads the result
+ * (lib/nx_vulkan/backend.ex:665-720); this is the device form of its
+ * contiguous-row case.  0 on success, -1 for a NULL handle, -3 when a row
+ * would leave a buffer. */
+int nxv_buf_copy_2d(void* dst, unsigned long dst_offset, unsigned long dst_pitch,
+                    void* src, unsigned long src_offset, unsigned long src_pitch,
+                    unsigned long width, unsigned long rows);
 
 /* Device address and byte size behind a handle (NULL / 0 for NULL). */
 void* nxv_buf_device_ptr(void* handle);

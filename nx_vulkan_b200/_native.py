@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple] = {
     "nxv_set_device": (C.c_int, [C.c_int]),
     "nxv_set_stream": (C.c_int, [vp]),
     "nxv_synchronize": (C.c_int, []),
+    "nxv_buf_copy_2d": (C.c_int, [vp, ul, ul, vp, ul, ul, ul, ul]),
     "nxv_buf_wrap": (vp, [vp, ul]),
     "nxv_buf_device_ptr": (vp, [vp]),
     "nxv_buf_size": (ul, [vp]),

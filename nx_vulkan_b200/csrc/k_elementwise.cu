@@ -13,6 +13,8 @@
 #include "kernels.h"
 #include "ops_common.cuh"
 
+#include <type_traits>
+
 namespace nxv {
 
 namespace {
@@ -71,17 +73,31 @@ k_map(T* __restrict__ out, const T* __restrict__ in0, const T* __restrict__ in1,
             }
         }
     }
+    // the rest, one vector per step (the whole array when the grid covers it
+    // with one vector per thread); every input's load is issued before the math
     for (; v < nv; v += stride) {
+        T x[NIN > 0 ? NIN : 1][W];
+#pragma unroll
+        for (int q = 0; q < NIN; q++) {
+            if constexpr (VEC) {
+                vload(ins[q] + v * W, *reinterpret_cast<T(*)[16 / sizeof(T)]>(x[q]));
+            } else {
+                x[q][0] = ins[q][v];
+            }
+        }
         T r[W];
 #pragma unroll
         for (int j = 0; j < W; j++) {
             T args[NIN > 0 ? NIN : 1];
 #pragma unroll
-            for (int q = 0; q < NIN; q++) args[q] = ins[q][v * W + j];
+            for (int q = 0; q < NIN; q++) args[q] = x[q][j];
             r[j] = f(args);
         }
-#pragma unroll
-        for (int j = 0; j < W; j++) out[v * W + j] = r[j];
+        if constexpr (VEC) {
+            vstore(out + v * W, *reinterpret_cast<T(*)[16 / sizeof(T)]>(r));
+        } else {
+            out[v] = r[0];
+        }
     }
     if (VEC && blockIdx.x == 0) {  // tail of n % W elements
         size_t t = nv * W + threadIdx.x;
@@ -94,12 +110,155 @@ k_map(T* __restrict__ out, const T* __restrict__ in0, const T* __restrict__ in1,
     }
 }
 
+// ---- one-wave map with programmatic dependent launch ---------------------------
+//
+// Small f32 maps (a grid of one vector per thread that fits the SMs in one
+// wave, 2^20 elements and below) are bound by the launch, the DRAM latency of
+// their first loads and the drain of their last stores, not by bandwidth.
+// k_map1 runs them in one wave (launch bounds of 8 CTAs x 256 threads per SM)
+// and is launched with programmatic dependent launch: its CTAs may start while
+// the previous kernel on the stream finishes.  Each CTA
+//   1. loads its inputs at once when none of them overlaps the output of the
+//      previous kernel launched this way on the stream (`early`; the host
+//      tracks that range per stream, Device::pdl_last),
+//   2. waits for the previous kernel to complete (griddepcontrol.wait),
+//   3. lets the next kernel's CTAs launch (griddepcontrol.launch_dependents),
+//   4. loads its inputs now if it did not in step 1, computes and stores.
+// Every kernel passes step 2 before step 3, so when a kernel's CTAs start,
+// every kernel but the one immediately before it has completed: an early
+// load never reads memory that a running kernel writes, and no store happens
+// before the previous kernel has completed.  A predecessor that is not
+// launched this way (any other kernel) lets its dependents start only when it
+// completes.  NXV_MAP_PDL=0 launches k_map1 without the attribute.
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename T, int NIN, class F>
+__global__ void __launch_bounds__(kThreads, 8)
+k_map1(T* __restrict__ out, const T* __restrict__ in0, const T* __restrict__ in1,
+       const T* __restrict__ in2, const T* __restrict__ in3, size_t n, F f, int early) {
+    constexpr int W = (int)(16 / sizeof(T));
+    const T* ins[4] = {in0, in1, in2, in3};
+    const size_t nv = n / W;
+    const size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool have = v < nv;
+    T x[NIN > 0 ? NIN : 1][W];
+    if (early && have) {
+#pragma unroll
+        for (int q = 0; q < NIN; q++) vload(ins[q] + v * W, x[q]);
+    }
+    griddep_wait();
+    griddep_launch();
+    if (!early && have) {
+#pragma unroll
+        for (int q = 0; q < NIN; q++) vload(ins[q] + v * W, x[q]);
+    }
+    if (have) {
+        T r[W];
+#pragma unroll
+        for (int j = 0; j < W; j++) {
+            T args[NIN > 0 ? NIN : 1];
+#pragma unroll
+            for (int q = 0; q < NIN; q++) args[q] = x[q][j];
+            r[j] = f(args);
+        }
+        vstore(out + v * W, r);
+    }
+    if (blockIdx.x == 0) {  // tail of n % W elements
+        const size_t t = nv * W + threadIdx.x;
+        if (t < n) {
+            T args[NIN > 0 ? NIN : 1];
+#pragma unroll
+            for (int q = 0; q < NIN; q++) args[q] = ins[q][t];
+            out[t] = f(args);
+        }
+    }
+}
+
+// Functors whose f32 arithmetic goes through f64 (the exact mode) need more
+// registers than k_map1's launch bounds allow; they keep the grid-stride map.
+template <class F, class = void> struct Heavy { static constexpr bool value = false; };
+template <class F> struct Heavy<F, std::void_t<decltype(F::kHeavy)>> {
+    static constexpr bool value = F::kHeavy;
+};
+
+bool map_pdl() {
+    const char* e = getenv("NXV_MAP_PDL");
+    return !(e && e[0] == '0');
+}
+
+// True when none of the inputs [p, p + bytes) overlaps the output of the last
+// programmatic launch on c.stream; then records `out` as that output.
+bool pdl_independent_and_record(Ctx& c, const void* const* ins, int nin, size_t bytes,
+                                const void* out) {
+    std::lock_guard<std::mutex> lk(c.dev->pdl_mu);
+    auto it = c.dev->pdl_last.find(c.stream);
+    bool indep = true;
+    if (it != c.dev->pdl_last.end()) {
+        const uintptr_t lo = it->second.first, hi = lo + it->second.second;
+        for (int q = 0; q < nin; q++) {
+            const uintptr_t a = (uintptr_t)ins[q], b = a + bytes;
+            if (a < hi && lo < b) indep = false;
+        }
+    }
+    c.dev->pdl_last[c.stream] = {(uintptr_t)out, bytes};
+    return indep;
+}
+
+template <typename T, int NIN, class F>
+int launch_map1(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* i3, size_t n,
+                F f, unsigned grid) {
+    const void* ins[4] = {i0, i1, i2, i3};
+    const bool pdl = map_pdl();
+    const int early = pdl && pdl_independent_and_record(c, ins, NIN, n * sizeof(T), out) ? 1 : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_map1<T, NIN, F>, out, i0, i1, i2, i3, n, f, early);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(k_map1)");
+    count_launch();
+    return finish(c);
+}
+
+// Resident CTAs of k_map1<T, NIN, F> per SM (looked up once per instantiation).
+template <typename T, int NIN, class F>
+int map1_per_sm() {
+    static const int occ = []() {
+        int o = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_map1<T, NIN, F>, kThreads, 0) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        return o;
+    }();
+    return occ;
+}
+
 template <typename T, int NIN, class F>
 int run_map(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* i3, size_t n, F f) {
     if (n == 0) return OK;
     bool vec = al16(out) && al16(i0) && (NIN < 2 || al16(i1)) && (NIN < 3 || al16(i2)) &&
                (NIN < 4 || al16(i3));
     constexpr int W = (int)(16 / sizeof(T));
+    if constexpr (sizeof(T) == 4 && !Heavy<F>::value) {
+        // one vector per thread in a single wave
+        const size_t nv = n / W;
+        const size_t wave = (size_t)c.dev->sm_count * map1_per_sm<T, NIN, F>() * kThreads;
+        if (vec && map_wide() && nv >= 1 && nv <= wave)
+            return launch_map1<T, NIN, F>(c, out, i0, i1, i2, i3, n, f,
+                                          (unsigned)((nv + kThreads - 1) / kThreads));
+    }
     if (vec) {
         // f32 arrays that one full grid covers with a vector or so per thread
         // run wide (one vector per thread, up to 8 CTAs per SM): 2^20
@@ -124,10 +283,12 @@ int run_map(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* i3, 
 // semantics) when true, f32 library functions when false (the default;
 // NXV_EXACT_F32=1 selects the first).
 template <typename T, bool EX> struct BinF {
+    static constexpr bool kHeavy = EX;  // f64 math: many registers
     unsigned op;
     __device__ T operator()(const T* x) const { return bin_op<T, EX>(x[0], x[1], op); }
 };
 template <typename T, bool EX> struct UnF {
+    static constexpr bool kHeavy = EX;  // f64 math: many registers
     unsigned op;
     __device__ T operator()(const T* x) const { return un_op<T, EX>(x[0], op); }
 };
@@ -142,6 +303,7 @@ template <typename T> struct TapeDev {
 };
 
 template <typename T, bool EX> struct TapeF {
+    static constexpr bool kHeavy = EX;  // f64 math: many registers
     TapeDev<T> t;
     // x[0] = a, x[1] = b, x[2] = c, x[3] = d (unused ones are never read)
     __device__ T operator()(const T* x) const {
@@ -165,6 +327,7 @@ template <typename T, bool EX> struct TapeF {
 
 // tanh(exp(a*b + c) - imm0): the Nx.Defn chain tanh(exp(x*y + z) - 1.0).
 template <typename T, bool EX> struct ChainMulAddExpSubTanh {
+    static constexpr bool kHeavy = EX;  // f64 math: many registers
     T imm;
     __device__ T operator()(const T* x) const {
         return un_op<T, EX>(sub_(un_op<T, EX>(add_(mul_(x[0], x[1]), x[2]), 0), imm), 6);
@@ -557,6 +720,7 @@ __global__ void __launch_bounds__(256) k_transpose(T* __restrict__ out, const T*
 // EX: log sigma in f64 rounded once (the oracle's evaluation,
 // NXV_EXACT_F32=1), else logf (within 1 ulp).
 template <bool EX> struct NormalLogpdfF {
+    static constexpr bool kHeavy = EX;
     __device__ float operator()(const float* x) const {
         float z = div_(sub_(x[0], x[1]), x[2]);
         float z2 = mul_(z, z);

@@ -129,6 +129,7 @@ struct ChainArgs {
     const T* q0;
     const T* p0;
     const T* m;
+    size_t m_cs;      // chain stride of m in elements: n ([chain][i]) or 0 (one [i] row for all)
     size_t n;
     unsigned chains, tiles, K;
     T eps, he;
@@ -164,7 +165,7 @@ __global__ void __launch_bounds__(NT) k_chain(ChainArgs<T> g, Fam fam) {
             size_t ii = ok[v] ? i : 0;
             q[v] = ok[v] ? g.q0[cbase + ii] : T(0);
             p[v] = ok[v] ? g.p0[cbase + ii] : T(0);
-            em[v] = ok[v] ? g.m[cbase + ii] : T(0);
+            em[v] = ok[v] ? g.m[(size_t)chain * g.m_cs + ii] : T(0);
             ep[v] = fam.load(nullptr, ii);
             gr[v] = fam.grad(q[v], ep[v]);
         }
@@ -279,7 +280,7 @@ __global__ void __launch_bounds__(NT) k_chain_tma(ChainArgs<T> g, Fam fam) {
             size_t ii = ok[v] ? i : 0;
             q[v] = ok[v] ? g.q0[cbase + ii] : T(0);
             p[v] = ok[v] ? g.p0[cbase + ii] : T(0);
-            em[v] = ok[v] ? g.m[cbase + ii] : T(0);
+            em[v] = ok[v] ? g.m[(size_t)chain * g.m_cs + ii] : T(0);
             ep[v] = fam.load(nullptr, ii);
             gr[v] = fam.grad(q[v], ep[v]);
         }
@@ -465,12 +466,21 @@ int tma_steps() {
     return (s == 1 || s == 2 || s == 4) ? s : 0;
 }
 
+// The staged-store kernel takes a chain when its rows fit one 256-thread
+// tile (n <= 2048), are 16-byte multiples, and the double-buffered stage of
+// S steps plus the reduction buffers fit the opt-in shared memory.
+bool tma_fits(Ctx& c, size_t n, size_t elt, int S, bool ke) {
+    if (S == 0 || n > 2048 || (n * elt) % 16 != 0) return false;
+    size_t smem = 2 * 3 * (size_t)S * n * elt;
+    int per_block = 0;
+    cudaDeviceGetAttribute(&per_block, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.dev->id);
+    return smem + (ke ? 2 : 1) * KC * 8 * 8 <= (size_t)per_block;
+}
+
 template <typename T, class Fam, int VPT, int S, bool KE>
 int launch_tma(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
     size_t smem = 2 * 3 * (size_t)S * g.n * sizeof(T);
-    int per_block = 0;
-    cudaDeviceGetAttribute(&per_block, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.dev->id);
-    if (smem + (KE ? 2 : 1) * KC * 8 * 8 > (size_t)per_block) return E_KERNEL;  // caller falls back
+    if (!tma_fits(c, g.n, sizeof(T), S, KE)) return E_KERNEL;  // caller falls back
     cudaError_t e = cudaFuncSetAttribute(k_chain_tma<T, Fam, 256, VPT, S, KE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_chain_tma)");
@@ -509,6 +519,15 @@ int launch_family(Ctx& c, ChainArgs<T>& g, const Fam& fam) {
     }
 }
 
+// Tiles per chain of the kernel launch_family runs for an f64 chain
+// (mode 0): 1 on the staged-store kernel, else pick_cfg's tile count.  The
+// scratch for per-tile partial sums is sized from it.
+size_t gauss_tiles(Ctx& c, size_t n, size_t chains, bool ke) {
+    if (tma_fits(c, n, sizeof(double), tma_steps(), ke)) return 1;
+    const Cfg cf = pick_cfg(c, n, chains, 0);
+    return (n + (size_t)cf.nt * cf.vpt - 1) / ((size_t)cf.nt * cf.vpt);
+}
+
 }  // namespace
 
 int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void* gc,
@@ -522,6 +541,7 @@ int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void
     g.q0 = (const float*)q0;
     g.p0 = (const float*)p0;
     g.m = (const float*)m;
+    g.m_cs = n;
     g.n = n;
     g.chains = (unsigned)chains;
     g.K = K;
@@ -555,7 +575,8 @@ int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void
 
 int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                            const void* p0, const void* m, const void* prec, double prec_scalar,
-                           double mu, size_t n, size_t chains, unsigned K, double eps, void* ke) {
+                           double mu, size_t n, size_t chains, unsigned K, double eps, void* ke,
+                           bool m_shared) {
     ChainArgs<double> g{};
     g.qc = (double*)qc;
     g.pc = (double*)pc;
@@ -564,6 +585,7 @@ int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, con
     g.q0 = (const double*)q0;
     g.p0 = (const double*)p0;
     g.m = (const double*)m;
+    g.m_cs = m_shared ? 0 : n;
     g.n = n;
     g.chains = (unsigned)chains;
     g.K = K;
@@ -577,8 +599,7 @@ int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, con
     // Scratch: [256 B: the log-density constant][tile partials of logp][tile
     // partials of the kinetic energy], partials only when a chain spans
     // several tiles.
-    Cfg cf = pick_cfg(c, n, chains, 0);
-    size_t tiles = (n + (size_t)cf.nt * cf.vpt - 1) / ((size_t)cf.nt * cf.vpt);
+    size_t tiles = gauss_tiles(c, n, chains, ke != nullptr);
     size_t part = tiles > 1 ? chains * (size_t)K * tiles * sizeof(double) : 0;
     size_t need = 256 + part * (ke ? 2 : 1);
     char* base = (char*)scratch(c, need);
@@ -669,16 +690,16 @@ extern "C" int nxv_leapfrog_chain_gauss_f64_batched_noalloc(
     rc = noalloc_scratch(c, &base);
     if (rc) return rc;
     if (n == 0 || n_chains == 0) return OK;
-    const Cfg cf = pick_cfg(c, n, n_chains, 0);
-    const size_t tile = (size_t)cf.nt * cf.vpt;
-    const size_t tiles = (n + tile - 1) / tile;
+    // partial sums only when the kernel that launch_family picks splits a
+    // chain into several tiles
+    const size_t tiles = gauss_tiles(c, n, n_chains, false);
     const size_t need = 256 + (tiles > 1 ? (size_t)n_chains * K * tiles * sizeof(double) : 0);
     if (need > kNoAllocScratchBytes) {
-        set_error("leapfrog noalloc: %u chains x %u steps x %zu tiles of %zu elements need %zu "
-                  "bytes of scratch; the static scratch holds %zu (n_chains * K * ceil(n/%zu) "
-                  "must be <= %zu when n > %zu)",
-                  n_chains, K, tiles, tile, need, kNoAllocScratchBytes, tile,
-                  (kNoAllocScratchBytes - 256) / sizeof(double), tile);
+        set_error("leapfrog noalloc: %u chains x %u steps x %zu tiles per chain need %zu "
+                  "bytes of scratch; the static scratch holds %zu (n_chains * K * tiles "
+                  "must be <= %zu)",
+                  n_chains, K, tiles, need, kNoAllocScratchBytes,
+                  (kNoAllocScratchBytes - 256) / sizeof(double));
         return E_ARG;
     }
     ChainArgs<double> g{};
@@ -689,6 +710,7 @@ extern "C" int nxv_leapfrog_chain_gauss_f64_batched_noalloc(
     g.q0 = (const double*)q_init;
     g.p0 = (const double*)p_init;
     g.m = (const double*)inv_mass;
+    g.m_cs = n;
     g.n = n;
     g.chains = n_chains;
     g.K = K;

@@ -3,7 +3,7 @@
 // f64: DMMA tensor cores (mma.sync m16n8k4 .f64).  tcgen05 has no f64 kind,
 // so the FP64 tensor path on sm_100a is the warp-level DMMA instruction.
 // f32: 3xTF32 split on the warp-level TF32 MMA (mma.sync m16n8k8 .tf32):
-// x = hi + lo with hi = x rounded toward zero to TF32 and lo = tf32(x - hi);
+// x = hi + lo with hi = x rounded to nearest TF32 and lo = tf32(x - hi);
 // C += Ahi.Bhi + Ahi.Blo + Alo.Bhi, accumulated in f32.  The error is of the
 // order of f32 rounding (the dropped lo.lo term is ~2^-22 relative).
 //
@@ -135,7 +135,6 @@ __device__ __forceinline__ void dmma<16>(double (&d)[4], const double* a, const 
           "d"(b[0]), "d"(b[1]), "d"(b[2]), "d"(b[3]));
 }
 
-__device__ __forceinline__ unsigned f2tf32_rz(float x) { return __float_as_uint(x) & 0xFFFFE000u; }
 __device__ __forceinline__ unsigned f2tf32_rn(float x) {
     unsigned r;
     asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
@@ -274,7 +273,7 @@ __device__ __forceinline__ void gemm_mainloop(const GemmP<T>& P, const T* __rest
                     float x[4] = {pa[0], pa[8 * S::AS], pa[4], pa[8 * S::AS + 4]};
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        ahi[i][e] = f2tf32_rz(x[e]);
+                        ahi[i][e] = f2tf32_rn(x[e]);
                         alo[i][e] = f2tf32_rn(x[e] - __uint_as_float(ahi[i][e]));
                     }
                 }
@@ -284,7 +283,7 @@ __device__ __forceinline__ void gemm_mainloop(const GemmP<T>& P, const T* __rest
                     float x[2] = {pb[0], pb[4 * S::BS]};
 #pragma unroll
                     for (int e = 0; e < 2; e++) {
-                        bhi[j][e] = f2tf32_rz(x[e]);
+                        bhi[j][e] = f2tf32_rn(x[e]);
                         blo[j][e] = f2tf32_rn(x[e] - __uint_as_float(bhi[j][e]));
                     }
                 }
@@ -344,11 +343,19 @@ __global__ void __launch_bounds__(NTH, 1) k_gemm(GemmP<T> P, long long tile_base
                 const int row = ta.m0 + wm + i * 16 + g + h * 8;
                 if (row >= M) continue;
                 T* dst = C + (size_t)row * ldc + col;
+                T v0 = acc[i][j][2 * h], v1 = acc[i][j][2 * h + 1];
+                if constexpr (sizeof(T) == 4) {
+                    // 3xTF32: non-finite results are recomputed exactly
+                    if (P.ksplit == 0 && !isfinite(v0) && col < N)
+                        v0 = exact_dot_f32(A + (size_t)row * P.lda, B + col, K, P.ldb);
+                    if (P.ksplit == 0 && !isfinite(v1) && col + 1 < N)
+                        v1 = exact_dot_f32(A + (size_t)row * P.lda, B + col + 1, K, P.ldb);
+                }
                 if (col + 1 < N) {
-                    dst[0] = acc[i][j][2 * h];
-                    dst[1] = acc[i][j][2 * h + 1];
+                    dst[0] = v0;
+                    dst[1] = v1;
                 } else if (col < N) {
-                    dst[0] = acc[i][j][2 * h];
+                    dst[0] = v0;
                 }
             }
         }
@@ -465,6 +472,17 @@ k_gemm_fix(GemmP<T> P, long long tile_base, long long W, int G, int KT,
         }
         const int row = ta.m0 + e / BN, col0 = ta.n0 + e % BN;
         if (row >= M) continue;
+        if constexpr (sizeof(T) == 4) {
+            // 3xTF32 partials: a non-finite sum is recomputed exactly
+            if (P.ksplit == 0 && P.A != nullptr) {
+                const T* A = P.A + ta.z * P.sA + (size_t)row * P.lda;
+                const T* B = P.B + ta.z * P.sB;
+#pragma unroll
+                for (int u = 0; u < V; u++)
+                    if (col0 + u < N && !isfinite(sum[u]))
+                        sum[u] = exact_dot_f32(A, B + col0 + u, P.K, P.ldb);
+            }
+        }
 #pragma unroll
         for (int u = 0; u < V; u++)
             if (col0 + u < N) C[(size_t)row * ldc + col0 + u] = sum[u];
@@ -624,13 +642,20 @@ SkPlan gemm_sk_plan(long long tiles, int KT, int sms, int min_idle) {
     return pl;
 }
 
-int launch_gemm_fix_f32(Ctx& c, float* C, int M, int N, int batch, const SkPlan& pl, int KT,
-                        const float* ws) {
+int launch_gemm_fix_f32(Ctx& c, float* C, const float* A, const float* B, int M, int N, int K,
+                        int batch, const SkPlan& pl, int KT, const float* ws) {
     GemmP<float> P{};
+    P.A = A;
+    P.B = B;
     P.C = C;
     P.M = M;
     P.N = N;
+    P.K = K;
+    P.lda = K;
+    P.ldb = N;
     P.ldc = N;
+    P.sA = (long long)M * K;
+    P.sB = (long long)K * N;
     P.sC = (long long)M * N;
     P.batch = batch;
     int f = 1;

@@ -1,11 +1,14 @@
 // k_matmul_tc.cu -- f32 GEMM as 3xTF32 on the sm_100a tensor cores (tcgen05).
 //
 // C = A . B with A [M][K], B [K][N], C [M][N] row-major f32, batched.
-// Split: x = hi + lo with hi = x with its 13 low mantissa bits cleared (an
-// exact TF32 value) and lo = x - hi (exact in f32);
-// C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi accumulated in f32 in tensor memory.
-// The dropped A_lo.B_lo term and the TF32 reading of lo are ~2^-22 relative,
-// so the result has f32 accuracy.
+// Split: x = hi + lo with hi = x rounded to TF32 and lo = x - hi rounded to
+// TF32 (both exact TF32 values);
+// C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi accumulated in f32 in tensor memory
+// (three accumulators, summed in the epilogue).  The dropped A_lo.B_lo term
+// and the rounding of lo are ~2^-22 relative and unbiased, so the result has
+// f32 accuracy (as close to the exact product as an f32 FMA GEMM).  An element whose accumulated value is
+// not finite is recomputed exactly in the epilogue (exact_dot_f32), so
+// infinities and NaNs in the inputs give IEEE results.
 //
 // Pipeline (one CTA per 128 x 128 tile of C, 4 warps; the tiles after the
 // last full wave of SMs run stream-K, see k_gemm_tc):
@@ -38,7 +41,17 @@ constexpr int TBM = 128, TBN = 128, TBK = 32, TSTAGES = 3;
 constexpr int TILE_BYTES = TBM * TBK * 4;        // 16 KB: 128 rows x 128 B
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;      // A_hi, A_lo, B_hi, B_lo
 constexpr int SMEM_BYTES = TSTAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-constexpr uint32_t TMEM_COLS = 128;
+// Three 128 x 128 f32 accumulators in tensor memory (columns 0, 128, 256 of
+// a 512-column allocation): ACC_HI0 and ACC_HI1 take the A_hi.B_hi products
+// of the first and second half of every k-block, ACC_X the two cross terms.
+// The tensor core's accumulation loses up to ~1/2 ulp of the running sum per
+// MMA, with a bias; keeping the small cross terms apart and splitting the
+// large sum in two cuts the additions into each large sum by 6 and halves
+// its magnitude.  The epilogue adds the three in f32.  Measured on B200 for
+// 2048^3 with N(0, 1/2048) entries, max |error| against the exact product:
+// one accumulator, truncated split 1.82e-6; three accumulators 3.3e-7.
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t ACC_HI0 = 0, ACC_HI1 = 128, ACC_X = 256;
 
 __device__ int g_tc_error;  // 1 when a bounded wait ran out
 
@@ -129,7 +142,8 @@ __global__ void __launch_bounds__(128, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUtensorMap mA_lo,
           const __grid_constant__ CUtensorMap mB_hi, const __grid_constant__ CUtensorMap mB_lo,
           float* __restrict__ C, int M, int N, int Kp, long long sC, long long tile_base, int mode,
-          long long W, int G, float* __restrict__ ws) {
+          long long W, int G, float* __restrict__ ws, const float* __restrict__ A0,
+          const float* __restrict__ B0, int K) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t base = su32(smem_raw);
     unsigned char* smem = smem_raw + ((1024 - (base & 1023)) & 1023);
@@ -230,9 +244,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUt
 #pragma unroll
                 for (int j = 0; j < TBK / 8; j++) {
                     const uint64_t adv = (uint64_t)(j * 32) >> 4;  // 8 f32 = 32 bytes along K
-                    umma_tf32(tmem, alo + adv, bhi + adv, (kb != k0 || j != 0) ? 1u : 0u);
-                    umma_tf32(tmem, ahi + adv, blo + adv, 1);
-                    umma_tf32(tmem, ahi + adv, bhi + adv, 1);
+                    const uint32_t acc_hi = tmem + (j < TBK / 16 ? ACC_HI0 : ACC_HI1);
+                    const bool first = kb == k0 && j == 0;
+                    const uint32_t first_hi = (kb == k0 && (j == 0 || j == TBK / 16)) ? 0u : 1u;
+                    umma_tf32(tmem + ACC_X, alo + adv, bhi + adv, first ? 0u : 1u);
+                    umma_tf32(tmem + ACC_X, ahi + adv, blo + adv, 1);
+                    umma_tf32(acc_hi, ahi + adv, bhi + adv, first_hi);
                 }
                 umma_commit(&empty[s]);
             }
@@ -254,13 +271,27 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUt
         const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
         for (int c0 = 0; c0 < TBN; c0 += 8) {
-            uint32_t r[8];
+            uint32_t r[8], h1[8], x[8];
             asm volatile(
                 "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
                   "=r"(r[6]), "=r"(r[7])
-                : "r"(tl + c0));
+                : "r"(tl + ACC_HI0 + c0));
+            asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                    : "=r"(h1[0]), "=r"(h1[1]), "=r"(h1[2]), "=r"(h1[3]), "=r"(h1[4]), "=r"(h1[5]),
+                      "=r"(h1[6]), "=r"(h1[7])
+                    : "r"(tl + ACC_HI1 + c0));
+            asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                    : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]),
+                      "=r"(x[6]), "=r"(x[7])
+                    : "r"(tl + ACC_X + c0));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+                r[e] = __float_as_uint(__fadd_rn(
+                    __fadd_rn(__uint_as_float(r[e]), __uint_as_float(h1[e])), __uint_as_float(x[e])));
             if (mode == 1) {  // dense slot, every element
                 float4* d4 = reinterpret_cast<float4*>(crow + c0);
                 d4[0] = make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]),
@@ -269,6 +300,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUt
                                     __uint_as_float(r[6]), __uint_as_float(r[7]));
             } else if (row < M) {
                 const int col = n0 + c0;
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                    if (!isfinite(__uint_as_float(r[e])) && col + e < N)
+                        r[e] = __float_as_uint(exact_dot_f32(A0 + ((size_t)bz * M + row) * K,
+                                                             B0 + (size_t)bz * K * N + col + e, K, N));
                 if (col + 8 <= N && (((uintptr_t)(crow + col)) & 15) == 0) {
                     float4* d4 = reinterpret_cast<float4*>(crow + col);
                     d4[0] = make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]),
@@ -301,9 +337,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUt
     }
 }
 
-__device__ __forceinline__ float tf32_hi(float x) {
-    return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
 }
+// hi = x rounded to nearest TF32, lo = (x - hi) rounded to nearest TF32:
+// |lo| <= 2^-11 |x| with no sign bias, so the dropped lo.lo term averages
+// out (truncating hi leaves lo with x's sign and up to twice the size:
+// 1x1x3 products err by 1.3e-6 instead of 2.4e-8).  The tensor core reads
+// both exactly.  An infinite x gives hi = inf, lo = NaN (see the header).
+__device__ __forceinline__ float tf32_hi(float x) { return tf32_rna(x); }
+__device__ __forceinline__ float tf32_lo(float x, float hi) { return tf32_rna(__fsub_rn(x, hi)); }
 
 // Split A [M][K] (lda = K) into exact-TF32 hi and f32 lo parts, [M][Kp]
 // with zero padding in k in [K, Kp).  Grid (row blocks, batch); each warp
@@ -348,8 +393,8 @@ k_split_rows(const float* __restrict__ A, float* __restrict__ hi, float* __restr
                 float4 vh, vl;
                 vh.x = tf32_hi(x[u][0]), vh.y = tf32_hi(x[u][1]);
                 vh.z = tf32_hi(x[u][2]), vh.w = tf32_hi(x[u][3]);
-                vl.x = __fsub_rn(x[u][0], vh.x), vl.y = __fsub_rn(x[u][1], vh.y);
-                vl.z = __fsub_rn(x[u][2], vh.z), vl.w = __fsub_rn(x[u][3], vh.w);
+                vl.x = tf32_lo(x[u][0], vh.x), vl.y = tf32_lo(x[u][1], vh.y);
+                vl.z = tf32_lo(x[u][2], vh.z), vl.w = tf32_lo(x[u][3], vh.w);
                 *reinterpret_cast<float4*>(h + k) = vh;
                 *reinterpret_cast<float4*>(l + k) = vl;
             }
@@ -387,7 +432,7 @@ __global__ void k_split_cols(const float* __restrict__ B, float* __restrict__ hi
             const float x = t[threadIdx.x][r];
             const float h = tf32_hi(x);
             hi[(size_t)n * Kp + k] = h;
-            lo[(size_t)n * Kp + k] = __fsub_rn(x, h);
+            lo[(size_t)n * Kp + k] = tf32_lo(x, h);
         }
     }
 }
@@ -502,7 +547,7 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
     if (dp > 0) {
         k_gemm_tc<<<(unsigned)dp, 128, SMEM_BYTES, c.stream>>>(
             mah, mal, mbh, mbl, (float*)C, (int)m, (int)n, (int)Kp, (long long)(m * n), 0, 0, 0, 1,
-            nullptr);
+            nullptr, (const float*)A, (const float*)B, (int)k);
         count_launch();
     }
     if (pl.tail) {
@@ -512,9 +557,10 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
         if (!wsp) return E_CUDA;
         k_gemm_tc<<<(unsigned)pl.G, 128, SMEM_BYTES, c.stream>>>(
             mah, mal, mbh, mbl, (float*)C, (int)m, (int)n, (int)Kp, (long long)(m * n), pl.dp, 1,
-            pl.W, pl.G, wsp);
+            pl.W, pl.G, wsp, (const float*)A, (const float*)B, (int)k);
         count_launch();
-        int rc2 = launch_gemm_fix_f32(c, (float*)C, (int)m, (int)n, (int)batch, pl, KB, wsp);
+        int rc2 = launch_gemm_fix_f32(c, (float*)C, (const float*)A, (const float*)B, (int)m,
+                                      (int)n, (int)k, (int)batch, pl, KB, wsp);
         if (rc2) return rc2;
     }
     return finish(c);

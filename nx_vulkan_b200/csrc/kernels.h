@@ -60,10 +60,11 @@ int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void
                      size_t chains, unsigned K, float eps, int logp_mode);
 // f64 Gaussian: prec == nullptr means prec_i = prec_scalar for all i.
 // ke: optional [chain][k] kinetic energy 0.5 * sum(p*p*inv_mass) per step.
+// m_shared: m is one [n] row used by every chain (else [chain][n]).
 int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                            const void* p0, const void* m, const void* prec, double prec_scalar,
                            double mu, size_t n, size_t chains, unsigned K, double eps,
-                           void* ke = nullptr);
+                           void* ke = nullptr, bool m_shared = false);
 int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                             const void* p0, const void* X, const void* y, size_t n_obs,
                             size_t n_dim, size_t chains, unsigned K, double eps);
@@ -105,8 +106,28 @@ struct SkPlan {
 // min_idle k-tile times per SM (its fix-up and extra launches cost about that).
 bool gemm_sk_enabled();
 SkPlan gemm_sk_plan(long long tiles, int KT, int sms, int min_idle);
-int launch_gemm_fix_f32(Ctx& c, float* C, int M, int N, int batch, const SkPlan& pl, int KT,
-                        const float* ws);
+// A, B, K: the original operands ([batch][M][K], [batch][K][N]), for the
+// non-finite repair below.
+int launch_gemm_fix_f32(Ctx& c, float* C, const float* A, const float* B, int M, int N, int K,
+                        int batch, const SkPlan& pl, int KT, const float* ws);
+
+#ifdef __CUDACC__
+// One f32 product element as Nx.BinaryBackend defines it: the f32 operands
+// widened to double, products (exact in double) summed in k order, rounded
+// to f32 once.  The 3xTF32 GEMMs call it for elements whose tensor-core
+// result is not finite: the split x = hi + lo turns an infinite input into
+// hi = inf, lo = NaN, so every output that touches a non-finite input comes
+// out non-finite (and so does an f32 accumulation that overflowed); the
+// recomputation then gives inf, -inf or NaN exactly where IEEE arithmetic
+// does, and the exact value where only the f32 accumulator overflowed.
+static __device__ __noinline__ float exact_dot_f32(const float* __restrict__ a,
+                                                  const float* __restrict__ b, int K,
+                                                  long long ldb) {
+    double s = 0.0;
+    for (int t = 0; t < K; t++) s = __dadd_rn(s, __dmul_rn((double)a[t], (double)b[t * ldb]));
+    return __double2float_rn(s);
+}
+#endif
 
 // Grid helper: blocks for a grid-stride kernel.
 inline unsigned grid_for(Ctx& c, size_t work_items, unsigned threads, unsigned per_sm) {

@@ -51,6 +51,12 @@ struct Device {
     // enqueued, so two host threads sharing a stream cannot interleave
     // their multi-launch ops on the same scratch region.
     std::recursive_mutex scratch_mu;
+    // Per stream: the output range [ptr, ptr + bytes) of the last kernel
+    // this library launched with programmatic dependent launch
+    // (k_elementwise.cu); the next such kernel may read its inputs before the
+    // previous one completes only when they do not overlap this range.
+    std::mutex pdl_mu;
+    std::map<cudaStream_t, std::pair<uintptr_t, size_t>> pdl_last;
 };
 
 // Error codes of the C ABI.

@@ -26,6 +26,14 @@ int need(const void* h, size_t bytes, const char* what) {
     return OK;
 }
 
+// A batched chain's inverse mass is one [n] f64 row shared by every chain
+// when its buffer holds exactly n elements and there are several chains
+// (Nx broadcasting of an [n] tensor over [chain][n]); otherwise it must be
+// [chain][n].
+bool shared_row(const void* m, size_t n, size_t chains) {
+    return chains > 1 && nbytes(m) == n * 8;
+}
+
 #define NEED(h, bytes, what)                       \
     do {                                           \
         int rc_ = need((h), (bytes), (what));      \
@@ -79,6 +87,26 @@ int nxv_buf_upload(void* handle, const void* data, unsigned long n_bytes) {
 int nxv_buf_download(void* handle, void* data, unsigned long n_bytes) {
     if (!handle || (!data && n_bytes)) return E_NULL;
     return buf_download(handle, data, (size_t)n_bytes);
+}
+
+int nxv_buf_copy_2d(void* dst, unsigned long dst_offset, unsigned long dst_pitch, void* src,
+                    unsigned long src_offset, unsigned long src_pitch, unsigned long width,
+                    unsigned long rows) {
+    if (!dst || !src) return E_NULL;
+    if (rows == 0 || width == 0) return OK;
+    if (width > dst_pitch || width > src_pitch) {
+        set_error("copy_2d: row width %lu exceeds a pitch (%lu, %lu)", width, dst_pitch,
+                  src_pitch);
+        return E_ARG;
+    }
+    BEGIN(dst, src);
+    NEED(dst, (size_t)dst_offset + (size_t)(rows - 1) * dst_pitch + width, "copy_2d dst");
+    NEED(src, (size_t)src_offset + (size_t)(rows - 1) * src_pitch + width, "copy_2d src");
+    cudaError_t e = cudaMemcpy2DAsync(static_cast<char*>(dptr(dst)) + dst_offset, dst_pitch,
+                                      static_cast<const char*>(dptr(src)) + src_offset,
+                                      src_pitch, width, rows, cudaMemcpyDeviceToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync");
+    return finish(c);
 }
 
 // ---- elementwise ------------------------------------------------------------
@@ -624,7 +652,8 @@ int nxv_leapfrog_chain_gauss_f64_batched(void* q_chain, void* p_chain, void* gra
     size_t vec = (size_t)n * 8 * n_chains, chain = vec * K;
     NEED(q_init, vec, "q_init");
     NEED(p_init, vec, "p_init");
-    NEED(inv_mass, vec, "inv_mass");
+    const bool m_shared = shared_row(inv_mass, n, n_chains);
+    if (!m_shared) NEED(inv_mass, vec, "inv_mass");
     NEED(prec, (size_t)n * 8, "prec");
     NEED(q_chain, chain, "q_chain");
     NEED(p_chain, chain, "p_chain");
@@ -632,7 +661,7 @@ int nxv_leapfrog_chain_gauss_f64_batched(void* q_chain, void* p_chain, void* gra
     NEED(logp_chain, (size_t)K * n_chains * 8, "logp_chain");
     return launch_chain_gauss_f64(c, dptr(q_chain), dptr(p_chain), dptr(grad_chain),
                                   dptr(logp_chain), dptr(q_init), dptr(p_init), dptr(inv_mass),
-                                  dptr(prec), 0.0, mu, n, n_chains, K, eps);
+                                  dptr(prec), 0.0, mu, n, n_chains, K, eps, nullptr, m_shared);
 }
 
 int nxv_leapfrog_chain_gauss_f64_batched_ke(void* q_chain, void* p_chain, void* grad_chain,
@@ -653,7 +682,8 @@ int nxv_leapfrog_chain_gauss_f64_batched_ke(void* q_chain, void* p_chain, void* 
     size_t vec = (size_t)n * 8 * n_chains, chain = vec * K;
     NEED(q_init, vec, "q_init");
     NEED(p_init, vec, "p_init");
-    NEED(inv_mass, vec, "inv_mass");
+    const bool m_shared = shared_row(inv_mass, n, n_chains);
+    if (!m_shared) NEED(inv_mass, vec, "inv_mass");
     NEED(prec, (size_t)n * 8, "prec");
     NEED(q_chain, chain, "q_chain");
     NEED(p_chain, chain, "p_chain");
@@ -662,7 +692,8 @@ int nxv_leapfrog_chain_gauss_f64_batched_ke(void* q_chain, void* p_chain, void* 
     NEED(ke_chain, (size_t)K * n_chains * 8, "ke_chain");
     return launch_chain_gauss_f64(c, dptr(q_chain), dptr(p_chain), dptr(grad_chain),
                                   dptr(logp_chain), dptr(q_init), dptr(p_init), dptr(inv_mass),
-                                  dptr(prec), 0.0, mu, n, n_chains, K, eps, dptr(ke_chain));
+                                  dptr(prec), 0.0, mu, n, n_chains, K, eps, dptr(ke_chain),
+                                  m_shared);
 }
 
 int nxv_leapfrog_logreg_f64_batched(void* q_chain, void* p_chain, void* grad_chain,

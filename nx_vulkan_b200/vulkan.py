@@ -696,13 +696,16 @@ def leapfrog_chain_normal_f64(q, p, m, k, eps, mu, sigma):
 
 
 def leapfrog_chain_gauss_f64_batched(q, p, m, prec, n_chains, k, eps, mu=0.0, kinetic=False):
-    """Batched anisotropic Gaussian chains: q, p, m are [chain][n] f64, prec [n].
+    """Batched anisotropic Gaussian chains: q, p are [chain][n] f64, m is
+    [chain][n] or one [n] row broadcast over the chains, prec [n].
     Returns q, p, grad trajectories [chain][k][n] and logp [chain][k]; with
     kinetic=True also the kinetic energy 0.5 * sum(p^2 m) [chain][k]."""
-    if not (q.n_bytes == p.n_bytes == m.n_bytes) or k <= 0 or n_chains <= 0:
+    if q.n_bytes != p.n_bytes or k <= 0 or n_chains <= 0:
         return (ERROR, "size_mismatch" if k > 0 else "bad_op")
     n = q.n_bytes // 8 // n_chains
     if n * 8 * n_chains != q.n_bytes or prec.n_bytes != n * 8:
+        return (ERROR, "size_mismatch")
+    if m.n_bytes not in (q.n_bytes, n * 8):
         return (ERROR, "size_mismatch")
     outs = [_alloc(q.n_bytes * k), _alloc(q.n_bytes * k), _alloc(q.n_bytes * k),
             _alloc(n_chains * k * 8)]

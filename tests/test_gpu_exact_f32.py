@@ -1,0 +1,129 @@
+"""The exact f32 mode (NXV_EXACT_F32=1) of the elementwise kernels against the
+oracle, in units in the last place.
+
+Nx.BinaryBackend evaluates every f32 op in double and rounds the result to
+f32 once (oracle/oracle.c restates that).  With NXV_EXACT_F32=1 the GPU
+kernels do the same, with CUDA's double-precision functions in place of the C
+library's: both are within a couple of double ulps of the true value, so the
+f32 results agree bit for bit except where the true value lies within ~2^-29
+f32 ulp of a rounding boundary, where they may differ by one f32 ulp.  The
+tests assert at most 1 ulp everywhere, list the elements that are not
+bit-equal, and require at least 99.99 % of them to be.  NaN must meet NaN.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import down, unwrap, up
+
+pytestmark = pytest.mark.gpu
+
+
+def ordered(x):
+    """f32 bit patterns mapped to integers that are ordered like the floats
+    (adjacent floats differ by 1; +0 and -0 both map to 0)."""
+    i = np.asarray(x, np.float32).view(np.int32).astype(np.int64)
+    return np.where(i < 0, -(i & 0x7FFFFFFF), i)
+
+
+def assert_ulp(got, want, what, max_ulp=1, min_exact=0.9999):
+    got = np.asarray(got, np.float32)
+    want = np.asarray(want, np.float32)
+    assert got.shape == want.shape
+    nan_g, nan_w = np.isnan(got), np.isnan(want)
+    assert np.array_equal(nan_g, nan_w), f"{what}: NaN at {np.flatnonzero(nan_g != nan_w)[:5]}"
+    ok = ~nan_w
+    d = np.abs(ordered(got[ok]) - ordered(want[ok]))
+    bad = np.flatnonzero(d > 0)
+    listing = ", ".join(f"[{i}] got {got[ok][i]!r} want {want[ok][i]!r} ({d[i]} ulp)" for i in bad[:8])
+    print(f"{what}: {bad.size} of {d.size} elements not bit-equal{': ' + listing if bad.size else ''}")
+    assert d.max(initial=0) <= max_ulp, f"{what}: {listing}"
+    assert 1.0 - bad.size / max(d.size, 1) >= min_exact, f"{what}: {listing}"
+
+
+@pytest.fixture
+def exact(monkeypatch):
+    monkeypatch.setenv("NXV_EXACT_F32", "1")
+
+
+UNARY_TRANSCENDENTAL = {0: "exp", 1: "log", 5: "sigmoid", 6: "tanh", 13: "erf", 14: "expm1"}
+
+
+@pytest.mark.parametrize("n", [1, 7, 4097, 1 << 20])
+def test_exact_unary(nxv, orc, exact, n):
+    r = np.random.default_rng(21)
+    a = r.uniform(-10, 10, n).astype(np.float32)
+    a[: min(n, 6)] = np.array([0.0, -0.0, 1e-30, -1e-30, 88.7, -87.0], np.float32)[: min(n, 6)]
+    spv = nxv.shader_path("elementwise_unary.spv")
+    for op, name in UNARY_TRANSCENDENTAL.items():
+        src = np.abs(a) + np.float32(1e-3) if op == 1 else a
+        got = down(nxv, unwrap(nxv.apply_unary(up(nxv, src), op, spv, 4)), np.float32)
+        assert_ulp(got, orc.unary(src, op), f"{name} n={n}")
+
+
+def test_exact_unary_specials(nxv, orc, exact):
+    a = np.array([np.inf, -np.inf, np.nan, 0.0, -0.0, 1e-40, -1e-40, 88.0, -104.0, 89.0, -89.0,
+                  20.0, -20.0, 3.4e38], np.float32)
+    spv = nxv.shader_path("elementwise_unary.spv")
+    for op in range(15):
+        got = down(nxv, unwrap(nxv.apply_unary(up(nxv, a), op, spv, 4)), np.float32)
+        assert_ulp(got, orc.unary(a, op), f"unary op {op} specials", max_ulp=0, min_exact=1.0)
+
+
+@pytest.mark.parametrize("n", [5, 65536 + 3])
+def test_exact_binary_pow(nxv, orc, exact, n):
+    r = np.random.default_rng(22)
+    a = r.uniform(0.05, 4, n).astype(np.float32)
+    b = r.uniform(-6, 6, n).astype(np.float32)
+    spv = nxv.shader_path("elementwise_binary.spv")
+    got = down(nxv, unwrap(nxv.apply_binary(up(nxv, a), up(nxv, b), 4, spv, 4, 9)), np.float32)
+    assert_ulp(got, orc.binary(a, b, 4), f"pow n={n}")
+
+
+@pytest.mark.parametrize("n", [1, 5, 1000, 100003])
+def test_exact_generic_tapes(nxv, orc, exact, n):
+    """The generic op-tape interpreter (any op sequence, up to 4 inputs)."""
+    r = np.random.default_rng(9)
+    a, b, c, d = (r.uniform(0.1, 2, n).astype(np.float32) for _ in range(4))
+    tapes = [
+        ([0, 1, 2, 3, 112, 100, 101, 102], [1, 1, 1, 1, 1, 1, 1, 1]),
+        ([103, 105, 1, 2, 106], [1, 1, 2, 3, 1]),
+        ([1, 0], [1, 2]),
+        ([1, 1, 0], [1, 2, 3]),
+        ([110, 107, 108, 109, 104, 111, 0], [1, 1, 1, 1, 1, 1, 3]),
+        ([5, 6, 4], [2, 3, 1]),
+        ([113, 114, 100, 105], [1, 1, 1, 1]),
+    ]
+    ta, tb, tc, td = (up(nxv, v) for v in (a, b, c, d))
+    names = {0: "add", 1: "multiply", 2: "subtract", 3: "divide", 4: "pow", 5: "max", 6: "min"}
+    unames = {v: k for k, v in nxv.OP_CODES.items() if v >= 100}
+    for ops, src in tapes:
+        items = [(names[o], s) if o < 100 else unames[o] for o, s in zip(ops, src)]
+        got = down(nxv, unwrap(nxv.fused_chain_imm(ta, [tb, tc, td], items)), np.float32)
+        assert_ulp(got, orc.fused(a, [b, c, d], ops, src), f"tape {ops} n={n}")
+
+
+def test_exact_fused_chain_config1(nxv, orc, exact):
+    """tanh(exp(x*y + z) - 1.0) on f32[1,048,576] ~ U(-1,1), seed 0: the
+    fused-chain workload, one kernel, exact mode."""
+    n = 1 << 20
+    r = np.random.default_rng(0)
+    x, y, z = (r.uniform(-1, 1, n).astype(np.float32) for _ in range(3))
+    ops, src, imm = [1, 0, 100, 2, 106], [1, 2, 1, 0, 1], [0, 0, 0, 1.0, 0]
+    t = unwrap(nxv.fused_chain_imm(up(nxv, x), [up(nxv, y), up(nxv, z)],
+                                   [("multiply", 1), ("add", 2), "exp", ("subtract", ("imm", 1.0)), "tanh"]))
+    assert_ulp(down(nxv, t, np.float32), orc.fused(x, [y, z], ops, src, imm), "config-1 chain")
+
+
+def test_exact_fused_chain_reference_ops(nxv, orc, exact):
+    """nxv_fused_chain / nxv_fused_chain_4 (the reference's two entry points)
+    with transcendental steps, exact mode."""
+    n = 4099
+    r = np.random.default_rng(23)
+    a, b, c, d = (r.uniform(-1.5, 1.5, n).astype(np.float32) for _ in range(4))
+    ta, tb, tc, td = (up(nxv, v) for v in (a, b, c, d))
+    got = down(nxv, unwrap(nxv.fused_chain(ta, tb, ["multiply", "exp", "tanh", "add", "sigmoid"])),
+               np.float32)
+    assert_ulp(got, orc.fused(a, [b], [1, 100, 106, 0, 105], [1, 1, 1, 1, 1]), "fused_chain")
+    got = down(nxv, unwrap(nxv.fused_chain_4(ta, tb, tc, td, [("multiply", 1), ("add", 2), "erf",
+                                                          ("multiply", 3), "expm1"])), np.float32)
+    assert_ulp(got, orc.fused(a, [b, c, d], [1, 0, 113, 1, 114], [1, 2, 1, 3, 1]), "fused_chain_4")

@@ -171,6 +171,29 @@ def test_chain_families_tma_staged(nxv, orc, monkeypatch, family):
     close(down(nxv, lc, np.float32), wl, 1e-5, 1e-5)
 
 
+@pytest.mark.parametrize("d,chains,K", [(1000, 64, 8), (3000, 5, 4), (7, 3, 3), (1000, 1, 2)])
+@pytest.mark.parametrize("ke", [False, True])
+def test_gauss_shared_inverse_mass(nxv, orc, d, chains, K, ke):
+    """inv_mass given as one [d] row (broadcast over the chains) gives the
+    same trajectories, bit for bit, as the same row repeated per chain, on
+    the staged-store kernel (d <= 2048), the multi-tile kernel (d = 3000) and
+    odd rows (d = 7, register stores)."""
+    r = np.random.default_rng(12)
+    prec = r.uniform(0.5, 2.0, d)
+    q0, p0 = r.normal(size=(chains, d)), r.normal(size=(chains, d))
+    row = r.uniform(0.5, 1.5, d)
+    tiled = np.tile(row, (chains, 1))
+    a = unwrap(nxv.leapfrog_chain_gauss_f64_batched(up(nxv, q0), up(nxv, p0), up(nxv, row), up(nxv, prec),
+                                                    chains, K, 0.01, kinetic=ke))
+    b = unwrap(nxv.leapfrog_chain_gauss_f64_batched(up(nxv, q0), up(nxv, p0), up(nxv, tiled), up(nxv, prec),
+                                                    chains, K, 0.01, kinetic=ke))
+    for ta, tb in zip(a, b):
+        assert np.array_equal(down(nxv, ta, np.float64), down(nxv, tb, np.float64))
+    wq, wp, wg, wl = orc.chain_gauss_f64(q0, p0, tiled, prec, 0.0, d, chains, K, 0.01)
+    assert np.array_equal(down(nxv, a[0], np.float64), wq)
+    assert np.array_equal(down(nxv, a[1], np.float64), wp)
+
+
 def test_gauss_full_config(nxv, orc):
     """4096 chains x d=1000, L=32, eps=0.01 (the headline workload): 16 sampled
     chains against the oracle bit for bit; all chains: time reversibility

@@ -46,8 +46,14 @@ def _pool(lib):
     return [x.value for x in v]
 
 
-@pytest.mark.parametrize("chains,d,K", [(64, 1000, 32), (6, 5000, 7)])
-def test_noalloc_matches_allocating_entry_point(nxv, chains, d, K):
+@pytest.mark.parametrize("chains,d,K,cfg", [(64, 1000, 32, None), (6, 5000, 7, None),
+                                             # a register-store tile shape that would split
+                                             # each chain into 4 tiles: the staged-store
+                                             # kernel still takes it, so no partial sums
+                                             (1024, 1000, 32, "256x1")])
+def test_noalloc_matches_allocating_entry_point(nxv, monkeypatch, chains, d, K, cfg):
+    if cfg:
+        monkeypatch.setenv("NXV_LF_CFG", cfg)
     import torch
     from nx_vulkan_b200 import _native
 
