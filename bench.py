@@ -283,10 +283,12 @@ def main():
                     help="N > 1: steps whose final logps go out in one all-gather (default: every step)")
     ap.add_argument("--diag-depth", type=int, default=4,
                     help="N > 1: diagnostics buffers in flight (collective of step i waited for at step i + depth)")
-    ap.add_argument("--workload", default="gauss", choices=["gauss", "logreg"],
+    ap.add_argument("--workload", default="gauss", choices=["gauss", "logreg", "reduce"],
                     help="gauss: the headline anisotropic-Gaussian chain; logreg: the "
                          "logistic-regression HMC workload (256 chains over all ranks, "
-                         "X[10000,100], L=16, eps=0.002, momenta drawn on the device)")
+                         "X[10000,100], L=16, eps=0.002, momenta drawn on the device); "
+                         "reduce: the [4096,4096] row reductions, argmax and full sum "
+                         "sharded by rows over the ranks, results all-gathered on the device")
     ap.add_argument("--repeats", type=int, default=5,
                     help="timed regions of --steps steps each; value is their median")
     ap.add_argument("--suite", action="store_true",
@@ -307,6 +309,8 @@ def main():
         return suite(args)
     if args.workload == "logreg":
         return logreg_main(args, rank, world, local)
+    if args.workload == "reduce":
+        return reduce_main(args, rank, world, local)
 
     import torch
     import torch.distributed as dist
@@ -764,6 +768,75 @@ def logreg_main(args, rank, world, local):
                          "peak_source": "cuBLAS DGEMM 4096^3 measured in this run (rank 0)",
                          "note": "the step's whole time, momenta draws and carries included"},
             "clocks": clk.summary(),
+        }), flush=True)
+
+
+def reduce_main(args, rank, world, local):
+    """The reductions workload sharded by rows: x f32 and f64 [4096, 4096]
+    ~ N(0, 1) (seed 1), rank r holding rows chain_shard(4096, r, N) on its
+    GPU.  One step = sum over axis 1, max over axis 1, argmax over axis 1
+    (each rank's rows into device tensors, all-gathered device to device in
+    row order) and the full sum (rank partials all-gathered and folded in
+    rank order), for f32 and f64.  Strong scaling: the matrix is fixed."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from nx_vulkan_b200 import _native, dist as nd, vulkan as nxv
+    lib = _native.load()
+    assert nxv.init_devices([local]) == "ok", _native.last_error()
+    rows = cols = 4096
+    sh = nd.chain_shard(rows, rank, world)
+    x64 = np.random.default_rng(1).normal(size=(rows, cols))
+    bufs = {}
+    for name, dt in (("f64", np.float64), ("f32", np.float32)):
+        ok, t = nxv.upload_binary(np.ascontiguousarray(x64[sh.start:sh.stop].astype(dt)))
+        assert ok == "ok"
+        bufs[name] = t
+
+    def step():
+        res = []
+        for name, t in bufs.items():
+            res.append(nd.reduce_rows(nxv, t, sh.count, cols, 0, dtype=name))
+            res.append(nd.reduce_rows(nxv, t, sh.count, cols, 1, dtype=name))
+            res.append(nd.argmax_rows(nxv, t, sh.count, cols, dtype=name))
+            res.append(nd.reduce_full(nxv, t, 0, name) if world > 1 else
+                       (nxv.reduce_f64(t, 0) if name == "f64" else nxv.sum(t)))
+        return res
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    rep_ms = []
+    for _ in range(max(1, args.repeats)):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        rep_ms.append(max_over_ranks_ms((time.perf_counter() - t0) * 1e3, dev, world))
+    t_ms = statistics.median(rep_ms) / args.steps
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        nbytes = 3 * rows * cols * (4 + 8) + rows * cols * (4 + 8)  # each op reads the matrix
+        print(json.dumps({
+            "metric": "sharded [4096,4096] reductions: ms per step (sum/max/argmax over axis 1 + "
+                      "full sum, f32 and f64)", "value": t_ms, "unit": "ms", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "scaling": "strong", "dtype": "f32+f64", "data": "synthetic N(0,1) seed 1",
+            "algorithmic_gbs": nbytes / (t_ms / 1e3) / 1e9,
+            "config": {"workload": "row-sharded reductions with device all-gathers",
+                       "rows_per_gpu": sh.count,
+                       "timing": "host wall clock around the steps (each op waits for its kernel "
+                                 "before its collective), median of repeats, max over ranks"},
+            "repeats_ms_per_step": [ms / args.steps for ms in rep_ms],
         }), flush=True)
 
 
@@ -1228,6 +1301,7 @@ def suite(args):
     # -- NUTS over the speculative chain (the tree builder's call site) --------------------
     if "nuts" in want:
         from nx_vulkan_b200 import nuts
+        from oracle.chain import OracleChain
         lib.nxv_set_stream(None)
 
         class Timed:
@@ -1263,7 +1337,7 @@ def suite(args):
 
         Cn, Tn = 256, 5
         el, src, dep = run_nuts(nuts.GpuChain, Cn, Tn)
-        cel, csrc, _ = run_nuts(nuts.OracleChain, Cn, 2)
+        cel, csrc, _ = run_nuts(OracleChain, Cn, 2)
         cpu_us = cel / 2 * 1e6
         emit(workload="NUTS transitions, 256 chains, Gaussian d=100, eps=0.05, max depth 8",
              dtype="float64", us_per_call=el / Tn * 1e6, transitions_per_s=Cn * Tn / el,

@@ -413,27 +413,31 @@ __global__ void k_split_cols(const float* __restrict__ B, float* __restrict__ hi
     B += bz * sB;
     hi += bz * sO;
     lo += bz * sO;
-    const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 64;
+    const int n0 = blockIdx.x * 64;
+    // k tiles grid-stride over blockIdx.y (grid.y is capped at 65535)
+    for (int k0 = blockIdx.y * 32; k0 < Kp; k0 += gridDim.y * 32) {
 #pragma unroll
-    for (int r = threadIdx.y; r < 32; r += 8) {
-        const int k = k0 + r;
+        for (int r = threadIdx.y; r < 32; r += 8) {
+            const int k = k0 + r;
 #pragma unroll
-        for (int c = 0; c < 64; c += 32) {
-            const int n = n0 + c + threadIdx.x;
-            t[r][c + threadIdx.x] = (k < K && n < N) ? B[(size_t)k * N + n] : 0.0f;
+            for (int c = 0; c < 64; c += 32) {
+                const int n = n0 + c + threadIdx.x;
+                t[r][c + threadIdx.x] = (k < K && n < N) ? B[(size_t)k * N + n] : 0.0f;
+            }
         }
-    }
-    __syncthreads();
-    const int k = k0 + threadIdx.x;
+        __syncthreads();
+        const int k = k0 + threadIdx.x;
 #pragma unroll
-    for (int r = threadIdx.y; r < 64; r += 8) {
-        const int n = n0 + r;
-        if (n < N && k < Kp) {
-            const float x = t[threadIdx.x][r];
-            const float h = tf32_hi(x);
-            hi[(size_t)n * Kp + k] = h;
-            lo[(size_t)n * Kp + k] = tf32_lo(x, h);
+        for (int r = threadIdx.y; r < 64; r += 8) {
+            const int n = n0 + r;
+            if (n < N && k < Kp) {
+                const float x = t[threadIdx.x][r];
+                const float h = tf32_hi(x);
+                hi[(size_t)n * Kp + k] = h;
+                lo[(size_t)n * Kp + k] = tf32_lo(x, h);
+            }
         }
+        __syncthreads();  // the tile is refilled next iteration
     }
 }
 
@@ -498,11 +502,11 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
         return finish(c);
     }
-    if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff || batch > 65535) {
+    if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffe0 || batch > 65535) {
         set_error("matmul extents out of range");
         return E_ARG;
     }
-    const size_t Kp = (k + TBK - 1) / TBK * TBK;
+    const size_t Kp = (k + TBK - 1) / TBK * TBK;  // < 2^31: int indexing in the kernels
     ScratchGuard guard(c);
     const size_t a_elems = batch * m * Kp, b_elems = batch * n * Kp;
     float* s = (float*)scratch(c, (2 * a_elems + 2 * b_elems) * sizeof(float) + 256);
@@ -519,7 +523,8 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
         k_split_rows<<<dim3(gr, (unsigned)batch), 64, 0, c.stream>>>(
             (const float*)A, ahi, alo, (int)m, (int)k, (int)Kp, (long long)(m * k),
             (long long)(m * Kp));
-        dim3 g2((unsigned)((n + 63) / 64), (unsigned)(Kp / 32), (unsigned)batch);
+        dim3 g2((unsigned)((n + 63) / 64), (unsigned)std::min<size_t>(Kp / 32, 65535),
+                (unsigned)batch);
         k_split_cols<<<g2, dim3(32, 8), 0, c.stream>>>((const float*)B, bhi, blo, (int)k, (int)n,
                                                        (int)Kp, (long long)(k * n),
                                                        (long long)(n * Kp));

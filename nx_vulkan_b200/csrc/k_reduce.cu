@@ -415,8 +415,10 @@ int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* 
 // adds 0.  EX: exp in f64 (the oracle's evaluation; NXV_EXACT_F32=1), else
 // the hardware exponential __expf of the f32 difference, 16 terms summed in
 // f32 before the double add.  __expf's error grows with |x - max|, but a
-// term's weight in the sum falls as e^(x - max), so the sum stays within a
-// few ulp (13.9 us instead of 15.1 us with expf on [4096, 4096]).
+// term's weight in the sum falls as e^(x - max), so the result stays within
+// 4 ulp of the f64 evaluation rounded once (measured over rows of 1 to
+// 100,003 N(0, 100) elements; exact with EX) -- 13.9 us instead of 15.1 us
+// with expf on [4096, 4096].
 template <bool EX>
 struct LseLane {
     float m = -INFINITY;

@@ -20,6 +20,7 @@ NCCL over NVLink on the GPUs, gloo on CPU for the host-side tests.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 
@@ -100,16 +101,30 @@ REDUCE_IDENTITY = {0: 0.0, 1: float("inf"), 2: float("-inf")}
 
 
 def fold_in_rank_order(partials, op: int) -> float:
-    """Fold per-rank partials left to right in rank order (sum in double;
-    min/max propagate NaN like the single-GPU kernels)."""
+    """Fold per-rank partials left to right in rank order.  Sums are
+    compensated (Neumaier: the rounding error of every addition is carried
+    and added once at the end), so the fold adds at most about one rounding
+    of the total to the partials' own errors, also when slices cancel;
+    min/max propagate NaN like the single-GPU kernels."""
     if op not in REDUCE_IDENTITY:
         raise ValueError(f"reduce op {op} outside 0..2")
     acc = REDUCE_IDENTITY[op]
+    if op == 0:
+        comp, plain = 0.0, 0.0
+        for v in partials:
+            v = float(v)
+            plain += v
+            t = acc + v
+            if abs(acc) >= abs(v):
+                comp += (acc - t) + v
+            else:
+                comp += (v - t) + acc
+            acc = t
+        # infinities and NaN: the plain sum's IEEE result
+        return acc + comp if math.isfinite(plain) else plain
     for v in partials:
         v = float(v)
-        if op == 0:
-            acc = acc + v
-        elif v != v or acc != acc:
+        if v != v or acc != acc:
             acc = float("nan")
         elif op == 1:
             acc = v if v < acc else acc
@@ -174,70 +189,82 @@ def reduce_full(nxv, x_slice, op: int, dtype: str = "f64", group=None) -> float:
     return float(np.float32(v)) if dtype == "f32" else v
 
 
-def _gather_host(arr, group):
+def _rank_output(nxv, shape, np_dtype):
+    """The rank's output tensor and the handle a kernel writes it through.
+
+    With the CUDA library the tensor lives on the rank's GPU and the kernel
+    fills it in place (a non-owning handle over the tensor's memory), so the
+    result never leaves the device before the collective.  A host stand-in
+    of the library (tests without a GPU; `nxv.on_host`) gets a host tensor."""
     import numpy as np
     import torch
 
-    t = torch.from_numpy(np.ascontiguousarray(arr)).to(_coll_device())
-    return gather_rows(t, group=group).cpu().numpy()
+    tdt = {np.dtype(np.float64): torch.float64, np.dtype(np.float32): torch.float32,
+           np.dtype(np.int64): torch.int64}[np.dtype(np_dtype)]
+    host = getattr(nxv, "on_host", False)
+    dev = torch.device("cpu") if host else torch.device("cuda", torch.cuda.current_device())
+    t = torch.empty(shape, dtype=tdt, device=dev)
+    return t, (nxv.wrap_tensor(t) if t.numel() else None)
+
+
+def _finish_rank(nxv, local, what):
+    """Wait for the rank's kernel (the library runs on its own stream), then
+    put the tensor where the backend's collectives run: NCCL takes device
+    tensors as they are; gloo needs a host copy."""
+    import torch.distributed as dist
+
+    if not getattr(nxv, "on_host", False):
+        ok = nxv.synchronize()
+        if ok != "ok":
+            raise RuntimeError(f"{what} failed on this rank: {ok}")
+    if dist.get_backend() != "nccl" and local.is_cuda:
+        return local.cpu()
+    return local
 
 
 def reduce_rows(nxv, x_rows, n_rows: int, row_len: int, op: int, dtype: str = "f64",
                 group=None):
     """Per-row sum/max/min (nxv_reduce_axis op codes 0/1/2) of a row-sharded
-    matrix: each rank reduces its n_rows rows on its GPU, and the results are
-    all-gathered in row order.  Returns the full [total rows] vector (numpy)."""
+    matrix: each rank reduces its n_rows rows on its GPU into a device tensor,
+    and the results are all-gathered in row order (NCCL, device to device).
+    Returns the full [total rows] vector as a torch tensor on the collective
+    device (the rank's GPU under NCCL)."""
     import numpy as np
 
-    elt, np_t = (8, np.float64) if dtype == "f64" else (4, np.float32)
-    if n_rows == 0:
-        local = np.zeros(0, np_t)
-    else:
+    local, h = _rank_output(nxv, (n_rows,), np.float64 if dtype == "f64" else np.float32)
+    if n_rows:
         fn = nxv.reduce_axis_f64 if dtype == "f64" else nxv.reduce_axis
-        ok, out = fn(x_rows, n_rows, row_len, 1, op)
+        ok, out = fn(x_rows, n_rows, row_len, 1, op, out=h)
         if ok != "ok":
             raise RuntimeError(f"reduce_axis failed on this rank: {out}")
-        ok, b = nxv.download_binary(out, n_rows * elt)
-        if ok != "ok":
-            raise RuntimeError(f"download failed on this rank: {b}")
-        local = np.frombuffer(b, np_t)
-    return _gather_host(local, group)
+    return gather_rows(_finish_rank(nxv, local, "reduce_axis"), group)
 
 
 def argmax_rows(nxv, x_rows, n_rows: int, row_len: int, dtype: str = "f64", group=None):
     """Per-row argmax (lowest index on ties) of a row-sharded matrix; indices
-    are within the row, so sharding by rows leaves them unchanged."""
+    are within the row, so sharding by rows leaves them unchanged.  Returns
+    int64 indices as a torch tensor on the collective device."""
     import numpy as np
 
-    if n_rows == 0:
-        local = np.zeros(0, np.int64)
-    else:
-        ok, out = nxv.argmax_axis(x_rows, n_rows, row_len, 1, dtype=dtype)
+    local, h = _rank_output(nxv, (n_rows,), np.int64)
+    if n_rows:
+        ok, out = nxv.argmax_axis(x_rows, n_rows, row_len, 1, dtype=dtype, out=h)
         if ok != "ok":
             raise RuntimeError(f"argmax failed on this rank: {out}")
-        ok, b = nxv.download_binary(out, n_rows * 8)
-        if ok != "ok":
-            raise RuntimeError(f"download failed on this rank: {b}")
-        local = np.frombuffer(b, np.int64)
-    return _gather_host(local, group)
+    return gather_rows(_finish_rank(nxv, local, "argmax"), group)
 
 
 def matmul_batched(nxv, a, b, n_batch: int, m: int, n: int, k: int, dtype: str = "f64",
                    group=None):
     """Batched matmul sharded by batch entry: each rank multiplies its
-    n_batch entries on its GPU; the products are all-gathered in batch
-    order.  Returns [total batch, m, n] (numpy)."""
+    n_batch entries on its GPU into a device tensor; the products are
+    all-gathered in batch order.  Returns [total batch, m, n] as a torch
+    tensor on the collective device."""
     import numpy as np
 
-    elt, np_t = (8, np.float64) if dtype == "f64" else (4, np.float32)
-    if n_batch == 0:
-        local = np.zeros((0, m, n), np_t)
-    else:
-        ok, out = nxv.matmul_batched(a, b, n_batch, m, n, k, dtype=dtype)
+    local, h = _rank_output(nxv, (n_batch, m, n), np.float64 if dtype == "f64" else np.float32)
+    if n_batch:
+        ok, out = nxv.matmul_batched(a, b, n_batch, m, n, k, dtype=dtype, out=h)
         if ok != "ok":
             raise RuntimeError(f"matmul failed on this rank: {out}")
-        ok, raw = nxv.download_binary(out, n_batch * m * n * elt)
-        if ok != "ok":
-            raise RuntimeError(f"download failed on this rank: {raw}")
-        local = np.frombuffer(raw, np_t).reshape(n_batch, m, n)
-    return _gather_host(local, group)
+    return gather_rows(_finish_rank(nxv, local, "matmul"), group)

@@ -67,25 +67,6 @@ class GaussianTarget:
         return -0.5 * ((self.prec * d) * d).sum(axis=-1) + self.const
 
 
-class OracleChain:
-    """Trajectory source on the CPU: the oracle's batched Gaussian chain
-    (test infrastructure; the kinetic energy is computed from its p)."""
-
-    def __init__(self, target: GaussianTarget, inv_mass, eps: float):
-        from oracle import binding as orc
-        self.orc, self.t, self.m, self.eps = orc, target, np.asarray(inv_mass, np.float64), eps
-        self.calls = []
-
-    def extend(self, q, p, K):
-        c, d = q.shape
-        m = np.broadcast_to(self.m, (c, d)).copy()
-        qc, pc, gc, lp = self.orc.chain_gauss_f64(q, p, m, self.t.prec, self.t.mu, d, c, K, self.eps)
-        pc = pc.reshape(c, K, d)
-        ke = 0.5 * ((pc * pc) * m[:, None, :]).sum(axis=-1)
-        self.calls.append((c, K))
-        return qc.reshape(c, K, d), pc, lp.reshape(c, K), ke
-
-
 class GpuChain:
     """Trajectory source on the GPU: nxv_leapfrog_chain_gauss_f64_batched_ke
     through the Nx.Vulkan mirror; q, p, logp and kinetic energy of every step

@@ -336,38 +336,54 @@ def reduce_f64(t, op: int):
     return (OK, out.value)
 
 
-def _reduce_axis(a, outer, r, inner, op, spv, elt):
-    if op > 2:
-        return (ERROR, "bad_op")
-    out = _alloc(outer * inner * elt)
-    if out is None:
-        return (ERROR, "alloc_failed")
-    rc = _lib().nxv_reduce_axis(out.handle, a.handle, outer, r, inner, op, spv)
+def _out_buffer(out, n_bytes):
+    """The caller's output buffer (checked to hold n_bytes), or a new one."""
+    if out is not None:
+        return out if out.n_bytes >= n_bytes else None
+    return _alloc(n_bytes)
+
+
+def _dispatch_into(out, given, rc):
+    if given is not None:
+        return (OK, out) if rc == 0 else (ERROR, "dispatch_failed")
     return _dispatch([out], rc)
 
 
-def reduce_axis(a, outer, reduce_size, inner, op):
-    """(outer, reduce, inner) -> (outer, inner); op 0 sum, 1 max, 2 min."""
-    return _reduce_axis(a, outer, reduce_size, inner, op, shader_path("reduce_axis.spv"), 4)
+def _reduce_axis(a, outer, r, inner, op, spv, elt, out=None):
+    if op > 2:
+        return (ERROR, "bad_op")
+    o = _out_buffer(out, outer * inner * elt)
+    if o is None:
+        return (ERROR, "alloc_failed" if out is None else "size_mismatch")
+    rc = _lib().nxv_reduce_axis(o.handle, a.handle, outer, r, inner, op, spv)
+    return _dispatch_into(o, out, rc)
 
 
-def reduce_axis_f64(a, outer, reduce_size, inner, op):
-    return _reduce_axis(a, outer, reduce_size, inner, op, shader_path("reduce_axis_f64.spv"), 8)
+def reduce_axis(a, outer, reduce_size, inner, op, out=None):
+    """(outer, reduce, inner) -> (outer, inner); op 0 sum, 1 max, 2 min.
+    `out`: an existing buffer to write the result into (e.g. wrap_tensor)."""
+    return _reduce_axis(a, outer, reduce_size, inner, op, shader_path("reduce_axis.spv"), 4, out)
+
+
+def reduce_axis_f64(a, outer, reduce_size, inner, op, out=None):
+    return _reduce_axis(a, outer, reduce_size, inner, op, shader_path("reduce_axis_f64.spv"), 8,
+                        out)
 
 
 def logsumexp(a, outer, reduce_size, inner):
     return _reduce_axis(a, outer, reduce_size, inner, 0, shader_path("logsumexp.spv"), 4)
 
 
-def argmax_axis(a, outer, reduce_size, inner, *, dtype="f32", is_min=False, index_bytes=8):
+def argmax_axis(a, outer, reduce_size, inner, *, dtype="f32", is_min=False, index_bytes=8,
+                out=None):
     """argmax/argmin over the middle axis; lowest index wins ties (Nx :low)."""
-    out = _alloc(outer * inner * index_bytes)
-    if out is None:
-        return (ERROR, "alloc_failed")
-    rc = _lib().nxv_argmax_axis(out.handle, a.handle, outer, reduce_size, inner, int(is_min),
+    o = _out_buffer(out, outer * inner * index_bytes)
+    if o is None:
+        return (ERROR, "alloc_failed" if out is None else "size_mismatch")
+    rc = _lib().nxv_argmax_axis(o.handle, a.handle, outer, reduce_size, inner, int(is_min),
                                 0 if dtype == "f32" else 1, index_bytes,
                                 shader_path("argmax_axis.spv"))
-    return _dispatch([out], rc)
+    return _dispatch_into(o, out, rc)
 
 
 # ---- matmul (lib/nx_vulkan.ex:277-347; lib.rs:563-598, 1038-1078) --------------------
@@ -410,16 +426,26 @@ def matmul(a, b, m, n, k):
     return matmul_variant(a, b, m, n, k, shader, tm, tn)
 
 
-def matmul_batched(a, b, batch, m, n, k, dtype="f64"):
+def matmul_batched(a, b, batch, m, n, k, dtype="f64", out=None):
     elt = 4 if dtype == "f32" else 8
     if a.n_bytes != batch * m * k * elt or b.n_bytes != batch * k * n * elt:
         return (ERROR, "size_mismatch")
-    out = _alloc(batch * m * n * elt)
-    if out is None:
-        return (ERROR, "alloc_failed")
-    rc = _lib().nxv_matmul_batched(out.handle, a.handle, b.handle, batch, m, n, k,
+    o = _out_buffer(out, batch * m * n * elt)
+    if o is None:
+        return (ERROR, "alloc_failed" if out is None else "size_mismatch")
+    rc = _lib().nxv_matmul_batched(o.handle, a.handle, b.handle, batch, m, n, k,
                                    0 if dtype == "f32" else 1, shader_path("matmul_batched.spv"))
-    return _dispatch([out], rc)
+    return _dispatch_into(o, out, rc)
+
+
+def wrap_tensor(t):
+    """Non-owning handle over the memory of a torch CUDA tensor (nxv_buf_wrap),
+    for calls that write their result into it in place.  The tensor must stay
+    alive while work using the handle can run."""
+    n = t.numel() * t.element_size()
+    h = _lib().nxv_buf_wrap(C.c_void_p(t.data_ptr()), n)
+    return VulkanTensor(h, n) if h else None
+
 
 
 # ---- random (lib/nx_vulkan.ex:349-361; lib.rs:602-635) ----------------------------------

@@ -111,3 +111,20 @@ def close(got, want, rtol, atol):
     if not ok.all():
         i = np.flatnonzero(~ok)[:5]
         raise AssertionError(f"{(~ok).sum()} mismatches, e.g. idx {i}: got {got[i]} want {want[i]}")
+
+
+def ulp_diff(got, want):
+    """|got - want| in units in the last place of f32 (adjacent floats differ
+    by 1; +0 and -0 are equal).  Both arrays f32; NaN positions must match
+    and count 0."""
+    g = np.asarray(got, np.float32)
+    w = np.asarray(want, np.float32)
+    assert np.array_equal(np.isnan(g), np.isnan(w))
+
+    def ordered(x):
+        i = x.view(np.int32).astype(np.int64)
+        return np.where(i < 0, -(i & 0x7FFFFFFF), i)
+
+    d = np.abs(ordered(g) - ordered(w))
+    d[np.isnan(w)] = 0
+    return d

@@ -90,3 +90,13 @@ def test_unknown_fused_op_is_key_error():
     from nx_vulkan_b200 import vulkan
     with pytest.raises(KeyError):
         vulkan.OP_CODES["not_a_real_op"]
+
+
+def test_product_package_never_imports_the_oracle():
+    """The oracle is test infrastructure: no module of the product package
+    imports it (the CPU restatement is never one import away from the
+    product path)."""
+    pkg = ROOT / "nx_vulkan_b200"
+    offenders = [p.name for p in pkg.rglob("*.py")
+                 if re.search(r"^\s*(from|import)\s+oracle\b", p.read_text(), flags=re.M)]
+    assert not offenders, offenders

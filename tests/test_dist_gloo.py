@@ -92,9 +92,32 @@ class _Buf:
         self.n_bytes = self.arr.nbytes
 
 
+class _TensorBuf(_Buf):
+    """A host stand-in's view of a torch CPU tensor (FakeNxv.wrap_tensor)."""
+
+    def __init__(self, t):
+        self.t = t
+        self.arr = t.numpy()
+        self.n_bytes = self.arr.nbytes
+
+
 class FakeNxv:
     """Stands in for the Nx.Vulkan mirror on a machine without a GPU: the same
-    call signatures and ("ok", value) results, computed with numpy."""
+    call signatures and ("ok", value) results, computed with numpy; outputs
+    given with out= are written in place."""
+
+    on_host = True
+
+    @staticmethod
+    def wrap_tensor(t):
+        return _TensorBuf(t)
+
+    @staticmethod
+    def _into(out, value):
+        if out is None:
+            return ("ok", _Buf(value))
+        out.arr[...] = np.asarray(value).reshape(out.arr.shape)
+        return ("ok", out)
 
     def reduce_f64(self, t, op):
         return ("ok", float((np.sum, np.min, np.max)[op](t.arr)))
@@ -108,15 +131,15 @@ class FakeNxv:
     def reduce_max(self, t):
         return ("ok", float(np.max(t.arr)))
 
-    def reduce_axis_f64(self, t, outer, r, inner, op):
+    def reduce_axis_f64(self, t, outer, r, inner, op, out=None):
         x = t.arr.reshape(outer, r, inner)
-        return ("ok", _Buf((np.sum, np.max, np.min)[op](x, axis=1).reshape(-1)))
+        return self._into(out, (np.sum, np.max, np.min)[op](x, axis=1).reshape(-1))
 
-    def argmax_axis(self, t, outer, r, inner, dtype="f32"):
-        return ("ok", _Buf(np.argmax(t.arr.reshape(outer, r, inner), axis=1).astype(np.int64)))
+    def argmax_axis(self, t, outer, r, inner, dtype="f32", out=None):
+        return self._into(out, np.argmax(t.arr.reshape(outer, r, inner), axis=1).astype(np.int64))
 
-    def matmul_batched(self, a, b, batch, m, n, k, dtype="f64"):
-        return ("ok", _Buf(np.matmul(a.arr.reshape(batch, m, k), b.arr.reshape(batch, k, n))))
+    def matmul_batched(self, a, b, batch, m, n, k, dtype="f64", out=None):
+        return self._into(out, np.matmul(a.arr.reshape(batch, m, k), b.arr.reshape(batch, k, n)))
 
     def download_binary(self, t, n_bytes):
         assert n_bytes == t.n_bytes
@@ -135,7 +158,13 @@ def test_element_shard_keeps_rows_whole():
 
 def test_fold_in_rank_order():
     from nx_vulkan_b200.dist import fold_in_rank_order
-    assert fold_in_rank_order([1e16, 1.0, -1e16], 0) == 0.0   # left to right, in rank order
+    # compensated: the rounding error of 1e16 + 1.0 is carried, giving the exact sum
+    assert fold_in_rank_order([1e16, 1.0, -1e16], 0) == 1.0
+    assert fold_in_rank_order([1e300, 1e300, float("inf")], 0) == float("inf")
+    assert np.isnan(fold_in_rank_order([float("inf"), 1.0, float("-inf")], 0))
+    assert np.isnan(fold_in_rank_order([1.0, float("nan")], 0))
+    # slices that cancel: [a, -a + tiny] gives the tiny remainder exactly
+    assert fold_in_rank_order([0.1 + 0.2, -(0.1 + 0.2), 1e-17], 0) == 1e-17
     assert fold_in_rank_order([3.0, -1.0, 2.0], 1) == -1.0
     assert fold_in_rank_order([3.0, float("inf"), 2.0], 2) == float("inf")
     assert fold_in_rank_order([], 2) == float("-inf")
@@ -188,6 +217,8 @@ def _sharded_worker(rank, world, port, result_q, use_gpu):
                          for s in (nd.element_shard(rows * row_len, q, world, row_len)
                                    for q in range(world))],
         }
+        for key in ("row_sum", "row_max", "argmax", "bmm"):
+            out[key] = out[key].cpu().numpy()
         result_q.put((rank, out))
     finally:
         dist.destroy_process_group()

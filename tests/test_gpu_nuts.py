@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 
 from nx_vulkan_b200 import nuts
+from oracle.chain import OracleChain
 
 pytestmark = pytest.mark.gpu
 
@@ -22,7 +23,7 @@ def test_nuts_gpu_matches_oracle(nxv, d, C, T):
     m = r.uniform(0.8, 1.2, d)
     eps = 0.1 if d <= 16 else 0.02
     q_init = r.normal(size=(C, d)) / np.sqrt(prec)
-    gpu, cpu = nuts.GpuChain(t, m, eps), nuts.OracleChain(t, m, eps)
+    gpu, cpu = nuts.GpuChain(t, m, eps), OracleChain(t, m, eps)
     qa, qb = q_init.copy(), q_init.copy()
     ra, rb = np.random.default_rng(9), np.random.default_rng(9)
     for _ in range(T):

@@ -8,7 +8,7 @@ relative (+1e-14 absolute for results near zero)."""
 import numpy as np
 import pytest
 
-from gpu_util import chain_error_bound, close, close_bound, down, unwrap, up
+from gpu_util import chain_error_bound, close, close_bound, down, ulp_diff, unwrap, up
 
 pytestmark = pytest.mark.gpu
 
@@ -275,15 +275,21 @@ def test_argmax_ties_and_nan(nxv, orc):
 
 @pytest.mark.parametrize("exact", ["0", "1"])
 def test_logsumexp(nxv, orc, monkeypatch, exact):
-    """f32 in/out within 1e-5 relative; exp in f32 (default) or f64
-    (NXV_EXACT_F32=1), sums in double.  Rows of 1..4096+ elements, odd and
-    unaligned lengths, the cols kernel."""
+    """f32 in/out within 1e-5 relative and within 4 ulp of the oracle (its
+    f64 evaluation rounded once) with the hardware exponential (default),
+    1 ulp with exp in f64 (NXV_EXACT_F32=1); sums in double.  Rows of
+    1..4096+ elements, odd and unaligned lengths, the cols kernel."""
     monkeypatch.setenv("NXV_EXACT_F32", exact)
+    worst = 0
     for shape in [(64, 1000, 1), (3, 50, 17), (4096, 4096, 1), (1, 100003, 1), (5000, 7, 1),
                   (9, 1, 1), (33, 4097, 1)]:
         x = np.random.default_rng(2).normal(size=int(np.prod(shape))).astype(np.float32) * 10
         got = down(nxv, unwrap(nxv.logsumexp(up(nxv, x), *shape)), np.float32)
-        close(got, orc.logsumexp(x, *shape), 1e-5, 1e-6)
+        want = orc.logsumexp(x, *shape)
+        close(got, want, 1e-5, 1e-6)
+        worst = max(worst, int(ulp_diff(got, want).max()))
+    print(f"logsumexp exact={exact}: worst {worst} ulp")
+    assert worst <= (1 if exact == "1" else 4)
 
 
 @pytest.mark.parametrize("exact", ["0", "1"])
@@ -368,6 +374,19 @@ def test_matmul_f32_3xtf32(nxv, orc, mnk):
           f"= {np.max(err / f32_dot_bound(k, bound)):.3e} of the dot bound")
     assert flat >= flat_host - 0.005
     assert np.all(err <= tol + f32_dot_bound(k, bound))
+
+
+@pytest.mark.parametrize("mnk", [(1, 1, 2_200_003), (2, 3, 2_097_153)])
+def test_matmul_f32_deep_k(nxv, orc, mnk):
+    """k past 65535 tiles of 32 (2,097,120): the transposing split of B
+    walks its k tiles grid-stride instead of one grid row per tile."""
+    m, n, k = mnk
+    r = np.random.default_rng(13)
+    a, b = r.normal(size=m * k).astype(np.float32), r.normal(size=k * n).astype(np.float32)
+    got = down(nxv, unwrap(nxv.matmul(up(nxv, a), up(nxv, b), m, n, k)), np.float32)
+    want = orc.matmul(a, b, m, n, k)
+    bound = (np.abs(a.reshape(m, k)).astype(np.float64) @ np.abs(b.reshape(k, n))).reshape(-1)
+    assert np.all(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-6 + f32_dot_bound(k, bound))
 
 
 @pytest.mark.parametrize("impl", ["tc", "mma"])

@@ -4,6 +4,7 @@ import numpy as np
 
 from nx_vulkan_b200 import nuts
 from oracle import binding as orc
+from oracle.chain import OracleChain
 
 
 def circle(n, dt=0.1, w=1.0):
@@ -47,7 +48,7 @@ def test_speculative_policy():
     assert [nuts.speculative_steps(1 << k) for k in range(8)] == [32, 32, 32, 32, 32, 64, 128, 256]
     prec = np.array([1.0, 2.0])
     t = nuts.GaussianTarget(prec)
-    src = nuts.OracleChain(t, np.ones(2), 0.1)
+    src = OracleChain(t, np.ones(2), 0.1)
     rng = np.random.default_rng(3)
     q = rng.normal(size=(4, 2))
     q1, st = nuts.nuts_transition(src, t, q, np.ones(2), rng, max_depth=8)
@@ -64,7 +65,7 @@ def test_nuts_samples_the_gaussian():
     prec = np.array([0.5, 1.0, 2.0, 4.0])
     t = nuts.GaussianTarget(prec)
     m = np.ones(4)
-    src = nuts.OracleChain(t, m, 0.25)
+    src = OracleChain(t, m, 0.25)
     rng = np.random.default_rng(7)
     C, T = 16, 300
     q = rng.normal(size=(C, 4)) / np.sqrt(prec)
