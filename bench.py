@@ -803,8 +803,7 @@ def reduce_main(args, rank, world, local):
             res.append(nd.reduce_rows(nxv, t, sh.count, cols, 0, dtype=name))
             res.append(nd.reduce_rows(nxv, t, sh.count, cols, 1, dtype=name))
             res.append(nd.argmax_rows(nxv, t, sh.count, cols, dtype=name))
-            res.append(nd.reduce_full(nxv, t, 0, name) if world > 1 else
-                       (nxv.reduce_f64(t, 0) if name == "f64" else nxv.sum(t)))
+            res.append(nd.reduce_full(nxv, t, 0, name))
         return res
 
     for _ in range(args.warmup):

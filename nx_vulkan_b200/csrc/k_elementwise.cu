@@ -13,6 +13,7 @@
 #include "kernels.h"
 #include "ops_common.cuh"
 
+#include <algorithm>
 #include <type_traits>
 
 namespace nxv {
@@ -245,6 +246,82 @@ int map1_per_sm() {
     return occ;
 }
 
+// ---- software-pipelined map for arithmetic-heavy functors ------------------------
+//
+// f64 maps and the exact f32 mode spend about as long in FP64 arithmetic as in
+// moving their bytes.  k_map_pipe runs one wave of CTAs whose threads walk
+// the array one vector at a time and load the next vector before doing the
+// math of the current one, so every warp keeps a load in flight while it
+// computes (the grid-stride form with all loads first and all math after
+// serialises the two across the whole GPU when one wave covers the array).
+
+template <typename T, int NIN, class F>
+__global__ void __launch_bounds__(kThreads)
+k_map_pipe(T* __restrict__ out, const T* __restrict__ in0, const T* __restrict__ in1,
+           const T* __restrict__ in2, const T* __restrict__ in3, size_t n, F f) {
+    constexpr int W = (int)(16 / sizeof(T));
+    const T* ins[4] = {in0, in1, in2, in3};
+    const size_t nv = n / W;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    T nx[NIN > 0 ? NIN : 1][W];
+    if (v < nv) {
+#pragma unroll
+        for (int q = 0; q < NIN; q++) vload(ins[q] + v * W, nx[q]);
+    }
+    for (; v < nv; v += stride) {
+        T x[NIN > 0 ? NIN : 1][W];
+#pragma unroll
+        for (int q = 0; q < NIN; q++)
+#pragma unroll
+            for (int j = 0; j < W; j++) x[q][j] = nx[q][j];
+        const size_t vn = v + stride;
+        if (vn < nv) {
+#pragma unroll
+            for (int q = 0; q < NIN; q++) vload(ins[q] + vn * W, nx[q]);
+        }
+        T r[W];
+#pragma unroll
+        for (int j = 0; j < W; j++) {
+            T args[NIN > 0 ? NIN : 1];
+#pragma unroll
+            for (int q = 0; q < NIN; q++) args[q] = x[q][j];
+            r[j] = f(args);
+        }
+        vstore(out + v * W, r);
+    }
+    if (blockIdx.x == 0) {  // tail of n % W elements
+        const size_t t = nv * W + threadIdx.x;
+        if (t < n) {
+            T args[NIN > 0 ? NIN : 1];
+#pragma unroll
+            for (int q = 0; q < NIN; q++) args[q] = ins[q][t];
+            out[t] = f(args);
+        }
+    }
+}
+
+// Resident CTAs of k_map_pipe<T, NIN, F> per SM (looked up once per instantiation).
+template <typename T, int NIN, class F>
+int pipe_per_sm() {
+    static const int occ = []() {
+        int o = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_map_pipe<T, NIN, F>, kThreads,
+                                                          0) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        return o;
+    }();
+    return occ;
+}
+
+// NXV_MAP_PIPE=0: arithmetic-heavy maps use the grid-stride kernel.
+bool map_pipe() {
+    const char* e = getenv("NXV_MAP_PIPE");
+    return !(e && e[0] == '0');
+}
+
 template <typename T, int NIN, class F>
 int run_map(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* i3, size_t n, F f) {
     if (n == 0) return OK;
@@ -258,6 +335,18 @@ int run_map(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* i3, 
         if (vec && map_wide() && nv >= 1 && nv <= wave)
             return launch_map1<T, NIN, F>(c, out, i0, i1, i2, i3, n, f,
                                           (unsigned)((nv + kThreads - 1) / kThreads));
+    }
+    if constexpr (sizeof(T) == 8 || Heavy<F>::value) {
+        const size_t nv = n / W;
+        const int occ = pipe_per_sm<T, NIN, F>();
+        if (vec && map_pipe() && nv >= 1 && occ > 0) {
+            const size_t want = (nv + kThreads - 1) / kThreads;
+            const unsigned g =
+                (unsigned)std::min<size_t>(want, (size_t)c.dev->sm_count * (size_t)occ);
+            k_map_pipe<T, NIN, F><<<g, kThreads, 0, c.stream>>>(out, i0, i1, i2, i3, n, f);
+            count_launch();
+            return finish(c);
+        }
     }
     if (vec) {
         // f32 arrays that one full grid covers with a vector or so per thread

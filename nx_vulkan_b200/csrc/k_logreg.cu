@@ -48,6 +48,39 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch with programmatic stream serialization: the kernel's CTAs may start
+// while the previous kernel on the stream finishes; each kernel here calls
+// griddep_wait() before it touches memory the previous one writes or reads,
+// and griddep_launch() only after that wait.  NXV_LR_PDL=0 launches plainly.
+bool lr_pdl() {
+    const char* e = getenv("NXV_LR_PDL");
+    return !(e && e[0] == '0');
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(Ctx& c, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+               const char* what, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = lr_pdl() ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    count_launch();
+    return OK;
+}
+
 // D += A(16x4) . B(4x8), f64.  A register r: (row g + 8r, col tig);
 // B: (row tig, col g); D registers: (g, 2tig), (g, 2tig+1), (g+8, 2tig),
 // (g+8, 2tig+1), with g = lane / 4, tig = lane % 4.
@@ -98,15 +131,42 @@ template <int DT, int NW_, int BN_> struct LrCfg {
 // k in [0, DP).  qa: this lane's A element (row g, col tig); xb: this lane's B
 // element (tile row g, col tig).  FULL: all NZ observation groups hold data
 // (no per-MMA guard); otherwise only the first ntz.
-template <int NZ, int DP, int DS, bool FULL>
+// D += A(16x8) . B(8x8), f64: A registers (row g, col tig), (g + 8, tig),
+// (g, tig + 4), (g + 8, tig + 4); B registers (row tig, col g), (tig + 4, g).
+__device__ __forceinline__ void dmma8(double (&d)[4], double a0, double a1, double a2, double a3,
+                                      double b0, double b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+        : "d"(a0), "d"(a1), "d"(a2), "d"(a3), "d"(b0), "d"(b1));
+}
+
+// Z uses the k = 8 shape when MK8: a warp's Z block has only NZ (2) chains
+// of dependent MMAs, so it is bound by their latency, and the k = 8 shape
+// halves the length of each chain (DP is a multiple of 8).
+template <int NZ, int DP, int DS, bool FULL, bool MK8>
 __device__ __forceinline__ void z_block(double (&z)[NZ][4], const double* qa, const double* xb,
                                         unsigned ntz) {
+    if constexpr (MK8) {
+        static_assert(DP % 8 == 0, "k8 steps");
 #pragma unroll
-    for (int kk = 0; kk < DP; kk += 4) {
-        const double a0 = qa[kk], a1 = qa[kk + 8 * DS];
+        for (int kk = 0; kk < DP; kk += 8) {
+            const double a0 = qa[kk], a1 = qa[kk + 8 * DS], a2 = qa[kk + 4],
+                         a3 = qa[kk + 4 + 8 * DS];
 #pragma unroll
-        for (int n = 0; n < NZ; n++)
-            if (FULL || n < (int)ntz) dmma4(z[n], a0, a1, xb[n * 8 * DS + kk]);
+            for (int n = 0; n < NZ; n++)
+                if (FULL || n < (int)ntz)
+                    dmma8(z[n], a0, a1, a2, a3, xb[n * 8 * DS + kk], xb[n * 8 * DS + kk + 4]);
+        }
+    } else {
+#pragma unroll
+        for (int kk = 0; kk < DP; kk += 4) {
+            const double a0 = qa[kk], a1 = qa[kk + 8 * DS];
+#pragma unroll
+            for (int n = 0; n < NZ; n++)
+                if (FULL || n < (int)ntz) dmma4(z[n], a0, a1, xb[n * 8 * DS + kk]);
+        }
     }
 }
 
@@ -134,7 +194,7 @@ __device__ __forceinline__ void g_block(double (&gacc)[DT][4], const double* rw,
 // wh = w / NW, taking observation tiles [wh NZW, wh NZW + NZW) of Z and
 // model-dimension tiles [wh DTW, ...) of G; with SPLIT = 2 a named barrier
 // per block orders the two warps' R writes before either reads R.
-template <int DT, int NW, int BN_, int SPLIT>
+template <int DT, int NW, int BN_, int SPLIT, bool MK8>
 __global__ void __launch_bounds__(32 * NW * SPLIT, SPLIT == 1 ? 8 / NW : 1)
 k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
           const double* __restrict__ y, double* __restrict__ part, double* __restrict__ lpart,
@@ -164,6 +224,11 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
     // Both X buffers start as zeros: the padded columns [D, DP) stay zero and
     // rows past a partial tile hold finite values (R is zero there).
     for (int i = tid; i < 2 * BN * DS; i += NT) Xs[i] = 0.0;
+    // Launched with programmatic dependent launch after the previous step's
+    // fold: everything above overlaps its tail; q (written by the fold) is
+    // read, and part (read by the fold) written, only after this wait.
+    griddep_wait();
+    griddep_launch();
     // Q block: zeros outside [c0, C) x [0, D); the rest by cp.async (with the
     // first X tile) when rows are 16-byte aligned, else by plain loads.
     const bool vq = (D & 1) == 0;
@@ -239,9 +304,9 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
             for (int e = 0; e < 4; e++) z[n][e] = 0.0;
         const int ntzw = min(max((int)ntz - zoff, 0), NZW);
         if (ntzw == NZW)
-            z_block<NZW, DP, DS, true>(z, qa, xb + (zoff * 8 + g) * DS + tig, ntzw);
+            z_block<NZW, DP, DS, true, MK8>(z, qa, xb + (zoff * 8 + g) * DS + tig, ntzw);
         else
-            z_block<NZW, DP, DS, false>(z, qa, xb + (zoff * 8 + g) * DS + tig, ntzw);
+            z_block<NZW, DP, DS, false, MK8>(z, qa, xb + (zoff * 8 + g) * DS + tig, ntzw);
 
         // R = y - sigmoid(Z) into this warp's rows of Rs (zero past the slice),
         // with e = exp(-|z|), den = 1 + e in [1, 2], sigmoid(z) = (z >= 0 ? 1 : e)
@@ -260,7 +325,7 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
                 for (int e = 0; e < 2; e++) {
                     const int i = 2 * n + e;
                     const bool ok = (unsigned)((zoff + n) * 8 + 2 * tig + e) < valid;
-                    ev[i] = ok ? exp(-fabs(z[n][2 * h + e])) : 0.0;
+                    ev[i] = ok ? lean::exp(-fabs(z[n][2 * h + e])) : 0.0;
                     dn[i] = add_(1.0, ev[i]);
                 }
             pf[0] = dn[0];
@@ -406,7 +471,7 @@ k_lr_resid(double* __restrict__ Z, const double* __restrict__ y, size_t n_obs, d
 
 // ---- fold + leapfrog update ----------------------------------------------------------
 
-constexpr int kFT = 512;  // fold threads per chain
+constexpr int kFT = 1024;  // fold threads per chain (10 slice groups of a 100-dim chain)
 
 // In-order sum of a[t * stride] for t in [t0, t1), t1 > t0, with 8 loads in
 // flight (the partials come from L2; a dependent chain of loads would leave
@@ -433,12 +498,16 @@ __device__ __forceinline__ double sum_rows(const double* __restrict__ a, size_t 
 // written to the trajectories and logp[c][k] = sum lpart - 0.5 |q|^2.  With
 // drift: the next step's half-kick and drift, p_h = p + he*g;
 // q = q + eps*p_h; p = p_h  (inverse mass 1).
-__global__ void __launch_bounds__(kFT)
+__global__ void __launch_bounds__(kFT, 2)
 k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __restrict__ q,
           double* __restrict__ p, const double* __restrict__ lpart, unsigned nblk, size_t D,
           double eps, double he, int write_step, int drift, unsigned k, unsigned K, double* qc,
           double* pc, double* gc, double* logp) {
     extern __shared__ double fold_sm[];  // [H][D] group sums when H > 1
+    // programmatic dependent launch: the partials of the gradient kernel
+    // just before are read only after it has completed
+    griddep_wait();
+    griddep_launch();
     const unsigned c = blockIdx.x;
     const double* pc0 = part + (size_t)c * D;
     if (H > 1) {
@@ -484,28 +553,54 @@ k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __re
     for (int off = 16; off > 0; off >>= 1) qq = add_(qq, __shfl_down_sync(0xffffffffu, qq, off));
     if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = qq;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        double sq = sm[0];
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++) sq = add_(sq, sm[w]);
-        const double l = sum_rows(lpart + (size_t)c * nblk, 1, 0, (int)nblk);
-        logp[(size_t)c * K + k] = sub_(l, mul_(0.5, sq));
+    if (threadIdx.x < 32) {
+        // the chain's logp partials: lane j sums partials j, j + 32, ... (a
+        // few loads in flight per lane instead of one thread's dependent
+        // chain), then a fixed shuffle tree; the order is the same on every
+        // call, so the result is deterministic
+        const unsigned lane = threadIdx.x;
+        const double* lp = lpart + (size_t)c * nblk;
+        double l = 0.0;
+        for (unsigned j = lane; j < nblk; j += 32) l = add_(l, lp[j]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) l = add_(l, __shfl_down_sync(0xffffffffu, l, off));
+        if (lane == 0) {
+            double sq = sm[0];
+            for (int w = 1; w < (int)(blockDim.x >> 5); w++) sq = add_(sq, sm[w]);
+            logp[(size_t)c * K + k] = sub_(l, mul_(0.5, sq));
+        }
     }
+}
+
+// NXV_LR_MK=4 keeps Z on the k = 4 MMA shape (default k = 8).
+bool lr_mk8() {
+    const char* e = getenv("NXV_LR_MK");
+    return !(e && atoi(e) == 4);
+}
+
+template <int DT, int NW, int BN, int SPLIT, bool MK8>
+int launch_lr_grad_mk(Ctx& c, const double* q, const double* X, const double* y, double* part,
+                      double* lpart, unsigned C, unsigned D, unsigned n_obs, unsigned L,
+                      unsigned S, int vecX) {
+    using G = LrCfg<DT, NW, BN>;
+    const size_t smem = G::BYTES;
+    cudaError_t e = cudaFuncSetAttribute(k_lr_grad<DT, NW, BN, SPLIT, MK8>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_lr_grad)");
+    dim3 grid(S, (C + G::BC - 1) / G::BC);
+    return launch_pdl(c, k_lr_grad<DT, NW, BN, SPLIT, MK8>, grid, dim3(G::NT * SPLIT), smem,
+                      "k_lr_grad", q, X, y, part, lpart, C, D, n_obs, L, S, vecX);
 }
 
 template <int DT, int NW, int BN, int SPLIT>
 int launch_lr_grad(Ctx& c, const double* q, const double* X, const double* y, double* part,
                    double* lpart, unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S,
                    int vecX) {
-    using G = LrCfg<DT, NW, BN>;
-    const size_t smem = G::BYTES;
-    cudaError_t e = cudaFuncSetAttribute(k_lr_grad<DT, NW, BN, SPLIT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_lr_grad)");
-    dim3 grid(S, (C + G::BC - 1) / G::BC);
-    k_lr_grad<DT, NW, BN, SPLIT><<<grid, G::NT * SPLIT, smem, c.stream>>>(
-        q, X, y, part, lpart, C, D, n_obs, L, S, vecX);
-    count_launch();
-    return OK;
+    if (lr_mk8())
+        return launch_lr_grad_mk<DT, NW, BN, SPLIT, true>(c, q, X, y, part, lpart, C, D, n_obs,
+                                                          L, S, vecX);
+    return launch_lr_grad_mk<DT, NW, BN, SPLIT, false>(c, q, X, y, part, lpart, C, D, n_obs, L,
+                                                       S, vecX);
 }
 
 }  // namespace
@@ -615,19 +710,19 @@ int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, co
     const int H = (D <= (size_t)kFT / 2) ? (int)std::min<size_t>(S, kFT / D) : 1;
     const size_t fold_smem = H > 1 ? (size_t)H * D * 8 : 0;
     auto fold = [&](int write_step, int drift, unsigned k) {
-        k_lr_fold<<<(unsigned)C, kFT, fold_smem, c.stream>>>(
-            part, (int)S, H, CD, q, p, lp, nblk, D, eps, he, write_step, drift, k, K, (double*)qc,
-            (double*)pc, (double*)gc, (double*)logp);
-        count_launch();
+        return launch_pdl(c, k_lr_fold, dim3((unsigned)C), dim3(kFT), fold_smem, "k_lr_fold",
+                          (const double*)part, (int)S, H, CD, q, p, (const double*)lp, nblk, D,
+                          eps, he, write_step, drift, k, K, (double*)qc, (double*)pc,
+                          (double*)gc, (double*)logp);
     };
     // gradient at q0, then step 0's half-kick and drift
     int rc = grad();
     if (rc) return rc;
-    fold(0, 1, 0);
+    if ((rc = fold(0, 1, 0))) return rc;
     for (unsigned k = 0; k < K; k++) {
         rc = grad();
         if (rc) return rc;
-        fold(1, k + 1 < K, k);
+        if ((rc = fold(1, k + 1 < K, k))) return rc;
     }
     return finish(c);
 }

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "lean_math.cuh"
+
 namespace nxv {
 
 __device__ __forceinline__ float add_(float a, float b) { return __fadd_rn(a, b); }
@@ -74,17 +76,32 @@ __device__ __forceinline__ T bin_op(T a, T b, unsigned op) {
 // expm1/pow agree with the CPU oracle bit for bit except where the two
 // libraries' f64 results straddle an f32 rounding boundary.  EXACT = false
 // uses the f32 library functions (2-4 ulp) for throughput.
+//
+// In the exact mode exp, sigmoid, tanh and expm1 are evaluated with the
+// table-driven f64 functions (lean_math.cuh) and rounded once; the library
+// f64 function is taken instead only where the lean value lies near an f32
+// rounding boundary, so the result is the one the library path gives.
 template <bool EXACT>
 __device__ __forceinline__ float tr_f32(float x, unsigned op) {
     if constexpr (EXACT) {
         double d = (double)x;
+        bool ok;
+        float r;
         switch (op) {
-            case 0: return (float)exp(d);
+            case 0:
+                r = lean::round_f32_checked(lean::exp(d), ok);
+                return ok ? r : (float)exp(d);
             case 1: return (float)log(d);
-            case 5: return (float)(1.0 / (1.0 + exp(-d)));
-            case 6: return (float)tanh(d);
+            case 5:
+                r = lean::round_f32_checked(__ddiv_rn(1.0, __dadd_rn(1.0, lean::exp(-d))), ok);
+                return ok ? r : (float)(1.0 / (1.0 + exp(-d)));
+            case 6:
+                r = lean::round_f32_checked(lean::tanh(d), ok);
+                return ok ? r : (float)tanh(d);
             case 13: return (float)erf(d);
-            default: return (float)expm1(d);
+            default:
+                r = lean::round_f32_checked(lean::expm1(d), ok);
+                return ok ? r : (float)expm1(d);
         }
     } else {
         switch (op) {
@@ -110,13 +127,15 @@ __device__ __forceinline__ T un_op(T x, unsigned op) {
             if constexpr (sizeof(T) == 4) {
                 return tr_f32<EXACT>(x, op);
             } else {
+                // exp, sigmoid, tanh, expm1: the table-driven f64 functions
+                // (a few ulp; lean_math.cuh)
                 switch (op) {
-                    case 0: return exp(x);
+                    case 0: return lean::exp(x);
                     case 1: return log(x);
-                    case 5: return div_(T(1), add_(T(1), exp(-x)));
-                    case 6: return tanh(x);
+                    case 5: return div_(T(1), add_(T(1), lean::exp(-x)));
+                    case 6: return lean::tanh(x);
                     case 13: return erf(x);
-                    default: return expm1(x);
+                    default: return lean::expm1(x);
                 }
             }
         case 2: return sqrt_(x);

@@ -63,6 +63,8 @@ def gather_diagnostics(local, group=None):
     import torch
     import torch.distributed as dist
 
+    if not dist.is_initialized():  # a single process: nothing to exchange
+        return local
     world = dist.get_world_size(group)
     n = torch.tensor([local.numel()], dtype=torch.int64, device=local.device)
     sizes = [torch.zeros_like(n) for _ in range(world)]
@@ -140,6 +142,8 @@ def fold_partials(local: float, op: int, group=None, device=None) -> float:
     import torch
     import torch.distributed as dist
 
+    if not dist.is_initialized():
+        return fold_in_rank_order([local], op)
     world = dist.get_world_size(group)
     t = torch.tensor([float(local)], dtype=torch.float64, device=device)
     out = torch.empty(world, dtype=torch.float64, device=device)
@@ -160,7 +164,7 @@ def _coll_device():
     import torch
     import torch.distributed as dist
 
-    if dist.get_backend() == "nccl":
+    if not dist.is_initialized() or dist.get_backend() == "nccl":
         return torch.device("cuda", torch.cuda.current_device())
     return torch.device("cpu")
 
@@ -217,7 +221,7 @@ def _finish_rank(nxv, local, what):
         ok = nxv.synchronize()
         if ok != "ok":
             raise RuntimeError(f"{what} failed on this rank: {ok}")
-    if dist.get_backend() != "nccl" and local.is_cuda:
+    if dist.is_initialized() and dist.get_backend() != "nccl" and local.is_cuda:
         return local.cpu()
     return local
 
