@@ -194,26 +194,26 @@ __device__ __forceinline__ void g_block(double (&gacc)[DT][4], const double* rw,
 // wh = w / NW, taking observation tiles [wh NZW, wh NZW + NZW) of Z and
 // model-dimension tiles [wh DTW, ...) of G; with SPLIT = 2 a named barrier
 // per block orders the two warps' R writes before either reads R.
-template <int DT, int NW, int BN_, int SPLIT, bool MK8>
-__global__ void __launch_bounds__(32 * NW * SPLIT, SPLIT == 1 ? 8 / NW : 1)
-k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
-          const double* __restrict__ y, double* __restrict__ part, double* __restrict__ lpart,
-          unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S, int vecX) {
+// The gradient of slice s, chain block cb (one CTA); PDL: the kernel was
+// launched with programmatic dependent launch (wait before touching q/part).
+template <int DT, int NW, int BN_, int SPLIT, bool MK8, bool PDL>
+__device__ __forceinline__ void lr_grad_body(
+    const double* __restrict__ q, const double* __restrict__ X, const double* __restrict__ y,
+    double* __restrict__ part, double* __restrict__ lpart, unsigned C, unsigned D, unsigned n_obs,
+    unsigned L, unsigned S, int vecX, unsigned s, unsigned cb, double* lr_smem) {
     using G = LrCfg<DT, NW, BN_>;
     constexpr int BN = G::BN, DS = G::DS, RS = G::RS, DP = G::DP, NT = G::NT * SPLIT;
     constexpr int NZ = BN / 8;              // 8-observation tiles of Z per chain block
     constexpr int NZW = NZ / SPLIT;         // ... per warp
     constexpr int DTW = (DT + SPLIT - 1) / SPLIT;  // 8-wide tiles of G per warp
     static_assert(NZ % SPLIT == 0, "SPLIT must divide the Z tiles");
-    extern __shared__ __align__(16) double lr_smem[];
     double* Qs = lr_smem + G::Q_OFF;
     double* Xs = lr_smem + G::X_OFF;
     double* Rs = lr_smem + G::R_OFF;
     double* Ys = lr_smem + G::Y_OFF;
-    const unsigned s = blockIdx.x;
-    const unsigned c0 = blockIdx.y * G::BC;
+    const unsigned c0 = cb * G::BC;
     const unsigned j0 = s * L;
-    const unsigned j1 = min(n_obs, j0 + L);
+    const unsigned j1 = max(j0, min(n_obs, j0 + L));  // empty past the last observation
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
     const int pr = warp % NW, wh = warp / NW;    // chain block, part
@@ -227,8 +227,10 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
     // Launched with programmatic dependent launch after the previous step's
     // fold: everything above overlaps its tail; q (written by the fold) is
     // read, and part (read by the fold) written, only after this wait.
-    griddep_wait();
-    griddep_launch();
+    if constexpr (PDL) {
+        griddep_wait();
+        griddep_launch();
+    }
     // Q block: zeros outside [c0, C) x [0, D); the rest by cp.async (with the
     // first X tile) when rows are 16-byte aligned, else by plain loads.
     const bool vq = (D & 1) == 0;
@@ -434,6 +436,16 @@ k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
     }
 }
 
+template <int DT, int NW, int BN_, int SPLIT, bool MK8>
+__global__ void __launch_bounds__(32 * NW * SPLIT, SPLIT == 1 ? 8 / NW : 1)
+k_lr_grad(const double* __restrict__ q, const double* __restrict__ X,
+          const double* __restrict__ y, double* __restrict__ part, double* __restrict__ lpart,
+          unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S, int vecX) {
+    extern __shared__ __align__(16) double lr_smem[];
+    lr_grad_body<DT, NW, BN_, SPLIT, MK8, true>(q, X, y, part, lpart, C, D, n_obs, L, S, vecX,
+                                                blockIdx.x, blockIdx.y, lr_smem);
+}
+
 // ---- general path: residual over Z from the GEMM -------------------------------------
 
 constexpr int kRT = 256;  // residual kernel threads
@@ -476,18 +488,27 @@ constexpr int kFT = 1024;  // fold threads per chain (10 slice groups of a 100-d
 // In-order sum of a[t * stride] for t in [t0, t1), t1 > t0, with 8 loads in
 // flight (the partials come from L2; a dependent chain of loads would leave
 // the fold latency-bound).
+// COH: the data were written earlier in the same (persistent) kernel by other
+// CTAs: load through L2 (ld.global.cg), never from a non-coherent cache.
+template <bool COH>
+__device__ __forceinline__ double ld_part(const double* p) {
+    if constexpr (COH) return __ldcg(p);
+    else return *p;
+}
+
+template <bool COH = false>
 __device__ __forceinline__ double sum_rows(const double* __restrict__ a, size_t stride, int t0,
                                            int t1) {
-    double s = a[(size_t)t0 * stride];
+    double s = ld_part<COH>(a + (size_t)t0 * stride);
     int t = t0 + 1;
     for (; t + 8 <= t1; t += 8) {
         double v[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++) v[u] = a[(size_t)(t + u) * stride];
+        for (int u = 0; u < 8; u++) v[u] = ld_part<COH>(a + (size_t)(t + u) * stride);
 #pragma unroll
         for (int u = 0; u < 8; u++) s = add_(s, v[u]);
     }
-    for (; t < t1; t++) s = add_(s, a[(size_t)t * stride]);
+    for (; t < t1; t++) s = add_(s, ld_part<COH>(a + (size_t)t * stride));
     return s;
 }
 
@@ -498,24 +519,22 @@ __device__ __forceinline__ double sum_rows(const double* __restrict__ a, size_t 
 // written to the trajectories and logp[c][k] = sum lpart - 0.5 |q|^2.  With
 // drift: the next step's half-kick and drift, p_h = p + he*g;
 // q = q + eps*p_h; p = p_h  (inverse mass 1).
-__global__ void __launch_bounds__(kFT, 2)
-k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __restrict__ q,
-          double* __restrict__ p, const double* __restrict__ lpart, unsigned nblk, size_t D,
-          double eps, double he, int write_step, int drift, unsigned k, unsigned K, double* qc,
-          double* pc, double* gc, double* logp) {
-    extern __shared__ double fold_sm[];  // [H][D] group sums when H > 1
-    // programmatic dependent launch: the partials of the gradient kernel
-    // just before are read only after it has completed
-    griddep_wait();
-    griddep_launch();
-    const unsigned c = blockIdx.x;
+// fold_sm: [H][D] doubles; sm: one double per warp of the CTA.  Every thread
+// of the CTA calls it (H * D <= blockDim.x).
+template <bool COH>
+__device__ __forceinline__ void lr_fold_chain(
+    unsigned c, const double* __restrict__ part, int S, int H, size_t CD, double* __restrict__ q,
+    double* __restrict__ p, const double* __restrict__ lpart, unsigned nblk, size_t D, double eps,
+    double he, int write_step, int drift, unsigned k, unsigned K, double* qc, double* pc,
+    double* gc, double* logp, double* fold_sm, double* sm) {
+    __syncthreads();  // fold_sm and sm may still be read for the previous chain
     const double* pc0 = part + (size_t)c * D;
     if (H > 1) {
         const unsigned tid = threadIdx.x;
         if (tid < (unsigned)H * D) {
             const unsigned h = tid / (unsigned)D, i = tid - h * (unsigned)D;
             const int t0 = (int)((size_t)h * S / H), t1 = (int)((size_t)(h + 1) * S / H);
-            fold_sm[tid] = sum_rows(pc0 + i, CD, t0, t1);
+            fold_sm[tid] = sum_rows<COH>(pc0 + i, CD, t0, t1);
         }
         __syncthreads();
     }
@@ -527,7 +546,7 @@ k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __re
             s = fold_sm[i];
             for (int h = 1; h < H; h++) s = add_(s, fold_sm[(size_t)h * D + i]);
         } else {
-            s = sum_rows(pc0 + i, CD, 0, S);
+            s = sum_rows<COH>(pc0 + i, CD, 0, S);
         }
         double qi = q[o];
         double gi = sub_(s, qi);
@@ -548,7 +567,6 @@ k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __re
         p[o] = pi;
     }
     if (!write_step) return;
-    __shared__ double sm[kFT / 32];
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) qq = add_(qq, __shfl_down_sync(0xffffffffu, qq, off));
     if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = qq;
@@ -561,7 +579,7 @@ k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __re
         const unsigned lane = threadIdx.x;
         const double* lp = lpart + (size_t)c * nblk;
         double l = 0.0;
-        for (unsigned j = lane; j < nblk; j += 32) l = add_(l, lp[j]);
+        for (unsigned j = lane; j < nblk; j += 32) l = add_(l, ld_part<COH>(lp + j));
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) l = add_(l, __shfl_down_sync(0xffffffffu, l, off));
         if (lane == 0) {
@@ -570,6 +588,21 @@ k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __re
             logp[(size_t)c * K + k] = sub_(l, mul_(0.5, sq));
         }
     }
+}
+
+__global__ void __launch_bounds__(kFT, 2)
+k_lr_fold(const double* __restrict__ part, int S, int H, size_t CD, double* __restrict__ q,
+          double* __restrict__ p, const double* __restrict__ lpart, unsigned nblk, size_t D,
+          double eps, double he, int write_step, int drift, unsigned k, unsigned K, double* qc,
+          double* pc, double* gc, double* logp) {
+    extern __shared__ double fold_sm[];  // [H][D] group sums when H > 1
+    __shared__ double sm[kFT / 32];
+    // programmatic dependent launch: the partials of the gradient kernel
+    // just before are read only after it has completed
+    griddep_wait();
+    griddep_launch();
+    lr_fold_chain<false>(blockIdx.x, part, S, H, CD, q, p, lpart, nblk, D, eps, he, write_step,
+                         drift, k, K, qc, pc, gc, logp, fold_sm, sm);
 }
 
 // NXV_LR_MK=4 keeps Z on the k = 4 MMA shape (default k = 8).
@@ -603,7 +636,157 @@ int launch_lr_grad(Ctx& c, const double* q, const double* X, const double* y, do
                                                        S, vecX);
 }
 
+// ---- persistent trajectory kernel -------------------------------------------------
+//
+// One cooperative launch per chain call: CTA (s, cb) computes its slice's
+// gradient partials, all CTAs meet at a grid barrier, every CTA folds a
+// share of the chains (chain c by CTA c mod the grid: slice sums in slice
+// order, kick, drift, trajectory rows, logp), and a second barrier makes the
+// new positions visible before the next gradient.  This replaces two
+// launches per leapfrog step (the gradient kernel's 148 CTAs of 203 KB and
+// the fold's) with two barriers.  Cooperative launch keeps every CTA
+// resident, so a barrier cannot wait on a CTA that never runs; each wait is
+// still bounded (about a second): on timeout the kernel records g_lr_error,
+// leaves no copy in flight and returns.
+
+__device__ int g_lr_error;  // 1 when a grid barrier's bounded wait ran out
+
+// bar[0]: arrivals of the current barrier, bar[1]: generation.  Returns
+// false (on every thread of the CTA) when the wait ran out here or another
+// CTA reported a timeout.
+__device__ __forceinline__ bool lr_grid_barrier(unsigned* bar, unsigned nctas) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        volatile unsigned* vgen = bar + 1;
+        const unsigned gen = *vgen;
+        __threadfence();
+        if (atomicAdd(bar, 1u) == nctas - 1) {
+            atomicExch(bar, 0u);
+            __threadfence();
+            atomicAdd(bar + 1, 1u);
+        } else {
+            for (unsigned i = 0; *vgen == gen; i++) {
+                if (i > (1u << 22)) {
+                    ok = 0;
+                    atomicExch(&g_lr_error, 1);
+                    break;
+                }
+                if (i > 64) __nanosleep(256);
+            }
+        }
+        __threadfence();
+        s_ok = ok && *(volatile int*)&g_lr_error == 0;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+template <int DT, int NW, int BN_, int SPLIT, bool MK8>
+__global__ void __launch_bounds__(32 * NW * SPLIT, 1)
+k_lr_traj(const double* __restrict__ X, const double* __restrict__ y, double* __restrict__ q,
+          double* __restrict__ p, double* __restrict__ part, double* __restrict__ lpart,
+          unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S, int vecX, int H,
+          double eps, double he, unsigned K, double* qc, double* pc, double* gc, double* logp,
+          unsigned* bar) {
+    extern __shared__ __align__(16) double lr_smem[];
+    __shared__ double sm_red[NW * SPLIT];
+    const unsigned nctas = gridDim.x * gridDim.y;
+    const unsigned cta = blockIdx.y * gridDim.x + blockIdx.x;
+    const size_t CD = (size_t)C * D;
+    for (unsigned it = 0; it <= K; it++) {
+        lr_grad_body<DT, NW, BN_, SPLIT, MK8, false>(q, X, y, part, lpart, C, D, n_obs, L, S,
+                                                     vecX, blockIdx.x, blockIdx.y, lr_smem);
+        if (!lr_grid_barrier(bar, nctas)) return;
+        // it = 0: the gradient at q0, then step 0's half-kick and drift;
+        // it = k + 1: step k's final half-kick and rows, then step k+1's drift
+        for (unsigned c = cta; c < C; c += nctas)
+            lr_fold_chain<true>(c, part, (int)S, H, CD, q, p, lpart, S, D, eps, he, it > 0 ? 1 : 0,
+                          it < K ? 1 : 0, it > 0 ? it - 1 : 0, K, qc, pc, gc, logp, lr_smem,
+                          sm_red);
+        if (it < K && !lr_grid_barrier(bar, nctas)) return;
+    }
+}
+
+// NXV_LR_PERSIST=1 selects the persistent kernel.  It is off by default:
+// measured on B200 for 256 chains x X[10000, 100], L = 16, one trajectory
+// takes 1.140 ms persistent against 0.985 ms with two launches per step on
+// programmatic dependent launch -- the fold with one 512-thread CTA per SM
+// (2 chains on most CTAs) and the two barriers cost more than the launches
+// they replace, which the dependent launch already overlaps.
+bool lr_persist() {
+    const char* e = getenv("NXV_LR_PERSIST");
+    return e && e[0] == '1';
+}
+
+// Launches k_lr_traj when the grid fits the GPU at once (cooperative
+// launch); E_KERNEL when it does not (the caller takes the per-step
+// launches).
+template <int DT, int NW, int BN, int SPLIT, bool MK8>
+int launch_lr_traj_mk(Ctx& c, const double* X, const double* y, double* q, double* p,
+                      double* part, double* lpart, unsigned C, unsigned D, unsigned n_obs,
+                      unsigned L, unsigned S, int vecX, int H, double eps, double he, unsigned K,
+                      double* qc, double* pc, double* gc, double* logp, unsigned* bar) {
+    using G = LrCfg<DT, NW, BN>;
+    const size_t smem = G::BYTES;
+    auto kern = k_lr_traj<DT, NW, BN, SPLIT, MK8>;
+    if ((size_t)H * D > (size_t)G::NT * SPLIT || (size_t)H * D * 8 > smem) return E_KERNEL;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_lr_traj)");
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, G::NT * SPLIT, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    const dim3 grid(S, (C + G::BC - 1) / G::BC);
+    if ((size_t)grid.x * grid.y > (size_t)per_sm * c.dev->sm_count) return E_KERNEL;
+    NXV_CK(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned), c.stream));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(G::NT * SPLIT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, X, y, q, p, part, lpart, C, D, n_obs, L, S, vecX, H, eps,
+                           he, K, qc, pc, gc, logp, bar);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(k_lr_traj)");
+    count_launch();
+    return OK;
+}
+
+template <int DT, int NW, int BN, int SPLIT>
+int launch_lr_traj(Ctx& c, const double* X, const double* y, double* q, double* p, double* part,
+                   double* lpart, unsigned C, unsigned D, unsigned n_obs, unsigned L, unsigned S,
+                   int vecX, int H, double eps, double he, unsigned K, double* qc, double* pc,
+                   double* gc, double* logp, unsigned* bar) {
+    if (lr_mk8())
+        return launch_lr_traj_mk<DT, NW, BN, SPLIT, true>(c, X, y, q, p, part, lpart, C, D, n_obs,
+                                                          L, S, vecX, H, eps, he, K, qc, pc, gc,
+                                                          logp, bar);
+    return launch_lr_traj_mk<DT, NW, BN, SPLIT, false>(c, X, y, q, p, part, lpart, C, D, n_obs, L,
+                                                       S, vecX, H, eps, he, K, qc, pc, gc, logp,
+                                                       bar);
+}
+
+
 }  // namespace
+
+int lr_traj_error() {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_lr_error, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (v) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_lr_error, &z, sizeof(int));
+    }
+    return v;
+}
 
 int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                             const void* p0, const void* X, const void* y, size_t n_obs,
@@ -646,6 +829,7 @@ int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, co
         return o;
     };
     size_t oq = take(CD * 8), op = take(CD * 8), oL = take(C * nblk * 8), oP = take(S * CD * 8);
+    size_t oB = take(2 * sizeof(unsigned));  // grid-barrier state of the persistent kernel
     size_t oXt = fused ? 0 : take(D * n_obs * 8), oZ = fused ? 0 : take(C * n_obs * 8);
     ScratchGuard guard(c);
     char* base = (char*)scratch(c, off);
@@ -715,6 +899,45 @@ int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, co
                           eps, he, write_step, drift, k, K, (double*)qc, (double*)pc,
                           (double*)gc, (double*)logp);
     };
+    if (fused && lr_persist() && D % 2 == 0) {
+        // (even D: the gradient loads its Q block by cp.async.cg, through L2,
+        // which sees the positions the previous fold wrote in the same kernel)
+        // one cooperative launch for the whole trajectory when the grid fits
+        const int vecX = (D % 2 == 0) && ((uintptr_t)X % 16 == 0);
+        const char* sv = getenv("NXV_LR_SPLIT");
+        const int split = (sv && atoi(sv) == 1) ? 1 : 2;
+        const unsigned Cu = (unsigned)C, Du = (unsigned)D, Nu = (unsigned)n_obs,
+                       Lu = (unsigned)L, Su = (unsigned)S;
+        const int Hp = (int)std::max<size_t>(1, std::min<size_t>(S, (size_t)(256 * split) / D));
+        const double* Xd = (const double*)X;
+        const double* yd = (const double*)y;
+        unsigned* bar = (unsigned*)(base + oB);
+        double *qcd = (double*)qc, *pcd = (double*)pc, *gcd = (double*)gc, *lgd = (double*)logp;
+        int rc;
+        if (split == 2) {
+            if (D <= 32)
+                rc = launch_lr_traj<4, 8, 32, 2>(c, Xd, yd, q, p, part, lp, Cu, Du, Nu, Lu, Su, vecX,
+                                                 Hp, eps, he, K, qcd, pcd, gcd, lgd, bar);
+            else if (D <= 64)
+                rc = launch_lr_traj<8, 8, 32, 2>(c, Xd, yd, q, p, part, lp, Cu, Du, Nu, Lu, Su, vecX,
+                                                 Hp, eps, he, K, qcd, pcd, gcd, lgd, bar);
+            else
+                rc = launch_lr_traj<13, 8, 32, 2>(c, Xd, yd, q, p, part, lp, Cu, Du, Nu, Lu, Su,
+                                                  vecX, Hp, eps, he, K, qcd, pcd, gcd, lgd, bar);
+        } else {
+            if (D <= 32)
+                rc = launch_lr_traj<4, 8, 32, 1>(c, Xd, yd, q, p, part, lp, Cu, Du, Nu, Lu, Su, vecX,
+                                                 Hp, eps, he, K, qcd, pcd, gcd, lgd, bar);
+            else if (D <= 64)
+                rc = launch_lr_traj<8, 8, 32, 1>(c, Xd, yd, q, p, part, lp, Cu, Du, Nu, Lu, Su, vecX,
+                                                 Hp, eps, he, K, qcd, pcd, gcd, lgd, bar);
+            else
+                rc = launch_lr_traj<13, 8, 32, 1>(c, Xd, yd, q, p, part, lp, Cu, Du, Nu, Lu, Su,
+                                                  vecX, Hp, eps, he, K, qcd, pcd, gcd, lgd, bar);
+        }
+        if (rc == OK) return finish(c);
+        if (rc != E_KERNEL) return rc;
+    }
     // gradient at q0, then step 0's half-kick and drift
     int rc = grad();
     if (rc) return rc;

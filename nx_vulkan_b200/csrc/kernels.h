@@ -92,6 +92,9 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
                          size_t n, size_t k);
 // Reads and clears the tensor-core GEMM's timeout flag (1 = a bounded wait ran out).
 int tc_gemm_error();
+// Reads and clears the persistent logistic kernel's flag (1 = a grid barrier's
+// bounded wait ran out).
+int lr_traj_error();
 
 // Stream-K schedule for 128 x 128 tiles (k_matmul.cu): tiles [0, dp) run
 // data-parallel; the k-tile iterations of tiles [dp, dp + tail) are cut into

@@ -738,6 +738,11 @@ int nxv_synchronize(void) {
         set_error("tensor-core GEMM: a bounded pipeline wait ran out; results are invalid");
         return E_CUDA;
     }
+    if (rc == OK && lr_traj_error()) {
+        set_error("logistic trajectory kernel: a grid barrier's bounded wait ran out; results "
+                  "are invalid");
+        return E_CUDA;
+    }
     return rc;
 }
 

@@ -233,9 +233,12 @@ def test_gauss_full_config(nxv, orc):
     (1001, 50, 33, 2), (1, 2, 1, 1), (160000, 4, 4, 1),
     # general (two-GEMM) path
     (300, 120, 4, 2)])
-@pytest.mark.parametrize("split", ["1", "2"])
-def test_logreg_vs_oracle(nxv, orc, monkeypatch, N, D, C, K, split):
+@pytest.mark.parametrize("split,persist", [("1", "0"), ("2", "0"), ("2", "1")])
+def test_logreg_vs_oracle(nxv, orc, monkeypatch, N, D, C, K, split, persist):
     monkeypatch.setenv("NXV_LR_SPLIT", split)  # warps per 16-chain block in the fused kernel
+    # 1: the whole chain call as one cooperative kernel with grid barriers
+    # (used for even D that fits one wave; the others run the per-step launches)
+    monkeypatch.setenv("NXV_LR_PERSIST", persist)
     r = np.random.default_rng(4)
     X = r.normal(size=(N, D))
     w = r.normal(size=D)
