@@ -289,6 +289,8 @@ def main():
                          "X[10000,100], L=16, eps=0.002, momenta drawn on the device); "
                          "reduce: the [4096,4096] row reductions, argmax and full sum "
                          "sharded by rows over the ranks, results all-gathered on the device")
+    ap.add_argument("--lr-chains", type=int, default=256,
+                    help="logistic workload: chains over all ranks (the workload's 256 by default)")
     ap.add_argument("--repeats", type=int, default=5,
                     help="timed regions of --steps steps each; value is their median")
     ap.add_argument("--suite", action="store_true",
@@ -680,8 +682,9 @@ def logreg_main(args, rank, world, local):
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)
     lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
-    assert LR_CHAINS % world == 0, "the 256 chains split evenly over 1, 2, 4 or 8 ranks"
-    lo, hi = rank * LR_CHAINS // world, (rank + 1) * LR_CHAINS // world
+    total = args.lr_chains
+    assert total % world == 0, "the chains split evenly over the ranks"
+    lo, hi = rank * total // world, (rank + 1) * total // world
     cr = hi - lo
     X, y = logreg_data()
     ok, tX = nxv.upload_binary(X)
@@ -690,12 +693,12 @@ def logreg_main(args, rank, world, local):
     assert ok == ok2 == ok3 == "ok"
     seed = 7
     lps = torch.empty(cr, dtype=torch.float64, device=dev)
-    gathered = torch.empty(LR_CHAINS, dtype=torch.float64, device=dev) if world > 1 else None
+    gathered = torch.empty(total, dtype=torch.float64, device=dev) if world > 1 else None
     h_lps = lib.nxv_buf_wrap(C.c_void_p(lps.data_ptr()), cr * 8)
     spv = nxv.shader_path("leapfrog_logreg_f64_batched.spv")
     # this rank's momenta: the rows [lo, hi) of the global [256][100] draw
     def momenta(t):
-        ok, p = nxv.random_f64(LR_CHAINS * LR_DIM, hmc.momentum_key(seed, t), 1)
+        ok, p = nxv.random_f64(total * LR_DIM, hmc.momentum_key(seed, t), 1)
         assert ok == "ok", _native.last_error()
         if world == 1:
             return p
@@ -740,7 +743,7 @@ def logreg_main(args, rank, world, local):
             rep_ms.append(max_over_ranks_ms(e0.elapsed_time(e1), dev, world))
     launches = (lib.nxv_launch_count() - n_launch0) // repeats
     t_ms = statistics.median(rep_ms)
-    value = LR_CHAINS * LR_STEPS * args.steps / (t_ms / 1e3)
+    value = total * LR_STEPS * args.steps / (t_ms / 1e3)
     peak = dgemm_peak_tflops(torch, dev) if rank == 0 else None
     flops = (LR_STEPS + 1) * 2 * 2 * cr * LR_DIM * LR_OBS  # per trajectory, this rank
     achieved = flops / (t_ms / args.steps / 1e3) / 1e12
@@ -752,11 +755,11 @@ def logreg_main(args, rank, world, local):
             "metric": "f64 logistic-regression leapfrog steps/s (chains×L)", "value": value,
             "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": t_ms / args.steps, "higher_is_better": True,
-            "scaling": "strong (256 chains in total)", "vs_baseline": None, "dtype": "f64",
+            "scaling": f"strong ({total} chains in total)", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic (seeded numpy: X~N(0,1) [10000,100], w*~N(0,1), y~Bernoulli, seed 4; "
                     "q0=0; momenta from the device Philox generator)",
             "config": {"workload": "Bayesian logistic-regression HMC, one trajectory per step",
-                       "chains_total": LR_CHAINS, "chains_per_gpu": cr, "n_obs": LR_OBS,
+                       "chains_total": total, "chains_per_gpu": cr, "n_obs": LR_OBS,
                        "d": LR_DIM, "L": LR_STEPS, "eps": LR_EPS,
                        "timing": f"{repeats} timed regions of {args.steps} trajectories (CUDA events "
                                  "on the launching stream, max over ranks); value is the median"},

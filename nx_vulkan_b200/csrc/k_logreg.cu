@@ -298,6 +298,10 @@ __device__ __forceinline__ void lr_grad_body(
         const unsigned valid = min((unsigned)BN, j1 - jt);
         const unsigned ntz = (valid + 7) >> 3;  // 8-observation tiles holding data
 
+        // A 16-chain block past the last chain (C below the CTA's 128) has
+        // no work: its warp pair skips the MMAs, the residual and its named
+        // barrier together and only meets the CTA barriers.
+        if (pr * 16 < (int)crows) {
         // Z block (16 chains x this warp's observation tiles) = Q . X_tile^T.
         double z[NZW][4];
 #pragma unroll
@@ -372,6 +376,7 @@ __device__ __forceinline__ void lr_grad_body(
             g_block<DTW, BN, DS, RS, true>(gacc, rw + g * RS + tig, xr, kv, ncnt);
         else
             g_block<DTW, BN, DS, RS, false>(gacc, rw + g * RS + tig, xr, kv, ncnt);
+        }  // active chain block
         __syncthreads();  // buffer t & 1 and Rs are rewritten next iteration
     }
     cp_wait<0>();
