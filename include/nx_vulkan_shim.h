@@ -399,6 +399,46 @@ int nxv_leapfrog_logreg_f64_batched(void* q_chain, void* p_chain,
                                     double eps,
                                     const char* spv_path);
 
+/* ---- NUTS tree builder on the device (NEW) ------------------------------
+ * eXMC's NUTS tree builder (an external repository; its call site is
+ * PLAN_FUSED_LEAPFROG.md:331-358) walks the leaves that the fused chain
+ * returns.  These three calls do that walk on the device, over a leaf store
+ * that the batched Gaussian chain (_ke variant) writes into, so the
+ * trajectories never leave the GPU; the caller keeps the row bookkeeping
+ * and draws the random numbers.  Store rows hold q, p (p in its
+ * integration sign: negated for backward leaves), logp and the kinetic
+ * energy; H = -logp + KE.  Arrays of chain / slot indices and directions
+ * are int32, store rows int64, the rest f64.  0 on success, -1 NULL, -3 a
+ * buffer smaller than its extent. */
+
+/* H0[c] = 0.5 sum prec (q - mu)^2 - logp_const + 0.5 sum p^2 inv_mass over
+ * [n_chains][d] q and p (the Gaussian target's Hamiltonian). */
+int nxv_nuts_energy(void* H0, void* q, void* p, void* prec, void* inv_mass,
+                    double mu, double logp_const,
+                    unsigned int n_chains, unsigned int d);
+
+/* Starting points of a speculative extension of chains chain[i] (i < n_need):
+ * store row src_row[i], or the initial point (q0[c], dir[i] * p0[c]) when
+ * src_row[i] < 0; written to qs, ps [n_need][d]. */
+int nxv_nuts_start(void* qs, void* ps, void* q0, void* p0, void* st_q, void* st_p,
+                   void* chain, void* src_row, void* dir,
+                   unsigned int n_need, unsigned int n_chains, unsigned int d);
+
+/* One tree level for n_active chains: slot a is chain chain[a], whose new
+ * subtree is the n (a power of two, <= 2048) store rows rows[a][0..n) in time
+ * order, extending the tree forward (fwd[a] = 1) or backward.  Per chain:
+ * divergence (H - H0 > 1000 or NaN), the subtree's U-turn checks, the
+ * multinomial leaf (u_sel[a]) and the biased move (u_move[a]) into `sample`,
+ * logw, the merge checks with the tree (rho, end_p / end_ps: [2][C][d], left
+ * end first), active[c] (1 while the tree grows) and divergent[c].  node:
+ * [n_active][n][d] f64 scratch. */
+int nxv_nuts_level(void* rows, void* chain, void* fwd, void* u_sel, void* u_move,
+                   unsigned int n_active, unsigned int n, unsigned int d,
+                   void* st_q, void* st_p, void* st_logp, void* st_ke, void* inv_mass,
+                   void* H0, void* logw, void* rho, void* end_p, void* end_ps,
+                   void* sample, void* active, void* divergent, void* node,
+                   unsigned int n_chains);
+
 /* ---- Devices, streams, interop (NEW) ----------------------------------- */
 
 /* Use exactly these CUDA devices (e.g. the local rank's GPU).  Calls nxv_init

@@ -72,6 +72,9 @@ SIGNATURES: dict[str, tuple] = {
     "nxv_leapfrog_chain_gauss_f64_batched_ke": (C.c_int, [vp] * 9 + [u32, u32, u32, f64, f64, cstr]),
     "nxv_leapfrog_chain_gauss_f64_batched_noalloc": (C.c_int, [vp] * 8 + [u32, u32, u32, f64, f64]),
     "nxv_leapfrog_logreg_f64_batched": (C.c_int, [vp] * 8 + [u32, u32, u32, u32, f64, cstr]),
+    "nxv_nuts_energy": (C.c_int, [vp] * 5 + [f64, f64, u32, u32]),
+    "nxv_nuts_start": (C.c_int, [vp] * 9 + [u32, u32, u32]),
+    "nxv_nuts_level": (C.c_int, [vp] * 5 + [u32, u32, u32] + [vp] * 14 + [u32]),
     "nxv_init_devices": (C.c_int, [intp, C.c_int]),
     "nxv_set_device": (C.c_int, [C.c_int]),
     "nxv_set_stream": (C.c_int, [vp]),

@@ -1,0 +1,417 @@
+// k_nuts.cu -- the NUTS tree builder's per-level logic on the device.
+//
+// eXMC's NUTS tree builder (PLAN_FUSED_LEAPFROG.md:331-358) extends every
+// chain speculatively with the fused leapfrog chain and then walks the new
+// leaves: divergence, the generalized U-turn checks of the balanced subtree
+// and of its merge with the tree so far, multinomial selection of a leaf and
+// the biased move into the subtree (Betancourt 2017, "A Conceptual
+// Introduction to Hamiltonian Monte Carlo", A.3-A.4).  These kernels do that
+// walk where the leaves are -- in a device store that the chain calls write
+// into -- so that no trajectory crosses PCIe; the host keeps only the
+// bookkeeping of which stored rows are the next leaves of each chain and
+// draws the random numbers (the same stream as the host tree builder).
+//
+// Store: q, p (p in the sign it was integrated with: negated for backward
+// leaves), logp and kinetic energy per row; H = -logp + KE.
+#include "../../include/nx_vulkan_shim.h"
+#include "kernels.h"
+#include "ops_common.cuh"
+
+#include <math.h>
+
+namespace nxv {
+namespace {
+
+constexpr int kNT = 128;          // threads per chain
+constexpr int kNW = kNT / 32;
+constexpr int kMaxLeaves = 2048;  // leaves per level: 2^(max depth - 1), max depth 12
+constexpr double kMaxDeltaH = 1000.0;
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = add_(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+__device__ __forceinline__ double warp_max(double v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+// Block sums of R values (every thread passes its R partials; all threads
+// get the totals, added in warp order).
+template <int R>
+__device__ __forceinline__ void block_sums(double (&v)[R], double (*sm)[kNW]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int r = 0; r < R; r++) v[r] = warp_sum(v[r]);
+    __syncthreads();
+    if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < R; r++) sm[r][warp] = v[r];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        double s = sm[r][0];
+        for (int w = 1; w < kNW; w++) s = add_(s, sm[r][w]);
+        v[r] = s;
+    }
+}
+
+struct LevelArgs {
+    const long long* rows;  // [A][n] store rows of the level's leaves, in time order
+    const int* chain;       // [A] chain of each active slot
+    const int* fwd;         // [A] 1: the subtree extends the tree forward in time
+    const double* u_sel;    // [A] uniform for the leaf within the subtree
+    const double* u_move;   // [A] uniform for the move into the subtree
+    int n, d;
+    const double* st_q;
+    const double* st_p;
+    const double* st_logp;
+    const double* st_ke;
+    const double* m;        // [d] inverse mass
+    const double* H0;       // [C]
+    double* logw;           // [C] log of the tree's weight
+    double* rho;            // [C][d] the tree's summed momentum
+    double* end_p;          // [2][C][d] momentum at the left (0) / right (1) end
+    double* end_ps;         // [2][C][d] velocity at the ends
+    double* sample;         // [C][d]
+    int* active;            // [C] 1 while the tree keeps growing
+    int* divergent;         // [C]
+    double* node;           // [A][n][d] scratch: summed momenta of subtree nodes
+    int C;
+};
+
+// One CTA per active chain.  Subtree U-turn check: node [a, b) of the
+// balanced subtree is the merge of [a, m) and [m, b); level by level the
+// node sums are built in `node` (node[a] holds the sum of [a, a + size)),
+// and every merge is tested as the host tree builder tests it:
+//   ps_first . rho > 0 and ps_last . rho > 0 (rho = rho_A + rho_B),
+//   (rho_A + p_B,first) against ps_A,first and ps_B,first,
+//   (rho_B + p_A,last) against ps_A,last and ps_B,last.
+__global__ void __launch_bounds__(kNT) k_nuts_level(LevelArgs a) {
+    __shared__ double h[kMaxLeaves];
+    __shared__ double cs[kMaxLeaves];
+    __shared__ double red[8][kNW];
+    __shared__ int s_ok, s_sel;
+    const int slot = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int c = a.chain[slot], n = a.n, d = a.d;
+    const bool fwd = a.fwd[slot] != 0;
+    const double sg = fwd ? 1.0 : -1.0;  // backward leaves were integrated with -p
+    const long long* rows = a.rows + (size_t)slot * n;
+    double* nd = a.node + (size_t)slot * n * d;
+    const double H0 = a.H0[c];
+
+    // H of every leaf, divergence (NaN counts as divergent)
+    int div_l = 0;
+    for (int j = tid; j < n; j += kNT) {
+        const long long r = rows[j];
+        const double hj = sub_(a.st_ke[r], a.st_logp[r]);
+        h[j] = hj;
+        if (!(sub_(hj, H0) <= kMaxDeltaH)) div_l = 1;
+    }
+    const int div = __syncthreads_or(div_l);
+
+    // leaf momenta into the node sums
+    for (int j = warp; j < n; j += kNW) {
+        const double* src = a.st_p + (size_t)rows[j] * d;
+        for (int i = lane; i < d; i += 32) nd[(size_t)j * d + i] = mul_(sg, src[i]);
+    }
+    if (tid == 0) s_ok = 1;
+    __syncthreads();
+    for (int size = 2; size <= n; size *= 2) {
+        const int half = size / 2;
+        for (int t = warp; t < n / size; t += kNW) {
+            const int a0 = t * size, mid = a0 + half, b1 = a0 + size - 1;
+            const double* pf = a.st_p + (size_t)rows[a0] * d;
+            const double* pal = a.st_p + (size_t)rows[mid - 1] * d;
+            const double* pbf = a.st_p + (size_t)rows[mid] * d;
+            const double* pl = a.st_p + (size_t)rows[b1] * d;
+            double s[6] = {0, 0, 0, 0, 0, 0};
+            for (int i = lane; i < d; i += 32) {
+                const double mi = a.m[i];
+                const double rA = nd[(size_t)a0 * d + i], rB = nd[(size_t)mid * d + i];
+                const double r = add_(rA, rB);
+                const double vf = mul_(sg, pf[i]), val = mul_(sg, pal[i]);
+                const double vbf = mul_(sg, pbf[i]), vl = mul_(sg, pl[i]);
+                const double v2 = add_(rA, vbf), v3 = add_(rB, val);
+                s[0] = add_(s[0], mul_(mul_(mi, vf), r));
+                s[1] = add_(s[1], mul_(mul_(mi, vl), r));
+                s[2] = add_(s[2], mul_(mul_(mi, vf), v2));
+                s[3] = add_(s[3], mul_(mul_(mi, vbf), v2));
+                s[4] = add_(s[4], mul_(mul_(mi, val), v3));
+                s[5] = add_(s[5], mul_(mul_(mi, vl), v3));
+                nd[(size_t)a0 * d + i] = r;
+            }
+            bool ok = true;
+#pragma unroll
+            for (int k = 0; k < 6; k++) ok = ok && warp_sum(s[k]) > 0.0;
+            if (lane == 0 && !ok) s_ok = 0;
+        }
+        __syncthreads();
+    }
+    const bool ok_sub = s_ok != 0 && !div;
+
+    // multinomial choice of a leaf: w = -H (0 for every leaf of a divergent
+    // subtree), weights exp(w - max w), chosen where the running sum first
+    // reaches u * total
+    double wmax = -INFINITY;
+    for (int j = tid; j < n; j += kNT) wmax = fmax(wmax, div ? 0.0 : -h[j]);
+    wmax = warp_max(wmax);
+    if (lane == 0) red[0][warp] = wmax;
+    __syncthreads();
+    wmax = red[0][0];
+    for (int w = 1; w < kNW; w++) wmax = fmax(wmax, red[0][w]);
+    // per-thread contiguous chunk: local prefix sums, then chunk offsets
+    const int per = (n + kNT - 1) / kNT, j0 = tid * per, j1 = min(n, j0 + per);
+    double run = 0.0;
+    for (int j = j0; j < j1; j++) {
+        run = add_(run, exp(sub_(div ? 0.0 : -h[j], wmax)));
+        cs[j] = run;
+    }
+    __shared__ double chunk[kNT];
+    chunk[tid] = run;
+    __syncthreads();
+    if (tid == 0) {
+        double acc = 0.0;
+        for (int t = 0; t < kNT; t++) {
+            const double v = chunk[t];
+            chunk[t] = acc;  // offset of chunk t
+            acc = add_(acc, v);
+        }
+        red[1][0] = acc;  // total
+        s_sel = n - 1;
+    }
+    __syncthreads();
+    const double tot = red[1][0], target = mul_(a.u_sel[slot], tot);
+    for (int j = j0; j < j1; j++) {
+        const double cdf = add_(cs[j], chunk[tid]);
+        if (!(cdf < target)) {
+            atomicMin(&s_sel, j);
+            break;
+        }
+    }
+    __syncthreads();
+    const int sel = s_sel;
+    const double logw_sub = add_(wmax, log(tot));
+    const double logw_old = a.logw[c];
+    const bool move = a.u_move[slot] < exp(fmin(0.0, sub_(logw_sub, logw_old)));
+    if (ok_sub && move) {
+        const double* src = a.st_q + (size_t)rows[sel] * d;
+        for (int i = tid; i < d; i += kNT) a.sample[(size_t)c * d + i] = src[i];
+    }
+
+    // merge with the tree so far; A is the earlier of (tree, subtree) in time
+    const double* rho_sub = nd;  // node[0]: the sum of all n leaves
+    const size_t CD = (size_t)a.C * d;
+    double* rho = a.rho + (size_t)c * d;
+    const double* lp = a.end_p + (size_t)c * d;        // tree, left end
+    const double* lps = a.end_ps + (size_t)c * d;
+    const double* rp = a.end_p + CD + (size_t)c * d;   // tree, right end
+    const double* rps = a.end_ps + CD + (size_t)c * d;
+    const double* p_first = a.st_p + (size_t)rows[0] * d;
+    const double* p_last = a.st_p + (size_t)rows[n - 1] * d;
+    double s[6] = {0, 0, 0, 0, 0, 0};
+    for (int i = tid; i < d; i += kNT) {
+        const double mi = a.m[i];
+        const double fp = mul_(sg, p_first[i]), lsp = mul_(sg, p_last[i]);
+        const double fps = mul_(mi, fp), lps_ = mul_(mi, lsp);
+        const double rA = fwd ? rho[i] : rho_sub[i], rB = fwd ? rho_sub[i] : rho[i];
+        const double pAl = fwd ? rp[i] : lsp;
+        const double psAf = fwd ? lps[i] : fps, psAl = fwd ? rps[i] : lps_;
+        const double pBf = fwd ? fp : lp[i];
+        const double psBf = fwd ? fps : lps[i], psBl = fwd ? lps_ : rps[i];
+        const double r = add_(rA, rB), v2 = add_(rA, pBf), v3 = add_(rB, pAl);
+        s[0] = add_(s[0], mul_(psAf, r));
+        s[1] = add_(s[1], mul_(psBl, r));
+        s[2] = add_(s[2], mul_(psAf, v2));
+        s[3] = add_(s[3], mul_(psBf, v2));
+        s[4] = add_(s[4], mul_(psAl, v3));
+        s[5] = add_(s[5], mul_(psBl, v3));
+    }
+    block_sums<6>(s, red);
+    bool ok_m = true;
+#pragma unroll
+    for (int k = 0; k < 6; k++) ok_m = ok_m && s[k] > 0.0;
+    const bool cont = ok_sub && ok_m;
+    // every thread has read rho, the ends and node[0] (block_sums synchronised)
+    for (int i = tid; i < d; i += kNT) {
+        if (cont) rho[i] = add_(rho[i], rho_sub[i]);
+        if (ok_sub) {
+            // the subtree's far end becomes the tree's end on its side
+            const double* pe = fwd ? p_last : p_first;
+            const double v = mul_(sg, pe[i]);
+            double* ep = a.end_p + (fwd ? CD : 0) + (size_t)c * d;
+            double* eps_ = a.end_ps + (fwd ? CD : 0) + (size_t)c * d;
+            ep[i] = v;
+            eps_[i] = mul_(a.m[i], v);
+        }
+    }
+    if (tid == 0) {
+        if (ok_sub) {
+            // log(e^logw + e^logw_sub)
+            const double hi = fmax(logw_old, logw_sub), lo = fmin(logw_old, logw_sub);
+            a.logw[c] = hi == -INFINITY ? hi : add_(hi, log1p(exp(sub_(lo, hi))));
+        }
+        a.active[c] = cont ? 1 : 0;
+        if (div) a.divergent[c] = 1;
+    }
+}
+
+// H0 = -logp(q) + KE(p) for the Gaussian target, logp(q) = -0.5 sum
+// prec (q - mu)^2 + logp_const; one warp per chain.
+__global__ void __launch_bounds__(kNT) k_nuts_energy(double* H0, const double* q, const double* p,
+                                                     const double* prec, const double* m,
+                                                     double mu, double logp_const, int C, int d) {
+    const int c = blockIdx.x * kNW + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (c >= C) return;
+    double u = 0.0, k = 0.0;
+    for (int i = lane; i < d; i += 32) {
+        const double dq = sub_(q[(size_t)c * d + i], mu), pi = p[(size_t)c * d + i];
+        u = add_(u, mul_(mul_(prec[i], dq), dq));
+        k = add_(k, mul_(mul_(pi, pi), m[i]));
+    }
+    u = warp_sum(u);
+    k = warp_sum(k);
+    if (lane == 0) H0[c] = add_(sub_(mul_(0.5, u), logp_const), mul_(0.5, k));
+}
+
+// Starting points of a speculative extension: chain chain[i] continues from
+// store row src_row[i] (the last leaf in its direction), or from the
+// initial point (q0, dir[i] * p0) when src_row[i] < 0.
+__global__ void __launch_bounds__(kNT) k_nuts_start(double* qs, double* ps, const double* q0,
+                                                    const double* p0, const double* st_q,
+                                                    const double* st_p, const int* chain,
+                                                    const long long* src_row, const int* dir,
+                                                    int d) {
+    const int i = blockIdx.x, c = chain[i];
+    const long long r = src_row[i];
+    for (int k = threadIdx.x; k < d; k += kNT) {
+        if (r >= 0) {
+            qs[(size_t)i * d + k] = st_q[(size_t)r * d + k];
+            ps[(size_t)i * d + k] = st_p[(size_t)r * d + k];
+        } else {
+            qs[(size_t)i * d + k] = q0[(size_t)c * d + k];
+            ps[(size_t)i * d + k] = mul_((double)dir[i], p0[(size_t)c * d + k]);
+        }
+    }
+}
+
+}  // namespace
+}  // namespace nxv
+
+using namespace nxv;
+
+namespace {
+bool holds(const void* h, size_t bytes) { return h && nbytes(h) >= bytes; }
+}  // namespace
+
+extern "C" {
+
+int nxv_nuts_energy(void* H0, void* q, void* p, void* prec, void* inv_mass, double mu,
+                    double logp_const, unsigned int n_chains, unsigned int d) {
+    if (!H0 || !q || !p || !prec || !inv_mass) return E_NULL;
+    Ctx c;
+    int rc = begin(c, {H0, q, p, prec, inv_mass});
+    if (rc) return rc;
+    const size_t CD = (size_t)n_chains * d * 8;
+    if (!holds(H0, (size_t)n_chains * 8) || !holds(q, CD) || !holds(p, CD) ||
+        !holds(prec, (size_t)d * 8) || !holds(inv_mass, (size_t)d * 8)) {
+        set_error("nuts_energy: a buffer is smaller than n_chains x d");
+        return E_ARG;
+    }
+    if (n_chains == 0 || d == 0) return OK;
+    k_nuts_energy<<<(n_chains + kNW - 1) / kNW, kNT, 0, c.stream>>>(
+        (double*)dptr(H0), (const double*)dptr(q), (const double*)dptr(p),
+        (const double*)dptr(prec), (const double*)dptr(inv_mass), mu, logp_const, (int)n_chains,
+        (int)d);
+    count_launch();
+    return finish(c);
+}
+
+int nxv_nuts_start(void* qs, void* ps, void* q0, void* p0, void* st_q, void* st_p, void* chain,
+                   void* src_row, void* dir, unsigned int n_need, unsigned int n_chains,
+                   unsigned int d) {
+    if (!qs || !ps || !q0 || !p0 || !st_q || !st_p || !chain || !src_row || !dir) return E_NULL;
+    Ctx c;
+    int rc = begin(c, {qs, ps, q0, p0, st_q, st_p, chain, src_row, dir});
+    if (rc) return rc;
+    const size_t ND = (size_t)n_need * d * 8, CD = (size_t)n_chains * d * 8;
+    if (!holds(qs, ND) || !holds(ps, ND) || !holds(q0, CD) || !holds(p0, CD) ||
+        !holds(chain, (size_t)n_need * 4) || !holds(src_row, (size_t)n_need * 8) ||
+        !holds(dir, (size_t)n_need * 4)) {
+        set_error("nuts_start: a buffer is smaller than its extent");
+        return E_ARG;
+    }
+    if (n_need == 0 || d == 0) return OK;
+    k_nuts_start<<<n_need, kNT, 0, c.stream>>>(
+        (double*)dptr(qs), (double*)dptr(ps), (const double*)dptr(q0), (const double*)dptr(p0),
+        (const double*)dptr(st_q), (const double*)dptr(st_p), (const int*)dptr(chain),
+        (const long long*)dptr(src_row), (const int*)dptr(dir), (int)d);
+    count_launch();
+    return finish(c);
+}
+
+int nxv_nuts_level(void* rows, void* chain, void* fwd, void* u_sel, void* u_move,
+                   unsigned int n_active, unsigned int n, unsigned int d, void* st_q, void* st_p,
+                   void* st_logp, void* st_ke, void* inv_mass, void* H0, void* logw, void* rho,
+                   void* end_p, void* end_ps, void* sample, void* active, void* divergent,
+                   void* node, unsigned int n_chains) {
+    if (!rows || !chain || !fwd || !u_sel || !u_move || !st_q || !st_p || !st_logp || !st_ke ||
+        !inv_mass || !H0 || !logw || !rho || !end_p || !end_ps || !sample || !active ||
+        !divergent || !node)
+        return E_NULL;
+    if (n == 0 || n > (unsigned)kMaxLeaves || (n & (n - 1)) != 0) {
+        set_error("nuts_level: n must be a power of two up to %d", kMaxLeaves);
+        return E_ARG;
+    }
+    Ctx c;
+    int rc = begin(c, {rows, chain, fwd, u_sel, u_move, st_q, st_p, st_logp, st_ke, inv_mass, H0,
+                       logw, rho, end_p, end_ps, sample, active, divergent, node});
+    if (rc) return rc;
+    const size_t A = n_active, C = n_chains, CD = C * d * 8;
+    if (!holds(rows, A * n * 8) || !holds(chain, A * 4) || !holds(fwd, A * 4) ||
+        !holds(u_sel, A * 8) || !holds(u_move, A * 8) || !holds(inv_mass, (size_t)d * 8) ||
+        !holds(H0, C * 8) || !holds(logw, C * 8) || !holds(rho, CD) || !holds(end_p, 2 * CD) ||
+        !holds(end_ps, 2 * CD) || !holds(sample, CD) || !holds(active, C * 4) ||
+        !holds(divergent, C * 4) || !holds(node, A * n * d * 8)) {
+        set_error("nuts_level: a buffer is smaller than its extent");
+        return E_ARG;
+    }
+    if (A == 0 || d == 0) return OK;
+    const size_t st_rows = nbytes(st_logp) / 8;
+    if (!holds(st_q, st_rows * d * 8) || !holds(st_p, st_rows * d * 8) ||
+        !holds(st_ke, st_rows * 8)) {
+        set_error("nuts_level: the store's q/p/ke hold fewer rows than its logp");
+        return E_ARG;
+    }
+    LevelArgs g;
+    g.rows = (const long long*)dptr(rows);
+    g.chain = (const int*)dptr(chain);
+    g.fwd = (const int*)dptr(fwd);
+    g.u_sel = (const double*)dptr(u_sel);
+    g.u_move = (const double*)dptr(u_move);
+    g.n = (int)n;
+    g.d = (int)d;
+    g.st_q = (const double*)dptr(st_q);
+    g.st_p = (const double*)dptr(st_p);
+    g.st_logp = (const double*)dptr(st_logp);
+    g.st_ke = (const double*)dptr(st_ke);
+    g.m = (const double*)dptr(inv_mass);
+    g.H0 = (const double*)dptr(H0);
+    g.logw = (double*)dptr(logw);
+    g.rho = (double*)dptr(rho);
+    g.end_p = (double*)dptr(end_p);
+    g.end_ps = (double*)dptr(end_ps);
+    g.sample = (double*)dptr(sample);
+    g.active = (int*)dptr(active);
+    g.divergent = (int*)dptr(divergent);
+    g.node = (double*)dptr(node);
+    g.C = (int)C;
+    k_nuts_level<<<(unsigned)A, kNT, 0, c.stream>>>(g);
+    count_launch();
+    return finish(c);
+}
+
+}  // extern "C"

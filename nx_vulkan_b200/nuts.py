@@ -396,3 +396,183 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
         active[act] = cont
     n_leap = leaves[+1].used + leaves[-1].used
     return sample, Stats(depth=depth, n_leapfrog=n_leap, divergent=divergent, energy=H0)
+
+
+class DeviceTree:
+    """The tree builder's walk on the device (nxv_nuts_energy / _start /
+    _level): the chain calls write their leaves into a device store and the
+    per-level logic runs over it, so the trajectories never cross PCIe.  The
+    host keeps the row bookkeeping (_Leaves) and draws the random numbers in
+    the order of nuts_transition, so with the same generator both take the
+    same draws (their sums run in different orders, so a decision within
+    rounding of a threshold can differ).  Gaussian targets, f64."""
+
+    def __init__(self, target: GaussianTarget, inv_mass, eps: float):
+        import torch
+        from nx_vulkan_b200 import _native
+        from nx_vulkan_b200 import vulkan as nxv
+        self.torch, self.nxv, self.lib = torch, nxv, _native.load()
+        self.t, self.eps = target, eps
+        self.m = np.ascontiguousarray(inv_mass, np.float64)
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        f64 = dict(dtype=torch.float64, device=self.dev)
+        self.prec = torch.from_numpy(self.t.prec).to(self.dev)
+        self.m_dev = torch.from_numpy(self.m).to(self.dev)
+        self.f64 = f64
+        self.cap = 0           # store rows
+        self.node_cap = 0      # f64 scratch elements
+        self.calls = []
+
+    # -- device buffers -------------------------------------------------------------
+    def _h(self, t, offset_elems=0, n_elems=None):
+        """Non-owning handle over (part of) a torch tensor."""
+        es = t.element_size()
+        n = t.numel() - offset_elems if n_elems is None else n_elems
+        h = self.lib.nxv_buf_wrap(self._ptr(t, offset_elems), n * es)
+        if not h:
+            raise RuntimeError("nxv_buf_wrap failed")
+        return h
+
+    @staticmethod
+    def _ptr(t, offset_elems=0):
+        import ctypes
+        return ctypes.c_void_p(t.data_ptr() + offset_elems * t.element_size())
+
+    def _call(self, fn, *args):
+        rc = fn(*args)
+        if rc != 0:
+            raise RuntimeError(f"{fn.__name__} failed: {rc} {self.lib.nxv_last_error()}")
+
+    def _reserve(self, rows: int, d: int):
+        if rows <= self.cap:
+            return
+        torch = self.torch
+        cap = max(rows, 2 * self.cap, 1 << 14)
+        new = [torch.empty(cap * d, **self.f64), torch.empty(cap * d, **self.f64),
+               torch.empty(cap, **self.f64), torch.empty(cap, **self.f64)]
+        if self.cap:
+            for a, b in zip(new, (self.st_q, self.st_p, self.st_logp, self.st_ke)):
+                a[: b.numel()].copy_(b)
+        self.st_q, self.st_p, self.st_logp, self.st_ke = new
+        self.cap = cap
+
+    def _free(self, *hs):
+        for h in hs:
+            self.lib.nxv_buf_free(h)
+
+    def transition(self, q0, rng, max_depth=10):
+        """One NUTS transition for every chain of q0 [C, d] (a torch CUDA
+        tensor or an array); returns (q as a torch CUDA tensor, Stats).  The
+        library runs on torch's current stream during the call (the state
+        tensors are torch's) and on its own stream again afterwards."""
+        import ctypes
+        s = self.torch.cuda.current_stream(self.dev).cuda_stream
+        self.lib.nxv_set_stream(ctypes.c_void_p(s if s else 1))  # 1: the legacy default stream
+        try:
+            return self._transition(q0, rng, max_depth)
+        finally:
+            self.lib.nxv_set_stream(None)
+
+    def _transition(self, q0, rng, max_depth):
+        torch, lib = self.torch, self.lib
+        q0 = torch.as_tensor(q0, dtype=torch.float64).to(self.dev).contiguous()
+        C, d = q0.shape
+        m = self.m
+        p0_h = rng.standard_normal((C, d)) / np.sqrt(m)
+        p0 = torch.from_numpy(p0_h).to(self.dev)
+        H0 = torch.empty(C, **self.f64)
+        hH0, hq0, hp0, hprec, hm = (self._h(x) for x in (H0, q0, p0, self.prec, self.m_dev))
+        self._call(lib.nxv_nuts_energy, hH0, hq0, hp0, hprec, hm, self.t.mu, self.t.const, C, d)
+        logw = -H0
+        sample = q0.clone()
+        rho = p0.clone()
+        ends_p = torch.from_numpy(np.stack([p0_h, p0_h])).to(self.dev).contiguous()
+        ends_ps = torch.from_numpy(np.stack([p0_h * m, p0_h * m])).to(self.dev).contiguous()
+        active_d = torch.ones(C, dtype=torch.int32, device=self.dev)
+        div_d = torch.zeros(C, dtype=torch.int32, device=self.dev)
+        hlogw, hsample, hrho, hep, heps, hact, hdiv = (
+            self._h(x) for x in (logw, sample, rho, ends_p, ends_ps, active_d, div_d))
+        store = _Store(d)  # bookkeeping only: rows counted, data on the device
+        leaves = {+1: _Leaves(store, C), -1: _Leaves(store, C)}
+        active = np.ones(C, bool)
+        depth = np.zeros(C, np.int64)
+        grad_tmp = None
+        for level in range(max_depth):
+            if not active.any():
+                break
+            n_new = 1 << level
+            dirs = np.where(rng.random(C) < 0.5, -1, 1)
+            fwd_all = dirs > 0
+            have = np.where(fwd_all, leaves[+1].have, leaves[-1].have)
+            used = np.where(fwd_all, leaves[+1].used, leaves[-1].used)
+            need = np.flatnonzero(active & (have < used + n_new))
+            if need.size:
+                K = speculative_steps(n_new)
+                src = np.full(need.size, -1, np.int64)
+                for sgn in (+1, -1):
+                    L = leaves[sgn]
+                    sel = (dirs[need] == sgn) & (L.have[need] > 0)
+                    if sel.any():
+                        src[sel] = L.last(need[sel])
+                nn = need.size
+                qs = torch.empty(nn * d, **self.f64)
+                ps = torch.empty(nn * d, **self.f64)
+                chain_t = torch.from_numpy(need.astype(np.int32)).to(self.dev)
+                src_t = torch.from_numpy(src).to(self.dev)
+                dir_t = torch.from_numpy(dirs[need].astype(np.int32)).to(self.dev)
+                s0 = store.size
+                self._reserve(s0 + nn * K, d)
+                hs = [self._h(x) for x in (qs, ps, self.st_q, self.st_p, chain_t, src_t, dir_t)]
+                self._call(lib.nxv_nuts_start, hs[0], hs[1], hq0, hp0, hs[2], hs[3], hs[4],
+                           hs[5], hs[6], nn, C, d)
+                if grad_tmp is None or grad_tmp.numel() < nn * K * d:
+                    grad_tmp = torch.empty(nn * K * d, **self.f64)
+                outs = [self._h(self.st_q, s0 * d, nn * K * d), self._h(self.st_p, s0 * d, nn * K * d),
+                        self._h(grad_tmp, 0, nn * K * d), self._h(self.st_logp, s0, nn * K),
+                        self._h(self.st_ke, s0, nn * K)]
+                rc = lib.nxv_leapfrog_chain_gauss_f64_batched_ke(
+                    *outs, hs[0], hs[1], hm, hprec, d, nn, K, self.eps, self.t.mu,
+                    self.nxv.shader_path("leapfrog_chain_gauss_f64_batched.spv"))
+                self._free(*hs, *outs)
+                if rc != 0:
+                    raise RuntimeError(f"chain call failed: {lib.nxv_last_error()}")
+                store.size = s0 + nn * K
+                starts = s0 + np.arange(nn) * K
+                for sgn in (+1, -1):
+                    sel = dirs[need] == sgn
+                    if sel.any():
+                        leaves[sgn].add_block(need[sel], starts[sel], K)
+                self.calls.append((nn, K))
+            act = np.flatnonzero(active)
+            A = act.size
+            fwd = dirs[act] > 0
+            rows = np.empty((A, n_new), np.int64)
+            for sgn, sel in ((+1, fwd), (-1, ~fwd)):
+                if sel.any():
+                    r_ = leaves[sgn].take(act[sel], n_new)
+                    rows[sel] = r_ if sgn > 0 else r_[:, ::-1]  # backward leaves run leftward
+            u_sel = rng.random(A)
+            u_move = rng.random(A)
+            depth[act] = level + 1
+            if self.node_cap < A * n_new * d:
+                self.node = torch.empty(A * n_new * d, **self.f64)
+                self.node_cap = A * n_new * d
+            lv = [torch.from_numpy(np.ascontiguousarray(rows)).to(self.dev),
+                  torch.from_numpy(act.astype(np.int32)).to(self.dev),
+                  torch.from_numpy(fwd.astype(np.int32)).to(self.dev),
+                  torch.from_numpy(u_sel).to(self.dev), torch.from_numpy(u_move).to(self.dev)]
+            hl = [self._h(x) for x in lv]
+            hst = [self._h(x) for x in (self.st_q, self.st_p)]
+            hst += [self._h(self.st_logp, 0, store.size), self._h(self.st_ke, 0, store.size)]
+            hnode = self._h(self.node)
+            rc = lib.nxv_nuts_level(*hl, A, n_new, d, *hst, hm, hH0, hlogw, hrho, hep, heps,
+                                    hsample, hact, hdiv, hnode, C)
+            self._free(*hl, *hst, hnode)
+            if rc != 0:
+                raise RuntimeError(f"nuts_level failed: {lib.nxv_last_error()}")
+            # the only per-level transfer to the host: which trees keep growing
+            active = active_d.cpu().numpy().astype(bool)
+        stats = Stats(depth=depth, n_leapfrog=leaves[+1].used + leaves[-1].used,
+                      divergent=div_d.cpu().numpy().astype(bool), energy=H0.cpu().numpy())
+        self._free(hH0, hq0, hp0, hprec, hm, hlogw, hsample, hrho, hep, heps, hact, hdiv)
+        return sample.view(C, d), stats
