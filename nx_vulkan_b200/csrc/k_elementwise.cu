@@ -209,12 +209,15 @@ bool pdl_independent_and_record(Ctx& c, const void* const* ins, int nin, size_t 
     return indep;
 }
 
-template <typename T, int NIN, class F>
-int launch_map1(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* i3, size_t n,
-                F f, unsigned grid) {
+// Launches a map kernel (k_map1 or k_map_pipe: parameters out, in0..in3,
+// n, f, early) with programmatic dependent launch unless NXV_MAP_PDL=0.
+template <typename T, class F>
+int launch_pdl(Ctx& c, void (*kern)(T*, const T*, const T*, const T*, const T*, size_t, F, int),
+               const char* name, unsigned grid, T* out, const T* i0, const T* i1, const T* i2,
+               const T* i3, size_t n, F f, int nin) {
     const void* ins[4] = {i0, i1, i2, i3};
     const bool pdl = map_pdl();
-    const int early = pdl && pdl_independent_and_record(c, ins, NIN, n * sizeof(T), out) ? 1 : 0;
+    const int early = pdl && pdl_independent_and_record(c, ins, nin, n * sizeof(T), out) ? 1 : 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -225,8 +228,8 @@ int launch_map1(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, k_map1<T, NIN, F>, out, i0, i1, i2, i3, n, f, early);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(k_map1)");
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, out, i0, i1, i2, i3, n, f, early);
+    if (e != cudaSuccess) return cuda_fail(e, name);
     count_launch();
     return finish(c);
 }
@@ -258,14 +261,22 @@ int map1_per_sm() {
 template <typename T, int NIN, class F>
 __global__ void __launch_bounds__(kThreads)
 k_map_pipe(T* __restrict__ out, const T* __restrict__ in0, const T* __restrict__ in1,
-           const T* __restrict__ in2, const T* __restrict__ in3, size_t n, F f) {
+           const T* __restrict__ in2, const T* __restrict__ in3, size_t n, F f, int early) {
     constexpr int W = (int)(16 / sizeof(T));
     const T* ins[4] = {in0, in1, in2, in3};
     const size_t nv = n / W;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     T nx[NIN > 0 ? NIN : 1][W];
-    if (v < nv) {
+    // programmatic dependent launch as in k_map1: the first vector is loaded
+    // before the wait only when no input overlaps the previous kernel's output
+    if (early && v < nv) {
+#pragma unroll
+        for (int q = 0; q < NIN; q++) vload(ins[q] + v * W, nx[q]);
+    }
+    griddep_wait();
+    griddep_launch();
+    if (!early && v < nv) {
 #pragma unroll
         for (int q = 0; q < NIN; q++) vload(ins[q] + v * W, nx[q]);
     }
@@ -333,8 +344,9 @@ int run_map(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* i3, 
         const size_t nv = n / W;
         const size_t wave = (size_t)c.dev->sm_count * map1_per_sm<T, NIN, F>() * kThreads;
         if (vec && map_wide() && nv >= 1 && nv <= wave)
-            return launch_map1<T, NIN, F>(c, out, i0, i1, i2, i3, n, f,
-                                          (unsigned)((nv + kThreads - 1) / kThreads));
+            return launch_pdl(c, k_map1<T, NIN, F>, "cudaLaunchKernelEx(k_map1)",
+                              (unsigned)((nv + kThreads - 1) / kThreads), out, i0, i1, i2, i3,
+                              n, f, NIN);
     }
     if constexpr (sizeof(T) == 8 || Heavy<F>::value) {
         const size_t nv = n / W;
@@ -343,9 +355,8 @@ int run_map(Ctx& c, T* out, const T* i0, const T* i1, const T* i2, const T* i3, 
             const size_t want = (nv + kThreads - 1) / kThreads;
             const unsigned g =
                 (unsigned)std::min<size_t>(want, (size_t)c.dev->sm_count * (size_t)occ);
-            k_map_pipe<T, NIN, F><<<g, kThreads, 0, c.stream>>>(out, i0, i1, i2, i3, n, f);
-            count_launch();
-            return finish(c);
+            return launch_pdl(c, k_map_pipe<T, NIN, F>, "cudaLaunchKernelEx(k_map_pipe)", g, out,
+                              i0, i1, i2, i3, n, f, NIN);
         }
     }
     if (vec) {

@@ -19,10 +19,11 @@
 //
 // For f32 results evaluated in f64 and rounded once (Nx.BinaryBackend's
 // semantics), round_f32_checked rounds a lean result to f32 unless it lies
-// within 64 double ulps of an f32 rounding boundary (about 1 in 4 million
-// values), where the caller takes the library's f64 function instead: both
-// are within a few double ulps of the true value, so away from a boundary
-// they round to the same f32.
+// within M double ulps of an f32 rounding boundary, where the caller takes
+// the library's f64 function instead: both are within M double ulps of the
+// true value, so away from a boundary they round to the same f32.  The
+// f32-argument functions at the end (exp_f32 .. sigmoid_f32) use a shorter
+// core for that purpose.
 #pragma once
 #include <cuda_runtime.h>
 
@@ -92,14 +93,23 @@ __device__ __forceinline__ double reduce(double x, double& s, double& s_lo) {
     const double p = __fma_rn(__dmul_rn(r, r), q, r);
     const int m = k >> 6;  // floor(k / 64)
     const double pw = __longlong_as_double((long long)(m + 1023) << 52);
-    s = __dmul_rn(__ldg(&kExp2J64[k & 63]), pw);
+    // 2^m s is a normal double for |m| <= 1010: the power of two goes into
+    // the head's exponent field; the tail (possibly 0) is scaled by a product
+    const double tj = __ldg(&kExp2J64[k & 63]);
+    s = __hiloint2double(__double2hiint(tj) + (m << 20), __double2loint(tj));
     s_lo = __dmul_rn(__ldg(&kExp2J64Lo[k & 63]), pw);
     return p;
 }
 
+// The C library's functions for the arguments the table-driven ones leave
+// to it (overflow, underflow, inf, NaN), out of line so that their code
+// holds no registers in the kernels that inline the fast paths.
+static __device__ __noinline__ double lib_exp(double x) { return ::exp(x); }
+static __device__ __noinline__ double lib_expm1(double x) { return ::expm1(x); }
+
 // e^x = s + (s p + s_lo (1 + p))
 __device__ __forceinline__ double exp(double x) {
-    if (!(fabs(x) <= 700.0)) return ::exp(x);  // overflow, underflow, inf, NaN
+    if (!(fabs(x) <= 700.0)) return lib_exp(x);  // overflow, underflow, inf, NaN
     double s, s_lo;
     const double p = reduce(x, s, s_lo);
     return __dadd_rn(s, __fma_rn(s, p, __fma_rn(s_lo, p, s_lo)));
@@ -108,7 +118,7 @@ __device__ __forceinline__ double exp(double x) {
 // e^x - 1 = (s - 1) + (s p + s_lo (1 + p)); the table tail keeps the result
 // accurate where s - 1 cancels (|x| below about 1)
 __device__ __forceinline__ double expm1(double x) {
-    if (!(fabs(x) <= 700.0)) return ::expm1(x);
+    if (!(fabs(x) <= 700.0)) return lib_expm1(x);
     double s, s_lo;
     const double p = reduce(x, s, s_lo);
     return __dadd_rn(__dsub_rn(s, 1.0), __fma_rn(s, p, __fma_rn(s_lo, p, s_lo)));
@@ -132,15 +142,102 @@ __device__ __forceinline__ double tanh(double x) {
     return copysign(__dmul_rn(-e, recip_1_2(__dadd_rn(2.0, e))), x);
 }
 
-// y rounded to f32 when that rounding is certain for a value within a few
+// y rounded to f32 when that rounding is certain for a value within M
 // double ulps of y; `ok` false otherwise (near an f32 rounding boundary,
 // f32 subnormal or out of f32 range: the caller falls back).
+template <unsigned M = 64>
 __device__ __forceinline__ float round_f32_checked(double y, bool& ok) {
-    const double ay = fabs(y);
+    const unsigned ahi = (unsigned)__double2hiint(y) & 0x7fffffffu;
     const unsigned low = (unsigned)__double2loint(y) & ((1u << 29) - 1u);  // bits below f32
-    ok = ay >= 0x1p-126 && ay < 0x1p+128 &&
-         (low + 64u - (1u << 28)) > 128u;  // not within 64 units of the midpoint 2^28
+    // 2^-126 <= |y| < 2^128 (false for inf and NaN), as a test of the high word
+    ok = ahi - 0x38100000u < 0x47f00000u - 0x38100000u &&
+         (low + M - (1u << 28)) > 2u * M;  // not within M units of the midpoint 2^28
     return __double2float_rn(y);
+}
+
+// ---------------------------------------------------------------------------
+// f32-argument exp, expm1, tanh and sigmoid for results that are rounded to
+// f32 at once.  Only about 2^-44 relative accuracy is needed before the
+// rounding check, so the core is shorter than exp above: one ln2/64 constant
+// in the reduction (|k| <= 2^13 for |x| <= 104, so k * its rounding error
+// stays below 2^-47), e^r - 1 to r^5 (truncation below 2^-47 relative to
+// e^r - 1), the table head alone (2^-53), the power of two added to the
+// exponent field, and a reciprocal from the f32 hardware estimate with one
+// Newton step.  Over a sweep of 2^26 f32 arguments against 64-bit long
+// double references, with the f32 estimate taken one ulp off, the largest
+// errors were 27 (exp), 65 (expm1), 391 (tanh) and 217 (sigmoid) double
+// ulps; results within kMarginF32 = 2048 double ulps of an f32 rounding
+// boundary (about 8 in a million) go to the caller's library fallback.
+
+constexpr unsigned kMarginF32 = 2048;
+constexpr double kLn2d64 = 0x1.62e42fefa39efp-7;  // ln 2 / 64 rounded to double
+
+// d = e^r - 1 (returned) and s = 2^(k/64) with x = k ln2/64 + r, for
+// |x| <= 208 (the callers clamp)
+__device__ __forceinline__ double reduce_short(double x, double& s) {
+    const double t = __fma_rn(x, kInvLn2x64, kShift);
+    const int k = __double2loint(t);
+    const double kd = __dsub_rn(t, kShift);
+    const double r = __fma_rn(-kd, kLn2d64, x);
+    double q = __fma_rn(r, 1.0 / 120.0, 1.0 / 24.0);
+    q = __fma_rn(r, q, 1.0 / 6.0);
+    q = __fma_rn(r, q, 0.5);
+    const double p = __fma_rn(__dmul_rn(r, r), q, r);
+    const double tj = __ldg(&kExp2J64[k & 63]);
+    s = __hiloint2double(__double2hiint(tj) + ((k >> 6) << 20), __double2loint(tj));
+    return p;
+}
+
+__device__ __forceinline__ double recip_f32_newton(double d) {
+    float rf;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rf) : "f"(__double2float_rn(d)));
+    const double r = (double)rf;
+    return __fma_rn(r, __fma_rn(-d, r, 1.0), r);
+}
+
+// exp(x) rounded to f32 as (float) of a double exp would round it; `ok`
+// false where the caller must fall back (near a rounding boundary, f32
+// overflow or subnormal results, NaN: the clamp maps those outside the
+// certified range)
+__device__ __forceinline__ float exp_f32(float x, bool& ok) {
+    double s;
+    const double p = reduce_short((double)fminf(fmaxf(x, -104.f), 104.f), s);
+    return round_f32_checked<kMarginF32>(__fma_rn(s, p, s), ok);
+}
+
+// e^x - 1 = s p + (s - 1); s - 1 is exact for s in [1/2, 2] (|x| <= ln 2)
+__device__ __forceinline__ float expm1_f32(float x, bool& ok) {
+    double s;
+    const double p = reduce_short((double)fminf(fmaxf(x, -104.f), 104.f), s);
+    const float r = round_f32_checked<kMarginF32>(__fma_rn(s, p, __dsub_rn(s, 1.0)), ok);
+    ok = ok && x == x;  // NaN would be clamped to -104 (-> -1)
+    return r;
+}
+
+// tanh |x| = -e / (2 + e), e = expm1(-2|x|); tanh(10) already rounds to 1
+// in f32, so |x| is clamped there
+__device__ __forceinline__ float tanh_f32(float x, bool& ok) {
+    const float ax = fminf(fabsf(x), 10.f);
+    double s;
+    const double p = reduce_short(-2.0 * (double)ax, s);
+    const double e = __fma_rn(s, p, __dsub_rn(s, 1.0));
+    const double den = __dadd_rn(2.0, e);
+    const double r = recip_f32_newton(den);
+    const double q0 = __dmul_rn(-e, r);
+    const double q = __fma_rn(r, __fma_rn(-q0, den, -e), q0);  // one quotient correction
+    const float v = round_f32_checked<kMarginF32>(q, ok);
+    ok = ok && x == x;
+    return copysignf(v, x);
+}
+
+// 1 / (1 + e^-x) for x >= -80 (clamped above at 80, where it rounds to 1)
+__device__ __forceinline__ float sigmoid_f32(float x, bool& ok) {
+    double s;
+    const double p = reduce_short(-(double)fminf(fmaxf(x, -81.f), 80.f), s);
+    const double den = __dadd_rn(1.0, __fma_rn(s, p, s));
+    const float v = round_f32_checked<kMarginF32>(recip_f32_newton(den), ok);
+    ok = ok && x >= -80.f;  // false for NaN too
+    return v;
 }
 
 }  // namespace lean

@@ -78,31 +78,37 @@ __device__ __forceinline__ T bin_op(T a, T b, unsigned op) {
 // uses the f32 library functions (2-4 ulp) for throughput.
 //
 // In the exact mode exp, sigmoid, tanh and expm1 are evaluated with the
-// table-driven f64 functions (lean_math.cuh) and rounded once; the library
-// f64 function is taken instead only where the lean value lies near an f32
-// rounding boundary, so the result is the one the library path gives.
+// short f32-argument f64 cores (lean_math.cuh: about 2^-44 relative) and
+// rounded once; the library f64 function is taken instead only where that
+// value lies within 2048 double ulps of an f32 rounding boundary, so the
+// result is the one the library path gives.
+// The library f64 function rounded to f32, out of line: it runs for about
+// 8 in a million elements, and inlined its code would hold registers (and
+// spill) in every kernel that evaluates the short cores.
+static __device__ __noinline__ float f64_rounded(float x, unsigned op) {
+    const double d = (double)x;
+    switch (op) {
+        case 0: return (float)exp(d);
+        case 5: return (float)(1.0 / (1.0 + exp(-d)));
+        case 6: return (float)tanh(d);
+        default: return (float)expm1(d);
+    }
+}
+
 template <bool EXACT>
 __device__ __forceinline__ float tr_f32(float x, unsigned op) {
     if constexpr (EXACT) {
-        double d = (double)x;
         bool ok;
         float r;
         switch (op) {
-            case 0:
-                r = lean::round_f32_checked(lean::exp(d), ok);
-                return ok ? r : (float)exp(d);
-            case 1: return (float)log(d);
-            case 5:
-                r = lean::round_f32_checked(__ddiv_rn(1.0, __dadd_rn(1.0, lean::exp(-d))), ok);
-                return ok ? r : (float)(1.0 / (1.0 + exp(-d)));
-            case 6:
-                r = lean::round_f32_checked(lean::tanh(d), ok);
-                return ok ? r : (float)tanh(d);
-            case 13: return (float)erf(d);
-            default:
-                r = lean::round_f32_checked(lean::expm1(d), ok);
-                return ok ? r : (float)expm1(d);
+            case 0: r = lean::exp_f32(x, ok); break;
+            case 1: return (float)log((double)x);
+            case 5: r = lean::sigmoid_f32(x, ok); break;
+            case 6: r = lean::tanh_f32(x, ok); break;
+            case 13: return (float)erf((double)x);
+            default: r = lean::expm1_f32(x, ok); break;
         }
+        return ok ? r : f64_rounded(x, op);
     } else {
         switch (op) {
             case 0: return expf(x);

@@ -158,3 +158,30 @@ def test_f64_table_driven_functions(nxv, orc):
         d = f64_ulps(got[ok], want[ok])
         print(f"f64 {name}: max {d.max()} ulp, {np.mean(d > 0):.3%} not bit-equal")
         assert d.max() <= 4, (name, x[ok][np.argmax(d)])
+
+
+@pytest.mark.parametrize("sign", [0, 1])
+def test_exact_unary_sweep_matches_f64_rounded(nxv, exact, sign):
+    """Every 128th f32 bit pattern of one sign (2^24 arguments: zeros,
+    subnormals, tiny, huge, inf and NaN): exact-mode exp, expm1, tanh and
+    sigmoid equal CUDA's f64 functions (through torch) rounded to f32, bit for
+    bit.  Where the short f64 core's value is more than 2048 double ulps from
+    an f32 rounding boundary it rounds like any value within that distance,
+    the f64 function's included; elsewhere the kernel calls the f64 function
+    itself."""
+    import torch
+
+    bits = (np.arange(0, 1 << 31, 128, dtype=np.uint64) + (sign << 31) + 37).astype(np.uint32)
+    x = bits.view(np.float32)
+    xd = torch.from_numpy(x).cuda().double()
+    refs = {0: torch.exp(xd), 14: torch.expm1(xd), 6: torch.tanh(xd),
+            5: 1.0 / (1.0 + torch.exp(-xd))}
+    spv = nxv.shader_path("elementwise_unary.spv")
+    tx = up(nxv, x)
+    for op, ref in refs.items():
+        got = down(nxv, unwrap(nxv.apply_unary(tx, op, spv, 4)), np.float32)
+        want = ref.float().cpu().numpy()
+        same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+        bad = np.flatnonzero(~same)
+        listing = ", ".join(f"x={x[i]!r}: got {got[i]!r} want {want[i]!r}" for i in bad[:8])
+        assert bad.size == 0, f"op {op}: {bad.size} differ: {listing}"
