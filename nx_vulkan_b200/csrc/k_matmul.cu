@@ -7,12 +7,15 @@
 // C += Ahi.Bhi + Ahi.Blo + Alo.Bhi, accumulated in f32.  The error is of the
 // order of f32 rounding (the dropped lo.lo term is ~2^-22 relative).
 //
-// Both kernels: CTA tile 128x128, 8 warps in a 2 (M) x 4 (N) grid with a
-// 64x32 warp tile, a 3-stage cp.async pipeline, shared-memory rows padded so
-// that every fragment load is bank-conflict free (A rows are BK+4 elements;
-// B rows are 128+4 doubles -- 4 mod 16 in 8-byte bank pairs -- or 128+8
-// floats -- 8 mod 32 in 4-byte banks), zero-filled out-of-range chunks, and a
-// scalar loader when a row is not 16-byte aligned.
+// Tiles: f64 products by default on 64x64 CTA tiles (4 warps, 32x32 warp
+// tiles, BK 16, three CTAs per SM); the 128x128 schedule -- 8 warps in a 2
+// (M) x 4 (N) grid with a 64x32 warp tile, one CTA per SM, a stream-K tail
+// for the last wave -- serves the f32 path and NXV_GEMM_TILE=128.  Both: a
+// 3-stage cp.async pipeline, shared-memory rows padded so that every
+// fragment load is bank-conflict free (A rows are BK+4 elements; B rows are
+// BN+4 doubles -- 4 mod 16 in 8-byte bank pairs -- or BN+8 floats -- 8 mod 32
+// in 4-byte banks), zero-filled out-of-range chunks, and a scalar loader
+// when a row is not 16-byte aligned.
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -40,8 +43,17 @@ __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0
 
 namespace {
 
-template <typename T, int BK>
-struct Smem {
+// CTA tile geometry: BM x BN tiles, BK-deep k-tiles, WARPS_M x WARPS_N warps
+// with (BM / WARPS_M) x (BN / WARPS_N) warp tiles, at least MINB CTAs per SM
+// (launch bounds).  The default is the 128 x 128 tile of the stream-K
+// schedule.
+template <typename T, int BK_, int BM_ = BM, int BN_ = BN, int WARPS_M_ = 2, int WARPS_N_ = 4,
+          int MINB_ = 1>
+struct Cfg {
+    using type = T;
+    static constexpr int BM = BM_, BN = BN_, BK = BK_;
+    static constexpr int WARPS_N = WARPS_N_, NTH = 32 * WARPS_M_ * WARPS_N_, MINB = MINB_;
+    static constexpr int MI = BM / WARPS_M_ / 16, NJ = BN / WARPS_N_ / 8;  // fragments per warp
     static constexpr int AS = BK + 4;      // A row stride (elements)
     static constexpr int BS = BN + (sizeof(T) == 8 ? 4 : 8);  // B row stride (elements)
     static constexpr int A_ELEMS = BM * AS;
@@ -50,13 +62,21 @@ struct Smem {
     static constexpr size_t BYTES = (size_t)STAGES * STAGE * sizeof(T);
 };
 
+// 64 x 64 f64 tiles: 4 warps with 32 x 32 warp tiles, BK 16 -- 57 KB of
+// shared memory and 150 registers per thread, so three CTAs share an SM and
+// hide each other's pipeline fill and epilogue, and a product's tiles
+// spread over the SMs to within a tile (64 x 256^3: 1024 tiles, 6.9 per SM,
+// against 1.7 of the 128 x 128 tiles).  A and B rows of 20 and 68 doubles
+// (4 mod 16) keep the fragment loads conflict-free as in the large tile.
+using Small64 = Cfg<double, 16, 64, 64, 2, 2, 3>;
+
 // Load one BMxBK tile of A and one BKxBN tile of B into stage buffers.
-template <typename T, int BK>
+template <class S, typename T = typename S::type>
 __device__ __forceinline__ void load_tile(T* sA, T* sB, const T* A, const T* B, int M, int N,
                                           int K, int lda, int ldb, int m0, int n0, int k0,
                                           bool vecA, bool vecB) {
     constexpr int EPC = 16 / sizeof(T);  // elements per 16-byte chunk
-    using S = Smem<T, BK>;
+    constexpr int BM = S::BM, BN = S::BN, BK = S::BK, NTH = S::NTH;
     const int tid = threadIdx.x;
     // A: BM rows x BK cols
     constexpr int A_CHUNKS = BM * BK / EPC;
@@ -152,11 +172,11 @@ __device__ __forceinline__ void tmma_16x8x8(float (&d)[4], const unsigned (&a)[4
 
 // Interior tile: every 16-byte chunk of the A and B tiles is in range and
 // aligned, so the loads need no guards.
-template <typename T, int BK>
+template <class S, typename T = typename S::type>
 __device__ __forceinline__ void load_tile_fast(T* sA, T* sB, const T* A, const T* B, int lda,
                                                int ldb, int m0, int n0, int k0) {
     constexpr int EPC = 16 / sizeof(T);
-    using S = Smem<T, BK>;
+    constexpr int BM = S::BM, BN = S::BN, BK = S::BK, NTH = S::NTH;
     const int tid = threadIdx.x;
     constexpr int A_CHUNKS = BM * BK / EPC;
 #pragma unroll
@@ -176,13 +196,13 @@ __device__ __forceinline__ void load_tile_fast(T* sA, T* sB, const T* A, const T
 struct TileAt {
     int z, m0, n0;
 };
-template <typename T>
+template <typename T, int TM = BM, int TN = BN>
 __device__ __forceinline__ TileAt tile_at(const GemmP<T>& P, long long lin) {
-    const int tm = (P.M + BM - 1) / BM, tn = (P.N + BN - 1) / BN;
+    const int tm = (P.M + TM - 1) / TM, tn = (P.N + TN - 1) / TN;
     const long long per_z = (long long)tm * tn;
     const int z = (int)(lin / per_z);
     const int r = (int)(lin - (long long)z * per_z);
-    return TileAt{z, (r / tn) * BM, (r % tn) * BN};
+    return TileAt{z, (r / tn) * TM, (r % tn) * TN};
 }
 
 // Operands of slice/batch z: A, B advanced and the K extent of the slice.
@@ -206,25 +226,26 @@ __device__ __forceinline__ void operands_at(const GemmP<T>& P, int z, const T*& 
 
 // acc += A[m0.., k] . B[k, n0..] over k-tiles [kt0, kt1) of this operand pair,
 // through the STAGES-deep cp.async pipeline in `smem`.
-template <typename T, int BK, int MK>
+template <class S, int MK, typename T = typename S::type>
 __device__ __forceinline__ void gemm_mainloop(const GemmP<T>& P, const T* __restrict__ A,
                                               const T* __restrict__ B, int K, int m0, int n0,
-                                              int kt0, int kt1, T* smem, T (&acc)[4][4][4]) {
-    using S = Smem<T, BK>;
+                                              int kt0, int kt1, T* smem,
+                                              T (&acc)[S::MI][S::NJ][4]) {
+    constexpr int BM = S::BM, BN = S::BN, BK = S::BK, MI = S::MI, NJ = S::NJ;
     const int M = P.M, N = P.N, lda = P.lda, ldb = P.ldb;
     const bool vecA = P.vecA, vecB = P.vecB;
     const bool inner_mn = vecA && vecB && m0 + BM <= M && n0 + BN <= N;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, tig = lane & 3;
-    const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
+    const int wm = (warp / S::WARPS_N) * (MI * 16), wn = (warp % S::WARPS_N) * (NJ * 8);
     auto load = [&](int st, int kt) {
         T* sA = smem + st * S::STAGE;
         T* sB = sA + S::A_ELEMS;
         const int k0 = kt * BK;
         if (inner_mn && k0 + BK <= K)
-            load_tile_fast<T, BK>(sA, sB, A, B, lda, ldb, m0, n0, k0);
+            load_tile_fast<S>(sA, sB, A, B, lda, ldb, m0, n0, k0);
         else
-            load_tile<T, BK>(sA, sB, A, B, M, N, K, lda, ldb, m0, n0, k0, vecA, vecB);
+            load_tile<S>(sA, sB, A, B, M, N, K, lda, ldb, m0, n0, k0, vecA, vecB);
     };
 #pragma unroll
     for (int s = 0; s < STAGES - 1; s++) {
@@ -247,28 +268,28 @@ __device__ __forceinline__ void gemm_mainloop(const GemmP<T>& P, const T* __rest
             constexpr int AR = MK / 2, BR = MK / 4;
 #pragma unroll
             for (int kk = 0; kk < BK; kk += MK) {
-                double af[4][AR], bf[4][BR];
+                double af[MI][AR], bf[NJ][BR];
 #pragma unroll
-                for (int i = 0; i < 4; i++)
+                for (int i = 0; i < MI; i++)
 #pragma unroll
                     for (int r = 0; r < AR; r++)
                         af[i][r] = sA[(wm + i * 16 + g + 8 * (r % 2)) * S::AS + kk + tig + 4 * (r / 2)];
 #pragma unroll
-                for (int j = 0; j < 4; j++)
+                for (int j = 0; j < NJ; j++)
 #pragma unroll
                     for (int r = 0; r < BR; r++) bf[j][r] = sB[(kk + tig + 4 * r) * S::BS + wn + j * 8 + g];
 #pragma unroll
-                for (int i = 0; i < 4; i++)
+                for (int i = 0; i < MI; i++)
 #pragma unroll
-                    for (int j = 0; j < 4; j++)
+                    for (int j = 0; j < NJ; j++)
                         dmma<MK>(*reinterpret_cast<double(*)[4]>(acc[i][j]), af[i], bf[j]);
             }
         } else {
 #pragma unroll
             for (int kk = 0; kk < BK; kk += 8) {
-                unsigned ahi[4][4], alo[4][4], bhi[4][2], blo[4][2];
+                unsigned ahi[MI][4], alo[MI][4], bhi[NJ][2], blo[NJ][2];
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
+                for (int i = 0; i < MI; i++) {
                     const float* pa = reinterpret_cast<const float*>(sA) + (wm + i * 16 + g) * S::AS + kk + tig;
                     float x[4] = {pa[0], pa[8 * S::AS], pa[4], pa[8 * S::AS + 4]};
 #pragma unroll
@@ -278,7 +299,7 @@ __device__ __forceinline__ void gemm_mainloop(const GemmP<T>& P, const T* __rest
                     }
                 }
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
+                for (int j = 0; j < NJ; j++) {
                     const float* pb = reinterpret_cast<const float*>(sB) + (kk + tig) * S::BS + wn + j * 8 + g;
                     float x[2] = {pb[0], pb[4 * S::BS]};
 #pragma unroll
@@ -288,9 +309,9 @@ __device__ __forceinline__ void gemm_mainloop(const GemmP<T>& P, const T* __rest
                     }
                 }
 #pragma unroll
-                for (int i = 0; i < 4; i++)
+                for (int i = 0; i < MI; i++)
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
+                    for (int j = 0; j < NJ; j++) {
                         float(&d)[4] = *reinterpret_cast<float(*)[4]>(acc[i][j]);
                         tmma_16x8x8(d, alo[i], bhi[j]);
                         tmma_16x8x8(d, ahi[i], blo[j]);
@@ -303,40 +324,41 @@ __device__ __forceinline__ void gemm_mainloop(const GemmP<T>& P, const T* __rest
     __syncthreads();  // the caller may reuse smem or start another tile
 }
 
-template <typename T>
-__device__ __forceinline__ void zero_acc(T (&acc)[4][4][4]) {
+template <typename T, int MI, int NJ>
+__device__ __forceinline__ void zero_acc(T (&acc)[MI][NJ][4]) {
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < MI; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++)
+        for (int j = 0; j < NJ; j++)
 #pragma unroll
             for (int e = 0; e < 4; e++) acc[i][j][e] = T(0);
 }
 
 // Data-parallel kernel: CTA b computes linear tile tile_base + b over its
 // whole K and writes C (bounds-checked).
-template <typename T, int BK, int MK = 4>
-__global__ void __launch_bounds__(NTH, 1) k_gemm(GemmP<T> P, long long tile_base) {
+template <class S, int MK = 4, typename T = typename S::type>
+__global__ void __launch_bounds__(S::NTH, S::MINB) k_gemm(GemmP<T> P, long long tile_base) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T* smem = reinterpret_cast<T*>(smem_raw);
-    const TileAt ta = tile_at(P, tile_base + blockIdx.x);
+    constexpr int MI = S::MI, NJ = S::NJ;
+    const TileAt ta = tile_at<T, S::BM, S::BN>(P, tile_base + blockIdx.x);
     const T* A;
     const T* B;
     int K;
     operands_at(P, ta.z, A, B, K);
     T* __restrict__ C = P.C + ta.z * P.sC;
-    T acc[4][4][4];
+    T acc[MI][NJ][4];
     zero_acc(acc);
-    gemm_mainloop<T, BK, MK>(P, A, B, K, ta.m0, ta.n0, 0, (K + BK - 1) / BK, smem, acc);
+    gemm_mainloop<S, MK>(P, A, B, K, ta.m0, ta.n0, 0, (K + S::BK - 1) / S::BK, smem, acc);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, tig = lane & 3;
-    const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
+    const int wm = (warp / S::WARPS_N) * (MI * 16), wn = (warp % S::WARPS_N) * (NJ * 8);
     const int M = P.M, N = P.N, ldc = P.ldc;
     // accumulator (i, j): c0,c1 at (g, 2tig..2tig+1), c2,c3 at (g+8, 2tig..)
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < MI; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
+        for (int j = 0; j < NJ; j++) {
             const int col = ta.n0 + wn + j * 8 + 2 * tig;
 #pragma unroll
             for (int h = 0; h < 2; h++) {
@@ -377,6 +399,7 @@ __host__ __device__ inline long long sk_lo(long long p, long long W, int G) { re
 template <typename T, int BK, int MK = 4>
 __global__ void __launch_bounds__(NTH, 1)
 k_gemm_sk(GemmP<T> P, long long tile_base, long long W, int G, int KT, T* __restrict__ ws) {
+    using S = Cfg<T, BK>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T* smem = reinterpret_cast<T*>(smem_raw);
     const int p = blockIdx.x;
@@ -396,7 +419,7 @@ k_gemm_sk(GemmP<T> P, long long tile_base, long long W, int G, int KT, T* __rest
         operands_at(P, ta.z, A, B, K);
         T acc[4][4][4];
         zero_acc(acc);
-        gemm_mainloop<T, BK, MK>(P, A, B, K, ta.m0, ta.n0, kt0, kt1, smem, acc);
+        gemm_mainloop<S, MK>(P, A, B, K, ta.m0, ta.n0, kt0, kt1, smem, acc);
         T* dst = ws + ((size_t)p * 2 + slot) * (BM * BN);
 #pragma unroll
         for (int i = 0; i < 4; i++)
@@ -502,7 +525,8 @@ int run_gemm_p(Ctx& c, GemmP<T> P) {
     constexpr int EPC = 16 / sizeof(T);
     P.vecA = ((uintptr_t)P.A % 16 == 0) && (P.lda % EPC == 0) && (P.ksplit % EPC == 0);
     P.vecB = ((uintptr_t)P.B % 16 == 0) && (P.ldb % EPC == 0);
-    size_t smem = Smem<T, BK>::BYTES;
+    using S = Cfg<T, BK>;
+    size_t smem = S::BYTES;
     const long long tiles = (long long)((P.M + BM - 1) / BM) * ((P.N + BN - 1) / BN) * P.batch;
     if (tiles <= 0) return finish(c);
     if (tiles > 0x7fffffffLL) {
@@ -512,10 +536,10 @@ int run_gemm_p(Ctx& c, GemmP<T> P) {
     const int KT = (P.K + BK - 1) / BK;
     const SkPlan pl = P.ksplit == 0 ? gemm_sk_plan(tiles, KT, c.dev->sm_count, 6) : SkPlan{};
     if (pl.tail == 0) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm<T, BK, MK>,
+        cudaError_t e = cudaFuncSetAttribute(k_gemm<S, MK>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
-        k_gemm<T, BK, MK><<<(unsigned)tiles, NTH, smem, c.stream>>>(P, 0);
+        k_gemm<S, MK><<<(unsigned)tiles, NTH, smem, c.stream>>>(P, 0);
         count_launch();
         return finish(c);
     }
@@ -524,14 +548,14 @@ int run_gemm_p(Ctx& c, GemmP<T> P) {
     ScratchGuard guard(c);
     T* ws = (T*)scratch(c, (size_t)G * 2 * BM * BN * sizeof(T), kScratchGemm);
     if (!ws) return E_CUDA;
-    cudaError_t e = cudaFuncSetAttribute(k_gemm<T, BK, MK>,
+    cudaError_t e = cudaFuncSetAttribute(k_gemm<S, MK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_gemm_sk<T, BK, MK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
     if (dp > 0) {
-        k_gemm<T, BK, MK><<<(unsigned)dp, NTH, smem, c.stream>>>(P, 0);
+        k_gemm<S, MK><<<(unsigned)dp, NTH, smem, c.stream>>>(P, 0);
         count_launch();
     }
     k_gemm_sk<T, BK, MK><<<G, NTH, smem, c.stream>>>(P, dp, W, G, KT, ws);
@@ -582,7 +606,38 @@ int dmma_cfg() {
     return 3204;
 }
 
+// f64 products run on the 64 x 64 tile (Small64) unless NXV_GEMM_TILE=128
+// selects the 128 x 128 schedule with its stream-K tail.  Measured on B200
+// (TF/s, 64 x 64 / 128 x 128 / cuBLAS): 64 x 256^3 batched 28.1 / 23.6 / 29.4;
+// 256 x 128^3 24.5 / 20.5 / 24.9; 1024^3 26.0 / 23.5 / 26.1; 2048^3 31.9 /
+// 30.3 / 33.7; 4096^3 33.3 / 32.0 / 35.4; 3000 x 3000 x 512 30.5 / 26.3 /
+// 32.1; 256 x 10000 x 104 18.4 / 10.0 / 19.8; 8 x 512^3 24.4 / 25.3 / 27.1.
+bool small64_pick() {
+    const char* v = getenv("NXV_GEMM_TILE");
+    return !(v && strcmp(v, "128") == 0);
+}
+
+int run_gemm_small(Ctx& c, GemmP<double> P) {
+    using S = Small64;
+    constexpr int EPC = 2;
+    P.vecA = ((uintptr_t)P.A % 16 == 0) && (P.lda % EPC == 0) && (P.ksplit % EPC == 0);
+    P.vecB = ((uintptr_t)P.B % 16 == 0) && (P.ldb % EPC == 0);
+    const long long tiles = (long long)((P.M + S::BM - 1) / S::BM) * ((P.N + S::BN - 1) / S::BN) * P.batch;
+    if (tiles <= 0) return finish(c);
+    if (tiles > 0x7fffffffLL) {
+        set_error("matmul grid out of range");
+        return E_ARG;
+    }
+    cudaError_t e = cudaFuncSetAttribute(k_gemm<S, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)S::BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm 64x64)");
+    k_gemm<S, 4><<<(unsigned)tiles, S::NTH, S::BYTES, c.stream>>>(P, 0);
+    count_launch();
+    return finish(c);
+}
+
 int gemm_f64_dispatch(Ctx& c, const GemmP<double>& P) {
+    if (small64_pick()) return run_gemm_small(c, P);
     switch (dmma_cfg()) {
         case 1608: return run_gemm_p<double, 16, 8>(c, P);
         case 1616: return run_gemm_p<double, 16, 16>(c, P);

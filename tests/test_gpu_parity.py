@@ -575,8 +575,10 @@ def test_matmul_f32_tensor_core_vs_oracle_and_mma(nxv, orc, monkeypatch, bmnk):
 @pytest.mark.parametrize("cfg", ["16x4", "16x8", "16x16", "32x4", "32x8", "32x16"])
 @pytest.mark.parametrize("bmnk", [(1, 130, 70, 257), (2, 256, 256, 100), (1, 33, 200, 17)])
 def test_matmul_f64_dmma_shapes(nxv, orc, monkeypatch, cfg, bmnk):
-    """Every DMMA configuration (k-tile x MMA K-shape) against the oracle."""
+    """Every DMMA configuration (k-tile x MMA K-shape) of the 128 x 128 tile
+    against the oracle."""
     monkeypatch.setenv("NXV_DMMA", cfg)
+    monkeypatch.setenv("NXV_GEMM_TILE", "128")
     batch, m, n, k = bmnk
     r = np.random.default_rng(12)
     a, b = r.normal(size=batch * m * k), r.normal(size=batch * k * n)
@@ -592,13 +594,17 @@ def test_matmul_f64_dmma_shapes(nxv, orc, monkeypatch, cfg, bmnk):
                                   (1, 2304, 1152, 320), (1, 100, 120, 3000)])
 def test_matmul_f64_stream_k(nxv, orc, monkeypatch, bmnk):
     """Tile counts that leave a partial last wave run their tail as stream-K
-    (k-ranges split evenly over the SMs, partials summed in k order).  The
-    result is within the f64 bound, identical bit for bit on a second call,
-    and within the bound of the plain data-parallel schedule (NXV_GEMM_SK=0)."""
+    (k-ranges split evenly over the SMs, partials summed in k order) on the
+    128 x 128 schedule (NXV_GEMM_TILE=128).  The result is within the f64
+    bound, identical bit for bit on a second call, and within the bound of
+    the plain data-parallel schedule (NXV_GEMM_SK=0) and of the default
+    64 x 64 tiles."""
     batch, m, n, k = bmnk
     r = np.random.default_rng(13)
     a, b = r.normal(size=batch * m * k), r.normal(size=batch * k * n)
     ta, tb = up(nxv, a), up(nxv, b)
+    small = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f64")), np.float64)
+    monkeypatch.setenv("NXV_GEMM_TILE", "128")
     got = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f64")), np.float64)
     again = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f64")), np.float64)
     assert np.array_equal(got, again)
@@ -611,6 +617,29 @@ def test_matmul_f64_stream_k(nxv, orc, monkeypatch, bmnk):
     tol = 1e-12 * np.abs(want) + 2 * k * 2.2e-16 * bound
     assert np.all(np.abs(got - want) <= tol)
     assert np.all(np.abs(plain - want) <= tol)
+    assert np.all(np.abs(small - want) <= tol)
+
+
+@pytest.mark.parametrize("bmnk", [(1, 1, 1, 1), (1, 33, 200, 17), (2, 65, 129, 31), (5, 64, 64, 64),
+                                  (1, 300, 1, 7), (3, 100, 120, 3000), (64, 256, 256, 256),
+                                  (1, 256, 10000, 104)])
+def test_matmul_f64_tile64(nxv, orc, bmnk):
+    """The default f64 tile (64 x 64, three CTAs per SM): ragged edges, odd K
+    (rows not 16-byte aligned: the scalar loader), deep K, many batches and
+    the batched and logistic-gradient shapes, within the f64 bound and
+    identical bit for bit on a second call."""
+    batch, m, n, k = bmnk
+    r = np.random.default_rng(14)
+    a, b = r.normal(size=batch * m * k), r.normal(size=batch * k * n)
+    ta, tb = up(nxv, a), up(nxv, b)
+    got = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f64")), np.float64)
+    again = down(nxv, unwrap(nxv.matmul_batched(ta, tb, batch, m, n, k, "f64")), np.float64)
+    assert np.array_equal(got, again)
+    want = orc.matmul(a, b, m, n, k, batch=batch)
+    bound = np.concatenate([
+        (np.abs(a.reshape(batch, m, k)[q]) @ np.abs(b.reshape(batch, k, n)[q])).reshape(-1)
+        for q in range(batch)])
+    assert np.all(np.abs(got - want) <= 1e-12 * np.abs(want) + 2 * k * 2.2e-16 * bound)
 
 
 @pytest.mark.parametrize("bmnk", [(1, 100, 120, 3000), (1, 500, 400, 4000), (2, 256, 256, 2048),
