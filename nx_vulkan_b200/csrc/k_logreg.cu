@@ -490,9 +490,9 @@ k_lr_resid(double* __restrict__ Z, const double* __restrict__ y, size_t n_obs, d
 
 constexpr int kFT = 1024;  // fold threads per chain (10 slice groups of a 100-dim chain)
 
-// In-order sum of a[t * stride] for t in [t0, t1), t1 > t0, with 8 loads in
-// flight (the partials come from L2; a dependent chain of loads would leave
-// the fold latency-bound).
+// In-order sum of a[t * stride] for t in [t0, t1), t1 > t0: the loads of a
+// block of 8 are all issued before its additions (the partials come from L2;
+// a load behind each addition would leave the fold latency-bound).
 // COH: the data were written earlier in the same (persistent) kernel by other
 // CTAs: load through L2 (ld.global.cg), never from a non-coherent cache.
 template <bool COH>
@@ -504,16 +504,16 @@ __device__ __forceinline__ double ld_part(const double* p) {
 template <bool COH = false>
 __device__ __forceinline__ double sum_rows(const double* __restrict__ a, size_t stride, int t0,
                                            int t1) {
-    double s = ld_part<COH>(a + (size_t)t0 * stride);
-    int t = t0 + 1;
-    for (; t + 8 <= t1; t += 8) {
+    double s = 0.0;
+    for (int t = t0; t < t1; t += 8) {
         double v[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++) v[u] = ld_part<COH>(a + (size_t)(t + u) * stride);
+        for (int u = 0; u < 8; u++)
+            v[u] = t + u < t1 ? ld_part<COH>(a + (size_t)(t + u) * stride) : 0.0;
 #pragma unroll
-        for (int u = 0; u < 8; u++) s = add_(s, v[u]);
+        for (int u = 0; u < 8; u++)
+            if (t + u < t1) s = t + u == t0 ? v[u] : add_(s, v[u]);
     }
-    for (; t < t1; t++) s = add_(s, ld_part<COH>(a + (size_t)t * stride));
     return s;
 }
 
@@ -534,6 +534,25 @@ __device__ __forceinline__ void lr_fold_chain(
     double* gc, double* logp, double* fold_sm, double* sm) {
     __syncthreads();  // fold_sm and sm may still be read for the previous chain
     const double* pc0 = part + (size_t)c * D;
+    // this thread's position and momentum (D <= blockDim.x in the fused
+    // path), loaded while the partials are summed
+    const bool one = D <= blockDim.x && threadIdx.x < D;
+    const double q_pre = one ? q[(size_t)c * D + threadIdx.x] : 0.0;
+    const double p_pre = one ? p[(size_t)c * D + threadIdx.x] : 0.0;
+    // and the chain's logp partials (lane j: j, j + 32, j + 64, ...)
+    double l = 0.0;
+    if (write_step && threadIdx.x < 32) {
+        const double* lp = lpart + (size_t)c * nblk;
+        for (unsigned j0 = threadIdx.x; j0 < nblk; j0 += 4 * 32) {
+            double v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                v[u] = j0 + 32 * u < nblk ? ld_part<COH>(lp + j0 + 32 * u) : 0.0;
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (j0 + 32 * u < nblk) l = add_(l, v[u]);
+        }
+    }
     if (H > 1) {
         const unsigned tid = threadIdx.x;
         if (tid < (unsigned)H * D) {
@@ -553,10 +572,10 @@ __device__ __forceinline__ void lr_fold_chain(
         } else {
             s = sum_rows<COH>(pc0 + i, CD, 0, S);
         }
-        double qi = q[o];
+        double qi = one ? q_pre : q[o];
         double gi = sub_(s, qi);
         qq = add_(qq, mul_(qi, qi));
-        double pi = p[o];
+        double pi = one ? p_pre : p[o];
         if (write_step) {
             pi = add_(pi, mul_(he, gi));
             size_t row = ((size_t)c * K + k) * D + i;
@@ -577,14 +596,10 @@ __device__ __forceinline__ void lr_fold_chain(
     if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = qq;
     __syncthreads();
     if (threadIdx.x < 32) {
-        // the chain's logp partials: lane j sums partials j, j + 32, ... (a
-        // few loads in flight per lane instead of one thread's dependent
-        // chain), then a fixed shuffle tree; the order is the same on every
-        // call, so the result is deterministic
+        // the chain's logp partials: lane j summed partials j, j + 32, ...
+        // above (their loads issued together), then a fixed shuffle tree; the
+        // order is the same on every call, so the result is deterministic
         const unsigned lane = threadIdx.x;
-        const double* lp = lpart + (size_t)c * nblk;
-        double l = 0.0;
-        for (unsigned j = lane; j < nblk; j += 32) l = add_(l, ld_part<COH>(lp + j));
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) l = add_(l, __shfl_down_sync(0xffffffffu, l, off));
         if (lane == 0) {
