@@ -1359,25 +1359,33 @@ def suite(args):
         r = np.random.default_rng(3)
         prec = r.uniform(0.5, 2.0, 100)
         tg = nuts.GaussianTarget(prec)
-        dt = nuts.DeviceTree(tg, np.ones(100), 0.05)
-        qd = torch.from_numpy(r.normal(size=(Cn, 100)) / np.sqrt(prec)).to(dev)
-        rng = np.random.default_rng(4)
-        qd, _ = dt.transition(qd, rng, max_depth=8)  # warm-up
-        torch.cuda.synchronize()
-        depths, t0 = [], time.perf_counter()
-        for _ in range(Tn):
-            qd, st = dt.transition(qd, rng, max_depth=8)
-            depths.append(float(st.depth.mean()))
-        torch.cuda.synchronize()
-        el_d = time.perf_counter() - t0
-        emit(workload="NUTS transitions, 256 chains, Gaussian d=100, eps=0.05, max depth 8, "
-                      "tree walk on the device",
-             dtype="float64", us_per_call=el_d / Tn * 1e6, transitions_per_s=Cn * Tn / el_d,
-             mean_tree_depth=statistics.mean(depths),
-             speedup_over_host_tree=el / Tn / (el_d / Tn),
-             note="leaves written by the chain calls into a device store and walked there "
-                  "(nxv_nuts_energy/_start/_level); the host keeps the row bookkeeping, draws "
-                  "the random numbers and reads one active flag per chain and level")
+        q_start = r.normal(size=(Cn, 100)) / np.sqrt(prec)
+        for driver in ("layout", "host"):
+            dt = nuts.DeviceTree(tg, np.ones(100), 0.05, driver=driver)
+            qd = torch.from_numpy(q_start).to(dev)
+            rng = np.random.default_rng(4)
+            qd, _ = dt.transition(qd, rng, max_depth=8)  # warm-up
+            torch.cuda.synchronize()
+            depths, t0 = [], time.perf_counter()
+            for _ in range(Tn):
+                qd, st = dt.transition(qd, rng, max_depth=8)
+                depths.append(float(st.depth.mean()))
+            torch.cuda.synchronize()
+            el_d = time.perf_counter() - t0
+            note = ("momenta and uniforms drawn by Philox on the device, tree state on the device, "
+                    "every chain's leaves at fixed store rows: per level one start kernel, one "
+                    "chain call of 2^l steps for all chains and one level kernel "
+                    "(nxv_nuts_start_layout/_level_layout); the host reads one flag per level"
+                    if driver == "layout" else
+                    "leaves written by the chain calls into a device store and walked there "
+                    "(nxv_nuts_energy/_start/_level); the host keeps the row bookkeeping "
+                    "(speculative extension), draws the random numbers and reads one active "
+                    "flag per chain and level")
+            emit(workload="NUTS transitions, 256 chains, Gaussian d=100, eps=0.05, max depth 8, "
+                          f"tree walk on the device ({driver} driver)",
+                 dtype="float64", us_per_call=el_d / Tn * 1e6, transitions_per_s=Cn * Tn / el_d,
+                 mean_tree_depth=statistics.mean(depths),
+                 speedup_over_host_tree=el / Tn / (el_d / Tn), note=note)
         lib.nxv_set_stream(C.c_void_p(stream.cuda_stream))
 
     for h in handles:

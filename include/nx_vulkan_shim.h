@@ -402,7 +402,7 @@ int nxv_leapfrog_logreg_f64_batched(void* q_chain, void* p_chain,
 /* ---- NUTS tree builder on the device (NEW) ------------------------------
  * eXMC's NUTS tree builder (an external repository; its call site is
  * PLAN_FUSED_LEAPFROG.md:331-358) walks the leaves that the fused chain
- * returns.  These three calls do that walk on the device, over a leaf store
+ * returns.  These calls do that walk on the device, over a leaf store
  * that the batched Gaussian chain (_ke variant) writes into, so the
  * trajectories never leave the GPU; the caller keeps the row bookkeeping
  * and draws the random numbers.  Store rows hold q, p (p in its
@@ -438,6 +438,35 @@ int nxv_nuts_level(void* rows, void* chain, void* fwd, void* u_sel, void* u_move
                    void* H0, void* logw, void* rho, void* end_p, void* end_ps,
                    void* sample, void* active, void* divergent, void* node,
                    unsigned int n_chains);
+
+/* Device-driven levels: the tree's state stays on the device and every
+ * chain's level-l leaves sit at fixed store rows base_row + c n + i
+ * (i < n = 2^l, in integration order; base_row = n_chains (2^l - 1) when the
+ * levels are stacked), so that a driver launches one start, one chain call
+ * into those rows and one level call per level without reading anything
+ * back but the active flags.  u: [3][n_chains] uniforms of the level --
+ * direction (forward when >= 0.5), leaf, move.  end_row: [2][n_chains]
+ * int64 store row of each tree's left / right end leaf, -1 for the initial
+ * point. */
+
+/* Starting points of level u_dir's extension for every chain: the end
+ * leaf on the chosen side, or (q0[c], +-p0[c]) while that side has none;
+ * written to qs, ps [n_chains][d]. */
+int nxv_nuts_start_layout(void* qs, void* ps, void* q0, void* p0, void* st_q, void* st_p,
+                          void* end_row, void* u_dir, unsigned int n_chains,
+                          unsigned int d);
+
+/* One level for every chain still building (active[c] = 1): the walk of
+ * nxv_nuts_level over rows base_row + c n .. + n - 1 (reversed in time for a
+ * backward extension), then end_row of that side, depth[c] = level + 1 and
+ * n_leapfrog[c] += n (int32).  node: [n_chains][n][d] f64 scratch.  -3 also
+ * when the store holds fewer than base_row + n_chains n rows. */
+int nxv_nuts_level_layout(unsigned long long base_row, unsigned int n, unsigned int d,
+                          void* u, void* st_q, void* st_p, void* st_logp, void* st_ke,
+                          void* inv_mass, void* H0, void* logw, void* rho, void* end_p,
+                          void* end_ps, void* sample, void* active, void* divergent,
+                          void* end_row, void* depth, void* n_leapfrog, void* node,
+                          unsigned int n_chains, unsigned int level);
 
 /* ---- Devices, streams, interop (NEW) ----------------------------------- */
 

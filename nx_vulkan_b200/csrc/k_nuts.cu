@@ -7,9 +7,13 @@
 // the biased move into the subtree (Betancourt 2017, "A Conceptual
 // Introduction to Hamiltonian Monte Carlo", A.3-A.4).  These kernels do that
 // walk where the leaves are -- in a device store that the chain calls write
-// into -- so that no trajectory crosses PCIe; the host keeps only the
-// bookkeeping of which stored rows are the next leaves of each chain and
-// draws the random numbers (the same stream as the host tree builder).
+// into -- so that no trajectory crosses PCIe.  Two drivers: nxv_nuts_start /
+// nxv_nuts_level take the store rows of each active chain's next leaves from
+// a host that keeps that bookkeeping (speculative extension, as eXMC calls
+// the chain); nxv_nuts_start_layout / nxv_nuts_level_layout keep the tree
+// ends, depth and leaf counts on the device, with every chain's level-l
+// leaves at fixed store rows, so that a host only launches one start, one
+// chain call and one level kernel per level and reads one flag.
 //
 // Store: q, p (p in the sign it was integrated with: negated for backward
 // leaves), logp and kinetic energy per row; H = -logp + KE.
@@ -18,6 +22,8 @@
 #include "ops_common.cuh"
 
 #include <math.h>
+
+#include <algorithm>
 
 namespace nxv {
 namespace {
@@ -90,23 +96,24 @@ struct LevelArgs {
 //   ps_first . rho > 0 and ps_last . rho > 0 (rho = rho_A + rho_B),
 //   (rho_A + p_B,first) against ps_A,first and ps_B,first,
 //   (rho_B + p_A,last) against ps_A,last and ps_B,last.
-__global__ void __launch_bounds__(kNT) k_nuts_level(LevelArgs a) {
+// The walk of chain c over its level's leaves rows(0) .. rows(n - 1) (time
+// order); nd: the chain's [n][d] node scratch.
+template <class Rows>
+__device__ __forceinline__ void level_walk(const LevelArgs& a, int c, bool fwd, double u_sel,
+                                           double u_move, double* nd, Rows rows) {
     __shared__ double h[kMaxLeaves];
     __shared__ double cs[kMaxLeaves];
     __shared__ double red[8][kNW];
     __shared__ int s_ok, s_sel;
-    const int slot = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int c = a.chain[slot], n = a.n, d = a.d;
-    const bool fwd = a.fwd[slot] != 0;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n = a.n, d = a.d;
     const double sg = fwd ? 1.0 : -1.0;  // backward leaves were integrated with -p
-    const long long* rows = a.rows + (size_t)slot * n;
-    double* nd = a.node + (size_t)slot * n * d;
     const double H0 = a.H0[c];
 
     // H of every leaf, divergence (NaN counts as divergent)
     int div_l = 0;
     for (int j = tid; j < n; j += kNT) {
-        const long long r = rows[j];
+        const long long r = rows(j);
         const double hj = sub_(a.st_ke[r], a.st_logp[r]);
         h[j] = hj;
         if (!(sub_(hj, H0) <= kMaxDeltaH)) div_l = 1;
@@ -115,7 +122,7 @@ __global__ void __launch_bounds__(kNT) k_nuts_level(LevelArgs a) {
 
     // leaf momenta into the node sums
     for (int j = warp; j < n; j += kNW) {
-        const double* src = a.st_p + (size_t)rows[j] * d;
+        const double* src = a.st_p + (size_t)rows(j) * d;
         for (int i = lane; i < d; i += 32) nd[(size_t)j * d + i] = mul_(sg, src[i]);
     }
     if (tid == 0) s_ok = 1;
@@ -124,10 +131,10 @@ __global__ void __launch_bounds__(kNT) k_nuts_level(LevelArgs a) {
         const int half = size / 2;
         for (int t = warp; t < n / size; t += kNW) {
             const int a0 = t * size, mid = a0 + half, b1 = a0 + size - 1;
-            const double* pf = a.st_p + (size_t)rows[a0] * d;
-            const double* pal = a.st_p + (size_t)rows[mid - 1] * d;
-            const double* pbf = a.st_p + (size_t)rows[mid] * d;
-            const double* pl = a.st_p + (size_t)rows[b1] * d;
+            const double* pf = a.st_p + (size_t)rows(a0) * d;
+            const double* pal = a.st_p + (size_t)rows(mid - 1) * d;
+            const double* pbf = a.st_p + (size_t)rows(mid) * d;
+            const double* pl = a.st_p + (size_t)rows(b1) * d;
             double s[6] = {0, 0, 0, 0, 0, 0};
             for (int i = lane; i < d; i += 32) {
                 const double mi = a.m[i];
@@ -184,7 +191,7 @@ __global__ void __launch_bounds__(kNT) k_nuts_level(LevelArgs a) {
         s_sel = n - 1;
     }
     __syncthreads();
-    const double tot = red[1][0], target = mul_(a.u_sel[slot], tot);
+    const double tot = red[1][0], target = mul_(u_sel, tot);
     for (int j = j0; j < j1; j++) {
         const double cdf = add_(cs[j], chunk[tid]);
         if (!(cdf < target)) {
@@ -196,9 +203,9 @@ __global__ void __launch_bounds__(kNT) k_nuts_level(LevelArgs a) {
     const int sel = s_sel;
     const double logw_sub = add_(wmax, log(tot));
     const double logw_old = a.logw[c];
-    const bool move = a.u_move[slot] < exp(fmin(0.0, sub_(logw_sub, logw_old)));
+    const bool move = u_move < exp(fmin(0.0, sub_(logw_sub, logw_old)));
     if (ok_sub && move) {
-        const double* src = a.st_q + (size_t)rows[sel] * d;
+        const double* src = a.st_q + (size_t)rows(sel) * d;
         for (int i = tid; i < d; i += kNT) a.sample[(size_t)c * d + i] = src[i];
     }
 
@@ -210,8 +217,8 @@ __global__ void __launch_bounds__(kNT) k_nuts_level(LevelArgs a) {
     const double* lps = a.end_ps + (size_t)c * d;
     const double* rp = a.end_p + CD + (size_t)c * d;   // tree, right end
     const double* rps = a.end_ps + CD + (size_t)c * d;
-    const double* p_first = a.st_p + (size_t)rows[0] * d;
-    const double* p_last = a.st_p + (size_t)rows[n - 1] * d;
+    const double* p_first = a.st_p + (size_t)rows(0) * d;
+    const double* p_last = a.st_p + (size_t)rows(n - 1) * d;
     double s[6] = {0, 0, 0, 0, 0, 0};
     for (int i = tid; i < d; i += kNT) {
         const double mi = a.m[i];
@@ -259,6 +266,43 @@ __global__ void __launch_bounds__(kNT) k_nuts_level(LevelArgs a) {
     }
 }
 
+// One CTA per active slot: store rows, chain, direction and uniforms from
+// the host.
+__global__ void __launch_bounds__(kNT) k_nuts_level(LevelArgs a) {
+    const int slot = blockIdx.x;
+    const long long* rows = a.rows + (size_t)slot * a.n;
+    level_walk(a, a.chain[slot], a.fwd[slot] != 0, a.u_sel[slot], a.u_move[slot],
+               a.node + (size_t)slot * a.n * a.d, [rows](int j) { return rows[j]; });
+}
+
+// Device-driven levels: every chain's n leaves of this level are store rows
+// base + c n .. base + c n + n - 1 in integration order; u[0][C] decides
+// the direction (forward when >= 0.5), u[1][C] the leaf and u[2][C] the
+// move.  One CTA per chain; chains whose tree has stopped return at once.
+struct LayoutArgs {
+    long long base;
+    const double* u;       // [3][C] uniforms of this level
+    long long* end_row;    // [2][C] store row of the tree's left / right end leaf (-1: the start)
+    int* depth;            // [C]
+    int* n_leapfrog;       // [C]
+    int level;
+};
+
+__global__ void __launch_bounds__(kNT) k_nuts_level_layout(LevelArgs a, LayoutArgs L) {
+    const int c = blockIdx.x, n = a.n, C = a.C;
+    if (a.active[c] == 0) return;
+    const bool fwd = L.u[c] >= 0.5;
+    const long long first = L.base + (long long)c * n;
+    level_walk(a, c, fwd, L.u[C + c], L.u[2 * C + c], a.node + (size_t)c * n * a.d,
+               [first, fwd, n](int j) { return fwd ? first + j : first + (n - 1 - j); });
+    if (threadIdx.x == 0) {
+        // the last leaf integrated is the tree's new end on its side
+        L.end_row[(fwd ? C : 0) + c] = first + n - 1;
+        L.depth[c] = L.level + 1;
+        L.n_leapfrog[c] += n;
+    }
+}
+
 // H0 = -logp(q) + KE(p) for the Gaussian target, logp(q) = -0.5 sum
 // prec (q - mu)^2 + logp_const; one warp per chain.
 __global__ void __launch_bounds__(kNT) k_nuts_energy(double* H0, const double* q, const double* p,
@@ -294,6 +338,32 @@ __global__ void __launch_bounds__(kNT) k_nuts_start(double* qs, double* ps, cons
         } else {
             qs[(size_t)i * d + k] = q0[(size_t)c * d + k];
             ps[(size_t)i * d + k] = mul_((double)dir[i], p0[(size_t)c * d + k]);
+        }
+    }
+}
+
+// Starting points of a device-driven level: chain c continues from its
+// tree's end leaf on the side u_dir[c] picks (the initial point (q0, +-p0)
+// while that side has none).
+__global__ void __launch_bounds__(kNT) k_nuts_start_layout(double* qs, double* ps,
+                                                           const double* q0, const double* p0,
+                                                           const double* st_q, const double* st_p,
+                                                           const long long* end_row,
+                                                           const double* u_dir, int C, int d,
+                                                           long long st_rows) {
+    const int c = blockIdx.x;
+    const bool fwd = u_dir[c] >= 0.5;
+    long long r = end_row[(fwd ? C : 0) + c];
+    if (r >= st_rows) r = -1;  // not a row of this store: restart from the initial point
+    const double sg = fwd ? 1.0 : -1.0;
+    for (int k = threadIdx.x; k < d; k += kNT) {
+        const size_t o = (size_t)c * d + k;
+        if (r >= 0) {
+            qs[o] = st_q[(size_t)r * d + k];
+            ps[o] = st_p[(size_t)r * d + k];
+        } else {
+            qs[o] = q0[o];
+            ps[o] = mul_(sg, p0[o]);
         }
     }
 }
@@ -410,6 +480,93 @@ int nxv_nuts_level(void* rows, void* chain, void* fwd, void* u_sel, void* u_move
     g.node = (double*)dptr(node);
     g.C = (int)C;
     k_nuts_level<<<(unsigned)A, kNT, 0, c.stream>>>(g);
+    count_launch();
+    return finish(c);
+}
+
+int nxv_nuts_start_layout(void* qs, void* ps, void* q0, void* p0, void* st_q, void* st_p,
+                          void* end_row, void* u_dir, unsigned int n_chains, unsigned int d) {
+    if (!qs || !ps || !q0 || !p0 || !st_q || !st_p || !end_row || !u_dir) return E_NULL;
+    Ctx c;
+    int rc = begin(c, {qs, ps, q0, p0, st_q, st_p, end_row, u_dir});
+    if (rc) return rc;
+    const size_t CD = (size_t)n_chains * d * 8;
+    if (!holds(qs, CD) || !holds(ps, CD) || !holds(q0, CD) || !holds(p0, CD) ||
+        !holds(end_row, (size_t)n_chains * 16) || !holds(u_dir, (size_t)n_chains * 8)) {
+        set_error("nuts_start_layout: a buffer is smaller than its extent");
+        return E_ARG;
+    }
+    if (n_chains == 0 || d == 0) return OK;
+    // end rows are read only below the store's row count
+    const long long st_rows = (long long)std::min(nbytes(st_q), nbytes(st_p)) / ((long long)d * 8);
+    k_nuts_start_layout<<<n_chains, kNT, 0, c.stream>>>(
+        (double*)dptr(qs), (double*)dptr(ps), (const double*)dptr(q0), (const double*)dptr(p0),
+        (const double*)dptr(st_q), (const double*)dptr(st_p), (const long long*)dptr(end_row),
+        (const double*)dptr(u_dir), (int)n_chains, (int)d, st_rows);
+    count_launch();
+    return finish(c);
+}
+
+int nxv_nuts_level_layout(unsigned long long base_row, unsigned int n, unsigned int d, void* u,
+                          void* st_q, void* st_p, void* st_logp, void* st_ke, void* inv_mass,
+                          void* H0, void* logw, void* rho, void* end_p, void* end_ps,
+                          void* sample, void* active, void* divergent, void* end_row,
+                          void* depth, void* n_leapfrog, void* node, unsigned int n_chains,
+                          unsigned int level) {
+    if (!u || !st_q || !st_p || !st_logp || !st_ke || !inv_mass || !H0 || !logw || !rho ||
+        !end_p || !end_ps || !sample || !active || !divergent || !end_row || !depth ||
+        !n_leapfrog || !node)
+        return E_NULL;
+    if (n == 0 || n > (unsigned)kMaxLeaves || (n & (n - 1)) != 0) {
+        set_error("nuts_level_layout: n must be a power of two up to %d", kMaxLeaves);
+        return E_ARG;
+    }
+    Ctx c;
+    int rc = begin(c, {u, st_q, st_p, st_logp, st_ke, inv_mass, H0, logw, rho, end_p, end_ps,
+                       sample, active, divergent, end_row, depth, n_leapfrog, node});
+    if (rc) return rc;
+    const size_t C = n_chains, CD = C * d * 8;
+    if (!holds(u, 3 * C * 8) || !holds(inv_mass, (size_t)d * 8) || !holds(H0, C * 8) ||
+        !holds(logw, C * 8) || !holds(rho, CD) || !holds(end_p, 2 * CD) ||
+        !holds(end_ps, 2 * CD) || !holds(sample, CD) || !holds(active, C * 4) ||
+        !holds(divergent, C * 4) || !holds(end_row, 2 * C * 8) || !holds(depth, C * 4) ||
+        !holds(n_leapfrog, C * 4) || !holds(node, C * n * d * 8)) {
+        set_error("nuts_level_layout: a buffer is smaller than its extent");
+        return E_ARG;
+    }
+    if (C == 0 || d == 0) return OK;
+    const size_t rows_needed = (size_t)base_row + C * n;
+    if (!holds(st_logp, rows_needed * 8) || !holds(st_ke, rows_needed * 8) ||
+        !holds(st_q, rows_needed * d * 8) || !holds(st_p, rows_needed * d * 8)) {
+        set_error("nuts_level_layout: the store holds fewer than base_row + n_chains * n rows");
+        return E_ARG;
+    }
+    LevelArgs g{};
+    g.n = (int)n;
+    g.d = (int)d;
+    g.st_q = (const double*)dptr(st_q);
+    g.st_p = (const double*)dptr(st_p);
+    g.st_logp = (const double*)dptr(st_logp);
+    g.st_ke = (const double*)dptr(st_ke);
+    g.m = (const double*)dptr(inv_mass);
+    g.H0 = (const double*)dptr(H0);
+    g.logw = (double*)dptr(logw);
+    g.rho = (double*)dptr(rho);
+    g.end_p = (double*)dptr(end_p);
+    g.end_ps = (double*)dptr(end_ps);
+    g.sample = (double*)dptr(sample);
+    g.active = (int*)dptr(active);
+    g.divergent = (int*)dptr(divergent);
+    g.node = (double*)dptr(node);
+    g.C = (int)C;
+    LayoutArgs L;
+    L.base = (long long)base_row;
+    L.u = (const double*)dptr(u);
+    L.end_row = (long long*)dptr(end_row);
+    L.depth = (int*)dptr(depth);
+    L.n_leapfrog = (int*)dptr(n_leapfrog);
+    L.level = (int)level;
+    k_nuts_level_layout<<<(unsigned)C, kNT, 0, c.stream>>>(g, L);
     count_launch();
     return finish(c);
 }

@@ -34,8 +34,10 @@ and eXMC:
     the sum of exp(-H) over leaves, and within a subtree a leaf is chosen with
     probability proportional to exp(-H).
 
-The tree logic runs on the host in numpy: it touches 2^depth leaves per
-doubling, against 2^depth d-dimensional leapfrog steps per chain on the GPU.
+nuts_transition runs the tree logic on the host in numpy (it touches
+2^depth leaves per doubling, against 2^depth d-dimensional leapfrog steps
+per chain on the GPU); DeviceTree runs the same logic on the device over a
+leaf store that the chain calls write into.
 """
 from __future__ import annotations
 
@@ -276,17 +278,22 @@ class _Leaves:
         return flat
 
 
-def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth=10):
+def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth=10,
+                    p0=None, uniforms=None):
     """One NUTS transition for every chain of q0 [C, d]; returns (q, Stats).
 
     Leaves are drawn from `source` with speculative extension: all chains that
     need more steps at a tree level share one batched call of
     speculative_steps(2^depth) steps.  The tree logic is vectorized over the
-    chains that are still building."""
+    chains that are still building.  The momenta and the uniforms come from
+    `rng` (momenta first, then per level the directions of every chain and
+    the leaf and move uniforms of the chains still building), or are given:
+    p0 [C, d] and uniforms [max_depth][3][C] (direction, leaf, move of chain
+    c at each level), the draws DeviceTree makes on the device."""
     q0 = np.asarray(q0, np.float64)
     C, d = q0.shape
     m = np.asarray(inv_mass, np.float64)
-    p0 = rng.standard_normal((C, d)) / np.sqrt(m)
+    p0 = rng.standard_normal((C, d)) / np.sqrt(m) if p0 is None else np.asarray(p0, np.float64)
     H0 = -target.logp(q0) + 0.5 * ((p0 * p0) * m).sum(axis=-1)
     # per direction: the leaves beyond the initial point (kept on the source
     # between transitions, so the store's pages stay mapped)
@@ -315,7 +322,7 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
         if not active.any():
             break
         n_new = 1 << level
-        dirs = np.where(rng.random(C) < 0.5, -1, 1)
+        dirs = np.where((rng.random(C) if uniforms is None else uniforms[level, 0]) < 0.5, -1, 1)
         fwd_all = dirs > 0
         have = np.where(fwd_all, leaves[+1].have, leaves[-1].have)
         used = np.where(fwd_all, leaves[+1].used, leaves[-1].used)
@@ -369,9 +376,10 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
         tot = ew.sum(axis=1)
         logw_sub = wmax + np.log(tot)
         cdf = np.cumsum(ew, axis=1)
-        u = rng.random(A) * tot
+        u = (rng.random(A) if uniforms is None else uniforms[level, 1][act]) * tot
         j = np.minimum((cdf < u[:, None]).sum(axis=1), n_new - 1)
-        move = rng.random(A) < np.exp(np.minimum(0.0, logw_sub - logw[act]))
+        u_move = rng.random(A) if uniforms is None else uniforms[level, 2][act]
+        move = u_move < np.exp(np.minimum(0.0, logw_sub - logw[act]))
         take = ok_sub & move
         sample[act[take]] = store.q[rows[take, j[take]]]
         logw[act] = np.where(ok_sub, np.logaddexp(logw[act], logw_sub), logw[act])
@@ -399,20 +407,36 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
 
 
 class DeviceTree:
-    """The tree builder's walk on the device (nxv_nuts_energy / _start /
-    _level): the chain calls write their leaves into a device store and the
-    per-level logic runs over it, so the trajectories never cross PCIe.  The
-    host keeps the row bookkeeping (_Leaves) and draws the random numbers in
-    the order of nuts_transition, so with the same generator both take the
-    same draws (their sums run in different orders, so a decision within
-    rounding of a threshold can differ).  Gaussian targets, f64."""
+    """The tree builder's walk on the device over a leaf store that the chain
+    calls write into, so the trajectories never cross PCIe.  Gaussian
+    targets, f64.  Two drivers:
 
-    def __init__(self, target: GaussianTarget, inv_mass, eps: float):
+    * "layout" (default): everything per transition is drawn and kept on the
+      device -- momenta p0 = N(0, 1) / sqrt(inv_mass) and per-level uniforms
+      from the Philox generator (`randomness`), the tree ends, depth and leaf
+      counts -- and every chain's level-l leaves sit at fixed store rows.
+      Each level is one start kernel, one batched chain call of 2^l steps for
+      all chains and one level kernel (nxv_nuts_start_layout / _level_layout);
+      the host reads one flag per level (is any tree still growing).  With
+      the same momenta and uniforms, nuts_transition takes the same
+      decisions (the leaves are bit-identical: a chain restarted from a
+      stored leaf continues exactly as the uninterrupted integration).
+    * "host": the host keeps the row bookkeeping of nuts_transition
+      (speculative extension, as eXMC calls the chain) and draws from
+      `rng` in its order; only the walk (nxv_nuts_start / _level) runs on
+      the device."""
+
+    MAX_DEPTH = 12  # leaves per level up to 2^11 (the level kernel's limit)
+
+    def __init__(self, target: GaussianTarget, inv_mass, eps: float, driver: str = "layout",
+                 seed: int = 0):
         import torch
         from nx_vulkan_b200 import _native
         from nx_vulkan_b200 import vulkan as nxv
+        if driver not in ("layout", "host"):
+            raise ValueError(f"driver must be 'layout' or 'host', not {driver!r}")
         self.torch, self.nxv, self.lib = torch, nxv, _native.load()
-        self.t, self.eps = target, eps
+        self.t, self.eps, self.driver = target, eps, driver
         self.m = np.ascontiguousarray(inv_mass, np.float64)
         self.dev = torch.device("cuda", torch.cuda.current_device())
         f64 = dict(dtype=torch.float64, device=self.dev)
@@ -422,6 +446,7 @@ class DeviceTree:
         self.cap = 0           # store rows
         self.node_cap = 0      # f64 scratch elements
         self.calls = []
+        self.seed, self.count = seed & 0xFFFFFFFF, 0
 
     # -- device buffers -------------------------------------------------------------
     def _h(self, t, offset_elems=0, n_elems=None):
@@ -460,18 +485,115 @@ class DeviceTree:
         for h in hs:
             self.lib.nxv_buf_free(h)
 
-    def transition(self, q0, rng, max_depth=10):
+    @staticmethod
+    def keys(seed: int):
+        """Philox keys of a transition's momenta and of its uniforms."""
+        return seed & 0xFFFFFFFF, (seed ^ 0x5BD1E995) & 0xFFFFFFFF
+
+    def randomness(self, n_chains: int, seed: int, max_depth: int):
+        """The layout driver's draws for one transition, on the device:
+        p0 [C, d] = N(0, 1) / sqrt(inv_mass) (Philox normals, key keys(seed)[0],
+        element c d + i) and uniforms [max_depth][3][C] (key keys(seed)[1]):
+        per level the direction (forward when >= 0.5), the leaf and the move
+        uniform of every chain."""
+        torch, lib = self.torch, self.lib
+        d = self.m.size
+        kp, ku = self.keys(seed)
+        z = torch.empty(n_chains * d, **self.f64)
+        u = torch.empty(max_depth * 3 * n_chains, **self.f64)
+        hz, hu = self._h(z), self._h(u)
+        try:
+            self._call(lib.nxv_random_f64, hz, n_chains * d, kp, 1,
+                       self.nxv.shader_path("random_philox_f64.spv"))
+            self._call(lib.nxv_random_f64, hu, max_depth * 3 * n_chains, ku, 0,
+                       self.nxv.shader_path("random_philox_f64.spv"))
+        finally:
+            self._free(hz, hu)
+        p0 = z.view(n_chains, d) / torch.sqrt(self.m_dev)
+        return p0, u.view(max_depth, 3, n_chains)
+
+    def transition(self, q0, rng=None, max_depth=10, seed=None):
         """One NUTS transition for every chain of q0 [C, d] (a torch CUDA
         tensor or an array); returns (q as a torch CUDA tensor, Stats).  The
-        library runs on torch's current stream during the call (the state
-        tensors are torch's) and on its own stream again afterwards."""
+        layout driver draws with Philox key `seed` (by default one integer
+        from `rng`, or the tree's seed plus a transition count); the host
+        driver draws from `rng`.  The library runs on torch's current stream
+        during the call (the state tensors are torch's) and on its own stream
+        again afterwards."""
         import ctypes
+        if max_depth > self.MAX_DEPTH:
+            raise ValueError(f"max_depth {max_depth} > {self.MAX_DEPTH}")
         s = self.torch.cuda.current_stream(self.dev).cuda_stream
         self.lib.nxv_set_stream(ctypes.c_void_p(s if s else 1))  # 1: the legacy default stream
         try:
-            return self._transition(q0, rng, max_depth)
+            if self.driver == "host":
+                return self._transition(q0, rng, max_depth)
+            if seed is None:
+                if rng is not None:
+                    seed = int(rng.integers(1 << 32))
+                else:
+                    seed = (self.seed + self.count) & 0xFFFFFFFF
+                    self.count += 1
+            return self._transition_layout(q0, seed, max_depth)
         finally:
             self.lib.nxv_set_stream(None)
+
+    def _transition_layout(self, q0, seed, max_depth):
+        torch, lib = self.torch, self.lib
+        q0 = torch.as_tensor(q0, dtype=torch.float64).to(self.dev).contiguous()
+        C, d = q0.shape
+        p0, u = self.randomness(C, seed, max_depth)
+        i32 = dict(dtype=torch.int32, device=self.dev)
+        H0 = torch.empty(C, **self.f64)
+        logw = torch.empty(C, **self.f64)
+        sample, rho = q0.clone(), p0.clone()
+        ends_p = torch.stack([p0, p0]).contiguous()
+        ends_ps = (ends_p * self.m_dev).contiguous()
+        active, div = torch.ones(C, **i32), torch.zeros(C, **i32)
+        depth, n_leap = torch.zeros(C, **i32), torch.zeros(C, **i32)
+        end_row = torch.full((2, C), -1, dtype=torch.int64, device=self.dev)
+        top = 1 << (max_depth - 1)
+        self._reserve(C * ((1 << max_depth) - 1), d)
+        if self.node_cap < C * top * d:
+            self.node = torch.empty(C * top * d, **self.f64)
+            self.node_cap = C * top * d
+        if getattr(self, "grad_tmp", None) is None or self.grad_tmp.numel() < C * top * d:
+            self.grad_tmp = torch.empty(C * top * d, **self.f64)
+        qs, ps = torch.empty(C * d, **self.f64), torch.empty(C * d, **self.f64)
+        keep = [self._h(x) for x in (H0, q0, p0, self.prec, self.m_dev, logw, sample, rho, ends_p,
+                                     ends_ps, active, div, end_row, depth, n_leap, self.node, qs,
+                                     ps, self.st_q, self.st_p, self.st_logp, self.st_ke)]
+        (hH0, hq0, hp0, hprec, hm, hlogw, hsample, hrho, hep, heps, hact, hdiv, hend, hdepth,
+         hleap, hnode, hqs, hps, hsq, hsp, hsl, hsk) = keep
+        try:
+            self._call(lib.nxv_nuts_energy, hH0, hq0, hp0, hprec, hm, self.t.mu, self.t.const, C, d)
+            torch.neg(H0, out=logw)
+            spv = self.nxv.shader_path("leapfrog_chain_gauss_f64_batched.spv")
+            for level in range(max_depth):
+                n = 1 << level
+                base = C * (n - 1)
+                hu = self._h(u, level * 3 * C, 3 * C)
+                outs = [self._h(self.st_q, base * d, C * n * d), self._h(self.st_p, base * d, C * n * d),
+                        self._h(self.grad_tmp, 0, C * n * d), self._h(self.st_logp, base, C * n),
+                        self._h(self.st_ke, base, C * n)]
+                try:
+                    self._call(lib.nxv_nuts_start_layout, hqs, hps, hq0, hp0, hsq, hsp, hend, hu, C, d)
+                    self._call(lib.nxv_leapfrog_chain_gauss_f64_batched_ke, *outs, hqs, hps, hm, hprec,
+                               d, C, n, self.eps, self.t.mu, spv)
+                    self._call(lib.nxv_nuts_level_layout, base, n, d, hu, hsq, hsp, hsl, hsk, hm, hH0,
+                               hlogw, hrho, hep, heps, hsample, hact, hdiv, hend, hdepth, hleap, hnode,
+                               C, level)
+                finally:
+                    self._free(hu, *outs)
+                self.calls.append((C, n))
+                if level + 1 < max_depth and not bool(active.any()):
+                    break
+        finally:
+            self._free(*keep)
+        stats = Stats(depth=depth.cpu().numpy().astype(np.int64),
+                      n_leapfrog=n_leap.cpu().numpy().astype(np.int64),
+                      divergent=div.cpu().numpy().astype(bool), energy=H0.cpu().numpy())
+        return sample.view(C, d), stats
 
     def _transition(self, q0, rng, max_depth):
         torch, lib = self.torch, self.lib
