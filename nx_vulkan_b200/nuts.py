@@ -552,19 +552,11 @@ class DeviceTree:
         active, div = torch.ones(C, **i32), torch.zeros(C, **i32)
         depth, n_leap = torch.zeros(C, **i32), torch.zeros(C, **i32)
         end_row = torch.full((2, C), -1, dtype=torch.int64, device=self.dev)
-        top = 1 << (max_depth - 1)
-        self._reserve(C * ((1 << max_depth) - 1), d)
-        if self.node_cap < C * top * d:
-            self.node = torch.empty(C * top * d, **self.f64)
-            self.node_cap = C * top * d
-        if getattr(self, "grad_tmp", None) is None or self.grad_tmp.numel() < C * top * d:
-            self.grad_tmp = torch.empty(C * top * d, **self.f64)
         qs, ps = torch.empty(C * d, **self.f64), torch.empty(C * d, **self.f64)
         keep = [self._h(x) for x in (H0, q0, p0, self.prec, self.m_dev, logw, sample, rho, ends_p,
-                                     ends_ps, active, div, end_row, depth, n_leap, self.node, qs,
-                                     ps, self.st_q, self.st_p, self.st_logp, self.st_ke)]
+                                     ends_ps, active, div, end_row, depth, n_leap, qs, ps)]
         (hH0, hq0, hp0, hprec, hm, hlogw, hsample, hrho, hep, heps, hact, hdiv, hend, hdepth,
-         hleap, hnode, hqs, hps, hsq, hsp, hsl, hsk) = keep
+         hleap, hqs, hps) = keep
         try:
             self._call(lib.nxv_nuts_energy, hH0, hq0, hp0, hprec, hm, self.t.mu, self.t.const, C, d)
             torch.neg(H0, out=logw)
@@ -572,7 +564,17 @@ class DeviceTree:
             for level in range(max_depth):
                 n = 1 << level
                 base = C * (n - 1)
+                # the store and scratch grow with the depth the trees reach
+                # (levels 0 .. l take C (2^(l+1) - 1) rows); the store keeps
+                # its rows when it grows (earlier leaves are tree ends)
+                self._reserve(base + C * n, d)
+                if self.node_cap < C * n * d:
+                    self.node = torch.empty(C * n * d, **self.f64)
+                    self.grad_tmp = torch.empty(C * n * d, **self.f64)
+                    self.node_cap = C * n * d
                 hu = self._h(u, level * 3 * C, 3 * C)
+                hst = [self._h(x) for x in (self.st_q, self.st_p, self.st_logp, self.st_ke, self.node)]
+                hsq, hsp, hsl, hsk, hnode = hst
                 outs = [self._h(self.st_q, base * d, C * n * d), self._h(self.st_p, base * d, C * n * d),
                         self._h(self.grad_tmp, 0, C * n * d), self._h(self.st_logp, base, C * n),
                         self._h(self.st_ke, base, C * n)]
@@ -584,7 +586,7 @@ class DeviceTree:
                                hlogw, hrho, hep, heps, hsample, hact, hdiv, hend, hdepth, hleap, hnode,
                                C, level)
                 finally:
-                    self._free(hu, *outs)
+                    self._free(hu, *hst, *outs)
                 self.calls.append((C, n))
                 if level + 1 < max_depth and not bool(active.any()):
                     break
