@@ -139,12 +139,21 @@ __device__ void write_out(void* out, size_t idx, typename R::Acc a, int index_by
     }
 }
 
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // rows kernel: grid (S, rows).  Segment s of row r covers [s*L, min(R, (s+1)*L)).
-// final: S == 1, writes the output; else writes Acc partial [r][s].
+// final: S == 1, writes the output; else writes Acc partial [r][s].  It lets
+// its dependent (the fold, launched with programmatic dependent launch)
+// start at once: the fold's CTAs wait for this grid to complete, so they are
+// resident and begin the moment the last partial is written.
 template <class R, typename T>
 __global__ void __launch_bounds__(kThreads)
 k_rows(const T* __restrict__ a, size_t R_, size_t L, void* out, typename R::Acc* partial,
        int S, int index_bytes) {
+    griddep_launch();
     size_t r = blockIdx.y;
     size_t s = blockIdx.x;
     size_t beg = s * L, end = beg + L < R_ ? beg + L : R_;
@@ -282,6 +291,7 @@ __global__ void k_fold(const typename R::Acc* __restrict__ partial, size_t n_out
 template <class R, typename T>
 __global__ void __launch_bounds__(kThreads)
 k_fold_rows(const typename R::Acc* __restrict__ partial, int S, void* out, int index_bytes) {
+    griddep_wait();  // every partial of the segment kernel is written
     const size_t o = blockIdx.x;
     typename R::Acc acc = R::init();
     for (int s = threadIdx.x; s < S; s += blockDim.x) acc = R::combine(acc, partial[o * S + s]);
@@ -361,8 +371,19 @@ int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* 
         k_rows<R, T><<<grid, kThreads, 0, c.stream>>>(a, R_, L, out, part, (int)S, index_bytes);
         count_launch();
         if (S > 1) {
-            k_fold_rows<R, T><<<(unsigned)outer, kThreads, 0, c.stream>>>(part, (int)S, out,
-                                                                           index_bytes);
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)outer);
+            cfg.blockDim = dim3(kThreads);
+            cfg.stream = c.stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            cudaError_t e = cudaLaunchKernelEx(&cfg, k_fold_rows<R, T>,
+                                               (const typename R::Acc*)part, (int)S, out,
+                                               index_bytes);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(k_fold_rows)");
             count_launch();
         }
         return finish(c);
