@@ -100,3 +100,17 @@ def test_product_package_never_imports_the_oracle():
     offenders = [p.name for p in pkg.rglob("*.py")
                  if re.search(r"^\s*(from|import)\s+oracle\b", p.read_text(), flags=re.M)]
     assert not offenders, offenders
+
+
+def test_nuts_layout_entry_points_validate_before_any_device_work():
+    """The device-driven NUTS calls reject a missing buffer (-1) and a level
+    width that is not a power of two up to 2048 (-3) before touching a
+    device (none exists here)."""
+    from nx_vulkan_b200 import _native
+    lib = _native.load()
+    p = ctypes.c_void_p(16)  # never dereferenced on these paths
+    bufs = [p] * 18
+    assert lib.nxv_nuts_level_layout(0, 4, 8, None, *bufs[1:], 2, 0) == -1
+    assert lib.nxv_nuts_level_layout(0, 3, 8, *bufs, 2, 1) == -3
+    assert lib.nxv_nuts_level_layout(0, 4096, 8, *bufs, 2, 12) == -3
+    assert lib.nxv_nuts_start_layout(None, p, p, p, p, p, p, p, 2, 8) == -1
