@@ -350,91 +350,92 @@ __device__ __forceinline__ float tf32_rna(float x) {
 __device__ __forceinline__ float tf32_hi(float x) { return tf32_rna(x); }
 __device__ __forceinline__ float tf32_lo(float x, float hi) { return tf32_rna(__fsub_rn(x, hi)); }
 
-// Split A [M][K] (lda = K) into exact-TF32 hi and f32 lo parts, [M][Kp]
-// with zero padding in k in [K, Kp).  Grid (row blocks, batch); each warp
-// walks rows, lane l covering 4-column groups l, l+32, ... of a row with
-// 16-byte loads when the row is 16-byte aligned (K % 4 == 0), four groups in
-// flight.
-__global__ void __launch_bounds__(256)
-k_split_rows(const float* __restrict__ A, float* __restrict__ hi, float* __restrict__ lo, int M,
-             int K, int Kp, long long sA, long long sO) {
+// One launch splits both operands (blockIdx.y: the batch entry).
+//   CTAs [0, ga): A [M][K] -> A_hi, A_lo [M][Kp], one warp per row, lane l
+//     taking 4-column groups l, l+32, ... with 8 groups' loads in flight
+//     and 16-byte accesses when rows are 16-byte aligned;
+//   CTAs [ga, ga + gb): B [K][N] -> B^T_hi, B^T_lo [N][Kp] in tiles of
+//     32 k x 128 n through shared memory (rows padded to 129 floats: the
+//     column reads are conflict-free), 16 loads in flight per thread,
+//     grid-stride over the tiles.
+// Columns k in [K, Kp) are written as zeros.  Four CTAs per SM (64
+// registers): 128 KB of A or 64 KB of B loads in flight per SM.
+constexpr int kSplitU = 8;
+
+__global__ void __launch_bounds__(256, 4)
+k_split_ab(const float* __restrict__ A, float* __restrict__ ahi, float* __restrict__ alo, int M,
+           const float* __restrict__ B, float* __restrict__ bhi, float* __restrict__ blo, int N,
+           int K, int Kp, long long sA, long long sB, long long sOA, long long sOB, int ga,
+           int gb) {
+    __shared__ float t[32][129];
     const int bz = blockIdx.y;
-    A += bz * sA;
-    hi += bz * sO;
-    lo += bz * sO;
-    const int lane = threadIdx.x & 31;
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    const bool vec = (K & 3) == 0 && (((uintptr_t)A) & 15) == 0;
-    for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < M; r += warps) {
-        const float* src = A + (size_t)r * K;
-        float* h = hi + (size_t)r * Kp;
-        float* l = lo + (size_t)r * Kp;
-        // U groups of 4 columns per lane in flight (loads first, then the
-        // splits and stores); Kp % 32 == 0, so groups never straddle Kp
-        constexpr int U = 4;
-        for (int k0 = lane * 4; k0 < Kp; k0 += 128 * U) {
-            float x[U][4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if ((int)blockIdx.x < ga) {
+        A += bz * sA;
+        ahi += bz * sOA;
+        alo += bz * sOA;
+        const bool vec = (K & 3) == 0 && (((uintptr_t)A) & 15) == 0;
+        for (int r = blockIdx.x * 8 + warp; r < M; r += ga * 8) {
+            const float* src = A + (size_t)r * K;
+            float* h = ahi + (size_t)r * Kp;
+            float* l = alo + (size_t)r * Kp;
+            // Kp % 32 == 0, so groups never straddle Kp
+            for (int k0 = lane * 4; k0 < Kp; k0 += 128 * kSplitU) {
+                float x[kSplitU][4];
 #pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int k = k0 + u * 128;
-                if (k >= Kp) continue;
-                if (vec && k + 4 <= K) {
-                    const float4 v = *reinterpret_cast<const float4*>(src + k);
-                    x[u][0] = v.x, x[u][1] = v.y, x[u][2] = v.z, x[u][3] = v.w;
-                } else {
+                for (int u = 0; u < kSplitU; u++) {
+                    const int k = k0 + u * 128;
+                    if (k >= Kp) continue;
+                    if (vec && k + 4 <= K) {
+                        const float4 v = *reinterpret_cast<const float4*>(src + k);
+                        x[u][0] = v.x, x[u][1] = v.y, x[u][2] = v.z, x[u][3] = v.w;
+                    } else {
 #pragma unroll
-                    for (int e = 0; e < 4; e++) x[u][e] = k + e < K ? src[k + e] : 0.0f;
+                        for (int e = 0; e < 4; e++) x[u][e] = k + e < K ? src[k + e] : 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < kSplitU; u++) {
+                    const int k = k0 + u * 128;
+                    if (k >= Kp) continue;
+                    float4 vh, vl;
+                    vh.x = tf32_hi(x[u][0]), vh.y = tf32_hi(x[u][1]);
+                    vh.z = tf32_hi(x[u][2]), vh.w = tf32_hi(x[u][3]);
+                    vl.x = tf32_lo(x[u][0], vh.x), vl.y = tf32_lo(x[u][1], vh.y);
+                    vl.z = tf32_lo(x[u][2], vh.z), vl.w = tf32_lo(x[u][3], vh.w);
+                    *reinterpret_cast<float4*>(h + k) = vh;
+                    *reinterpret_cast<float4*>(l + k) = vl;
                 }
             }
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int k = k0 + u * 128;
-                if (k >= Kp) continue;
-                float4 vh, vl;
-                vh.x = tf32_hi(x[u][0]), vh.y = tf32_hi(x[u][1]);
-                vh.z = tf32_hi(x[u][2]), vh.w = tf32_hi(x[u][3]);
-                vl.x = tf32_lo(x[u][0], vh.x), vl.y = tf32_lo(x[u][1], vh.y);
-                vl.z = tf32_lo(x[u][2], vh.z), vl.w = tf32_lo(x[u][3], vh.w);
-                *reinterpret_cast<float4*>(h + k) = vh;
-                *reinterpret_cast<float4*>(l + k) = vl;
-            }
         }
+        return;
     }
-}
-
-// Split and transpose B [K][N] into B^T hi/lo [N][Kp]: tiles of 32 k x 64 n,
-// 32 x 8 threads, 8 elements in flight per thread; the padded row (65) keeps
-// the column reads conflict-free.
-__global__ void k_split_cols(const float* __restrict__ B, float* __restrict__ hi,
-                             float* __restrict__ lo, int K, int N, int Kp, long long sB,
-                             long long sO) {
-    __shared__ float t[32][65];
-    const int bz = blockIdx.z;
     B += bz * sB;
-    hi += bz * sO;
-    lo += bz * sO;
-    const int n0 = blockIdx.x * 64;
-    // k tiles grid-stride over blockIdx.y (grid.y is capped at 65535)
-    for (int k0 = blockIdx.y * 32; k0 < Kp; k0 += gridDim.y * 32) {
+    bhi += bz * sOB;
+    blo += bz * sOB;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    const long long ntn = (N + 127) / 128, ntiles = ntn * (Kp / 32);
+    for (long long tile = (long long)blockIdx.x - ga; tile < ntiles; tile += gb) {
+        const int n0 = (int)(tile % ntn) * 128, k0 = (int)(tile / ntn) * 32;
 #pragma unroll
-        for (int r = threadIdx.y; r < 32; r += 8) {
+        for (int r = ty; r < 32; r += 8) {
             const int k = k0 + r;
 #pragma unroll
-            for (int c = 0; c < 64; c += 32) {
-                const int n = n0 + c + threadIdx.x;
-                t[r][c + threadIdx.x] = (k < K && n < N) ? B[(size_t)k * N + n] : 0.0f;
+            for (int c = 0; c < 128; c += 32) {
+                const int n = n0 + c + tx;
+                t[r][c + tx] = (k < K && n < N) ? B[(size_t)k * N + n] : 0.0f;
             }
         }
         __syncthreads();
-        const int k = k0 + threadIdx.x;
-#pragma unroll
-        for (int r = threadIdx.y; r < 64; r += 8) {
+        const int k = k0 + tx;
+#pragma unroll 4
+        for (int r = ty; r < 128; r += 8) {
             const int n = n0 + r;
-            if (n < N && k < Kp) {
-                const float x = t[threadIdx.x][r];
+            if (n < N) {
+                const float x = t[tx][r];
                 const float h = tf32_hi(x);
-                hi[(size_t)n * Kp + k] = h;
-                lo[(size_t)n * Kp + k] = tf32_lo(x, h);
+                bhi[(size_t)n * Kp + k] = h;
+                blo[(size_t)n * Kp + k] = tf32_lo(x, h);
             }
         }
         __syncthreads();  // the tile is refilled next iteration
@@ -516,19 +517,16 @@ int launch_matmul_f32_tc(Ctx& c, void* C, const void* A, const void* B, size_t b
     float* bhi = alo + a_elems;
     float* blo = bhi + b_elems;
     {
-        // rows: 2 warps (rows) per CTA, so that a few thousand rows spread
-        // evenly over the SMs; at most 32 CTAs per SM
-        const size_t row_ctas = (m + 1) / 2;
-        const unsigned gr = (unsigned)std::min<size_t>(row_ctas, (size_t)c.dev->sm_count * 32);
-        k_split_rows<<<dim3(gr, (unsigned)batch), 64, 0, c.stream>>>(
-            (const float*)A, ahi, alo, (int)m, (int)k, (int)Kp, (long long)(m * k),
-            (long long)(m * Kp));
-        dim3 g2((unsigned)((n + 63) / 64), (unsigned)std::min<size_t>(Kp / 32, 65535),
-                (unsigned)batch);
-        k_split_cols<<<g2, dim3(32, 8), 0, c.stream>>>((const float*)B, bhi, blo, (int)k, (int)n,
-                                                       (int)Kp, (long long)(k * n),
-                                                       (long long)(n * Kp));
-        count_launch(2);
+        // one launch for both splits: a row per warp for A, 32 x 128 tiles
+        // for B, each part at most a few CTAs per SM
+        const int ga = (int)std::min<size_t>((m + 7) / 8, (size_t)c.dev->sm_count * 4);
+        const size_t btiles = (n + 127) / 128 * (Kp / 32);
+        const int gb = (int)std::min<size_t>(btiles, (size_t)c.dev->sm_count * 8);
+        k_split_ab<<<dim3((unsigned)(ga + gb), (unsigned)batch), 256, 0, c.stream>>>(
+            (const float*)A, ahi, alo, (int)m, (const float*)B, bhi, blo, (int)n, (int)k, (int)Kp,
+            (long long)(m * k), (long long)(k * n), (long long)(m * Kp), (long long)(n * Kp), ga,
+            gb);
+        count_launch();
     }
     CUtensorMap mah, mal, mbh, mbl;
     int rc;
