@@ -442,6 +442,7 @@ class DeviceTree:
         f64 = dict(dtype=torch.float64, device=self.dev)
         self.prec = torch.from_numpy(self.t.prec).to(self.dev)
         self.m_dev = torch.from_numpy(self.m).to(self.dev)
+        self.sqrt_m = torch.sqrt(self.m_dev)
         self.f64 = f64
         self.cap = 0           # store rows
         self.node_cap = 0      # f64 scratch elements
@@ -496,20 +497,15 @@ class DeviceTree:
         element c d + i) and uniforms [max_depth][3][C] (key keys(seed)[1]):
         per level the direction (forward when >= 0.5), the leaf and the move
         uniform of every chain."""
-        torch, lib = self.torch, self.lib
+        torch = self.torch
         d = self.m.size
-        kp, ku = self.keys(seed)
         z = torch.empty(n_chains * d, **self.f64)
         u = torch.empty(max_depth * 3 * n_chains, **self.f64)
         hz, hu = self._h(z), self._h(u)
         try:
-            self._call(lib.nxv_random_f64, hz, n_chains * d, kp, 1,
-                       self.nxv.shader_path("random_philox_f64.spv"))
-            self._call(lib.nxv_random_f64, hu, max_depth * 3 * n_chains, ku, 0,
-                       self.nxv.shader_path("random_philox_f64.spv"))
+            p0 = self._draw(n_chains, seed, max_depth, z, u, hz, hu)
         finally:
             self._free(hz, hu)
-        p0 = z.view(n_chains, d) / torch.sqrt(self.m_dev)
         return p0, u.view(max_depth, 3, n_chains)
 
     def transition(self, q0, rng=None, max_depth=10, seed=None):
@@ -538,64 +534,129 @@ class DeviceTree:
         finally:
             self.lib.nxv_set_stream(None)
 
+    def _layout_state(self, C, d, max_depth):
+        """Device buffers of the layout driver for C chains of dimension d and
+        their library handles, made once and reused by every transition of
+        that shape (the handles of the store's level ranges are kept until
+        the store or the scratch grows)."""
+        torch = self.torch
+        st = getattr(self, "_state", None)
+        if st is not None and st["shape"] == (C, d, max_depth):
+            return st
+        self._free_state()
+        i32 = dict(dtype=torch.int32, device=self.dev)
+        t = dict(
+            q0=torch.empty(C, d, **self.f64), z=torch.empty(C * d, **self.f64),
+            u=torch.empty(max_depth * 3 * C, **self.f64), H0=torch.empty(C, **self.f64),
+            logw=torch.empty(C, **self.f64), sample=torch.empty(C, d, **self.f64),
+            rho=torch.empty(C, d, **self.f64), ends_p=torch.empty(2, C, d, **self.f64),
+            ends_ps=torch.empty(2, C, d, **self.f64), flags=torch.empty(4, C, **i32),
+            end_row=torch.empty(2, C, dtype=torch.int64, device=self.dev),
+            qs=torch.empty(C * d, **self.f64), ps=torch.empty(C * d, **self.f64))
+        st = {"shape": (C, d, max_depth), "t": t, "levels": {}, "gen": None}
+        fl = t["flags"]  # active, divergent, depth, n_leapfrog
+        st["h"] = {k: self._h(v) for k, v in t.items() if k != "flags"}
+        st["h"].update(active=self._h(fl[0]), div=self._h(fl[1]), depth=self._h(fl[2]),
+                       leap=self._h(fl[3]), prec=self._h(self.prec), m=self._h(self.m_dev))
+        self._state = st
+        return st
+
+    def _free_state(self):
+        st = getattr(self, "_state", None)
+        if st is None:
+            return
+        for hs in st["levels"].values():
+            self._free(*hs)
+        self._free(*st["h"].values())
+        self._state = None
+
+    def __del__(self):
+        try:
+            self._free_state()
+        except Exception:
+            pass
+
+    def _level_handles(self, st, level, C, d):
+        """Handles of level `level`'s store rows and of the whole store (the
+        level kernel reads the tree ends anywhere in it)."""
+        n = 1 << level
+        base = C * (n - 1)
+        self._reserve(base + C * n, d)
+        torch = self.torch
+        if self.node_cap < C * n * d:
+            self.node = torch.empty(C * n * d, **self.f64)
+            self.grad_tmp = torch.empty(C * n * d, **self.f64)
+            self.node_cap = C * n * d
+        gen = (self.st_q.data_ptr(), self.node.data_ptr())
+        if st["gen"] != gen:  # the store or the scratch moved: new handles
+            for hs in st["levels"].values():
+                self._free(*hs)
+            st["levels"] = {}
+            st["gen"] = gen
+        hs = st["levels"].get(level)
+        if hs is None:
+            u = st["t"]["u"]
+            hs = (self._h(u, level * 3 * C, 3 * C),
+                  self._h(self.st_q), self._h(self.st_p), self._h(self.st_logp), self._h(self.st_ke),
+                  self._h(self.node),
+                  self._h(self.st_q, base * d, C * n * d), self._h(self.st_p, base * d, C * n * d),
+                  self._h(self.grad_tmp, 0, C * n * d), self._h(self.st_logp, base, C * n),
+                  self._h(self.st_ke, base, C * n))
+            st["levels"][level] = hs
+        return hs
+
     def _transition_layout(self, q0, seed, max_depth):
         torch, lib = self.torch, self.lib
-        q0 = torch.as_tensor(q0, dtype=torch.float64).to(self.dev).contiguous()
+        q0 = torch.as_tensor(q0, dtype=torch.float64).to(self.dev)
         C, d = q0.shape
-        p0, u = self.randomness(C, seed, max_depth)
-        i32 = dict(dtype=torch.int32, device=self.dev)
-        H0 = torch.empty(C, **self.f64)
-        logw = torch.empty(C, **self.f64)
-        sample, rho = q0.clone(), p0.clone()
-        ends_p = torch.stack([p0, p0]).contiguous()
-        ends_ps = (ends_p * self.m_dev).contiguous()
-        active, div = torch.ones(C, **i32), torch.zeros(C, **i32)
-        depth, n_leap = torch.zeros(C, **i32), torch.zeros(C, **i32)
-        end_row = torch.full((2, C), -1, dtype=torch.int64, device=self.dev)
-        qs, ps = torch.empty(C * d, **self.f64), torch.empty(C * d, **self.f64)
-        keep = [self._h(x) for x in (H0, q0, p0, self.prec, self.m_dev, logw, sample, rho, ends_p,
-                                     ends_ps, active, div, end_row, depth, n_leap, qs, ps)]
-        (hH0, hq0, hp0, hprec, hm, hlogw, hsample, hrho, hep, heps, hact, hdiv, hend, hdepth,
-         hleap, hqs, hps) = keep
-        try:
-            self._call(lib.nxv_nuts_energy, hH0, hq0, hp0, hprec, hm, self.t.mu, self.t.const, C, d)
-            torch.neg(H0, out=logw)
-            spv = self.nxv.shader_path("leapfrog_chain_gauss_f64_batched.spv")
-            for level in range(max_depth):
-                n = 1 << level
-                base = C * (n - 1)
-                # the store and scratch grow with the depth the trees reach
-                # (levels 0 .. l take C (2^(l+1) - 1) rows); the store keeps
-                # its rows when it grows (earlier leaves are tree ends)
-                self._reserve(base + C * n, d)
-                if self.node_cap < C * n * d:
-                    self.node = torch.empty(C * n * d, **self.f64)
-                    self.grad_tmp = torch.empty(C * n * d, **self.f64)
-                    self.node_cap = C * n * d
-                hu = self._h(u, level * 3 * C, 3 * C)
-                hst = [self._h(x) for x in (self.st_q, self.st_p, self.st_logp, self.st_ke, self.node)]
-                hsq, hsp, hsl, hsk, hnode = hst
-                outs = [self._h(self.st_q, base * d, C * n * d), self._h(self.st_p, base * d, C * n * d),
-                        self._h(self.grad_tmp, 0, C * n * d), self._h(self.st_logp, base, C * n),
-                        self._h(self.st_ke, base, C * n)]
-                try:
-                    self._call(lib.nxv_nuts_start_layout, hqs, hps, hq0, hp0, hsq, hsp, hend, hu, C, d)
-                    self._call(lib.nxv_leapfrog_chain_gauss_f64_batched_ke, *outs, hqs, hps, hm, hprec,
-                               d, C, n, self.eps, self.t.mu, spv)
-                    self._call(lib.nxv_nuts_level_layout, base, n, d, hu, hsq, hsp, hsl, hsk, hm, hH0,
-                               hlogw, hrho, hep, heps, hsample, hact, hdiv, hend, hdepth, hleap, hnode,
-                               C, level)
-                finally:
-                    self._free(hu, *hst, *outs)
-                self.calls.append((C, n))
-                if level + 1 < max_depth and not bool(active.any()):
-                    break
-        finally:
-            self._free(*keep)
-        stats = Stats(depth=depth.cpu().numpy().astype(np.int64),
-                      n_leapfrog=n_leap.cpu().numpy().astype(np.int64),
-                      divergent=div.cpu().numpy().astype(bool), energy=H0.cpu().numpy())
-        return sample.view(C, d), stats
+        st = self._layout_state(C, d, max_depth)
+        t, h = st["t"], st["h"]
+        t["q0"].copy_(q0)
+        p0 = self._draw(C, seed, max_depth, t["z"], t["u"], h["z"], h["u"])
+        t["sample"].copy_(t["q0"])
+        t["rho"].copy_(p0)
+        t["ends_p"][0].copy_(p0)
+        t["ends_p"][1].copy_(p0)
+        torch.mul(t["ends_p"], self.m_dev, out=t["ends_ps"])
+        fl = t["flags"]
+        fl.zero_()
+        fl[0].fill_(1)
+        t["end_row"].fill_(-1)
+        spv = self.nxv.shader_path("leapfrog_chain_gauss_f64_batched.spv")
+        # p0 = z / sqrt(inv_mass) was written into z in place
+        self._call(lib.nxv_nuts_energy, h["H0"], h["q0"], h["z"], h["prec"], h["m"], self.t.mu,
+                   self.t.const, C, d)
+        torch.neg(t["H0"], out=t["logw"])
+        for level in range(max_depth):
+            n = 1 << level
+            base = C * (n - 1)
+            hu, hsq, hsp, hsl, hsk, hnode, *outs = self._level_handles(st, level, C, d)
+            self._call(lib.nxv_nuts_start_layout, h["qs"], h["ps"], h["q0"], h["z"], hsq, hsp,
+                       h["end_row"], hu, C, d)
+            self._call(lib.nxv_leapfrog_chain_gauss_f64_batched_ke, *outs, h["qs"], h["ps"], h["m"],
+                       h["prec"], d, C, n, self.eps, self.t.mu, spv)
+            self._call(lib.nxv_nuts_level_layout, base, n, d, hu, hsq, hsp, hsl, hsk, h["m"],
+                       h["H0"], h["logw"], h["rho"], h["ends_p"], h["ends_ps"], h["sample"],
+                       h["active"], h["div"], h["end_row"], h["depth"], h["leap"], hnode, C, level)
+            self.calls.append((C, n))
+            if level + 1 < max_depth and not bool(fl[0].any()):
+                break
+        flags = fl.cpu().numpy()  # one read: active, divergent, depth, leaf count
+        stats = Stats(depth=flags[2].astype(np.int64), n_leapfrog=flags[3].astype(np.int64),
+                      divergent=flags[1].astype(bool), energy=t["H0"].cpu().numpy())
+        return t["sample"].clone(), stats
+
+    def _draw(self, n_chains, seed, max_depth, z, u, hz, hu):
+        """Fills z with p0 = N(0, 1) / sqrt(inv_mass) and u with the uniforms
+        (the draws of `randomness`); returns z viewed as [C, d]."""
+        d = self.m.size
+        kp, ku = self.keys(seed)
+        spv = self.nxv.shader_path("random_philox_f64.spv")
+        self._call(self.lib.nxv_random_f64, hz, n_chains * d, kp, 1, spv)
+        self._call(self.lib.nxv_random_f64, hu, max_depth * 3 * n_chains, ku, 0, spv)
+        zv = z.view(n_chains, d)
+        zv.div_(self.sqrt_m)
+        return zv
 
     def _transition(self, q0, rng, max_depth):
         torch, lib = self.torch, self.lib
