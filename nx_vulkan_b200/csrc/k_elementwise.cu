@@ -253,10 +253,13 @@ int map1_per_sm() {
 //
 // f64 maps and the exact f32 mode spend about as long in FP64 arithmetic as in
 // moving their bytes.  k_map_pipe runs one wave of CTAs whose threads walk
-// the array one vector at a time and load the next vector before doing the
-// math of the current one, so every warp keeps a load in flight while it
-// computes (the grid-stride form with all loads first and all math after
-// serialises the two across the whole GPU when one wave covers the array).
+// the array one vector at a time and keep the next two vectors' loads in
+// flight while they do the math of the current one (the grid-stride form
+// with all loads first and all math after serialises the two across the
+// whole GPU when one wave covers the array).  Two vectors ahead rather than
+// one: config 1 exact f32 6.59 -> 6.12 us, f64 8.03 -> 8.00 us.  Under
+// programmatic dependent launch the first two vectors are loaded before the
+// wait only when no input overlaps the previous kernel's output.
 
 template <typename T, int NIN, class F>
 __global__ void __launch_bounds__(kThreads)
@@ -267,29 +270,42 @@ k_map_pipe(T* __restrict__ out, const T* __restrict__ in0, const T* __restrict__
     const size_t nv = n / W;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    T nx[NIN > 0 ? NIN : 1][W];
-    // programmatic dependent launch as in k_map1: the first vector is loaded
-    // before the wait only when no input overlaps the previous kernel's output
-    if (early && v < nv) {
+    T nx[NIN > 0 ? NIN : 1][W], ny[NIN > 0 ? NIN : 1][W];
+    if (early) {
+        if (v < nv) {
 #pragma unroll
-        for (int q = 0; q < NIN; q++) vload(ins[q] + v * W, nx[q]);
+            for (int q = 0; q < NIN; q++) vload(ins[q] + v * W, nx[q]);
+        }
+        if (v + stride < nv) {
+#pragma unroll
+            for (int q = 0; q < NIN; q++) vload(ins[q] + (v + stride) * W, ny[q]);
+        }
     }
     griddep_wait();
     griddep_launch();
-    if (!early && v < nv) {
+    if (!early) {
+        if (v < nv) {
 #pragma unroll
-        for (int q = 0; q < NIN; q++) vload(ins[q] + v * W, nx[q]);
+            for (int q = 0; q < NIN; q++) vload(ins[q] + v * W, nx[q]);
+        }
+        if (v + stride < nv) {
+#pragma unroll
+            for (int q = 0; q < NIN; q++) vload(ins[q] + (v + stride) * W, ny[q]);
+        }
     }
     for (; v < nv; v += stride) {
         T x[NIN > 0 ? NIN : 1][W];
 #pragma unroll
         for (int q = 0; q < NIN; q++)
 #pragma unroll
-            for (int j = 0; j < W; j++) x[q][j] = nx[q][j];
-        const size_t vn = v + stride;
+            for (int j = 0; j < W; j++) {
+                x[q][j] = nx[q][j];
+                nx[q][j] = ny[q][j];
+            }
+        const size_t vn = v + 2 * stride;
         if (vn < nv) {
 #pragma unroll
-            for (int q = 0; q < NIN; q++) vload(ins[q] + vn * W, nx[q]);
+            for (int q = 0; q < NIN; q++) vload(ins[q] + vn * W, ny[q]);
         }
         T r[W];
 #pragma unroll
