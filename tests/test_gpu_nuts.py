@@ -122,3 +122,32 @@ def test_nuts_layout_sampler_moments(nxv):
     x = np.concatenate(acc) * np.sqrt(prec)  # standardised: N(0, 1) per coordinate
     assert np.all(np.abs(x.mean(axis=0)) < 0.12)
     assert np.all(np.abs(x.var(axis=0) - 1) < 0.2)
+
+
+@pytest.mark.parametrize("d,C,depth", [(1, 1, 1), (3, 5, 2), (2000, 3, 5), (7, 300, 10)])
+def test_nuts_layout_edge_shapes(nxv, d, C, depth):
+    """The layout driver at the edges -- one dimension, one chain, a single
+    level, deep trees, many chains -- against the host walk given the same
+    draws, and twice in a row on one tree object (the buffers it keeps are
+    reused, and the second transition continues from the first's draws)."""
+    import torch
+
+    r = np.random.default_rng(13)
+    prec = r.uniform(0.5, 2.0, d)
+    t = nuts.GaussianTarget(prec)
+    m = r.uniform(0.8, 1.2, d)
+    eps = 0.2 if d < 10 else 0.02
+    host_src, dev = nuts.GpuChain(t, m, eps), nuts.DeviceTree(t, m, eps)
+    qa = r.normal(size=(C, d)) / np.sqrt(prec)
+    same = 0
+    for k in range(2):
+        p0, u = dev.randomness(C, 50 + k, depth)
+        qa_new, sa = nuts.nuts_transition(host_src, t, qa, m, None, max_depth=depth,
+                                          p0=p0.cpu().numpy(), uniforms=u.cpu().numpy())
+        qb_new, sb = dev.transition(torch.from_numpy(qa).cuda(), max_depth=depth, seed=50 + k)
+        assert sb.depth.max() <= depth and sb.depth.min() >= 1
+        assert np.array_equal(sa.n_leapfrog >= 1, np.ones(C, bool))
+        same += int(np.sum(np.all(qb_new.cpu().numpy() == qa_new, axis=1)
+                           & (sa.depth == sb.depth) & (sa.n_leapfrog == sb.n_leapfrog)))
+        qa = qa_new
+    assert same >= 0.98 * 2 * C
