@@ -191,24 +191,6 @@ bool map_pdl() {
     return !(e && e[0] == '0');
 }
 
-// True when none of the inputs [p, p + bytes) overlaps the output of the last
-// programmatic launch on c.stream; then records `out` as that output.
-bool pdl_independent_and_record(Ctx& c, const void* const* ins, int nin, size_t bytes,
-                                const void* out) {
-    std::lock_guard<std::mutex> lk(c.dev->pdl_mu);
-    auto it = c.dev->pdl_last.find(c.stream);
-    bool indep = true;
-    if (it != c.dev->pdl_last.end()) {
-        const uintptr_t lo = it->second.first, hi = lo + it->second.second;
-        for (int q = 0; q < nin; q++) {
-            const uintptr_t a = (uintptr_t)ins[q], b = a + bytes;
-            if (a < hi && lo < b) indep = false;
-        }
-    }
-    c.dev->pdl_last[c.stream] = {(uintptr_t)out, bytes};
-    return indep;
-}
-
 // Launches a map kernel (k_map1 or k_map_pipe: parameters out, in0..in3,
 // n, f, early) with programmatic dependent launch unless NXV_MAP_PDL=0.
 template <typename T, class F>

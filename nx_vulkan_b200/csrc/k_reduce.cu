@@ -148,12 +148,17 @@ __device__ __forceinline__ void griddep_launch() {
 // final: S == 1, writes the output; else writes Acc partial [r][s].  It lets
 // its dependent (the fold, launched with programmatic dependent launch)
 // start at once: the fold's CTAs wait for this grid to complete, so they are
-// resident and begin the moment the last partial is written.
+// resident and begin the moment the last partial is written.  Launched
+// itself with programmatic dependent launch (the segmented path), it waits
+// for the previous kernel before its loads, or -- `early`: its input is not
+// that kernel's output -- only before its writes (the previous call's fold
+// may still be reading the partials).
 template <class R, typename T>
 __global__ void __launch_bounds__(kThreads)
 k_rows(const T* __restrict__ a, size_t R_, size_t L, void* out, typename R::Acc* partial,
-       int S, int index_bytes) {
+       int S, int index_bytes, int early) {
     griddep_launch();
+    if (!early) griddep_wait();
     size_t r = blockIdx.y;
     size_t s = blockIdx.x;
     size_t beg = s * L, end = beg + L < R_ ? beg + L : R_;
@@ -195,6 +200,7 @@ k_rows(const T* __restrict__ a, size_t R_, size_t L, void* out, typename R::Acc*
     }
     for (size_t e = i + threadIdx.x; e < end; e += blockDim.x) acc = R::add(acc, row[e], (long long)e);
     acc = block_reduce<R>(acc);
+    if (early) griddep_wait();
     if (threadIdx.x == 0) {
         if (S == 1) write_out<R, T>(out, r, acc, index_bytes);
         else partial[r * S + s] = acc;
@@ -292,6 +298,7 @@ template <class R, typename T>
 __global__ void __launch_bounds__(kThreads)
 k_fold_rows(const typename R::Acc* __restrict__ partial, int S, void* out, int index_bytes) {
     griddep_wait();  // every partial of the segment kernel is written
+    griddep_launch();
     const size_t o = blockIdx.x;
     typename R::Acc acc = R::init();
     for (int s = threadIdx.x; s < S; s += blockDim.x) acc = R::combine(acc, partial[o * S + s]);
@@ -362,13 +369,32 @@ int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* 
                 dim3 grid(1, (unsigned)rows);
                 void* o2 = (char*)out + r0 * (index_bytes ? (size_t)index_bytes : sizeof(typename R::Out));
                 k_rows<R, T><<<grid, kThreads, 0, c.stream>>>(a + r0 * R_, R_, L, o2, nullptr, 1,
-                                                              index_bytes);
+                                                              index_bytes, 0);
                 count_launch();
             }
             return finish(c);
         }
         dim3 grid((unsigned)S, (unsigned)outer);
-        k_rows<R, T><<<grid, kThreads, 0, c.stream>>>(a, R_, L, out, part, (int)S, index_bytes);
+        {
+            // programmatic dependent launch unless NXV_MAP_PDL=0
+            const char* ev = getenv("NXV_MAP_PDL");
+            const bool pdl = !(ev && ev[0] == '0');
+            const void* ins[1] = {a};
+            const int early =
+                pdl && pdl_independent_and_record(c, ins, 1, outer * R_ * sizeof(T), out) ? 1 : 0;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = grid;
+            cfg.blockDim = dim3(kThreads);
+            cfg.stream = c.stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = pdl ? 1 : 0;
+            cudaError_t e = cudaLaunchKernelEx(&cfg, k_rows<R, T>, a, R_, L, out, part, (int)S,
+                                               index_bytes, early);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(k_rows)");
+        }
         count_launch();
         if (S > 1) {
             cudaLaunchConfig_t cfg = {};

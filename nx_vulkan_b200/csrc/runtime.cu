@@ -274,6 +274,26 @@ void* scratch(Ctx& c, size_t bytes, int slot) {
     return p;
 }
 
+// True when none of the inputs [p, p + bytes) overlaps the output of the last
+// programmatic launch on c.stream; then records [out, out + bytes) as that
+// output (kernels with a smaller output record more than they write, which
+// only makes a later early load less likely).
+bool pdl_independent_and_record(Ctx& c, const void* const* ins, int nin, size_t bytes,
+                                const void* out) {
+    std::lock_guard<std::mutex> lk(c.dev->pdl_mu);
+    auto it = c.dev->pdl_last.find(c.stream);
+    bool indep = true;
+    if (it != c.dev->pdl_last.end()) {
+        const uintptr_t lo = it->second.first, hi = lo + it->second.second;
+        for (int q = 0; q < nin; q++) {
+            const uintptr_t a = (uintptr_t)ins[q], b = a + bytes;
+            if (a < hi && lo < b) indep = false;
+        }
+    }
+    c.dev->pdl_last[c.stream] = {(uintptr_t)out, bytes};
+    return indep;
+}
+
 std::string spv_base(const char* spv_path) {
     if (!spv_path) return std::string();
     const char* s = strrchr(spv_path, '/');

@@ -109,6 +109,13 @@ const char* last_error();
 extern std::atomic<unsigned long> g_launches;
 inline void count_launch(unsigned long k = 1) { g_launches.fetch_add(k, std::memory_order_relaxed); }
 
+// Programmatic dependent launch bookkeeping (Device::pdl_last): true when
+// none of the nin inputs [p, p + bytes) overlaps the output of the last
+// kernel launched with programmatic serialization on c.stream; records
+// [out, out + bytes) as the output of the launch being made.
+bool pdl_independent_and_record(Ctx& c, const void* const* ins, int nin, size_t bytes,
+                                const void* out);
+
 // spv basename helpers.
 std::string spv_base(const char* spv_path);
 
