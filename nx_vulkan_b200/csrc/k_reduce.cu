@@ -217,10 +217,12 @@ k_rows(const T* __restrict__ a, size_t R_, size_t L, void* out, typename R::Acc*
 // (32-bit element index).
 template <class R, typename T, int RPC>
 __global__ void __launch_bounds__(32 * RPC)
-k_rows_warp(const T* __restrict__ a, size_t outer, unsigned R_, void* out, int index_bytes) {
+k_rows_warp(const T* __restrict__ a, size_t outer, unsigned R_, void* out, int index_bytes,
+            int early) {
     const size_t r = (size_t)blockIdx.x * RPC + (threadIdx.x >> 5);
     const unsigned lane = threadIdx.x & 31;
     if (r >= outer) return;  // the whole warp leaves together
+    if (!early) griddep_wait();  // see pdl_row_launch
     const T* row = a + r * R_;
     constexpr int W = (int)(16 / sizeof(T));
     constexpr int U = sizeof(T) == 8 ? 8 : 4;  // 16-byte vectors in flight per lane
@@ -258,6 +260,8 @@ k_rows_warp(const T* __restrict__ a, size_t outer, unsigned R_, void* out, int i
     for (int u = 1; u < U; u++) acc = R::combine(acc, part[u]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc = R::combine(acc, R::shfl(acc, off));
+    if (early) griddep_wait();
+    griddep_launch();
     if (lane == 0) write_out<R, T>(out, r, acc, index_bytes);
 }
 
@@ -270,13 +274,46 @@ int rows_per_cta() {
     return 2;
 }
 
+// The one-pass row kernels (k_rows_warp, k_lse_rows) run on programmatic
+// dependent launch unless NXV_MAP_PDL=0: a kernel whose input is not the
+// output of the previous programmatic launch on the stream (`early`, from
+// the per-stream record) reads and reduces its rows while that kernel
+// finishes and waits for it only before writing its results; otherwise it
+// waits before its first load.  Either way it lets the next kernel start
+// only after its own wait.
+template <typename... KArgs, typename... Args>
+int pdl_row_launch(Ctx& c, void (*kern)(KArgs...), unsigned grid, unsigned block, const void* in,
+                   size_t in_bytes, const void* out, Args... args) {
+    const char* ev = getenv("NXV_MAP_PDL");
+    const bool pdl = !(ev && ev[0] == '0');
+    const void* ins[1] = {in};
+    const int early = pdl && pdl_independent_and_record(c, ins, 1, in_bytes, out) ? 1 : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args..., early);
+    return e == cudaSuccess ? OK : cuda_fail(e, "cudaLaunchKernelEx(row kernel)");
+}
+
 template <class R, typename T>
-void launch_rows_warp(Ctx& c, const T* a, size_t outer, unsigned R_, void* out, int index_bytes) {
+int launch_rows_warp(Ctx& c, const T* a, size_t outer, unsigned R_, void* out, int index_bytes) {
     const int rpc = rows_per_cta();
     const unsigned ctas = (unsigned)((outer + rpc - 1) / rpc);
-    if (rpc == 8) k_rows_warp<R, T, 8><<<ctas, 256, 0, c.stream>>>(a, outer, R_, out, index_bytes);
-    else if (rpc == 4) k_rows_warp<R, T, 4><<<ctas, 128, 0, c.stream>>>(a, outer, R_, out, index_bytes);
-    else k_rows_warp<R, T, 2><<<ctas, 64, 0, c.stream>>>(a, outer, R_, out, index_bytes);
+    const size_t nb = outer * (size_t)R_ * sizeof(T);
+    if (rpc == 8)
+        return pdl_row_launch(c, k_rows_warp<R, T, 8>, ctas, 256, a, nb, out, a, outer, R_, out,
+                              index_bytes);
+    if (rpc == 4)
+        return pdl_row_launch(c, k_rows_warp<R, T, 4>, ctas, 128, a, nb, out, a, outer, R_, out,
+                              index_bytes);
+    return pdl_row_launch(c, k_rows_warp<R, T, 2>, ctas, 64, a, nb, out, a, outer, R_, out,
+                          index_bytes);
 }
 
 // Fold S partials per output in index order.
@@ -349,7 +386,8 @@ int run_reduce(Ctx& c, const T* a, size_t outer, size_t R_, size_t inner, void* 
                 set_error("too many rows for a reduce");
                 return E_ARG;
             }
-            launch_rows_warp<R, T>(c, a, outer, (unsigned)R_, out, index_bytes);
+            int rc = launch_rows_warp<R, T>(c, a, outer, (unsigned)R_, out, index_bytes);
+            if (rc) return rc;
             count_launch();
             return finish(c);
         }
@@ -522,10 +560,12 @@ __device__ __forceinline__ void lse_merge(LseLane<EX>& L, float mo, double so) {
 // One warp per row, RPC rows per CTA (as k_rows_warp).
 template <bool EX, int RPC>
 __global__ void __launch_bounds__(32 * RPC)
-k_lse_rows(const float* __restrict__ a, size_t outer, unsigned R_, float* __restrict__ out) {
+k_lse_rows(const float* __restrict__ a, size_t outer, unsigned R_, float* __restrict__ out,
+           int early) {
     const size_t r = (size_t)blockIdx.x * RPC + (threadIdx.x >> 5);
     const unsigned lane = threadIdx.x & 31;
     if (r >= outer) return;
+    if (!early) griddep_wait();  // see pdl_row_launch
     const float* row = a + r * R_;
     const bool vec = (((uintptr_t)row) & 15) == 0;
     const unsigned nv = vec ? R_ / 4 : 0;
@@ -551,17 +591,20 @@ k_lse_rows(const float* __restrict__ a, size_t outer, unsigned R_, float* __rest
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
         lse_merge(L, __shfl_down_sync(0xffffffffu, L.m, off), __shfl_down_sync(0xffffffffu, L.s, off));
+    if (early) griddep_wait();
+    griddep_launch();
     if (lane == 0)
         out[r] = L.m == -INFINITY ? __int_as_float(0x7fc00000) : (float)(log(L.s) + (double)L.m);
 }
 
 template <bool EX>
-void launch_lse_rows(Ctx& c, const float* a, size_t outer, unsigned R_, float* out) {
+int launch_lse_rows(Ctx& c, const float* a, size_t outer, unsigned R_, float* out) {
     const int rpc = rows_per_cta();
     const unsigned ctas = (unsigned)((outer + rpc - 1) / rpc);
-    if (rpc == 8) k_lse_rows<EX, 8><<<ctas, 256, 0, c.stream>>>(a, outer, R_, out);
-    else if (rpc == 4) k_lse_rows<EX, 4><<<ctas, 128, 0, c.stream>>>(a, outer, R_, out);
-    else k_lse_rows<EX, 2><<<ctas, 64, 0, c.stream>>>(a, outer, R_, out);
+    const size_t nb = outer * (size_t)R_ * 4;
+    if (rpc == 8) return pdl_row_launch(c, k_lse_rows<EX, 8>, ctas, 256, a, nb, out, a, outer, R_, out);
+    if (rpc == 4) return pdl_row_launch(c, k_lse_rows<EX, 4>, ctas, 128, a, nb, out, a, outer, R_, out);
+    return pdl_row_launch(c, k_lse_rows<EX, 2>, ctas, 64, a, nb, out, a, outer, R_, out);
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -676,8 +719,10 @@ int launch_logsumexp(Ctx& c, void* out, const void* a, size_t outer, size_t R, s
             set_error("logsumexp extents out of range");
             return E_ARG;
         }
-        if (fast_f32()) launch_lse_rows<false>(c, (const float*)a, outer, (unsigned)R, (float*)out);
-        else launch_lse_rows<true>(c, (const float*)a, outer, (unsigned)R, (float*)out);
+        const int rc =
+            fast_f32() ? launch_lse_rows<false>(c, (const float*)a, outer, (unsigned)R, (float*)out)
+                       : launch_lse_rows<true>(c, (const float*)a, outer, (unsigned)R, (float*)out);
+        if (rc) return rc;
     } else {
         if (outer > 65535) return E_ARG;
         dim3 grid((unsigned)((inner + kThreads - 1) / kThreads), (unsigned)outer);
