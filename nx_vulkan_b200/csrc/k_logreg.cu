@@ -75,6 +75,9 @@ int launch_pdl(Ctx& c, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = lr_pdl() ? 1 : 0;
+    // these kernels let their successor start right after their own wait,
+    // before they write: no successor may load early
+    pdl_record_all(c);
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
     if (e != cudaSuccess) return cuda_fail(e, what);
     count_launch();

@@ -294,6 +294,13 @@ bool pdl_independent_and_record(Ctx& c, const void* const* ins, int nin, size_t 
     return indep;
 }
 
+// A programmatic launch that keeps no record of its output (its kernel lets
+// the next kernel start before it completes): no later kernel may load early.
+void pdl_record_all(Ctx& c) {
+    std::lock_guard<std::mutex> lk(c.dev->pdl_mu);
+    c.dev->pdl_last[c.stream] = {(uintptr_t)0, ~(size_t)0};
+}
+
 std::string spv_base(const char* spv_path) {
     if (!spv_path) return std::string();
     const char* s = strrchr(spv_path, '/');

@@ -115,6 +115,10 @@ inline void count_launch(unsigned long k = 1) { g_launches.fetch_add(k, std::mem
 // [out, out + bytes) as the output of the launch being made.
 bool pdl_independent_and_record(Ctx& c, const void* const* ins, int nin, size_t bytes,
                                 const void* out);
+// For programmatic launches whose outputs are not tracked: marks all memory
+// as the last output, so the next programmatic launch loads only after its
+// wait.
+void pdl_record_all(Ctx& c);
 
 // spv basename helpers.
 std::string spv_base(const char* spv_path);

@@ -251,3 +251,26 @@ def test_logreg_vs_oracle(nxv, orc, monkeypatch, N, D, C, K, split, persist):
     assert nxv.synchronize() == "ok"  # no bounded pipeline wait ran out
     for t, wv in zip(outs, want):
         close(down(nxv, t, np.float64), wv, 1e-10, 1e-10)
+
+
+def test_logreg_outputs_feed_the_next_kernels(nxv):
+    """Kernels queued right after a logistic chain call -- an f64 map and a
+    per-row reduction, both on programmatic dependent launch -- read the
+    chain's finished outputs: the chain's kernels let their successor start
+    before they complete, so no successor may load early.  Checked against
+    the downloaded outputs, bit for bit."""
+    r = np.random.default_rng(8)
+    N, D, C, K = 4000, 64, 48, 6
+    X = r.normal(size=(N, D))
+    y = (r.random(N) < 0.5).astype(np.float64)
+    q0, p0 = r.normal(size=(C, D)) * 0.1, r.normal(size=(C, D))
+    qc, pc, gc, lg = unwrap(nxv.leapfrog_logreg_f64_batched(up(nxv, q0), up(nxv, p0), up(nxv, X),
+                                                             up(nxv, y), N, D, C, K, 0.002))
+    twice = unwrap(nxv.apply_binary_f64(qc, qc, "add"))          # queued behind the chain
+    row_sums = unwrap(nxv.reduce_axis_f64(gc, C * K, D, 1, 0))   # likewise
+    q_h = down(nxv, qc, np.float64)
+    g_h = down(nxv, gc, np.float64)
+    assert np.array_equal(down(nxv, twice, np.float64), q_h + q_h)
+    want = g_h.reshape(C * K, D).sum(axis=1)
+    got = down(nxv, row_sums, np.float64)
+    assert np.allclose(got, want, rtol=1e-12, atol=1e-12 * np.abs(g_h).reshape(C * K, D).sum(axis=1).max())
