@@ -49,24 +49,41 @@ __device__ const double kExp2J64[64] = {
     0x1.ea4afa2a490dap+0, 0x1.efa1bee615a27p+0, 0x1.f50765b6e4540p+0, 0x1.fa7c1819e90d8p+0,
 };
 
-// 2^(j/64) - kExp2J64[j], rounded to double (the table entries' rounding error)
-__device__ const double kExp2J64Lo[64] = {
-    0x0.0p+0, -0x1.19083535b085dp-56, 0x1.d73e2a475b465p-55, 0x1.186be4bb284ffp-57,
-    0x1.8a62e4adc610bp-54, 0x1.03a1727c57b53p-59, -0x1.6c51039449b3ap-54, -0x1.32fbf9af1369ep-54,
-    -0x1.19041b9d78a76p-55, 0x1.e5b4c7b4968e4p-55, 0x1.e016e00a2643cp-54, 0x1.dc775814a8495p-55,
-    0x1.9b07eb6c70573p-54, 0x1.2bd339940e9d9p-55, 0x1.612e8afad1255p-55, 0x1.0024754db41d5p-54,
-    0x1.6f46ad23182e4p-55, 0x1.32721843659a6p-54, -0x1.63aeabf42eae2p-54, -0x1.5e436d661f5e3p-56,
-    0x1.ada0911f09ebcp-55, -0x1.ef3691c309278p-58, 0x1.89b7a04ef80d0p-59, 0x1.3c1a3b69062f0p-56,
-    0x1.d4397afec42e2p-56, -0x1.4b309d25957e3p-54, -0x1.07abe1db13cadp-55, 0x1.9bb2c011d93adp-54,
-    0x1.6324c054647adp-54, 0x1.ba6f93080e65ep-54, -0x1.383c17e40b497p-54, -0x1.bb60987591c34p-54,
-    -0x1.bdd3413b26456p-54, -0x1.bbe3a683c88abp-57, -0x1.16e4786887a99p-55, -0x1.0245957316dd3p-54,
-    -0x1.41577ee04992fp-55, 0x1.05d02ba15797ep-56, -0x1.d4c1dd41532d8p-54, -0x1.fc6f89bd4f6bap-54,
-    0x1.6e9f156864b27p-54, 0x1.5cc13a2e3976cp-55, -0x1.75fc781b57ebcp-57, -0x1.d185b7c1b85d1p-54,
-    0x1.c7c46b071f2bep-56, -0x1.359495d1cd533p-54, -0x1.d2f6edb8d41e1p-54, 0x1.0fac90ef7fd31p-54,
-    0x1.7a1cd345dcc81p-54, -0x1.2805e3084d708p-57, -0x1.5584f7e54ac3bp-56, 0x1.23dd07a2d9e84p-55,
-    0x1.11065895048ddp-55, 0x1.2884dff483cadp-54, 0x1.503cbd1e949dbp-56, -0x1.cbc3743797a9cp-54,
-    0x1.2ed02d75b3707p-55, 0x1.c2300696db532p-54, -0x1.1a5cd4f184b5cp-54, 0x1.39e8980a9cc8fp-55,
-    -0x1.e9c23179c2893p-54, 0x1.dc7f486a4b6b0p-54, 0x1.9d3e12dd8a18bp-54, 0x1.74853f3a5931ep-55,
+// 2^(j/64) as the head above and a tail, 2^(j/64) - head rounded to double,
+// in one 16-byte entry (one load in the f64 functions)
+__device__ const double2 kExp2J64HL[64] = {
+    {0x1.0000000000000p+0, 0x0.0p+0}, {0x1.02c9a3e778061p+0, -0x1.19083535b085dp-56},
+    {0x1.059b0d3158574p+0, 0x1.d73e2a475b465p-55}, {0x1.0874518759bc8p+0, 0x1.186be4bb284ffp-57},
+    {0x1.0b5586cf9890fp+0, 0x1.8a62e4adc610bp-54}, {0x1.0e3ec32d3d1a2p+0, 0x1.03a1727c57b53p-59},
+    {0x1.11301d0125b51p+0, -0x1.6c51039449b3ap-54}, {0x1.1429aaea92de0p+0, -0x1.32fbf9af1369ep-54},
+    {0x1.172b83c7d517bp+0, -0x1.19041b9d78a76p-55}, {0x1.1a35beb6fcb75p+0, 0x1.e5b4c7b4968e4p-55},
+    {0x1.1d4873168b9aap+0, 0x1.e016e00a2643cp-54}, {0x1.2063b88628cd6p+0, 0x1.dc775814a8495p-55},
+    {0x1.2387a6e756238p+0, 0x1.9b07eb6c70573p-54}, {0x1.26b4565e27cddp+0, 0x1.2bd339940e9d9p-55},
+    {0x1.29e9df51fdee1p+0, 0x1.612e8afad1255p-55}, {0x1.2d285a6e4030bp+0, 0x1.0024754db41d5p-54},
+    {0x1.306fe0a31b715p+0, 0x1.6f46ad23182e4p-55}, {0x1.33c08b26416ffp+0, 0x1.32721843659a6p-54},
+    {0x1.371a7373aa9cbp+0, -0x1.63aeabf42eae2p-54}, {0x1.3a7db34e59ff7p+0, -0x1.5e436d661f5e3p-56},
+    {0x1.3dea64c123422p+0, 0x1.ada0911f09ebcp-55}, {0x1.4160a21f72e2ap+0, -0x1.ef3691c309278p-58},
+    {0x1.44e086061892dp+0, 0x1.89b7a04ef80d0p-59}, {0x1.486a2b5c13cd0p+0, 0x1.3c1a3b69062f0p-56},
+    {0x1.4bfdad5362a27p+0, 0x1.d4397afec42e2p-56}, {0x1.4f9b2769d2ca7p+0, -0x1.4b309d25957e3p-54},
+    {0x1.5342b569d4f82p+0, -0x1.07abe1db13cadp-55}, {0x1.56f4736b527dap+0, 0x1.9bb2c011d93adp-54},
+    {0x1.5ab07dd485429p+0, 0x1.6324c054647adp-54}, {0x1.5e76f15ad2148p+0, 0x1.ba6f93080e65ep-54},
+    {0x1.6247eb03a5585p+0, -0x1.383c17e40b497p-54}, {0x1.6623882552225p+0, -0x1.bb60987591c34p-54},
+    {0x1.6a09e667f3bcdp+0, -0x1.bdd3413b26456p-54}, {0x1.6dfb23c651a2fp+0, -0x1.bbe3a683c88abp-57},
+    {0x1.71f75e8ec5f74p+0, -0x1.16e4786887a99p-55}, {0x1.75feb564267c9p+0, -0x1.0245957316dd3p-54},
+    {0x1.7a11473eb0187p+0, -0x1.41577ee04992fp-55}, {0x1.7e2f336cf4e62p+0, 0x1.05d02ba15797ep-56},
+    {0x1.82589994cce13p+0, -0x1.d4c1dd41532d8p-54}, {0x1.868d99b4492edp+0, -0x1.fc6f89bd4f6bap-54},
+    {0x1.8ace5422aa0dbp+0, 0x1.6e9f156864b27p-54}, {0x1.8f1ae99157736p+0, 0x1.5cc13a2e3976cp-55},
+    {0x1.93737b0cdc5e5p+0, -0x1.75fc781b57ebcp-57}, {0x1.97d829fde4e50p+0, -0x1.d185b7c1b85d1p-54},
+    {0x1.9c49182a3f090p+0, 0x1.c7c46b071f2bep-56}, {0x1.a0c667b5de565p+0, -0x1.359495d1cd533p-54},
+    {0x1.a5503b23e255dp+0, -0x1.d2f6edb8d41e1p-54}, {0x1.a9e6b5579fdbfp+0, 0x1.0fac90ef7fd31p-54},
+    {0x1.ae89f995ad3adp+0, 0x1.7a1cd345dcc81p-54}, {0x1.b33a2b84f15fbp+0, -0x1.2805e3084d708p-57},
+    {0x1.b7f76f2fb5e47p+0, -0x1.5584f7e54ac3bp-56}, {0x1.bcc1e904bc1d2p+0, 0x1.23dd07a2d9e84p-55},
+    {0x1.c199bdd85529cp+0, 0x1.11065895048ddp-55}, {0x1.c67f12e57d14bp+0, 0x1.2884dff483cadp-54},
+    {0x1.cb720dcef9069p+0, 0x1.503cbd1e949dbp-56}, {0x1.d072d4a07897cp+0, -0x1.cbc3743797a9cp-54},
+    {0x1.d5818dcfba487p+0, 0x1.2ed02d75b3707p-55}, {0x1.da9e603db3285p+0, 0x1.c2300696db532p-54},
+    {0x1.dfc97337b9b5fp+0, -0x1.1a5cd4f184b5cp-54}, {0x1.e502ee78b3ff6p+0, 0x1.39e8980a9cc8fp-55},
+    {0x1.ea4afa2a490dap+0, -0x1.e9c23179c2893p-54}, {0x1.efa1bee615a27p+0, 0x1.dc7f486a4b6b0p-54},
+    {0x1.f50765b6e4540p+0, 0x1.9d3e12dd8a18bp-54}, {0x1.fa7c1819e90d8p+0, 0x1.74853f3a5931ep-55},
 };
 
 constexpr double kInvLn2x64 = 0x1.71547652b82fep+6;   // 64 / ln 2
@@ -74,11 +91,11 @@ constexpr double kLn2d64Hi = 0x1.62e42fefa0000p-7;    // ln 2 / 64, 36-bit head
 constexpr double kLn2d64Lo = 0x1.cf79abc9e3b3ap-46;   // ln 2 / 64 - head
 constexpr double kShift = 0x1.8p52;                   // round-to-integer shifter
 
-// Reduction of x (|x| <= 700): returns e^r - 1 (= p) and s + s_lo =
-// 2^m 2^(j/64) as a head and a tail.
-__device__ __forceinline__ double reduce(double x, double& s, double& s_lo) {
+// Reduction of x (|x| <= 700): x = k ln2/64 + r with |r| <= ln2/128;
+// returns e^r - 1 (= p) and k.
+__device__ __forceinline__ double reduce(double x, int& k) {
     const double t = __fma_rn(x, kInvLn2x64, kShift);
-    const int k = __double2loint(t);
+    k = __double2loint(t);
     const double kd = __dsub_rn(t, kShift);
     double r = __fma_rn(-kd, kLn2d64Hi, x);
     r = __fma_rn(-kd, kLn2d64Lo, r);
@@ -90,15 +107,13 @@ __device__ __forceinline__ double reduce(double x, double& s, double& s_lo) {
     q = __fma_rn(r, q, 1.0 / 24.0);
     q = __fma_rn(r, q, 1.0 / 6.0);
     q = __fma_rn(r, q, 0.5);
-    const double p = __fma_rn(__dmul_rn(r, r), q, r);
-    const int m = k >> 6;  // floor(k / 64)
-    const double pw = __longlong_as_double((long long)(m + 1023) << 52);
-    // 2^m s is a normal double for |m| <= 1010: the power of two goes into
-    // the head's exponent field; the tail (possibly 0) is scaled by a product
-    const double tj = __ldg(&kExp2J64[k & 63]);
-    s = __hiloint2double(__double2hiint(tj) + (m << 20), __double2loint(tj));
-    s_lo = __dmul_rn(__ldg(&kExp2J64Lo[k & 63]), pw);
-    return p;
+    return __fma_rn(__dmul_rn(r, r), q, r);
+}
+
+// v * 2^m by adding m to the exponent field: exact when v and the result
+// are normal doubles
+__device__ __forceinline__ double scale_pow2(double v, int m) {
+    return __hiloint2double(__double2hiint(v) + (m << 20), __double2loint(v));
 }
 
 // The C library's functions for the arguments the table-driven ones leave
@@ -107,21 +122,35 @@ __device__ __forceinline__ double reduce(double x, double& s, double& s_lo) {
 static __device__ __noinline__ double lib_exp(double x) { return ::exp(x); }
 static __device__ __noinline__ double lib_expm1(double x) { return ::expm1(x); }
 
-// e^x = s + (s p + s_lo (1 + p))
+// e^x = 2^m (t + (t p + t_lo (1 + p))) with t + t_lo = 2^(j/64), k = 64 m + j;
+// the bracket lies in [0.98, 2.03], and for |x| <= 700 the result is a
+// normal double, so the power of two goes into the exponent field exactly
 __device__ __forceinline__ double exp(double x) {
     if (!(fabs(x) <= 700.0)) return lib_exp(x);  // overflow, underflow, inf, NaN
-    double s, s_lo;
-    const double p = reduce(x, s, s_lo);
-    return __dadd_rn(s, __fma_rn(s, p, __fma_rn(s_lo, p, s_lo)));
+    int k;
+    const double p = reduce(x, k);
+    const double2 t = __ldg(&kExp2J64HL[k & 63]);
+    return scale_pow2(__dadd_rn(t.x, __fma_rn(t.x, p, __fma_rn(t.y, p, t.y))), k >> 6);
 }
 
-// e^x - 1 = (s - 1) + (s p + s_lo (1 + p)); the table tail keeps the result
-// accurate where s - 1 cancels (|x| below about 1)
+// e^x - 1 = (s - 1) + (s p + s_lo (1 + p)) with s + s_lo = 2^m 2^(j/64);
+// s - 1 is exact, and the table tail keeps the result accurate where s - 1
+// cancels (|x| below about 1).  For |x| <= 700 (the caller checks).
+__device__ __forceinline__ double expm1_core(double x) {
+    int k;
+    const double p = reduce(x, k);
+    const int m = k >> 6;  // floor(k / 64)
+    const double2 t = __ldg(&kExp2J64HL[k & 63]);
+    // 2^m s is a normal double for |m| <= 1010; the tail (possibly 0) is
+    // scaled by a product
+    const double s = scale_pow2(t.x, m);
+    const double s_lo = __dmul_rn(t.y, __longlong_as_double((long long)(m + 1023) << 52));
+    return __dadd_rn(__dsub_rn(s, 1.0), __fma_rn(s, p, __fma_rn(s_lo, p, s_lo)));
+}
+
 __device__ __forceinline__ double expm1(double x) {
     if (!(fabs(x) <= 700.0)) return lib_expm1(x);
-    double s, s_lo;
-    const double p = reduce(x, s, s_lo);
-    return __dadd_rn(__dsub_rn(s, 1.0), __fma_rn(s, p, __fma_rn(s_lo, p, s_lo)));
+    return expm1_core(x);
 }
 
 // 1 / d for d in [1, 2]: the f32 hardware reciprocal (~2^-23) refined by two
@@ -138,7 +167,7 @@ __device__ __forceinline__ double recip_1_2(double d) {
 __device__ __forceinline__ double tanh(double x) {
     const double a = fabs(x);
     if (a > 20.0) return copysign(1.0, x);
-    const double e = lean::expm1(-2.0 * a);  // in (-1, 0]
+    const double e = expm1_core(-2.0 * a);  // in (-1, 0]; -2a >= -40
     return copysign(__dmul_rn(-e, recip_1_2(__dadd_rn(2.0, e))), x);
 }
 
