@@ -4,7 +4,7 @@
 // implementation of the exponential function in IEEE floating-point
 // arithmetic", ACM TOMS 15(2), 1989: x = (64 m + j) ln2/64 + r with
 // |r| <= ln2/128, exp(x) = 2^m 2^(j/64) e^r, e^r - 1 by its Taylor series
-// to r^7 (truncation below 2^-64 relative to e^r - 1 for |r| <= ln2/128).  The table
+// to r^6 (truncation below 2^-57 relative to e^r - 1 for |r| <= ln2/128).  The table
 // holds 2^(j/64) as a double head and a double tail; ln2/64 is split into a 36-bit head
 // (so that k * head is exact for |k| < 2^17) and a tail.  Relative error
 // within a few units of 2^-53 for |x| <= 700; outside that range (and for
@@ -99,11 +99,10 @@ __device__ __forceinline__ double reduce(double x, int& k) {
     const double kd = __dsub_rn(t, kShift);
     double r = __fma_rn(-kd, kLn2d64Hi, x);
     r = __fma_rn(-kd, kLn2d64Lo, r);
-    // e^r - 1 = r + r^2 (1/2 + r (1/6 + r (1/24 + r (1/120 + r (1/720 + r / 5040)))));
-    // the first omitted term, r^8 / 8!, is below 2^-64 of e^r - 1 for
+    // e^r - 1 = r + r^2 (1/2 + r (1/6 + r (1/24 + r (1/120 + r / 720))));
+    // the first omitted term, r^7 / 7!, is below 2^-57 of e^r - 1 for
     // |r| <= ln2/128 (expm1 needs that relative to r, not to 1)
-    double q = __fma_rn(r, 1.0 / 5040.0, 1.0 / 720.0);
-    q = __fma_rn(r, q, 1.0 / 120.0);
+    double q = __fma_rn(r, 1.0 / 720.0, 1.0 / 120.0);
     q = __fma_rn(r, q, 1.0 / 24.0);
     q = __fma_rn(r, q, 1.0 / 6.0);
     q = __fma_rn(r, q, 0.5);
