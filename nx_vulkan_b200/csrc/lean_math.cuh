@@ -152,12 +152,12 @@ __device__ __forceinline__ double expm1(double x) {
     return expm1_core(x);
 }
 
-// 1 / d for d in [1, 2]: the f32 hardware reciprocal (~2^-23) refined by two
+// 1 / d for d in [1, 2]: the hardware's f64 reciprocal estimate (PTX
+// rcp.approx.ftz.f64, from the high word: about 20 bits) refined by two
 // Newton steps r <- r (2 - d r) to within an ulp or two of double.
 __device__ __forceinline__ double recip_1_2(double d) {
-    float rf;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rf) : "f"((float)d));
-    double r = (double)rf;
+    double r;
+    asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(d));
     r = __fma_rn(r, __fma_rn(-d, r, 1.0), r);
     r = __fma_rn(r, __fma_rn(-d, r, 1.0), r);
     return r;
