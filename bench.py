@@ -1360,7 +1360,7 @@ def suite(args):
         prec = r.uniform(0.5, 2.0, 100)
         tg = nuts.GaussianTarget(prec)
         q_start = r.normal(size=(Cn, 100)) / np.sqrt(prec)
-        for driver in ("layout", "host"):
+        for driver in ("layout", "levels", "host"):
             dt = nuts.DeviceTree(tg, np.ones(100), 0.05, driver=driver)
             qd = torch.from_numpy(q_start).to(dev)
             rng = np.random.default_rng(4)
@@ -1374,9 +1374,14 @@ def suite(args):
             el_d = time.perf_counter() - t0
             note = ("momenta and uniforms drawn by Philox on the device, tree state on the device, "
                     "every chain's leaves at fixed store rows: per level one start kernel, one "
-                    "chain call of 2^l steps for all chains and one level kernel "
-                    "(nxv_nuts_start_layout/_level_layout); the host reads one flag per level"
+                    "chain call of 2^l steps for all chains and one level kernel, the whole "
+                    "transition one library call (nxv_nuts_transition_layout) reading one "
+                    "4-byte flag per level"
                     if driver == "layout" else
+                    "the same kernels issued level by level from Python "
+                    "(nxv_nuts_start_layout, the batched chain call, nxv_nuts_level_layout); "
+                    "the host reads one flag per level"
+                    if driver == "levels" else
                     "leaves written by the chain calls into a device store and walked there "
                     "(nxv_nuts_energy/_start/_level); the host keeps the row bookkeeping "
                     "(speculative extension), draws the random numbers and reads one active "

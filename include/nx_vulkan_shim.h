@@ -468,6 +468,26 @@ int nxv_nuts_level_layout(unsigned long long base_row, unsigned int n, unsigned 
                           void* end_row, void* depth, void* n_leapfrog, void* node,
                           unsigned int n_chains, unsigned int level);
 
+/* One whole NUTS transition of every chain in one call, with the levels
+ * above run by the library: momenta p0 = N(0, 1) / sqrt(inv_mass) and the
+ * per-level uniforms [max_depth][3][n_chains] drawn by Philox-2x32-10 (the
+ * nxv_random_f64 streams of keys seed and seed ^ 0x5BD1E995), the initial
+ * energy, then per level one start kernel, one batched Gaussian chain call
+ * of 2^l steps (with kinetic energy) into the library's own leaf store and
+ * one level kernel, with one 4-byte read per level of whether any tree
+ * still grows.  q0 [n_chains][d], inv_mass and prec [d] (the Gaussian
+ * target's diagonal precision and mean mu, logp_const the log density's
+ * constant); outputs sample [n_chains][d], flags [4][n_chains] int32
+ * (active at the end, divergent, depth, leapfrog steps) and H0 [n_chains]
+ * (initial energy).  The tree state and the store (n_chains (2^max_depth -
+ * 1) leaves) live in library scratch, kept for the next call.  -3 when
+ * max_depth is outside 1..12.  Returns after the last level's flag read;
+ * the outputs are complete in stream order. */
+int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, void* inv_mass,
+                               void* prec, double mu, double logp_const, double eps,
+                               unsigned int n_chains, unsigned int d, unsigned int max_depth,
+                               unsigned int seed);
+
 /* ---- Devices, streams, interop (NEW) ----------------------------------- */
 
 /* Use exactly these CUDA devices (e.g. the local rank's GPU).  Calls nxv_init

@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     "nxv_nuts_level": (C.c_int, [vp] * 5 + [u32, u32, u32] + [vp] * 14 + [u32]),
     "nxv_nuts_start_layout": (C.c_int, [vp] * 8 + [u32, u32]),
     "nxv_nuts_level_layout": (C.c_int, [C.c_ulonglong, u32, u32] + [vp] * 18 + [u32, u32]),
+    "nxv_nuts_transition_layout": (C.c_int, [vp] * 6 + [f64, f64, f64, u32, u32, u32, u32]),
     "nxv_init_devices": (C.c_int, [intp, C.c_int]),
     "nxv_set_device": (C.c_int, [C.c_int]),
     "nxv_set_stream": (C.c_int, [vp]),

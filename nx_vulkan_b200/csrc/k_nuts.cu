@@ -24,13 +24,16 @@
 #include <math.h>
 
 #include <algorithm>
+#include <mutex>
 
 namespace nxv {
 namespace {
 
-constexpr int kNT = 128;          // threads per chain
+constexpr int kNT = 256;          // threads per chain
 constexpr int kNW = kNT / 32;
 constexpr int kMaxLeaves = 2048;  // leaves per level: 2^(max depth - 1), max depth 12
+constexpr int kMaxDepth = 12;
+static_assert(kMaxLeaves == 1 << (kMaxDepth - 1), "a level holds 2^(depth - 1) leaves");
 constexpr double kMaxDeltaH = 1000.0;
 
 __device__ __forceinline__ double warp_sum(double v) {
@@ -182,7 +185,8 @@ __device__ __forceinline__ void level_walk(const LevelArgs& a, int c, bool fwd, 
     __syncthreads();
     if (tid == 0) {
         double acc = 0.0;
-        for (int t = 0; t < kNT; t++) {
+        const int nch = (n + per - 1) / per;  // chunks that hold leaves
+        for (int t = 0; t < nch; t++) {
             const double v = chunk[t];
             chunk[t] = acc;  // offset of chunk t
             acc = add_(acc, v);
@@ -285,6 +289,7 @@ struct LayoutArgs {
     long long* end_row;    // [2][C] store row of the tree's left / right end leaf (-1: the start)
     int* depth;            // [C]
     int* n_leapfrog;       // [C]
+    int* any;              // optional: set to 1 by every chain that keeps building
     int level;
 };
 
@@ -300,14 +305,16 @@ __global__ void __launch_bounds__(kNT) k_nuts_level_layout(LevelArgs a, LayoutAr
         L.end_row[(fwd ? C : 0) + c] = first + n - 1;
         L.depth[c] = L.level + 1;
         L.n_leapfrog[c] += n;
+        if (L.any && a.active[c]) *L.any = 1;  // written by this thread in level_walk
     }
 }
 
 // H0 = -logp(q) + KE(p) for the Gaussian target, logp(q) = -0.5 sum
 // prec (q - mu)^2 + logp_const; one warp per chain.
-__global__ void __launch_bounds__(kNT) k_nuts_energy(double* H0, const double* q, const double* p,
-                                                     const double* prec, const double* m,
-                                                     double mu, double logp_const, int C, int d) {
+__global__ void __launch_bounds__(kNT) k_nuts_energy(double* H0, double* neg_H0, const double* q,
+                                                     const double* p, const double* prec,
+                                                     const double* m, double mu,
+                                                     double logp_const, int C, int d) {
     const int c = blockIdx.x * kNW + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (c >= C) return;
     double u = 0.0, k = 0.0;
@@ -318,7 +325,11 @@ __global__ void __launch_bounds__(kNT) k_nuts_energy(double* H0, const double* q
     }
     u = warp_sum(u);
     k = warp_sum(k);
-    if (lane == 0) H0[c] = add_(sub_(mul_(0.5, u), logp_const), mul_(0.5, k));
+    if (lane == 0) {
+        const double h = add_(sub_(mul_(0.5, u), logp_const), mul_(0.5, k));
+        H0[c] = h;
+        if (neg_H0) neg_H0[c] = -h;  // the tree's initial log weight
+    }
 }
 
 // Starting points of a speculative extension: chain chain[i] continues from
@@ -350,8 +361,9 @@ __global__ void __launch_bounds__(kNT) k_nuts_start_layout(double* qs, double* p
                                                            const double* st_q, const double* st_p,
                                                            const long long* end_row,
                                                            const double* u_dir, int C, int d,
-                                                           long long st_rows) {
+                                                           long long st_rows, int* any) {
     const int c = blockIdx.x;
+    if (any && c == 0 && threadIdx.x == 0) *any = 0;  // this level's level kernel sets it
     const bool fwd = u_dir[c] >= 0.5;
     long long r = end_row[(fwd ? C : 0) + c];
     if (r >= st_rows) r = -1;  // not a row of this store: restart from the initial point
@@ -366,6 +378,53 @@ __global__ void __launch_bounds__(kNT) k_nuts_start_layout(double* qs, double* p
             ps[o] = mul_(sg, p0[o]);
         }
     }
+}
+
+// A transition's initial state, one CTA per chain: p0 = z / sqrt(inv_mass)
+// in place (z: standard normal draws), sample = q0, rho and both tree ends
+// = p0, end velocities p0 * inv_mass, flags (active, divergent, depth,
+// leapfrog count) = (1, 0, 0, 0), end rows -1.
+__global__ void __launch_bounds__(kNT) k_nuts_init(double* z, const double* q0, const double* m,
+                                                   double* sample, double* rho, double* end_p,
+                                                   double* end_ps, int* flags,
+                                                   long long* end_row, int C, int d) {
+    const int c = blockIdx.x;
+    const size_t CD = (size_t)C * d;
+    for (int k = threadIdx.x; k < d; k += kNT) {
+        const size_t o = (size_t)c * d + k;
+        const double p = div_(z[o], __dsqrt_rn(m[k]));
+        z[o] = p;
+        sample[o] = q0[o];
+        rho[o] = p;
+        end_p[o] = p;
+        end_p[CD + o] = p;
+        const double v = mul_(p, m[k]);
+        end_ps[o] = v;
+        end_ps[CD + o] = v;
+    }
+    if (threadIdx.x == 0) {
+        flags[c] = 1;
+        flags[C + c] = 0;
+        flags[2 * C + c] = 0;
+        flags[3 * C + c] = 0;
+        end_row[c] = -1;
+        end_row[C + c] = -1;
+    }
+}
+
+// Pinned host word per device for the per-level "any tree still growing" read.
+std::mutex g_any_mu;
+int* g_any_host[64] = {};
+
+int* any_host(int dev) {
+    std::lock_guard<std::mutex> lk(g_any_mu);
+    if (dev < 0 || dev >= 64) return nullptr;
+    if (!g_any_host[dev] && cudaHostAlloc(&g_any_host[dev], sizeof(int), cudaHostAllocDefault) !=
+                                cudaSuccess) {
+        cudaGetLastError();
+        g_any_host[dev] = nullptr;
+    }
+    return g_any_host[dev];
 }
 
 }  // namespace
@@ -393,7 +452,7 @@ int nxv_nuts_energy(void* H0, void* q, void* p, void* prec, void* inv_mass, doub
     }
     if (n_chains == 0 || d == 0) return OK;
     k_nuts_energy<<<(n_chains + kNW - 1) / kNW, kNT, 0, c.stream>>>(
-        (double*)dptr(H0), (const double*)dptr(q), (const double*)dptr(p),
+        (double*)dptr(H0), nullptr, (const double*)dptr(q), (const double*)dptr(p),
         (const double*)dptr(prec), (const double*)dptr(inv_mass), mu, logp_const, (int)n_chains,
         (int)d);
     count_launch();
@@ -502,7 +561,7 @@ int nxv_nuts_start_layout(void* qs, void* ps, void* q0, void* p0, void* st_q, vo
     k_nuts_start_layout<<<n_chains, kNT, 0, c.stream>>>(
         (double*)dptr(qs), (double*)dptr(ps), (const double*)dptr(q0), (const double*)dptr(p0),
         (const double*)dptr(st_q), (const double*)dptr(st_p), (const long long*)dptr(end_row),
-        (const double*)dptr(u_dir), (int)n_chains, (int)d, st_rows);
+        (const double*)dptr(u_dir), (int)n_chains, (int)d, st_rows, nullptr);
     count_launch();
     return finish(c);
 }
@@ -565,9 +624,130 @@ int nxv_nuts_level_layout(unsigned long long base_row, unsigned int n, unsigned 
     L.end_row = (long long*)dptr(end_row);
     L.depth = (int*)dptr(depth);
     L.n_leapfrog = (int*)dptr(n_leapfrog);
+    L.any = nullptr;
     L.level = (int)level;
     k_nuts_level_layout<<<(unsigned)C, kNT, 0, c.stream>>>(g, L);
     count_launch();
+    return finish(c);
+}
+
+int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, void* inv_mass,
+                               void* prec, double mu, double logp_const, double eps,
+                               unsigned int n_chains, unsigned int d, unsigned int max_depth,
+                               unsigned int seed) {
+    if (!sample || !flags || !H0 || !q0 || !inv_mass || !prec) return E_NULL;
+    if (max_depth == 0 || max_depth > (unsigned)kMaxDepth) {
+        set_error("nuts_transition_layout: max_depth must be 1 .. %d", kMaxDepth);
+        return E_ARG;
+    }
+    Ctx c;
+    int rc = begin(c, {sample, flags, H0, q0, inv_mass, prec});
+    if (rc) return rc;
+    const size_t C = n_chains, D = d, CD = C * D;
+    if (!holds(sample, CD * 8) || !holds(flags, 4 * C * 4) || !holds(H0, C * 8) ||
+        !holds(q0, CD * 8) || !holds(inv_mass, D * 8) || !holds(prec, D * 8)) {
+        set_error("nuts_transition_layout: a buffer is smaller than its extent");
+        return E_ARG;
+    }
+    if (C == 0 || D == 0) return OK;
+    const size_t L = max_depth, nmax = size_t(1) << (L - 1), R = C * ((size_t(1) << L) - 1);
+    // scratch regions, each 256-byte aligned: momenta (z -> p0), uniforms,
+    // rho, tree ends and end velocities, log weight, start points, end rows,
+    // the flag word, the leaf store (q, p, logp, ke) and the level scratch
+    // (node sums, the chain call's gradients)
+    size_t off = 0;
+    auto take = [&off](size_t bytes) {
+        const size_t o = off;
+        off += (bytes + 255) & ~size_t(255);
+        return o;
+    };
+    const size_t o_z = take(CD * 8), o_u = take(L * 3 * C * 8), o_rho = take(CD * 8),
+                 o_ep = take(2 * CD * 8), o_eps = take(2 * CD * 8), o_logw = take(C * 8),
+                 o_qs = take(CD * 8), o_ps = take(CD * 8), o_er = take(2 * C * 8),
+                 o_any = take(4), o_sq = take(R * D * 8), o_sp = take(R * D * 8),
+                 o_sl = take(R * 8), o_sk = take(R * 8), o_node = take(C * nmax * D * 8),
+                 o_grad = take(C * nmax * D * 8);
+    ScratchGuard guard(c);
+    char* base = (char*)scratch(c, off, kScratchNuts);
+    if (!base) return E_CUDA;
+    int* any_h = any_host(c.dev->id);
+    if (!any_h) {
+        set_error("nuts_transition_layout: pinned host word allocation failed");
+        return E_CUDA;
+    }
+    double* z = (double*)(base + o_z);
+    const double* u = (const double*)(base + o_u);
+    long long* end_row = (long long*)(base + o_er);
+    int* any = (int*)(base + o_any);
+    double* st_q = (double*)(base + o_sq);
+    double* st_p = (double*)(base + o_sp);
+    double* st_logp = (double*)(base + o_sl);
+    double* st_ke = (double*)(base + o_sk);
+    double* qs = (double*)(base + o_qs);
+    double* ps = (double*)(base + o_ps);
+    const double* m = (const double*)dptr(inv_mass);
+    const double* pr = (const double*)dptr(prec);
+    const double* q0d = (const double*)dptr(q0);
+    int* fl = (int*)dptr(flags);
+    // Philox keys of the momenta and of the uniforms
+    const uint32_t kp = seed, ku = seed ^ 0x5BD1E995u;
+    if ((rc = launch_random(c, F64, z, CD, kp, 1))) return rc;
+    if ((rc = launch_random(c, F64, base + o_u, L * 3 * C, ku, 0))) return rc;
+    k_nuts_init<<<(unsigned)C, kNT, 0, c.stream>>>(
+        z, q0d, m, (double*)dptr(sample), (double*)(base + o_rho), (double*)(base + o_ep),
+        (double*)(base + o_eps), fl, end_row, (int)C, (int)D);
+    k_nuts_energy<<<(unsigned)((C + kNW - 1) / kNW), kNT, 0, c.stream>>>(
+        (double*)dptr(H0), (double*)(base + o_logw), q0d, z, pr, m, mu, logp_const, (int)C,
+        (int)D);
+    count_launch(2);
+    LevelArgs g{};
+    g.d = (int)D;
+    g.st_q = st_q;
+    g.st_p = st_p;
+    g.st_logp = st_logp;
+    g.st_ke = st_ke;
+    g.m = m;
+    g.H0 = (const double*)dptr(H0);
+    g.logw = (double*)(base + o_logw);
+    g.rho = (double*)(base + o_rho);
+    g.end_p = (double*)(base + o_ep);
+    g.end_ps = (double*)(base + o_eps);
+    g.sample = (double*)dptr(sample);
+    g.active = fl;
+    g.divergent = fl + C;
+    g.node = (double*)(base + o_node);
+    g.C = (int)C;
+    LayoutArgs Lg{};
+    Lg.end_row = end_row;
+    Lg.depth = fl + 2 * C;
+    Lg.n_leapfrog = fl + 3 * C;
+    Lg.any = any;
+    for (size_t level = 0; level < L; level++) {
+        const size_t n = size_t(1) << level, row0 = C * (n - 1);
+        const double* ul = u + level * 3 * C;
+        k_nuts_start_layout<<<(unsigned)C, kNT, 0, c.stream>>>(qs, ps, q0d, z, st_q, st_p,
+                                                             end_row, ul, (int)C, (int)D,
+                                                             (long long)R, any);
+        count_launch();
+        rc = launch_chain_gauss_f64(c, st_q + row0 * D, st_p + row0 * D, base + o_grad,
+                                    st_logp + row0, qs, ps, m, pr, 0.0, mu, D, C, (unsigned)n,
+                                    eps, st_ke + row0, true);
+        if (rc) return rc;
+        g.n = (int)n;
+        Lg.base = (long long)row0;
+        Lg.u = ul;
+        Lg.level = (int)level;
+        k_nuts_level_layout<<<(unsigned)C, kNT, 0, c.stream>>>(g, Lg);
+        count_launch();
+        if (level + 1 < L) {
+            // one 4-byte read per level: does any tree still grow?
+            cudaError_t e = cudaMemcpyAsync(any_h, any, sizeof(int), cudaMemcpyDeviceToHost,
+                                            c.stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(c.stream);
+            if (e != cudaSuccess) return cuda_fail(e, "nuts_transition_layout: flag read");
+            if (*any_h == 0) break;
+        }
+    }
     return finish(c);
 }
 

@@ -92,8 +92,10 @@ inline size_t nbytes(const void* h) { return h ? static_cast<const Buf*>(h)->n_b
 // work queued on c.stream until the next scratch() call with the same slot
 // on this device.  Callers hold a ScratchGuard for the whole op (see
 // Device::scratch_mu).  Slot 0 belongs to the op entry points; slot 1 to the
-// GEMM (its stream-K workspace), which ops holding slot 0 may call.
-enum { kScratchOp = 0, kScratchGemm = 1 };
+// GEMM (its stream-K workspace), which ops holding slot 0 may call; slot 2
+// to the one-call NUTS transition (its tree state and leaf store), which
+// calls the chain launcher (slot 0) between its own kernels.
+enum { kScratchOp = 0, kScratchGemm = 1, kScratchNuts = 2 };
 void* scratch(Ctx& c, size_t bytes, int slot = kScratchOp);
 struct ScratchGuard {
     std::lock_guard<std::recursive_mutex> lk;

@@ -409,18 +409,24 @@ def nuts_transition(source, target: GaussianTarget, q0, inv_mass, rng, max_depth
 class DeviceTree:
     """The tree builder's walk on the device over a leaf store that the chain
     calls write into, so the trajectories never cross PCIe.  Gaussian
-    targets, f64.  Two drivers:
+    targets, f64.  Three drivers:
 
     * "layout" (default): everything per transition is drawn and kept on the
       device -- momenta p0 = N(0, 1) / sqrt(inv_mass) and per-level uniforms
       from the Philox generator (`randomness`), the tree ends, depth and leaf
       counts -- and every chain's level-l leaves sit at fixed store rows.
       Each level is one start kernel, one batched chain call of 2^l steps for
-      all chains and one level kernel (nxv_nuts_start_layout / _level_layout);
-      the host reads one flag per level (is any tree still growing).  With
-      the same momenta and uniforms, nuts_transition takes the same
-      decisions (the leaves are bit-identical: a chain restarted from a
-      stored leaf continues exactly as the uninterrupted integration).
+      all chains and one level kernel; the whole transition is one library
+      call (nxv_nuts_transition_layout), which reads one 4-byte flag per
+      level (is any tree still growing).  With the same momenta and
+      uniforms, nuts_transition takes the same decisions (the leaves are
+      bit-identical: a chain restarted from a stored leaf continues exactly
+      as the uninterrupted integration).
+    * "levels": the same transition with this class issuing the per-level
+      calls (nxv_nuts_start_layout, the batched chain call,
+      nxv_nuts_level_layout) over torch tensors -- what a tree builder in
+      another host language does with those entry points; its draws are
+      bit-identical to "layout"'s.
     * "host": the host keeps the row bookkeeping of nuts_transition
       (speculative extension, as eXMC calls the chain) and draws from
       `rng` in its order; only the walk (nxv_nuts_start / _level) runs on
@@ -433,8 +439,8 @@ class DeviceTree:
         import torch
         from nx_vulkan_b200 import _native
         from nx_vulkan_b200 import vulkan as nxv
-        if driver not in ("layout", "host"):
-            raise ValueError(f"driver must be 'layout' or 'host', not {driver!r}")
+        if driver not in ("layout", "levels", "host"):
+            raise ValueError(f"driver must be 'layout', 'levels' or 'host', not {driver!r}")
         self.torch, self.nxv, self.lib = torch, nxv, _native.load()
         self.t, self.eps, self.driver = target, eps, driver
         self.m = np.ascontiguousarray(inv_mass, np.float64)
@@ -530,6 +536,8 @@ class DeviceTree:
                 else:
                     seed = (self.seed + self.count) & 0xFFFFFFFF
                     self.count += 1
+            if self.driver == "layout":
+                return self._transition_native(q0, seed, max_depth)
             return self._transition_layout(q0, seed, max_depth)
         finally:
             self.lib.nxv_set_stream(None)
@@ -563,12 +571,50 @@ class DeviceTree:
 
     def _free_state(self):
         st = getattr(self, "_state", None)
-        if st is None:
-            return
-        for hs in st["levels"].values():
-            self._free(*hs)
-        self._free(*st["h"].values())
-        self._state = None
+        if st is not None:
+            for hs in st["levels"].values():
+                self._free(*hs)
+            self._free(*st["h"].values())
+            self._state = None
+        nat = getattr(self, "_native", None)
+        if nat is not None:
+            self._free(*nat["h"].values())
+            self._native = None
+
+    def _native_state(self, C, d):
+        """Input and output tensors of the one-call transition for C chains of
+        dimension d, with their handles (the library keeps the tree state and
+        the leaf store in its own scratch)."""
+        torch = self.torch
+        nat = getattr(self, "_native", None)
+        if nat is not None and nat["shape"] == (C, d):
+            return nat
+        if nat is not None:
+            self._free(*nat["h"].values())
+        t = dict(q0=torch.empty(C, d, **self.f64), sample=torch.empty(C, d, **self.f64),
+                 flags=torch.empty(4, C, dtype=torch.int32, device=self.dev),
+                 H0=torch.empty(C, **self.f64))
+        h = {k: self._h(v) for k, v in t.items()}
+        h.update(prec=self._h(self.prec), m=self._h(self.m_dev))
+        self._native = {"shape": (C, d), "t": t, "h": h}
+        return self._native
+
+    def _transition_native(self, q0, seed, max_depth):
+        torch, lib = self.torch, self.lib
+        q0 = torch.as_tensor(q0, dtype=torch.float64).to(self.dev)
+        C, d = q0.shape
+        nat = self._native_state(C, d)
+        t, h = nat["t"], nat["h"]
+        t["q0"].copy_(q0)
+        self._call(lib.nxv_nuts_transition_layout, h["sample"], h["flags"], h["H0"], h["q0"],
+                   h["m"], h["prec"], self.t.mu, self.t.const, self.eps, C, d, max_depth,
+                   seed & 0xFFFFFFFF)
+        flags = t["flags"].cpu().numpy()  # active, divergent, depth, leaf count
+        for level in range(int(flags[2].max())):
+            self.calls.append((C, 1 << level))
+        stats = Stats(depth=flags[2].astype(np.int64), n_leapfrog=flags[3].astype(np.int64),
+                      divergent=flags[1].astype(bool), energy=t["H0"].cpu().numpy())
+        return t["sample"].clone(), stats
 
     def __del__(self):
         try:

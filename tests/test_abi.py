@@ -114,3 +114,6 @@ def test_nuts_layout_entry_points_validate_before_any_device_work():
     assert lib.nxv_nuts_level_layout(0, 3, 8, *bufs, 2, 1) == -3
     assert lib.nxv_nuts_level_layout(0, 4096, 8, *bufs, 2, 12) == -3
     assert lib.nxv_nuts_start_layout(None, p, p, p, p, p, p, p, 2, 8) == -1
+    assert lib.nxv_nuts_transition_layout(p, None, p, p, p, p, 0.0, 0.0, 0.1, 2, 8, 4, 1) == -1
+    assert lib.nxv_nuts_transition_layout(p, p, p, p, p, p, 0.0, 0.0, 0.1, 2, 8, 0, 1) == -3
+    assert lib.nxv_nuts_transition_layout(p, p, p, p, p, p, 0.0, 0.0, 0.1, 2, 8, 13, 1) == -3

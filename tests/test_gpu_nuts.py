@@ -35,16 +35,17 @@ def test_nuts_gpu_matches_oracle(nxv, d, C, T):
 
 
 @pytest.mark.parametrize("d,C,T,depth", [(16, 64, 6, 8), (100, 256, 3, 8), (1000, 8, 2, 6)])
-@pytest.mark.parametrize("driver", ["layout", "host"])
+@pytest.mark.parametrize("driver", ["layout", "levels", "host"])
 def test_nuts_device_tree_matches_host_tree(nxv, d, C, T, depth, driver):
     """The tree walk on the device against the host tree builder over the
     same GPU chain and the same random numbers: the same depth and leaf
     count for every chain, and the same draw except where a U-turn or
     selection decision lies within rounding of its threshold (the two sum in
     different orders); at least 98 % of the draws are bit-identical.
-    layout: the device draws the momenta and uniforms (Philox) and keeps the
-    tree state; the host walk is given the same draws.  host: both draw from
-    numpy generators with the same seed."""
+    layout / levels: the device draws the momenta and uniforms (Philox) and
+    keeps the tree state (one library call per transition / the per-level
+    calls from Python); the host walk is given the same draws.  host: both
+    draw from numpy generators with the same seed."""
     import torch
 
     r = np.random.default_rng(7)
@@ -57,7 +58,7 @@ def test_nuts_device_tree_matches_host_tree(nxv, d, C, T, depth, driver):
     qa = q_init.copy()
     same = total = same_depth = 0
     for k in range(T):
-        if driver == "layout":
+        if driver in ("layout", "levels"):
             seed = 1000 + k
             p0, u = dev.randomness(C, seed, depth)
             qa_new, sa = nuts.nuts_transition(host_src, t, qa, m, None, max_depth=depth,
@@ -79,6 +80,34 @@ def test_nuts_device_tree_matches_host_tree(nxv, d, C, T, depth, driver):
     print(f"device tree ({driver}): {same} of {total} draws and {same_depth} trees identical "
           f"to the host's")
     assert same >= 0.98 * total and same_depth >= 0.98 * total
+
+
+@pytest.mark.parametrize("d,C,depth", [(16, 64, 8), (100, 256, 8), (1, 1, 1), (2000, 3, 5),
+                                       (7, 300, 10)])
+def test_nuts_one_call_transition_matches_level_calls(nxv, d, C, depth):
+    """nxv_nuts_transition_layout (the whole transition in one library call)
+    against the same transition issued level by level from Python: the same
+    kernels in the same order, so draws, energies, depths, leaf counts and
+    divergence flags are bit-identical, over two transitions that continue
+    from each other and a new seed each time."""
+    import torch
+
+    r = np.random.default_rng(17)
+    prec = r.uniform(0.5, 2.0, d)
+    t = nuts.GaussianTarget(prec, mu=0.3)
+    m = r.uniform(0.8, 1.2, d)
+    eps = 0.2 if d < 10 else (0.05 if d <= 100 else 0.02)
+    one, lev = nuts.DeviceTree(t, m, eps, driver="layout"), nuts.DeviceTree(t, m, eps, driver="levels")
+    q = torch.from_numpy(r.normal(size=(C, d)) / np.sqrt(prec) + 0.3).cuda()
+    for k in range(2):
+        qa, sa = one.transition(q, max_depth=depth, seed=70 + k)
+        qb, sb = lev.transition(q, max_depth=depth, seed=70 + k)
+        assert torch.equal(qa, qb)
+        for f in ("depth", "n_leapfrog", "divergent", "energy"):
+            assert np.array_equal(getattr(sa, f), getattr(sb, f)), f
+        assert sa.depth.max() <= depth and sa.depth.min() >= 1
+        q = qa
+    assert one.calls == lev.calls
 
 
 def test_nuts_layout_randomness(nxv):
