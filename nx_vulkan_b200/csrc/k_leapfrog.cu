@@ -573,10 +573,16 @@ int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void
     return E_ARG;
 }
 
+int launch_gauss_const(Ctx& c, const void* prec, size_t n, void* out) {
+    k_gauss_const<<<1, 256, 0, c.stream>>>((const double*)prec, n, (double*)out);
+    count_launch();
+    return OK;
+}
+
 int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                            const void* p0, const void* m, const void* prec, double prec_scalar,
                            double mu, size_t n, size_t chains, unsigned K, double eps, void* ke,
-                           bool m_shared) {
+                           bool m_shared, const void* cst_dev) {
     ChainArgs<double> g{};
     g.qc = (double*)qc;
     g.pc = (double*)pc;
@@ -609,7 +615,12 @@ int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, con
         if (ke) g.ke_partial = (double*)(base + 256 + part);
     }
     FamGauss64 fam{(const double*)prec, prec_scalar, mu};
-    if (prec) {
+    if (prec && cst_dev) {
+        // the caller computed the constant (launch_gauss_const) for many calls
+        g.cst = 0.0;
+        g.cst_dev = (const double*)cst_dev;
+        fam.prec_s = 0.0;
+    } else if (prec) {
         // The constant needs sum(log prec): one tiny launch ahead of the
         // chain writes it to the first 256 bytes of scratch.
         k_gauss_const<<<1, 256, 0, c.stream>>>((const double*)prec, n, (double*)base);

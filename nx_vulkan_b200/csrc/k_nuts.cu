@@ -664,7 +664,7 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
     const size_t o_z = take(CD * 8), o_u = take(L * 3 * C * 8), o_rho = take(CD * 8),
                  o_ep = take(2 * CD * 8), o_eps = take(2 * CD * 8), o_logw = take(C * 8),
                  o_qs = take(CD * 8), o_ps = take(CD * 8), o_er = take(2 * C * 8),
-                 o_any = take(4), o_sq = take(R * D * 8), o_sp = take(R * D * 8),
+                 o_any = take(4), o_cst = take(8), o_sq = take(R * D * 8), o_sp = take(R * D * 8),
                  o_sl = take(R * 8), o_sk = take(R * 8), o_node = take(C * nmax * D * 8),
                  o_grad = take(C * nmax * D * 8);
     ScratchGuard guard(c);
@@ -700,6 +700,8 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
         (double*)dptr(H0), (double*)(base + o_logw), q0d, z, pr, m, mu, logp_const, (int)C,
         (int)D);
     count_launch(2);
+    // the chain's log-density constant, once for every level's chain call
+    if ((rc = launch_gauss_const(c, pr, D, base + o_cst))) return rc;
     LevelArgs g{};
     g.d = (int)D;
     g.st_q = st_q;
@@ -731,7 +733,7 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
         count_launch();
         rc = launch_chain_gauss_f64(c, st_q + row0 * D, st_p + row0 * D, base + o_grad,
                                     st_logp + row0, qs, ps, m, pr, 0.0, mu, D, C, (unsigned)n,
-                                    eps, st_ke + row0, true);
+                                    eps, st_ke + row0, true, base + o_cst);
         if (rc) return rc;
         g.n = (int)n;
         Lg.base = (long long)row0;
@@ -739,8 +741,11 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
         Lg.level = (int)level;
         k_nuts_level_layout<<<(unsigned)C, kNT, 0, c.stream>>>(g, Lg);
         count_launch();
-        if (level + 1 < L) {
-            // one 4-byte read per level: does any tree still grow?
+        // one 4-byte read per level from the third on: does any tree still
+        // grow?  The first two levels (1 and 2 leapfrog steps) always run:
+        // for chains whose tree has stopped, a level's kernels change nothing
+        // but scratch, so running one is cheaper than waiting for the flag.
+        if (level >= 1 && level + 1 < L) {
             cudaError_t e = cudaMemcpyAsync(any_h, any, sizeof(int), cudaMemcpyDeviceToHost,
                                             c.stream);
             if (e == cudaSuccess) e = cudaStreamSynchronize(c.stream);

@@ -61,10 +61,15 @@ int launch_chain_f32(Ctx& c, int fam, const float* prm, void* qc, void* pc, void
 // f64 Gaussian: prec == nullptr means prec_i = prec_scalar for all i.
 // ke: optional [chain][k] kinetic energy 0.5 * sum(p*p*inv_mass) per step.
 // m_shared: m is one [n] row used by every chain (else [chain][n]).
+// cst_dev: optional device double holding the log-density constant of prec
+// (from launch_gauss_const), for callers that make many calls with one prec.
 int launch_chain_gauss_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                            const void* p0, const void* m, const void* prec, double prec_scalar,
                            double mu, size_t n, size_t chains, unsigned K, double eps,
-                           void* ke = nullptr, bool m_shared = false);
+                           void* ke = nullptr, bool m_shared = false,
+                           const void* cst_dev = nullptr);
+// The f64 Gaussian chain's log-density constant for prec [n] into out[0].
+int launch_gauss_const(Ctx& c, const void* prec, size_t n, void* out);
 int launch_chain_logreg_f64(Ctx& c, void* qc, void* pc, void* gc, void* logp, const void* q0,
                             const void* p0, const void* X, const void* y, size_t n_obs,
                             size_t n_dim, size_t chains, unsigned K, double eps);
