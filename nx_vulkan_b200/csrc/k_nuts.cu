@@ -291,7 +291,39 @@ struct LayoutArgs {
     int* n_leapfrog;       // [C]
     int* any;              // optional: set to 1 by every chain that keeps building
     int level;
+    // optional: the next level's starting points, written here for the
+    // chains that keep building (the work of k_nuts_start_layout)
+    const double* next_u_dir;  // [C] the next level's direction uniforms
+    double* qs;
+    double* ps;
+    const double* q0;
+    const double* p0;
+    long long st_rows;
 };
+
+// Starting point of chain c's next extension: its tree's end leaf on the
+// side u_dir picks, or (q0[c], +-p0[c]) while that side has none (or the
+// row is outside the store).
+__device__ __forceinline__ void start_point(double* qs, double* ps, const double* q0,
+                                            const double* p0, const double* st_q,
+                                            const double* st_p, const long long* end_row,
+                                            double u_dir, int c, int C, int d,
+                                            long long st_rows) {
+    const bool fwd = u_dir >= 0.5;
+    long long r = end_row[(fwd ? C : 0) + c];
+    if (r >= st_rows) r = -1;  // not a row of this store: restart from the initial point
+    const double sg = fwd ? 1.0 : -1.0;
+    for (int k = threadIdx.x; k < d; k += kNT) {
+        const size_t o = (size_t)c * d + k;
+        if (r >= 0) {
+            qs[o] = st_q[(size_t)r * d + k];
+            ps[o] = st_p[(size_t)r * d + k];
+        } else {
+            qs[o] = q0[o];
+            ps[o] = mul_(sg, p0[o]);
+        }
+    }
+}
 
 __global__ void __launch_bounds__(kNT) k_nuts_level_layout(LevelArgs a, LayoutArgs L) {
     const int c = blockIdx.x, n = a.n, C = a.C;
@@ -306,6 +338,12 @@ __global__ void __launch_bounds__(kNT) k_nuts_level_layout(LevelArgs a, LayoutAr
         L.depth[c] = L.level + 1;
         L.n_leapfrog[c] += n;
         if (L.any && a.active[c]) *L.any = 1;  // written by this thread in level_walk
+    }
+    if (L.next_u_dir) {
+        __syncthreads();  // active and end_row as thread 0 left them
+        if (a.active[c])
+            start_point(L.qs, L.ps, L.q0, L.p0, a.st_q, a.st_p, L.end_row, L.next_u_dir[c], c, C,
+                        a.d, L.st_rows);
     }
 }
 
@@ -361,34 +399,22 @@ __global__ void __launch_bounds__(kNT) k_nuts_start_layout(double* qs, double* p
                                                            const double* st_q, const double* st_p,
                                                            const long long* end_row,
                                                            const double* u_dir, int C, int d,
-                                                           long long st_rows, int* any) {
-    const int c = blockIdx.x;
-    if (any && c == 0 && threadIdx.x == 0) *any = 0;  // this level's level kernel sets it
-    const bool fwd = u_dir[c] >= 0.5;
-    long long r = end_row[(fwd ? C : 0) + c];
-    if (r >= st_rows) r = -1;  // not a row of this store: restart from the initial point
-    const double sg = fwd ? 1.0 : -1.0;
-    for (int k = threadIdx.x; k < d; k += kNT) {
-        const size_t o = (size_t)c * d + k;
-        if (r >= 0) {
-            qs[o] = st_q[(size_t)r * d + k];
-            ps[o] = st_p[(size_t)r * d + k];
-        } else {
-            qs[o] = q0[o];
-            ps[o] = mul_(sg, p0[o]);
-        }
-    }
+                                                           long long st_rows) {
+    start_point(qs, ps, q0, p0, st_q, st_p, end_row, u_dir[blockIdx.x], blockIdx.x, C, d,
+                st_rows);
 }
 
 // A transition's initial state, one CTA per chain: p0 = z / sqrt(inv_mass)
 // in place (z: standard normal draws), sample = q0, rho and both tree ends
 // = p0, end velocities p0 * inv_mass, flags (active, divergent, depth,
-// leapfrog count) = (1, 0, 0, 0), end rows -1.
+// leapfrog count) = (1, 0, 0, 0), end rows -1, the per-level flags 0.
 __global__ void __launch_bounds__(kNT) k_nuts_init(double* z, const double* q0, const double* m,
                                                    double* sample, double* rho, double* end_p,
                                                    double* end_ps, int* flags,
-                                                   long long* end_row, int C, int d) {
+                                                   long long* end_row, int* any, int levels,
+                                                   int C, int d) {
     const int c = blockIdx.x;
+    if (c == 0 && threadIdx.x < levels) any[threadIdx.x] = 0;  // per-level "still growing"
     const size_t CD = (size_t)C * d;
     for (int k = threadIdx.x; k < d; k += kNT) {
         const size_t o = (size_t)c * d + k;
@@ -561,7 +587,7 @@ int nxv_nuts_start_layout(void* qs, void* ps, void* q0, void* p0, void* st_q, vo
     k_nuts_start_layout<<<n_chains, kNT, 0, c.stream>>>(
         (double*)dptr(qs), (double*)dptr(ps), (const double*)dptr(q0), (const double*)dptr(p0),
         (const double*)dptr(st_q), (const double*)dptr(st_p), (const long long*)dptr(end_row),
-        (const double*)dptr(u_dir), (int)n_chains, (int)d, st_rows, nullptr);
+        (const double*)dptr(u_dir), (int)n_chains, (int)d, st_rows);
     count_launch();
     return finish(c);
 }
@@ -626,6 +652,7 @@ int nxv_nuts_level_layout(unsigned long long base_row, unsigned int n, unsigned 
     L.n_leapfrog = (int*)dptr(n_leapfrog);
     L.any = nullptr;
     L.level = (int)level;
+    L.next_u_dir = nullptr;
     k_nuts_level_layout<<<(unsigned)C, kNT, 0, c.stream>>>(g, L);
     count_launch();
     return finish(c);
@@ -664,7 +691,7 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
     const size_t o_z = take(CD * 8), o_u = take(L * 3 * C * 8), o_rho = take(CD * 8),
                  o_ep = take(2 * CD * 8), o_eps = take(2 * CD * 8), o_logw = take(C * 8),
                  o_qs = take(CD * 8), o_ps = take(CD * 8), o_er = take(2 * C * 8),
-                 o_any = take(4), o_cst = take(8), o_sq = take(R * D * 8), o_sp = take(R * D * 8),
+                 o_any = take(L * 4), o_cst = take(8), o_sq = take(R * D * 8), o_sp = take(R * D * 8),
                  o_sl = take(R * 8), o_sk = take(R * 8), o_node = take(C * nmax * D * 8),
                  o_grad = take(C * nmax * D * 8);
     ScratchGuard guard(c);
@@ -695,7 +722,7 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
     if ((rc = launch_random(c, F64, base + o_u, L * 3 * C, ku, 0))) return rc;
     k_nuts_init<<<(unsigned)C, kNT, 0, c.stream>>>(
         z, q0d, m, (double*)dptr(sample), (double*)(base + o_rho), (double*)(base + o_ep),
-        (double*)(base + o_eps), fl, end_row, (int)C, (int)D);
+        (double*)(base + o_eps), fl, end_row, any, (int)L, (int)C, (int)D);
     k_nuts_energy<<<(unsigned)((C + kNW - 1) / kNW), kNT, 0, c.stream>>>(
         (double*)dptr(H0), (double*)(base + o_logw), q0d, z, pr, m, mu, logp_const, (int)C,
         (int)D);
@@ -723,14 +750,19 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
     Lg.end_row = end_row;
     Lg.depth = fl + 2 * C;
     Lg.n_leapfrog = fl + 3 * C;
-    Lg.any = any;
+    Lg.qs = qs;
+    Lg.ps = ps;
+    Lg.q0 = q0d;
+    Lg.p0 = z;
+    Lg.st_rows = (long long)R;
+    // level 0 starts from the initial point; every level kernel writes the
+    // next level's starting points
+    k_nuts_start_layout<<<(unsigned)C, kNT, 0, c.stream>>>(qs, ps, q0d, z, st_q, st_p, end_row,
+                                                         u, (int)C, (int)D, (long long)R);
+    count_launch();
     for (size_t level = 0; level < L; level++) {
         const size_t n = size_t(1) << level, row0 = C * (n - 1);
         const double* ul = u + level * 3 * C;
-        k_nuts_start_layout<<<(unsigned)C, kNT, 0, c.stream>>>(qs, ps, q0d, z, st_q, st_p,
-                                                             end_row, ul, (int)C, (int)D,
-                                                             (long long)R, any);
-        count_launch();
         rc = launch_chain_gauss_f64(c, st_q + row0 * D, st_p + row0 * D, base + o_grad,
                                     st_logp + row0, qs, ps, m, pr, 0.0, mu, D, C, (unsigned)n,
                                     eps, st_ke + row0, true, base + o_cst);
@@ -739,6 +771,8 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
         Lg.base = (long long)row0;
         Lg.u = ul;
         Lg.level = (int)level;
+        Lg.any = any + level;
+        Lg.next_u_dir = level + 1 < L ? ul + 3 * C : nullptr;
         k_nuts_level_layout<<<(unsigned)C, kNT, 0, c.stream>>>(g, Lg);
         count_launch();
         // one 4-byte read per level from the third on: does any tree still
@@ -746,8 +780,8 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
         // for chains whose tree has stopped, a level's kernels change nothing
         // but scratch, so running one is cheaper than waiting for the flag.
         if (level >= 1 && level + 1 < L) {
-            cudaError_t e = cudaMemcpyAsync(any_h, any, sizeof(int), cudaMemcpyDeviceToHost,
-                                            c.stream);
+            cudaError_t e = cudaMemcpyAsync(any_h, any + level, sizeof(int),
+                                            cudaMemcpyDeviceToHost, c.stream);
             if (e == cudaSuccess) e = cudaStreamSynchronize(c.stream);
             if (e != cudaSuccess) return cuda_fail(e, "nuts_transition_layout: flag read");
             if (*any_h == 0) break;
