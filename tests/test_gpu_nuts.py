@@ -83,7 +83,7 @@ def test_nuts_device_tree_matches_host_tree(nxv, d, C, T, depth, driver):
 
 
 @pytest.mark.parametrize("d,C,depth", [(16, 64, 8), (100, 256, 8), (1, 1, 1), (2000, 3, 5),
-                                       (7, 300, 10)])
+                                       (7, 300, 10), (2, 4, 12)])
 def test_nuts_one_call_transition_matches_level_calls(nxv, d, C, depth):
     """nxv_nuts_transition_layout (the whole transition in one library call)
     against the same transition issued level by level from Python: the same
