@@ -404,6 +404,44 @@ __global__ void __launch_bounds__(kNT) k_nuts_start_layout(double* qs, double* p
                 st_rows);
 }
 
+// Starting points of level `level` computed from the directions alone, so
+// that the level's chain call can run while the previous level's walk
+// does: a chain still building at this level extended its tree at level j
+// in direction u_j, and its end on a side is the last leaf of the latest
+// level in that direction (the initial point while there is none).
+// spec_end [2][C] holds those rows (the level kernels keep their own
+// end_row); level - 1's last leaf is row prev_base + c n_prev + n_prev - 1.
+// For chains that stopped, the point is never used.
+__global__ void __launch_bounds__(kNT) k_nuts_start_spec(double* qs, double* ps,
+                                                         const double* q0, const double* p0,
+                                                         const double* st_q, const double* st_p,
+                                                         long long* spec_end, const double* u_dir,
+                                                         const double* u_prev, long long prev_base,
+                                                         long long n_prev, int C, int d,
+                                                         long long st_rows) {
+    const int c = blockIdx.x;
+    const bool fwd = u_dir[c] >= 0.5;
+    long long r = -1;
+    if (u_prev) {
+        const bool fwd_prev = u_prev[c] >= 0.5;
+        const long long last = prev_base + (long long)c * n_prev + n_prev - 1;
+        r = fwd == fwd_prev ? last : spec_end[(fwd ? C : 0) + c];  // never the side written
+        if (threadIdx.x == 0) spec_end[(fwd_prev ? C : 0) + c] = last;
+    }
+    if (r >= st_rows) r = -1;
+    const double sg = fwd ? 1.0 : -1.0;
+    for (int k = threadIdx.x; k < d; k += kNT) {
+        const size_t o = (size_t)c * d + k;
+        if (r >= 0) {
+            qs[o] = st_q[(size_t)r * d + k];
+            ps[o] = st_p[(size_t)r * d + k];
+        } else {
+            qs[o] = q0[o];
+            ps[o] = mul_(sg, p0[o]);
+        }
+    }
+}
+
 // A transition's initial state, one CTA per chain: p0 = z / sqrt(inv_mass)
 // in place (z: standard normal draws), sample = q0, rho and both tree ends
 // = p0, end velocities p0 * inv_mass, flags (active, divergent, depth,
@@ -411,8 +449,8 @@ __global__ void __launch_bounds__(kNT) k_nuts_start_layout(double* qs, double* p
 __global__ void __launch_bounds__(kNT) k_nuts_init(double* z, const double* q0, const double* m,
                                                    double* sample, double* rho, double* end_p,
                                                    double* end_ps, int* flags,
-                                                   long long* end_row, int* any, int levels,
-                                                   int C, int d) {
+                                                   long long* end_row, long long* spec_end,
+                                                   int* any, int levels, int C, int d) {
     const int c = blockIdx.x;
     if (c == 0 && threadIdx.x < levels) any[threadIdx.x] = 0;  // per-level "still growing"
     const size_t CD = (size_t)C * d;
@@ -435,12 +473,37 @@ __global__ void __launch_bounds__(kNT) k_nuts_init(double* z, const double* q0, 
         flags[3 * C + c] = 0;
         end_row[c] = -1;
         end_row[C + c] = -1;
+        spec_end[c] = -1;
+        spec_end[C + c] = -1;
     }
 }
 
 // Pinned host word per device for the per-level "any tree still growing" read.
 std::mutex g_any_mu;
 int* g_any_host[64] = {};
+
+// Per device: a second stream for the level kernels of the one-call
+// transition (the chain calls stay on the caller's stream) and two events.
+struct NutsStreams {
+    cudaStream_t aux = nullptr;
+    cudaEvent_t chain_done = nullptr, level_done = nullptr;
+};
+NutsStreams g_nuts_streams[64];
+
+NutsStreams* nuts_streams(int dev) {
+    std::lock_guard<std::mutex> lk(g_any_mu);
+    if (dev < 0 || dev >= 64) return nullptr;
+    NutsStreams& s = g_nuts_streams[dev];
+    if (!s.aux) {
+        if (cudaStreamCreateWithFlags(&s.aux, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&s.chain_done, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&s.level_done, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+    }
+    return &s;
+}
 
 int* any_host(int dev) {
     std::lock_guard<std::mutex> lk(g_any_mu);
@@ -691,6 +754,7 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
     const size_t o_z = take(CD * 8), o_u = take(L * 3 * C * 8), o_rho = take(CD * 8),
                  o_ep = take(2 * CD * 8), o_eps = take(2 * CD * 8), o_logw = take(C * 8),
                  o_qs = take(CD * 8), o_ps = take(CD * 8), o_er = take(2 * C * 8),
+                 o_se = take(2 * C * 8),
                  o_any = take(L * 4), o_cst = take(8), o_sq = take(R * D * 8), o_sp = take(R * D * 8),
                  o_sl = take(R * 8), o_sk = take(R * 8), o_node = take(C * nmax * D * 8),
                  o_grad = take(C * nmax * D * 8);
@@ -698,13 +762,15 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
     char* base = (char*)scratch(c, off, kScratchNuts);
     if (!base) return E_CUDA;
     int* any_h = any_host(c.dev->id);
-    if (!any_h) {
-        set_error("nuts_transition_layout: pinned host word allocation failed");
+    NutsStreams* ns = nuts_streams(c.dev->id);
+    if (!any_h || !ns) {
+        set_error("nuts_transition_layout: pinned host word or stream creation failed");
         return E_CUDA;
     }
     double* z = (double*)(base + o_z);
     const double* u = (const double*)(base + o_u);
     long long* end_row = (long long*)(base + o_er);
+    long long* spec_end = (long long*)(base + o_se);
     int* any = (int*)(base + o_any);
     double* st_q = (double*)(base + o_sq);
     double* st_p = (double*)(base + o_sp);
@@ -722,7 +788,7 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
     if ((rc = launch_random(c, F64, base + o_u, L * 3 * C, ku, 0))) return rc;
     k_nuts_init<<<(unsigned)C, kNT, 0, c.stream>>>(
         z, q0d, m, (double*)dptr(sample), (double*)(base + o_rho), (double*)(base + o_ep),
-        (double*)(base + o_eps), fl, end_row, any, (int)L, (int)C, (int)D);
+        (double*)(base + o_eps), fl, end_row, spec_end, any, (int)L, (int)C, (int)D);
     k_nuts_energy<<<(unsigned)((C + kNW - 1) / kNW), kNT, 0, c.stream>>>(
         (double*)dptr(H0), (double*)(base + o_logw), q0d, z, pr, m, mu, logp_const, (int)C,
         (int)D);
@@ -750,43 +816,63 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
     Lg.end_row = end_row;
     Lg.depth = fl + 2 * C;
     Lg.n_leapfrog = fl + 3 * C;
-    Lg.qs = qs;
-    Lg.ps = ps;
-    Lg.q0 = q0d;
-    Lg.p0 = z;
-    Lg.st_rows = (long long)R;
-    // level 0 starts from the initial point; every level kernel writes the
-    // next level's starting points
-    k_nuts_start_layout<<<(unsigned)C, kNT, 0, c.stream>>>(qs, ps, q0d, z, st_q, st_p, end_row,
-                                                         u, (int)C, (int)D, (long long)R);
-    count_launch();
-    for (size_t level = 0; level < L; level++) {
+    // Two streams: the caller's runs the start kernels and the chain calls,
+    // the library's second stream the level kernels.  The starting points
+    // of level l + 1 depend only on the directions and on rows written by
+    // earlier chain calls (k_nuts_start_spec), so level l + 1's chain call
+    // runs while level l's walk does; level l + 1's walk waits for both.
+    // When the flag after level l says that every tree has stopped, the
+    // chain call of level l + 1 has been issued for nothing.
+    const long long RR = (long long)R;
+    auto chain_level = [&](size_t level) -> int {
         const size_t n = size_t(1) << level, row0 = C * (n - 1);
         const double* ul = u + level * 3 * C;
-        rc = launch_chain_gauss_f64(c, st_q + row0 * D, st_p + row0 * D, base + o_grad,
-                                    st_logp + row0, qs, ps, m, pr, 0.0, mu, D, C, (unsigned)n,
-                                    eps, st_ke + row0, true, base + o_cst);
-        if (rc) return rc;
+        const double* up = level ? ul - 3 * C : nullptr;
+        const long long nprev = level ? (long long)(n / 2) : 0;
+        const long long prev0 = level ? (long long)(C * (n / 2 - 1)) : 0;
+        k_nuts_start_spec<<<(unsigned)C, kNT, 0, c.stream>>>(qs, ps, q0d, z, st_q, st_p, spec_end,
+                                                           ul, up, prev0, nprev, (int)C, (int)D,
+                                                           RR);
+        count_launch();
+        int r2 = launch_chain_gauss_f64(c, st_q + row0 * D, st_p + row0 * D, base + o_grad,
+                                        st_logp + row0, qs, ps, m, pr, 0.0, mu, D, C,
+                                        (unsigned)n, eps, st_ke + row0, true, base + o_cst);
+        if (r2) return r2;
+        cudaError_t e = cudaEventRecord(ns->chain_done, c.stream);
+        return e == cudaSuccess ? OK : cuda_fail(e, "nuts_transition_layout: event");
+    };
+    if ((rc = chain_level(0))) return rc;
+    for (size_t level = 0; level < L; level++) {
+        const size_t n = size_t(1) << level, row0 = C * (n - 1);
         g.n = (int)n;
         Lg.base = (long long)row0;
-        Lg.u = ul;
+        Lg.u = u + level * 3 * C;
         Lg.level = (int)level;
         Lg.any = any + level;
-        Lg.next_u_dir = level + 1 < L ? ul + 3 * C : nullptr;
-        k_nuts_level_layout<<<(unsigned)C, kNT, 0, c.stream>>>(g, Lg);
+        Lg.next_u_dir = nullptr;
+        cudaError_t e = cudaStreamWaitEvent(ns->aux, ns->chain_done, 0);
+        if (e != cudaSuccess) return cuda_fail(e, "nuts_transition_layout: stream wait");
+        k_nuts_level_layout<<<(unsigned)C, kNT, 0, ns->aux>>>(g, Lg);
         count_launch();
-        // one 4-byte read per level from the third on: does any tree still
-        // grow?  The first two levels (1 and 2 leapfrog steps) always run:
-        // for chains whose tree has stopped, a level's kernels change nothing
-        // but scratch, so running one is cheaper than waiting for the flag.
-        if (level >= 1 && level + 1 < L) {
-            cudaError_t e = cudaMemcpyAsync(any_h, any + level, sizeof(int),
-                                            cudaMemcpyDeviceToHost, c.stream);
-            if (e == cudaSuccess) e = cudaStreamSynchronize(c.stream);
+        // one 4-byte read per level from the second on (the first level
+        // always continues: for chains whose tree has stopped, a level's
+        // kernels change nothing but scratch)
+        const bool check = level >= 1 && level + 1 < L;
+        if (check)
+            e = cudaMemcpyAsync(any_h, any + level, sizeof(int), cudaMemcpyDeviceToHost, ns->aux);
+        if (e == cudaSuccess) e = cudaEventRecord(ns->level_done, ns->aux);
+        if (e != cudaSuccess) return cuda_fail(e, "nuts_transition_layout: level");
+        if (level + 1 < L && (rc = chain_level(level + 1))) return rc;
+        if (check) {
+            e = cudaEventSynchronize(ns->level_done);
             if (e != cudaSuccess) return cuda_fail(e, "nuts_transition_layout: flag read");
             if (*any_h == 0) break;
         }
     }
+    // the outputs (and the next call's use of the scratch) follow the last
+    // level kernel in the caller's stream order
+    cudaError_t e = cudaStreamWaitEvent(c.stream, ns->level_done, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "nuts_transition_layout: stream wait");
     return finish(c);
 }
 
