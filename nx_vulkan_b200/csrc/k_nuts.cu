@@ -291,14 +291,6 @@ struct LayoutArgs {
     int* n_leapfrog;       // [C]
     int* any;              // optional: set to 1 by every chain that keeps building
     int level;
-    // optional: the next level's starting points, written here for the
-    // chains that keep building (the work of k_nuts_start_layout)
-    const double* next_u_dir;  // [C] the next level's direction uniforms
-    double* qs;
-    double* ps;
-    const double* q0;
-    const double* p0;
-    long long st_rows;
 };
 
 // Starting point of chain c's next extension: its tree's end leaf on the
@@ -338,12 +330,6 @@ __global__ void __launch_bounds__(kNT) k_nuts_level_layout(LevelArgs a, LayoutAr
         L.depth[c] = L.level + 1;
         L.n_leapfrog[c] += n;
         if (L.any && a.active[c]) *L.any = 1;  // written by this thread in level_walk
-    }
-    if (L.next_u_dir) {
-        __syncthreads();  // active and end_row as thread 0 left them
-        if (a.active[c])
-            start_point(L.qs, L.ps, L.q0, L.p0, a.st_q, a.st_p, L.end_row, L.next_u_dir[c], c, C,
-                        a.d, L.st_rows);
     }
 }
 
@@ -715,7 +701,6 @@ int nxv_nuts_level_layout(unsigned long long base_row, unsigned int n, unsigned 
     L.n_leapfrog = (int*)dptr(n_leapfrog);
     L.any = nullptr;
     L.level = (int)level;
-    L.next_u_dir = nullptr;
     k_nuts_level_layout<<<(unsigned)C, kNT, 0, c.stream>>>(g, L);
     count_launch();
     return finish(c);
@@ -849,7 +834,6 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
         Lg.u = u + level * 3 * C;
         Lg.level = (int)level;
         Lg.any = any + level;
-        Lg.next_u_dir = nullptr;
         cudaError_t e = cudaStreamWaitEvent(ns->aux, ns->chain_done, 0);
         if (e != cudaSuccess) return cuda_fail(e, "nuts_transition_layout: stream wait");
         k_nuts_level_layout<<<(unsigned)C, kNT, 0, ns->aux>>>(g, Lg);
