@@ -581,40 +581,51 @@ class DeviceTree:
             self._free(*nat["h"].values())
             self._native = None
 
-    def _native_state(self, C, d):
-        """Input and output tensors of the one-call transition for C chains of
-        dimension d, with their handles (the library keeps the tree state and
-        the leaf store in its own scratch)."""
+    def _native_state(self, C):
+        """Output tensors of the one-call transition for C chains (flags and
+        energies, with pinned host copies for one read per transition) and
+        the handles of the target's rows (the library keeps the tree state
+        and the leaf store in its own scratch)."""
         torch = self.torch
         nat = getattr(self, "_native", None)
-        if nat is not None and nat["shape"] == (C, d):
+        if nat is not None and nat["shape"] == C:
             return nat
         if nat is not None:
             self._free(*nat["h"].values())
-        t = dict(q0=torch.empty(C, d, **self.f64), sample=torch.empty(C, d, **self.f64),
-                 flags=torch.empty(4, C, dtype=torch.int32, device=self.dev),
+        t = dict(flags=torch.empty(4, C, dtype=torch.int32, device=self.dev),
                  H0=torch.empty(C, **self.f64))
         h = {k: self._h(v) for k, v in t.items()}
         h.update(prec=self._h(self.prec), m=self._h(self.m_dev))
-        self._native = {"shape": (C, d), "t": t, "h": h}
+        host = dict(flags=torch.empty(4, C, dtype=torch.int32, pin_memory=True),
+                    H0=torch.empty(C, dtype=torch.float64, pin_memory=True))
+        self._native = {"shape": C, "t": t, "h": h, "host": host}
         return self._native
 
     def _transition_native(self, q0, seed, max_depth):
         torch, lib = self.torch, self.lib
-        q0 = torch.as_tensor(q0, dtype=torch.float64).to(self.dev)
+        q0 = torch.as_tensor(q0, dtype=torch.float64, device=self.dev).contiguous()
         C, d = q0.shape
-        nat = self._native_state(C, d)
-        t, h = nat["t"], nat["h"]
-        t["q0"].copy_(q0)
-        self._call(lib.nxv_nuts_transition_layout, h["sample"], h["flags"], h["H0"], h["q0"],
-                   h["m"], h["prec"], self.t.mu, self.t.const, self.eps, C, d, max_depth,
-                   seed & 0xFFFFFFFF)
-        flags = t["flags"].cpu().numpy()  # active, divergent, depth, leaf count
+        nat = self._native_state(C)
+        t, h, host = nat["t"], nat["h"], nat["host"]
+        sample = torch.empty(C, d, **self.f64)
+        # the caller's positions and the new draws are wrapped, not copied;
+        # the library reads and writes them in this stream's order
+        hq, hs = self._h(q0), self._h(sample)
+        try:
+            self._call(lib.nxv_nuts_transition_layout, hs, h["flags"], h["H0"], hq, h["m"],
+                       h["prec"], self.t.mu, self.t.const, self.eps, C, d, max_depth,
+                       seed & 0xFFFFFFFF)
+        finally:
+            self._free(hq, hs)
+        host["flags"].copy_(t["flags"], non_blocking=True)
+        host["H0"].copy_(t["H0"], non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        flags = host["flags"].numpy()  # active, divergent, depth, leaf count
         for level in range(int(flags[2].max())):
             self.calls.append((C, 1 << level))
         stats = Stats(depth=flags[2].astype(np.int64), n_leapfrog=flags[3].astype(np.int64),
-                      divergent=flags[1].astype(bool), energy=t["H0"].cpu().numpy())
-        return t["sample"].clone(), stats
+                      divergent=flags[1].astype(bool), energy=host["H0"].numpy().copy())
+        return sample, stats
 
     def __del__(self):
         try:
