@@ -112,6 +112,31 @@ __device__ __forceinline__ void level_walk(const LevelArgs& a, int c, bool fwd, 
     const int n = a.n, d = a.d;
     const double sg = fwd ? 1.0 : -1.0;  // backward leaves were integrated with -p
     const double H0 = a.H0[c];
+    // the merge's operands (the tree's summed momentum and ends, the
+    // subtree's first and last leaf, the inverse mass): nothing before the
+    // merge changes them, so with one element per thread (d <= kNT) they
+    // are loaded here, under the latency of the walk's first loads
+    const size_t CD = (size_t)a.C * d;
+    double* rho = a.rho + (size_t)c * d;
+    const double* lp = a.end_p + (size_t)c * d;        // tree, left end
+    const double* lps = a.end_ps + (size_t)c * d;
+    const double* rp = a.end_p + CD + (size_t)c * d;   // tree, right end
+    const double* rps = a.end_ps + CD + (size_t)c * d;
+    const double* p_first = a.st_p + (size_t)rows(0) * d;
+    const double* p_last = a.st_p + (size_t)rows(n - 1) * d;
+    const bool pre = d <= kNT;
+    double x_rho = 0.0, x_lp = 0.0, x_lps = 0.0, x_rp = 0.0, x_rps = 0.0, x_pf = 0.0,
+           x_pl = 0.0, x_m = 0.0;
+    if (pre && tid < d) {
+        x_rho = rho[tid];
+        x_lp = lp[tid];
+        x_lps = lps[tid];
+        x_rp = rp[tid];
+        x_rps = rps[tid];
+        x_pf = p_first[tid];
+        x_pl = p_last[tid];
+        x_m = a.m[tid];
+    }
 
     // H of every leaf, divergence (NaN counts as divergent)
     int div_l = 0;
@@ -123,10 +148,11 @@ __device__ __forceinline__ void level_walk(const LevelArgs& a, int c, bool fwd, 
     }
     const int div = __syncthreads_or(div_l);
 
-    // leaf momenta into the node sums
-    for (int j = warp; j < n; j += kNW) {
-        const double* src = a.st_p + (size_t)rows(j) * d;
-        for (int i = lane; i < d; i += 32) nd[(size_t)j * d + i] = mul_(sg, src[i]);
+    // a single leaf is its own node sum; with two or more, the first round
+    // (size 2) reads the leaves themselves
+    if (n == 1 && warp == 0) {
+        const double* src = a.st_p + (size_t)rows(0) * d;
+        for (int i = lane; i < d; i += 32) nd[i] = mul_(sg, src[i]);
     }
     if (tid == 0) s_ok = 1;
     __syncthreads();
@@ -141,10 +167,12 @@ __device__ __forceinline__ void level_walk(const LevelArgs& a, int c, bool fwd, 
             double s[6] = {0, 0, 0, 0, 0, 0};
             for (int i = lane; i < d; i += 32) {
                 const double mi = a.m[i];
-                const double rA = nd[(size_t)a0 * d + i], rB = nd[(size_t)mid * d + i];
-                const double r = add_(rA, rB);
                 const double vf = mul_(sg, pf[i]), val = mul_(sg, pal[i]);
                 const double vbf = mul_(sg, pbf[i]), vl = mul_(sg, pl[i]);
+                // size 2: the halves are single leaves (a0 = mid - 1, mid = b1)
+                const double rA = size == 2 ? vf : nd[(size_t)a0 * d + i];
+                const double rB = size == 2 ? vbf : nd[(size_t)mid * d + i];
+                const double r = add_(rA, rB);
                 const double v2 = add_(rA, vbf), v3 = add_(rB, val);
                 s[0] = add_(s[0], mul_(mul_(mi, vf), r));
                 s[1] = add_(s[1], mul_(mul_(mi, vl), r));
@@ -215,24 +243,20 @@ __device__ __forceinline__ void level_walk(const LevelArgs& a, int c, bool fwd, 
 
     // merge with the tree so far; A is the earlier of (tree, subtree) in time
     const double* rho_sub = nd;  // node[0]: the sum of all n leaves
-    const size_t CD = (size_t)a.C * d;
-    double* rho = a.rho + (size_t)c * d;
-    const double* lp = a.end_p + (size_t)c * d;        // tree, left end
-    const double* lps = a.end_ps + (size_t)c * d;
-    const double* rp = a.end_p + CD + (size_t)c * d;   // tree, right end
-    const double* rps = a.end_ps + CD + (size_t)c * d;
-    const double* p_first = a.st_p + (size_t)rows(0) * d;
-    const double* p_last = a.st_p + (size_t)rows(n - 1) * d;
     double s[6] = {0, 0, 0, 0, 0, 0};
     for (int i = tid; i < d; i += kNT) {
-        const double mi = a.m[i];
-        const double fp = mul_(sg, p_first[i]), lsp = mul_(sg, p_last[i]);
+        const double mi = pre ? x_m : a.m[i];
+        const double rhoi = pre ? x_rho : rho[i];
+        const double lpi = pre ? x_lp : lp[i], lpsi = pre ? x_lps : lps[i];
+        const double rpi = pre ? x_rp : rp[i], rpsi = pre ? x_rps : rps[i];
+        const double fp = mul_(sg, pre ? x_pf : p_first[i]);
+        const double lsp = mul_(sg, pre ? x_pl : p_last[i]);
         const double fps = mul_(mi, fp), lps_ = mul_(mi, lsp);
-        const double rA = fwd ? rho[i] : rho_sub[i], rB = fwd ? rho_sub[i] : rho[i];
-        const double pAl = fwd ? rp[i] : lsp;
-        const double psAf = fwd ? lps[i] : fps, psAl = fwd ? rps[i] : lps_;
-        const double pBf = fwd ? fp : lp[i];
-        const double psBf = fwd ? fps : lps[i], psBl = fwd ? lps_ : rps[i];
+        const double rA = fwd ? rhoi : rho_sub[i], rB = fwd ? rho_sub[i] : rhoi;
+        const double pAl = fwd ? rpi : lsp;
+        const double psAf = fwd ? lpsi : fps, psAl = fwd ? rpsi : lps_;
+        const double pBf = fwd ? fp : lpi;
+        const double psBf = fwd ? fps : lpsi, psBl = fwd ? lps_ : rpsi;
         const double r = add_(rA, rB), v2 = add_(rA, pBf), v3 = add_(rB, pAl);
         s[0] = add_(s[0], mul_(psAf, r));
         s[1] = add_(s[1], mul_(psBl, r));
@@ -248,15 +272,15 @@ __device__ __forceinline__ void level_walk(const LevelArgs& a, int c, bool fwd, 
     const bool cont = ok_sub && ok_m;
     // every thread has read rho, the ends and node[0] (block_sums synchronised)
     for (int i = tid; i < d; i += kNT) {
-        if (cont) rho[i] = add_(rho[i], rho_sub[i]);
+        if (cont) rho[i] = add_(pre ? x_rho : rho[i], rho_sub[i]);
         if (ok_sub) {
             // the subtree's far end becomes the tree's end on its side
-            const double* pe = fwd ? p_last : p_first;
-            const double v = mul_(sg, pe[i]);
+            const double pe = pre ? (fwd ? x_pl : x_pf) : (fwd ? p_last : p_first)[i];
+            const double v = mul_(sg, pe);
             double* ep = a.end_p + (fwd ? CD : 0) + (size_t)c * d;
             double* eps_ = a.end_ps + (fwd ? CD : 0) + (size_t)c * d;
             ep[i] = v;
-            eps_[i] = mul_(a.m[i], v);
+            eps_[i] = mul_(pre ? x_m : a.m[i], v);
         }
     }
     if (tid == 0) {
