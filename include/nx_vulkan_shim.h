@@ -481,8 +481,12 @@ int nxv_nuts_level_layout(unsigned long long base_row, unsigned int n, unsigned 
  * (active at the end, divergent, depth, leapfrog steps) and H0 [n_chains]
  * (initial energy).  The tree state and the store (n_chains (2^max_depth -
  * 1) leaves) live in library scratch, kept for the next call.  -3 when
- * max_depth is outside 1..12.  Returns after the last level's flag read;
- * the outputs are complete in stream order. */
+ * max_depth is outside 1..12.  The level kernels run on a second stream of
+ * the library, ordered with the caller's stream by events, so that each
+ * level's walk overlaps the next level's chain call.  Returns after the
+ * last level's flag read (the call synchronises with the device once per
+ * level, so it cannot be captured into a CUDA graph); the outputs are
+ * complete in the caller's stream order. */
 int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, void* inv_mass,
                                void* prec, double mu, double logp_const, double eps,
                                unsigned int n_chains, unsigned int d, unsigned int max_depth,
