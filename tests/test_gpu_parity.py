@@ -474,6 +474,32 @@ def test_philox_matches_oracle(nxv, orc, monkeypatch, n, exact):
         close(g64, orc.random_f64(n, seed, 1), 1e-12, 1e-14)
 
 
+def test_f64_normals_against_exact_box_muller(nxv):
+    """f64 normals against the Box-Muller transform of the same uniforms
+    (pair c: u1 = uniform 2c + 2^-53, u2 = uniform 2c + 1) evaluated in
+    50-digit arithmetic: within 4 units in the last place of each result,
+    near the zeros of sin and cos too (sin(pi r) is evaluated on an exactly
+    reduced r)."""
+    import mpmath
+
+    mpmath.mp.dps = 50
+    n, seed = 4000, 77
+    u = down(nxv, unwrap(nxv.random_f64(n, seed, 0)), np.float64)
+    g = down(nxv, unwrap(nxv.random_f64(n, seed, 1)), np.float64)
+    worst = 0.0
+    for c in range(n // 2):
+        u1 = mpmath.mpf(float(u[2 * c])) + mpmath.mpf(2) ** -53
+        u2 = mpmath.mpf(float(u[2 * c + 1]))
+        r = mpmath.sqrt(-2 * mpmath.log(u1))
+        for got, want in ((g[2 * c], r * mpmath.cos(2 * mpmath.pi * u2)),
+                          (g[2 * c + 1], r * mpmath.sin(2 * mpmath.pi * u2))):
+            w = float(want)
+            ulp = np.spacing(abs(w)) if w != 0 else np.finfo(np.float64).tiny
+            worst = max(worst, float(abs(mpmath.mpf(float(got)) - want) / ulp))
+    print(f"f64 normals: max {worst:.2f} ulp against the exact transform")
+    assert worst <= 4.0
+
+
 @pytest.mark.parametrize("mn", [(1, 1), (3, 5), (33, 65), (1000, 17), (4096, 4096), (8, 3000), (3000, 9)])
 def test_transpose_and_cast(nxv, orc, mn):
     m, n = mn
