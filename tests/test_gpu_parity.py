@@ -500,6 +500,31 @@ def test_f64_normals_against_exact_box_muller(nxv):
     assert worst <= 4.0
 
 
+def test_f32_normals_against_exact_box_muller(nxv, monkeypatch):
+    """Default f32 normals (f32 arithmetic) against the Box-Muller transform
+    of the same uniforms (pair c: u1 = uniform 2c + 2^-24, u2 = uniform
+    2c + 1) in 50-digit arithmetic: within 4 f32 units in the last place."""
+    import mpmath
+
+    monkeypatch.setenv("NXV_EXACT_F32", "0")
+    mpmath.mp.dps = 50
+    n, seed = 4000, 91
+    u = down(nxv, unwrap(nxv.uniform(n, seed)), np.float32)
+    g = down(nxv, unwrap(nxv.normal(n, seed)), np.float32)
+    worst = 0.0
+    for c in range(n // 2):
+        u1 = mpmath.mpf(float(u[2 * c])) + mpmath.mpf(2) ** -24
+        u2 = mpmath.mpf(float(u[2 * c + 1]))
+        r = mpmath.sqrt(-2 * mpmath.log(u1))
+        for got, want in ((g[2 * c], r * mpmath.cos(2 * mpmath.pi * u2)),
+                          (g[2 * c + 1], r * mpmath.sin(2 * mpmath.pi * u2))):
+            w = np.float32(float(want))
+            ulp = float(np.spacing(abs(w))) if w != 0 else float(np.finfo(np.float32).tiny)
+            worst = max(worst, float(abs(mpmath.mpf(float(got)) - want) / ulp))
+    print(f"f32 normals: max {worst:.2f} ulp against the exact transform")
+    assert worst <= 4.0
+
+
 @pytest.mark.parametrize("mn", [(1, 1), (3, 5), (33, 65), (1000, 17), (4096, 4096), (8, 3000), (3000, 9)])
 def test_transpose_and_cast(nxv, orc, mn):
     m, n = mn
