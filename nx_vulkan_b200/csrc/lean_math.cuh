@@ -152,6 +152,20 @@ __device__ __forceinline__ double expm1(double x) {
     return expm1_core(x);
 }
 
+// expm1_core for x in [-40, 0] (tanh's argument), with 2^m (m >= -58)
+// applied to the bracket t p + t_lo (1 + p) through the exponent field
+// instead of a product with the tail: the same value, since the bracket is
+// 0 only where m = 0 and otherwise stays far above the normal range's
+// bottom when scaled.
+__device__ __forceinline__ double expm1_tanh(double x) {
+    int k;
+    const double p = reduce(x, k);
+    const int m = k >> 6;
+    const double2 t = __ldg(&kExp2J64HL[k & 63]);
+    const double s = scale_pow2(t.x, m);
+    return __dadd_rn(__dsub_rn(s, 1.0), scale_pow2(__fma_rn(t.x, p, __fma_rn(t.y, p, t.y)), m));
+}
+
 // 1 / d for d in [1, 2]: the hardware's f64 reciprocal estimate (PTX
 // rcp.approx.ftz.f64, from the high word: about 20 bits) refined by two
 // Newton steps r <- r (2 - d r) to within an ulp or two of double.
@@ -166,7 +180,7 @@ __device__ __forceinline__ double recip_1_2(double d) {
 __device__ __forceinline__ double tanh(double x) {
     const double a = fabs(x);
     if (a > 20.0) return copysign(1.0, x);
-    const double e = expm1_core(-2.0 * a);  // in (-1, 0]; -2a >= -40
+    const double e = expm1_tanh(-2.0 * a);  // in (-1, 0]; -2a >= -40
     return copysign(__dmul_rn(-e, recip_1_2(__dadd_rn(2.0, e))), x);
 }
 
@@ -191,11 +205,13 @@ __device__ __forceinline__ float round_f32_checked(double y, bool& ok) {
 // stays below 2^-47), e^r - 1 to r^5 (truncation below 2^-47 relative to
 // e^r - 1), the table head alone (2^-53), the power of two added to the
 // exponent field, and a reciprocal from the f32 hardware estimate with one
-// Newton step.  Over a sweep of 2^26 f32 arguments against 64-bit long
+// Newton step (tanh: the f64 estimate, one Newton step and a quotient
+// correction).  Over a sweep of 2^26 f32 arguments against 64-bit long
 // double references, with the f32 estimate taken one ulp off, the largest
-// errors were 27 (exp), 65 (expm1), 391 (tanh) and 217 (sigmoid) double
-// ulps; results within kMarginF32 = 2048 double ulps of an f32 rounding
-// boundary (about 8 in a million) go to the caller's library fallback.
+// errors were 27 (exp), 65 (expm1), 391 (tanh, with the f32 estimate) and
+// 217 (sigmoid) double ulps; results within kMarginF32 = 2048 double ulps of
+// an f32 rounding boundary (about 8 in a million) go to the caller's library
+// fallback.
 
 constexpr unsigned kMarginF32 = 2048;
 constexpr double kLn2d64 = 0x1.62e42fefa39efp-7;  // ln 2 / 64 rounded to double
@@ -250,9 +266,13 @@ __device__ __forceinline__ float tanh_f32(float x, bool& ok) {
     const double p = reduce_short(-2.0 * (double)ax, s);
     const double e = __fma_rn(s, p, __dsub_rn(s, 1.0));
     const double den = __dadd_rn(2.0, e);
-    const double r = recip_f32_newton(den);
+    // the f64 reciprocal estimate with one Newton step, then one quotient
+    // correction: the quotient's error is the square of the reciprocal's
+    double r;
+    asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(den));
+    r = __fma_rn(r, __fma_rn(-den, r, 1.0), r);
     const double q0 = __dmul_rn(-e, r);
-    const double q = __fma_rn(r, __fma_rn(-q0, den, -e), q0);  // one quotient correction
+    const double q = __fma_rn(r, __fma_rn(-q0, den, -e), q0);
     const float v = round_f32_checked<kMarginF32>(q, ok);
     ok = ok && x == x;
     return copysignf(v, x);
