@@ -862,10 +862,11 @@ int nxv_nuts_transition_layout(void* sample, void* flags, void* H0, void* q0, vo
         if (e != cudaSuccess) return cuda_fail(e, "nuts_transition_layout: stream wait");
         k_nuts_level_layout<<<(unsigned)C, kNT, 0, ns->aux>>>(g, Lg);
         count_launch();
-        // one 4-byte read per level from the second on (the first level
-        // always continues: for chains whose tree has stopped, a level's
-        // kernels change nothing but scratch)
-        const bool check = level >= 1 && level + 1 < L;
+        // one 4-byte read per level from the third on (the first two levels
+        // always continue: for chains whose tree has stopped, a level's
+        // kernels change nothing but scratch, and a level of 1, 2 or 4
+        // steps costs less than a wait for the flag)
+        const bool check = level >= 2 && level + 1 < L;
         if (check)
             e = cudaMemcpyAsync(any_h, any + level, sizeof(int), cudaMemcpyDeviceToHost, ns->aux);
         if (e == cudaSuccess) e = cudaEventRecord(ns->level_done, ns->aux);
