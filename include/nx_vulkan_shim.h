@@ -474,8 +474,8 @@ int nxv_nuts_level_layout(unsigned long long base_row, unsigned int n, unsigned 
  * nxv_random_f64 streams of keys seed and seed ^ 0x5BD1E995), the initial
  * energy, then per level one start kernel, one batched Gaussian chain call
  * of 2^l steps (with kinetic energy) into the library's own leaf store and
- * one level kernel, with one 4-byte read per level of whether any tree
- * still grows.  q0 [n_chains][d], inv_mass and prec [d] (the Gaussian
+ * one level kernel, with one 4-byte read per level (from the third on) of
+ * whether any tree still grows.  q0 [n_chains][d], inv_mass and prec [d] (the Gaussian
  * target's diagonal precision and mean mu, logp_const the log density's
  * constant); outputs sample [n_chains][d], flags [4][n_chains] int32
  * (active at the end, divergent, depth, leapfrog steps) and H0 [n_chains]
